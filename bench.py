@@ -1,0 +1,382 @@
+#!/usr/bin/env python3
+"""Benchmark of the decode MoE layer-step on B200: router top-k + W4A16 routed experts + shared expert + combine.
+
+Default workload: H=2048, 512 experts, top-10 renormalised, I=512 int4 group-128 experts,
+bf16 shared expert (Is=512), M=10 tokens. A "step" is one layer-step (router_topk + a16_moe_decode, two kernels);
+the timed loop replays a CUDA graph over L distinct synthetic layers (default 16, 13.6 GB of weights), so every
+step streams its experts from HBM (each step touches ~157 MB, a full cycle ~2.5 GB >> 126 MB L2).
+
+Output: one JSON line (rank 0). value = microseconds per layer-step (lower is better); roofline = the MoE kernel's
+algorithmic bytes per launch / its CUDA-event launch time vs the measured HBM copy bandwidth; e2e = the same step
+through the public ops with pinned-host x in and out copied back every step; cpu_baseline = the CPU oracle (a port
+of the reference's torch dequant-and-matmul path) on this host.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--M 10] [--layers 16]
+  python bench.py --sweep out.json      # config 2 (M sweep, Zipf routing) and config 3 (W8A8) extra records
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_ROOT = os.path.join(ROOT, "qwen-3.8-flash-next-pro6000_b200")
+for _p in (ROOT, PKG_ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "µs per MoE layer-step & achieved HBM GB/s at M=1–64, 1/2/4/8 B200"
+UNIT = "us/layer-step"
+PER_EXPERT_BYTES = None   # filled from the config: int4 weights + bf16 scales of gate_up and down
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=480)
+    ap.add_argument("--warmup", type=int, default=48)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--M", type=int, default=10)
+    ap.add_argument("--layers", type=int, default=16)
+    ap.add_argument("--zipf", type=float, default=0.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", default="")
+    return ap.parse_args()
+
+
+def expert_bytes(H, I, group=128):
+    return (2 * I * H + H * I) // 2 + 2 * (2 * I * H + H * I) // group
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic(name):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get(name)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------------------------------------ CPU legs
+def cpu_layer(cfg, seed=0):
+    """A CPU layer for the oracle whose experts are materialised lazily (only the routed ones are filled)."""
+    import torch
+    from qwenfast_b200 import synthetic
+    g = torch.Generator().manual_seed(seed)
+    H, E, I = cfg.H, cfg.E, cfg.I
+    L = dict(router=(torch.randn(E, H, generator=g) * 0.02).to(torch.bfloat16),
+             w_gate=(torch.randn(H, generator=g) * 0.02).to(torch.bfloat16),
+             sh_gu=(torch.randn(2 * cfg.Is, H, generator=g) * 0.02).to(torch.bfloat16),
+             sh_d=(torch.randn(H, cfg.Is, generator=g) * 0.02).to(torch.bfloat16),
+             w13=torch.empty(E, 2 * I, H // 8, dtype=torch.int32), s13=torch.empty(E, 2 * I, H // 128, dtype=torch.bfloat16),
+             w2=torch.empty(E, H, I // 8, dtype=torch.int32), s2=torch.empty(E, H, I // 128, dtype=torch.bfloat16),
+             filled=set())
+
+    def fill(ids):
+        for e in set(ids.flatten().tolist()) - L["filled"]:
+            ge = torch.Generator().manual_seed(seed * 100003 + e)
+            L["w13"][e] = synthetic.random_int4_words((2 * I, H // 8), ge, "cpu")
+            L["s13"][e] = synthetic.group_scales((2 * I, H // 128), ge, "cpu")
+            L["w2"][e] = synthetic.random_int4_words((H, I // 8), ge, "cpu")
+            L["s2"][e] = synthetic.group_scales((H, I // 128), ge, "cpu")
+            L["filled"].add(e)
+    L["fill"] = fill
+    return L
+
+
+def cpu_step(cfg, L, x):
+    from oracle import moe_ref, router_ref
+    w, ids, _ = router_ref.router_topk(x, L["router"], cfg.topk, True)
+    L["fill"](ids)
+    return moe_ref.moe_rounded(x, ids, w, L["w13"], L["s13"], L["w2"], L["s2"], w_gate=L["w_gate"],
+                               shared_w=(L["sh_gu"], L["sh_d"]))
+
+
+def time_cpu(cfg, M, steps, warmup, budget_s):
+    """Times the CPU oracle layer-step with every host thread. Returns (us per step, steps timed, threads)."""
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    from qwenfast_b200 import synthetic
+    L = cpu_layer(cfg)
+    xs = [synthetic.make_tokens(cfg, M=M, seed=s) for s in range(4)]
+    for i in range(max(4, warmup)):     # at least one pass over the inputs: every routed expert is materialised
+        cpu_step(cfg, L, xs[i % 4])
+    n, t0 = 0, time.perf_counter()
+    while n < steps and (n == 0 or time.perf_counter() - t0 < budget_s):
+        cpu_step(cfg, L, xs[n % 4])
+        n += 1
+    dt = time.perf_counter() - t0
+    return dt / n * 1e6, n, torch.get_num_threads()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from qwenfast_b200 import synthetic
+    cfg = synthetic.CONFIGS[1]
+    us, n, cores = time_cpu(cfg, args.M, args.steps, 4, budget_s=150.0)
+    line = {"impl": "reference", "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
+            "warmup": 4, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16/int4 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"config1 MoE layer-step M={args.M} (CPU oracle port of the reference torch path)",
+                       "H": cfg.H, "E": cfg.E, "I": cfg.I, "topk": cfg.topk, "Is": cfg.Is, "M": args.M},
+            "cpu_baseline": {"value": us, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"{n} layer-steps (router + routed experts + shared) on the host"},
+            "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ GPU arm
+def build_layers(cfg, nl, dev, zipf=0.0):
+    import torch
+    from qwenfast_b200 import synthetic
+    from qwenfast_b200.ops import MoELayerWeights
+    layers = []
+    for l in range(nl):
+        L = synthetic.make_moe_layer(cfg, device=dev, seed=1000 + l, zipf_s=zipf)
+        layers.append(MoELayerWeights.from_canonical(L["router"], L["w13"], L["s13"], L["w2"], L["s2"], L["w_gate"],
+                                                     L["sh_gu"], L["sh_d"]))
+        del L
+    torch.cuda.synchronize()
+    return layers
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from qwenfast_b200 import build as qbuild
+    from qwenfast_b200 import ops, synthetic
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    qbuild.build()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    cfg = synthetic.CONFIGS[1]
+    M, NL = args.M, args.layers
+    layers = build_layers(cfg, NL, dev, args.zipf)
+    bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, dev)
+    rb = ops.router_bufs(dev)
+    x0 = synthetic.make_tokens(cfg, M=M, device=dev, seed=rank)
+    xs = [x0] + [torch.empty_like(x0) for _ in range(NL)]
+    ids_keep = [None] * NL
+
+    def step(l, pdl=True):
+        _, tw, ids, _ = ops.moe_layer_step(xs[l], layers[l], cfg.topk, bufs, rb, xs[l + 1], pdl=pdl)
+        ids_keep[l] = ids
+        return tw, ids
+
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            for l in range(NL):
+                step(l)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    err = ops.moe_error_word(bufs["ctrl"])
+    if err:
+        raise RuntimeError(f"MoE kernel reported error word {err:#x}")
+
+    g_full = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_full):
+        tws = [step(l) for l in range(NL)]
+    ids_list = [t[1] for t in tws]
+    tw_list = [t[0] for t in tws]
+    # MoE-kernel-only graph over the same routing (for the per-launch kernel time of the roofline)
+    g_moe = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_moe):
+        for l in range(NL):
+            lw = layers[l]
+            ops.a16_moe_decode(xs[l], ids_list[l], tw_list[l], lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate,
+                               None, bufs["hbuf"], bufs["ybuf"], bufs["gl"], bufs["ctrl"], xs[l + 1], 4, None,
+                               bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None, bufs["shbuf"])
+    g_router = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_router):
+        for l in range(NL):
+            ops.router_topk(xs[l], layers[l].router, cfg.topk, True, rb[0], rb[1])
+
+    def timed(graph, reps):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0.record()
+        for _ in range(reps):
+            graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    warm_reps = max(1, math.ceil(max(args.warmup, 3) / NL))
+    reps = max(1, math.ceil(args.steps / NL))
+    for _ in range(warm_reps):
+        g_full.replay()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms_full = timed(g_full, reps)
+    steps = reps * NL
+    us_step = ms_full * 1e3 / steps
+    for _ in range(warm_reps):
+        g_moe.replay()
+    us_moe = timed(g_moe, reps) * 1e3 / steps
+    for _ in range(warm_reps):
+        g_router.replay()
+    us_router = timed(g_router, reps) * 1e3 / steps
+    torch.cuda.synchronize()
+    err = ops.moe_error_word(bufs["ctrl"])
+    if err:
+        raise RuntimeError(f"MoE kernel reported error word {err:#x}")
+
+    # algorithmic bytes (counted from the routing each layer actually produced)
+    per_e = expert_bytes(cfg.H, cfg.I)
+    U = [int(torch.unique(ids_list[l]).numel()) for l in range(NL)]
+    shared_b = (3 * cfg.H * cfg.Is + cfg.H) * 2
+    act_b = 2 * M * cfg.H * 2
+    moe_b = [u * per_e + shared_b + act_b for u in U]
+    router_b = cfg.E * cfg.H * 2 + M * cfg.H * 2
+    step_b = statistics.mean(moe_b) + router_b
+    peak, peak_kind = load_peaks()
+    achieved = statistics.mean(moe_b) / (us_moe * 1e-6) / 1e9
+
+    # end to end through the public ops: pinned host x in, result out, every step
+    xh = x0.cpu().pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(x0)
+    od = torch.empty_like(x0)
+    for l in range(NL):
+        xd.copy_(xh, non_blocking=True)
+        ops.moe_layer_step(xd, layers[l], cfg.topk, bufs, rb, od)
+        oh.copy_(od, non_blocking=True)
+    torch.cuda.synchronize()
+    n_e2e = min(args.steps, 4 * NL)
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(n_e2e):
+        xd.copy_(xh, non_blocking=True)
+        ops.moe_layer_step(xd, layers[i % NL], cfg.topk, bufs, rb, od)
+        oh.copy_(od, non_blocking=True)
+    ev1.record()
+    torch.cuda.synchronize()
+    e2e_ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    us_e2e = e2e_ms * 1e3 / n_e2e
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        us_cpu, n_cpu, cores = time_cpu(cfg, M, steps=40, warmup=4, budget_s=20.0)
+        cpu = {"value": us_cpu, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{n_cpu} config-1 layer-steps (M={M}) of the CPU oracle, torch fp32 on {cores} threads"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": us_step, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warm_reps * NL,
+            "ms_per_step": us_step / 1e3, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 activations, int4 experts, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": f"config1 decode MoE layer-step (router top-10 + 512-expert W4A16 + bf16 shared "
+                                   f"expert + combine), M={M}",
+                       "H": cfg.H, "E": cfg.E, "I": cfg.I, "topk": cfg.topk, "Is": cfg.Is, "M": M,
+                       "layers_cycled": NL, "zipf_s": args.zipf,
+                       "l2": f"weights cycled over {NL} layers (~{statistics.mean(moe_b) * NL / 1e9:.1f} GB touched "
+                             f"per cycle) > 126 MB L2; no flush",
+                       "parallelism": "replicas" if world > 1 else "single GPU", "graph": "CUDA graph + PDL"},
+            "hbm_gbs_step": step_b / (us_step * 1e-6) / 1e9,
+            "unique_experts_mean": statistics.mean(U),
+            "us_moe_kernel": us_moe, "us_router_kernel": us_router,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "kernel": "moe_persistent_kernel",
+                         "bytes_per_launch": statistics.mean(moe_b),
+                         "traffic": load_traffic("moe_persistent_kernel")},
+            "e2e": {"value": us_e2e, "unit": UNIT, "h2d_bytes_per_step": M * cfg.H * 2,
+                    "d2h_bytes_per_step": M * cfg.H * 2, "steps": n_e2e},
+            "gpu_launches": 2 * steps,
+            "clocks": clk.summary(),
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del g_full, g_moe, g_router
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

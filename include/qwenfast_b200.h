@@ -1,0 +1,145 @@
+/*
+ * qwenfast_b200 -- C ABI of the sm_100a decode-path kernels (router top-k, W4A16 routed-expert MoE with shared
+ * expert and combine, INT8 dense GEMMs).
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless stated otherwise; nothing here allocates device memory or
+ *     synchronises the stream. Work is enqueued on `stream` (a cudaStream_t).
+ *   - bf16 tensors are passed as `void*` (IEEE bfloat16, row-major, contiguous unless a leading dimension is given).
+ *   - Every entry point returns QF_OK (0) or a negative QF_ERR_* code; qf_last_error() then describes the failure
+ *     (thread-local text). Argument checks happen on the host before anything is enqueued.
+ *   - `pdl != 0` launches with programmatic stream serialization so the kernel can start while the previous kernel
+ *     in the stream drains; every kernel waits (griddepcontrol.wait) before it touches data that kernel produced.
+ *   - Kernels that wait on other CTAs bound each wait; a wait that runs out records a code in the kernel's control
+ *     block instead of hanging (see QF_MOE_CTRL_ERR).
+ */
+#ifndef QWENFAST_B200_H
+#define QWENFAST_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qf_stream_t; /* identical to cudaStream_t */
+
+enum {
+    QF_OK = 0,
+    QF_ERR_INVALID_ARGUMENT = -1, /* shape, dtype, alignment or size check failed */
+    QF_ERR_CUDA = -2,             /* a CUDA runtime call failed */
+    QF_ERR_UNSUPPORTED = -3       /* valid request this build does not implement */
+};
+
+/* Limits of this build. */
+#define QF_MAX_TOKENS 64   /* decode/verify rows per call (M) */
+#define QF_MAX_TOPK 16
+#define QF_MAX_EXPERTS 1024
+
+/* MoE control block: int32[QF_MOE_CTRL_WORDS], zeroed once by the caller, re-armed by the kernel itself.
+ * Word QF_MOE_CTRL_ERR is sticky: non-zero after a launch means a bounded wait ran out or a routed expert id was
+ * out of range (QF_MOE_ERR_* bits); the caller clears it. */
+#define QF_MOE_CTRL_WORDS 2048
+#define QF_MOE_CTRL_ERR 3
+#define QF_MOE_ERR_TIMEOUT 0x1
+#define QF_MOE_ERR_BAD_EXPERT 0x2
+#define QF_MOE_ERR_PIPELINE 0x4
+
+const char* qf_last_error(void);
+int qf_version(void);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Router: logits = bf16(x . w^T) (fp32 accumulation), fp32 softmax over the logits, top-k by logit value with the
+ * lower expert id winning ties (NaN ranks as -1e30, -0 equals +0), weights renormalised over the selection when
+ * `renormalize` (unless their sum is not positive).
+ * Replaces `router_topk` (serve/qwenfast/qf_router.cu:164-193, binding serve/qwenfast/qf_bind.cpp:14-15,121-123).
+ *   x bf16 [rows, hidden]; w bf16 [experts, hidden]; outputs topk_weights fp32 [rows, topk],
+ *   topk_ids int32 [rows, topk], logits bf16 [rows, experts];
+ *   scratch fp32 >= rows*experts; counter int32[1] zeroed once (re-armed by the kernel).
+ * rows 1..QF_MAX_TOKENS, hidden % 256 == 0 (<= 8192), experts % 16 == 0 (<= QF_MAX_EXPERTS), topk 1..16.
+ * ------------------------------------------------------------------------------------------------------------ */
+int qf_router_topk(const void* x, const void* w, int rows, int hidden, int experts, int topk, int renormalize,
+                   float* topk_weights, int32_t* topk_ids, void* logits, float* scratch, int64_t scratch_numel,
+                   int32_t* counter, int pdl, qf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * Routed experts (W4A16) + shared expert + combine, one persistent launch.
+ * Replaces `a16_moe_decode` (serve/qwenfast/qf_a16moe.cu:852-922, binding serve/qwenfast/qf_bind.cpp:90-97,142);
+ * same argument roles, with the synthetic configurations' int4 format instead of NVFP4:
+ *   x bf16 [M, H]; topk_ids int32 [M, topk]; topk_w fp32 [M, topk];
+ *   w13 / s13: gate_up experts, int4 (code - 8) and bf16 group-128 scales in the kernel layout made by
+ *              qf_w4_repack(gated = 1) from [E, 2I, H/8] int32 / [E, 2I, H/128] bf16;
+ *   w2 / s2:   down experts in the kernel layout made by qf_w4_repack(gated = 0) from [E, H, I/8] / [E, H, I/128];
+ *   gs13, gs2: bf16 [E] per-expert global scales or NULL (= 1);
+ *   w_gate:    bf16 [H] shared-expert gate vector (required when a shared term is present);
+ *   shared:    bf16 [M, H] precomputed shared-expert output, or NULL;
+ *   sh_w13, sh_w2: bf16 shared expert weights (gate_up [2*Is, H] and down [H, Is]) in the kernel layout made by
+ *              qf_bf16_repack (gated = 1 / 0), or NULL; Is = their intermediate size (0 when absent);
+ *   scratch (caller-owned, sizes from qf_a16_moe_workspace): hbuf, ybuf, gl, ctrl (zeroed once), pbuf, shbuf;
+ *   out bf16 [M, H].
+ * out[t] = bf16(sigmoid(x[t].w_gate) * shared[t] + bf16(sum over top-k positions, in order, of
+ *          bf16(bf16(expert_out) * bf16(gs2 * bf16(topk_w)))))  -- the reference's rounding points.
+ * phase: 3 or 4 (the whole layer); the reference's split phases 1 and 2 are not provided.
+ * mode 0: full layer. mode 1: expert-parallel shard -- only experts in [expert_lo, expert_hi) are computed; their
+ *   weighted slot outputs go to ybuf [M, topk + 1, H] with every other slot zero, slot `topk` holding the shared
+ *   expert output when this shard computes it; qf_moe_combine then finishes the layer (after the caller has summed
+ *   ybuf over the shards).
+ * dbg: optional int64 [grid * 32] per-CTA globaltimer stamps, or NULL.
+ * ------------------------------------------------------------------------------------------------------------ */
+int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64_t* hbuf_bytes, int64_t* ybuf_bytes,
+                         int64_t* gl_numel, int64_t* ctrl_numel, int64_t* pbuf_numel, int64_t* shbuf_bytes);
+
+int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* w13,
+                      const void* s13, const void* gs13, const int32_t* w2, const void* s2, const void* gs2,
+                      const void* w_gate, const void* shared, const void* sh_w13, const void* sh_w2, void* hbuf,
+                      int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl, int64_t gl_numel, int32_t* ctrl,
+                      int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel, void* shbuf, int64_t shbuf_bytes,
+                      void* out, int M, int H, int I, int E, int topk, int Is, int phase, int mode, int expert_lo,
+                      int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream);
+
+/* Expert-parallel finish: out = the mode-0 combine of a ybuf [M, topk + 1, H] summed over the shards.
+ * gl fp32 [M] is recomputed from x and w_gate when w_gate is given (has_shared != 0). */
+int qf_moe_combine(const void* ybuf, const void* x, const void* w_gate, int has_shared, void* out, int M, int H,
+                   int topk, int pdl, qf_stream_t stream);
+
+/* Offline weight preparation (load time). Canonical int4 experts -> kernel layout, and back (exact).
+ *   qweight int32 [E, N, K/8] (eight codes per word, lowest k in the low nibble), scales bf16 [E, N, K/128]
+ *   -> wk int32 [E, N*K/8], sk bf16 [E, N*K/128]. gated = 1 for gate_up (N = 2I rows: gate then up), else 0.
+ *   N % 128 == 0 and K % 128 == 0. */
+int qf_w4_repack(const int32_t* qweight, const void* scales, int32_t* wk, void* sk, int E, int N, int K, int gated,
+                 qf_stream_t stream);
+int qf_w4_unpack(const int32_t* wk, const void* sk, int32_t* qweight, void* scales, int E, int N, int K, int gated,
+                 qf_stream_t stream);
+/* bf16 [N, K] -> kernel layout [N*K] (and back). N % 128 == 0, K % 64 == 0. */
+int qf_bf16_repack(const void* w, void* wk, int N, int K, int gated, qf_stream_t stream);
+int qf_bf16_unpack(const void* wk, void* w, int N, int K, int gated, qf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * W8A16 group-scaled INT8 GEMM: y[M, N] = x[M, K] @ (q * s)^T, fp32 accumulation, bf16 out.
+ * Replaces `w8g_gemm` (serve/qwenfast/qf_w8g.cu:303-336, binding serve/qwenfast/qf_bind.cpp:42,133);
+ *   x bf16 [M, K] row stride ldx (ldx % 8 == 0, 16-byte aligned); q int8 [N, K]; s bf16 [N, K/group];
+ *   y bf16 [M, N] row stride ldy. M 1..QF_MAX_TOKENS, K % 128 == 0, group 128 (or 64).
+ *   rpw: accepted for signature parity (row-per-warp hint of the reference); the bits 0x100 / 0x200 are ignored.
+ * ------------------------------------------------------------------------------------------------------------ */
+int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const void* s, void* y, int64_t ldy, int M, int N,
+                int K, int group, int rpw, int pdl, qf_stream_t stream);
+/* w bf16 [rows, K] = bf16(q * s). Replaces `w8g_unpack` (serve/qwenfast/qf_w8g.cu:338-351). */
+int qf_w8g_unpack(const int8_t* q, const void* s, void* w, int64_t rows, int K, int group, qf_stream_t stream);
+
+/* ------------------------------------------------------------------------------------------------------------
+ * W8A8 INT8 GEMM (no counterpart kernel in the reference; the dense projections of the synthetic config 3):
+ *   sx[t] = absmax(x[t]) / 127 (1 for an all-zero row); xq = rint(x / sx) clamped to [-127, 127];
+ *   acc = sum_k xq * q (exact int32 on tcgen05 tensor cores); y = bf16((float(acc) * sx[t]) * sw[n]).
+ *   x bf16 [M, K] (row stride ldx); q int8 [N, K]; sw fp32 [N]; y bf16 [M, N] (row stride ldy);
+ *   scratch: xq int8 [M*K], sx fp32 [M], acc int32 [M*N] (split-K accumulators, zeroed by the call);
+ *   acc_out: optional int32 [M, N] copy of the exact accumulators (NULL to skip).
+ *   M 1..16, K % 128 == 0, N % 128 == 0.
+ * ------------------------------------------------------------------------------------------------------------ */
+int qf_w8a8_gemm(const void* x, int64_t ldx, const int8_t* q, const float* sw, void* y, int64_t ldy, int M, int N,
+                 int K, int8_t* xq, float* sx, int32_t* acc, int32_t* acc_out, int pdl, qf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWENFAST_B200_H */

@@ -1,0 +1,945 @@
+// Decode-size (1..64 tokens) W4A16 routed experts + shared expert + top-k combine in ONE persistent launch.
+//
+// Reference behaviour: serve/qwenfast/qf_a16moe.cu (persistent mode :342-837, host :852-922): gemm1 (gate_up) +
+// SwiGLU, gemm2 (down) with the top-k weight, a top-k-ordered combine per 128-column tile by the last arriving
+// work item, and the sigmoid-gated shared expert. Rounding points (qf_a16moe.cu:2-4):
+//   h  = bf16(silu(bf16(bf16(acc_gate) * gs13)) * bf16(bf16(acc_up) * gs13))
+//   y  = bf16(bf16(acc_down) * bf16(gs2 * bf16(topk_w)))            one slot per (token, top-k position)
+//   out = bf16(sigmoid(x . w_gate) * shared + bf16(sum_kpos y))      fp32 sum in top-k order
+// Expert weights are int4 codes (zero point 8) with one bf16 scale per 128 k: each 128-k group is reduced on the
+// tensor cores in fp32 and then scaled once (exact products, no per-weight scale multiply).
+//
+// B200 structure
+//   * 1 CTA per SM (148), 9 warps: warp 8 lane 0 is the producer, warps 0..7 are consumers.
+//   * Work items, claimed in order from a global queue:  GL (shared gate logits) | S1 (shared gate_up, 4-way
+//     split-K) | G1 (expert u, 128-row gate_up tile, 16-token group) | S2 (shared down) | G2 (expert u, 128-row
+//     down tile, token group). An item only depends on items claimed before it, so the queue cannot deadlock.
+//   * The producer streams each item through an NST-stage shared-memory ring with 1-D bulk copies (TMA engine,
+//     mbarrier completion): per stage 16 KB of weights (128 rows x 256 k int4, or x 64 k bf16), their scales,
+//     and the matching k-slice of the item's token rows (x for gate_up, h for down). It waits (bounded) on the
+//     gate_up -> down and shared gate_up -> down dependencies itself, so consumers never spin on other CTAs.
+//   * Each consumer warp owns 16 weight rows of the 128-row tile: int4 -> bf16 in registers (lop3 + hsub2),
+//     mma.m16n8k16 with the weights as A and tokens as B (n = 8 or 16), fp32 group partials scaled per group.
+//     gate_up tiles interleave gate row j and up row j in one fragment, so SwiGLU runs in registers.
+//   * The routing plan (unique experts, per-expert token lists, group offsets) is rebuilt identically by every
+//     CTA from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
+//   * Every wait is bounded (globaltimer); a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
+#include "qf_common.cuh"
+
+namespace {
+
+using qf::bf16_bits;
+using qf::bf16_hi;
+using qf::bf16_lo;
+using qf::bf16r;
+
+constexpr int NCW = 8;                        // consumer warps
+constexpr int MOE_THREADS = (NCW + 1) * 32;   // + the producer warp
+constexpr int CONS_THREADS = NCW * 32;
+constexpr int TG = 16;                        // tokens per token group (two n8 tiles)
+constexpr int NST = 8;                        // pipeline stages
+constexpr int W4_KC = 256;                    // int4 k per stage
+constexpr int BF_KC = 64;                     // bf16 k per stage
+constexpr int STAGE_W = 16384;                // weight bytes of a full stage
+constexpr int STAGE_S = 512;                  // scale bytes of a full int4 stage
+constexpr int STAGE_X = TG * (W4_KC + 8) * 2; // token rows of a stage (row stride kc + 8 elements)
+constexpr int STAGE_BYTES = STAGE_W + STAGE_S + STAGE_X;
+constexpr int NSPLIT = 4;                     // split-K of the shared expert's gate_up
+constexpr int MAXSLOTS = QF_MAX_TOKENS * QF_MAX_TOPK;
+constexpr uint64_t DEP_WAIT_NS = 1000000000ull;    // cross-CTA dependency waits
+constexpr uint64_t PIPE_WAIT_NS = 4000000000ull;   // ring waits (longer: they cover the dependency waits)
+
+// control block words
+enum : int {
+    C_QUEUE = 0,
+    C_EXIT = 1,
+    C_GLF = 2,
+    C_ERR = QF_MOE_CTRL_ERR,
+    C_CNT = 8,      // [64] column-tile arrivals
+    C_SDONE = 72,   // [4] finished shared gate_up tiles per token group
+    C_SPLIT = 80,   // [64] split-K arrivals per (shared tile, token group)
+    C_DONE = 160,   // [QF_MAX_EXPERTS] finished gate_up items per unique expert
+};
+static_assert(C_DONE + QF_MAX_EXPERTS <= QF_MOE_CTRL_WORDS, "ctrl layout");
+
+enum : int { K_STOP = 0, K_GL, K_S1, K_G1, K_S2, K_G2, K_CB };
+
+struct StageDesc {
+    int16_t kind, u, tile, tg, split, kidx, nk, kc, ntok, pad[3];
+};
+
+struct Params {
+    const __nv_bfloat16* x;
+    const int* ids;
+    const float* tw;
+    const uint8_t* w13;
+    const uint16_t* s13;
+    const uint16_t* gs13;
+    const uint8_t* w2;
+    const uint16_t* s2;
+    const uint16_t* gs2;
+    const __nv_bfloat16* wgate;
+    const __nv_bfloat16* shared;
+    const uint8_t* shw13;
+    const uint8_t* shw2;
+    __nv_bfloat16* hbuf;
+    __nv_bfloat16* ybuf;
+    float* gl;
+    uint32_t* ctrl;
+    float* pbuf;
+    __nv_bfloat16* hsh;
+    __nv_bfloat16* sbuf;
+    __nv_bfloat16* out;
+    long long* dbg;
+    int M, H, I, E, topk, Is, mode, elo, ehi;
+};
+
+// shared memory map (dynamic)
+constexpr int OFF_RING = 0;
+constexpr int OFF_BAR = OFF_RING + NST * STAGE_BYTES;
+constexpr int OFF_DESC = OFF_BAR + 2 * NST * 8;
+constexpr int OFF_PLAN = OFF_DESC + NST * (int)sizeof(StageDesc);
+constexpr int PLAN_ULIST = 0;                                  // int16 [QF_MAX_EXPERTS]
+constexpr int PLAN_GPRE = PLAN_ULIST + QF_MAX_EXPERTS * 2;     // int16 [QF_MAX_EXPERTS + 1]
+constexpr int PLAN_TOFF = PLAN_GPRE + (QF_MAX_EXPERTS + 8) * 2;
+constexpr int PLAN_TLIST = PLAN_TOFF + (QF_MAX_EXPERTS + 8) * 2;   // int16 [MAXSLOTS]
+constexpr int PLAN_SIDS = PLAN_TLIST + MAXSLOTS * 2;               // int16 [MAXSLOTS] copy of topk_ids
+constexpr int PLAN_MISC = PLAN_SIDS + MAXSLOTS * 2;                // int32 [64]
+constexpr int PLAN_BYTES = PLAN_MISC + 64 * 4;
+constexpr int MOE_SMEM = OFF_PLAN + PLAN_BYTES;
+static_assert(MOE_SMEM <= 227 * 1024, "shared memory budget");
+// plan-build scratch aliases the ring (the producer starts after the plan is built)
+constexpr int SCR_MASK = 0;                                        // uint64 [E]
+constexpr int SCR_EXF = SCR_MASK + QF_MAX_EXPERTS * 8;             // int16 [E] x 3 (flag, count, groups) in-chunk
+constexpr int SCR_TOFFE = SCR_EXF + 3 * QF_MAX_EXPERTS * 2;        // int16 [E] token offset per expert id
+constexpr int SCR_CHUNK = SCR_TOFFE + QF_MAX_EXPERTS * 2;          // int32 [32] x 3 chunk totals
+static_assert(SCR_CHUNK + 3 * 32 * 4 <= NST * STAGE_BYTES, "plan scratch");
+
+enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_LAST = 4, MISC_DBGN = 5 };
+
+__device__ __forceinline__ void set_err(uint32_t* ctrl, uint32_t bits) { atomicOr(ctrl + C_ERR, bits); }
+
+// Bounded wait until ctrl[idx] >= target. Gives up early when another CTA already recorded an error.
+__device__ bool wait_counter(uint32_t* ctrl, int idx, uint32_t target) {
+    if (qf::ld_acquire(ctrl + idx) >= target) return true;
+    const uint64_t t0 = qf::globaltimer();
+    while (qf::ld_acquire(ctrl + idx) < target) {
+        if (qf::ld_volatile(ctrl + C_ERR) != 0u) return false;
+        if (qf::globaltimer() - t0 > DEP_WAIT_NS) {
+            set_err(ctrl, QF_MOE_ERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+struct Layout {   // per-launch derived sizes, identical in every thread
+    int R1, R2, Rs1, ngs, U, Gt, has_gate, has_shw;
+    int b_s1, b_g1, b_s2, b_g2, b_cb, total;
+    uint32_t tile_target;
+};
+
+__device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   // largest u with gpre[u] <= key
+    int lo = 0, hi = U - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (gpre[mid] <= key) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// ---------------------------------------------------------------------------------------------- consumer math
+// One int4 stage: this warp's 16 rows x kc k, tokens in one or two n8 tiles; per-group partials scaled into acc.
+__device__ __forceinline__ void stage_w4(const uint8_t* stage, int warp, int lane, int kc, bool two,
+                                         float (&acc)[2][4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const int ngrp = kc >> 7;
+    const uint8_t* ws = stage + warp * (kc >> 6) * 512 + lane * 16;
+    const uint8_t* ss = stage + STAGE_W + warp * ngrp * 32 + g * 4;
+    const int xrb = (kc + 8) * 2;
+    const uint8_t* xs0 = stage + STAGE_W + STAGE_S + g * xrb + t * 16;
+    const uint8_t* xs1 = xs0 + 8 * xrb;
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+        if (gi < ngrp) {
+            float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                const uint4 wq = *reinterpret_cast<const uint4*>(ws + (2 * gi + cc) * 512);
+#pragma unroll
+                for (int hb = 0; hb < 2; ++hb) {
+                    const int b = 4 * gi + 2 * cc + hb;
+                    uint32_t P[4], Q[4];
+                    qf::dequant_w4(hb ? wq.z : wq.x, P);
+                    qf::dequant_w4(hb ? wq.w : wq.y, Q);
+                    const uint4 xv = *reinterpret_cast<const uint4*>(xs0 + b * 64);
+                    qf::mma_bf16(d0, P[0], Q[0], P[1], Q[1], xv.x, xv.y);
+                    qf::mma_bf16(d0, P[2], Q[2], P[3], Q[3], xv.z, xv.w);
+                    if (two) {
+                        const uint4 xw = *reinterpret_cast<const uint4*>(xs1 + b * 64);
+                        qf::mma_bf16(d1, P[0], Q[0], P[1], Q[1], xw.x, xw.y);
+                        qf::mma_bf16(d1, P[2], Q[2], P[3], Q[3], xw.z, xw.w);
+                    }
+                }
+            }
+            const uint32_t sc = *reinterpret_cast<const uint32_t*>(ss + gi * 32);
+            const float sa = bf16_lo(sc), sb = bf16_hi(sc);
+            acc[0][0] = fmaf(d0[0], sa, acc[0][0]);
+            acc[0][1] = fmaf(d0[1], sa, acc[0][1]);
+            acc[0][2] = fmaf(d0[2], sb, acc[0][2]);
+            acc[0][3] = fmaf(d0[3], sb, acc[0][3]);
+            if (two) {
+                acc[1][0] = fmaf(d1[0], sa, acc[1][0]);
+                acc[1][1] = fmaf(d1[1], sa, acc[1][1]);
+                acc[1][2] = fmaf(d1[2], sb, acc[1][2]);
+                acc[1][3] = fmaf(d1[3], sb, acc[1][3]);
+            }
+        }
+    }
+}
+
+// One bf16 stage (64 k): fragments are stored in mma order, k permuted so thread t owns k = 4t..4t+3 of a step.
+__device__ __forceinline__ void stage_bf16(const uint8_t* stage, int warp, int lane, bool two, float (&acc)[2][4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint8_t* ws = stage + warp * 2048 + lane * 16;
+    const int xrb = (BF_KC + 8) * 2;
+    const uint8_t* xs0 = stage + STAGE_W + STAGE_S + g * xrb + t * 8;
+    const uint8_t* xs1 = xs0 + 8 * xrb;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+        const uint4 a = *reinterpret_cast<const uint4*>(ws + ks * 512);
+        const uint2 xv = *reinterpret_cast<const uint2*>(xs0 + ks * 32);
+        qf::mma_bf16(acc[0], a.x, a.y, a.z, a.w, xv.x, xv.y);
+        if (two) {
+            const uint2 xw = *reinterpret_cast<const uint2*>(xs1 + ks * 32);
+            qf::mma_bf16(acc[1], a.x, a.y, a.z, a.w, xw.x, xw.y);
+        }
+    }
+}
+
+// Combine of one 128-column tile for all tokens: out = bf16(gate * shared + bf16(sum_kpos y)), 8 columns a thread.
+__device__ void combine_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int ctid) {
+    const int H = p.H, topk = p.topk;
+    for (int q = ctid; q < p.M * 16; q += CONS_THREADS) {
+        const int t = q >> 4, n = 128 * c + 8 * (q & 15);
+        float a[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] = 0.f;
+        for (int kp = 0; kp < topk; ++kp) {
+            const int s = t * topk + kp;
+            const int e = sids[s];
+            if (e < 0 || e < p.elo || e >= p.ehi) continue;
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n));
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a[2 * j] += bf16_lo(vv[j]);
+                a[2 * j + 1] += bf16_hi(vv[j]);
+            }
+        }
+        float r[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = bf16r(a[j]);
+        if (L.has_gate) {
+            const float gate = 1.f / (1.f + __expf(-__ldcg(p.gl + t)));
+            uint4 sv;
+            if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
+            else sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
+            const uint32_t ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                r[2 * j] = fmaf(gate, bf16_lo(ss[j]), r[2 * j]);
+                r[2 * j + 1] = fmaf(gate, bf16_hi(ss[j]), r[2 * j + 1]);
+            }
+        }
+        uint4 o;
+        uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __nv_bfloat162 b2 = __floats2bfloat162_rn(r[2 * j], r[2 * j + 1]);
+            op[j] = *reinterpret_cast<uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(p.out + (size_t)t * H + n) = o;
+    }
+}
+
+__global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __grid_constant__ Params p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint8_t* ring = smem + OFF_RING;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+    uint64_t* empty = full + NST;
+    StageDesc* desc = reinterpret_cast<StageDesc*>(smem + OFF_DESC);
+    uint8_t* plan = smem + OFF_PLAN;
+    int16_t* ulist = reinterpret_cast<int16_t*>(plan + PLAN_ULIST);
+    int16_t* gpre = reinterpret_cast<int16_t*>(plan + PLAN_GPRE);
+    int16_t* toff = reinterpret_cast<int16_t*>(plan + PLAN_TOFF);
+    int16_t* tlist = reinterpret_cast<int16_t*>(plan + PLAN_TLIST);
+    int16_t* sids = reinterpret_cast<int16_t*>(plan + PLAN_SIDS);
+    int* misc = reinterpret_cast<int*>(plan + PLAN_MISC);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int M = p.M, E = p.E, topk = p.topk, nslots = M * topk;
+    uint32_t* ctrl = p.ctrl;
+
+    if (tid == 0) {
+        for (int i = 0; i < NST; ++i) {
+            qf::mbar_init(full + i, 1);
+            qf::mbar_init(empty + i, NCW);
+        }
+        qf::mbar_fence_init();
+        misc[MISC_DBGN] = 0;
+    }
+    __syncwarp();
+    // Everything below reads data of the previous kernel (topk ids, x) or the control block it may re-arm.
+    qf::pdl_wait();
+
+    // ------------------------------------------------------------------ routing plan (all 288 threads)
+    {
+        uint64_t* mask = reinterpret_cast<uint64_t*>(ring + SCR_MASK);
+        int16_t* exf = reinterpret_cast<int16_t*>(ring + SCR_EXF);
+        int16_t* exc = exf + QF_MAX_EXPERTS;
+        int16_t* exg = exc + QF_MAX_EXPERTS;
+        int16_t* toffe = reinterpret_cast<int16_t*>(ring + SCR_TOFFE);
+        int* chunk = reinterpret_cast<int*>(ring + SCR_CHUNK);
+        for (int e = tid; e < E; e += MOE_THREADS) mask[e] = 0ull;
+        __syncthreads();
+        bool bad = false;
+        for (int s = tid; s < nslots; s += MOE_THREADS) {
+            const int e = p.ids[s];
+            if (e < 0 || e >= E) {
+                bad = true;
+                sids[s] = -1;
+                continue;
+            }
+            sids[s] = (int16_t)e;
+            if (e < p.elo || e >= p.ehi) continue;
+            atomicOr(reinterpret_cast<unsigned long long*>(mask + e), 1ull << (s / topk));
+        }
+        if (bad) set_err(ctrl, QF_MOE_ERR_BAD_EXPERT);
+        __syncthreads();
+        const int nch = (E + 31) >> 5;
+        for (int c = warp; c < nch; c += NCW + 1) {
+            const int e = 32 * c + lane;
+            const uint64_t m = e < E ? mask[e] : 0ull;
+            const int f = m != 0ull, cnt = __popcll(m), ng = (cnt + TG - 1) / TG;
+            int sf = f, sc = cnt, sg = ng;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int a = __shfl_up_sync(0xffffffffu, sf, o), b = __shfl_up_sync(0xffffffffu, sc, o),
+                          d = __shfl_up_sync(0xffffffffu, sg, o);
+                if (lane >= o) { sf += a; sc += b; sg += d; }
+            }
+            if (e < E) { exf[e] = (int16_t)(sf - f); exc[e] = (int16_t)(sc - cnt); exg[e] = (int16_t)(sg - ng); }
+            if (lane == 31) { chunk[c] = sf; chunk[32 + c] = sc; chunk[64 + c] = sg; }
+        }
+        __syncthreads();
+        if (warp == 0) {
+            int vf = lane < nch ? chunk[lane] : 0, vc = lane < nch ? chunk[32 + lane] : 0,
+                vg = lane < nch ? chunk[64 + lane] : 0;
+            int sf = vf, sc = vc, sg = vg;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int a = __shfl_up_sync(0xffffffffu, sf, o), b = __shfl_up_sync(0xffffffffu, sc, o),
+                          d = __shfl_up_sync(0xffffffffu, sg, o);
+                if (lane >= o) { sf += a; sc += b; sg += d; }
+            }
+            __syncwarp();
+            if (lane < nch) { chunk[lane] = sf - vf; chunk[32 + lane] = sc - vc; chunk[64 + lane] = sg - vg; }
+            if (lane == 31) { misc[MISC_U] = sf; misc[MISC_NTOK] = sc; misc[MISC_GT] = sg; }
+        }
+        __syncthreads();
+        for (int e = tid; e < E; e += MOE_THREADS) {
+            if (mask[e] != 0ull) {
+                const int c = e >> 5;
+                const int u = chunk[c] + exf[e];
+                ulist[u] = (int16_t)e;
+                toff[u] = (int16_t)(chunk[32 + c] + exc[e]);
+                gpre[u] = (int16_t)(chunk[64 + c] + exg[e]);
+                toffe[e] = toff[u];
+            }
+        }
+        if (tid == 0) {
+            toff[misc[MISC_U]] = (int16_t)misc[MISC_NTOK];
+            gpre[misc[MISC_U]] = (int16_t)misc[MISC_GT];
+        }
+        __syncthreads();
+        for (int s = tid; s < nslots; s += MOE_THREADS) {
+            const int e = sids[s];
+            if (e < 0 || e < p.elo || e >= p.ehi) continue;
+            const int t = s / topk, kp = s - t * topk;
+            bool first = true;
+            for (int k2 = 0; k2 < kp; ++k2) first &= sids[t * topk + k2] != e;
+            if (first) {
+                const int j = __popcll(mask[e] & ((1ull << t) - 1ull));
+                tlist[toffe[e] + j] = (int16_t)s;
+            }
+        }
+        __syncthreads();
+    }
+    qf::pdl_launch_dependents();
+
+    Layout L;
+    L.R1 = (2 * p.I) / 128;
+    L.R2 = p.H / 128;
+    L.has_shw = p.shw13 != nullptr;
+    L.has_gate = (p.shared != nullptr || L.has_shw) ? 1 : 0;
+    L.Rs1 = L.has_shw ? (2 * p.Is) / 128 : 0;
+    L.ngs = (M + TG - 1) / TG;
+    L.U = misc[MISC_U];
+    L.Gt = misc[MISC_GT];
+    L.b_s1 = L.has_gate ? 1 : 0;
+    L.b_g1 = L.b_s1 + (L.has_shw ? L.Rs1 * NSPLIT * L.ngs : 0);
+    L.b_s2 = L.b_g1 + L.R1 * L.Gt;
+    L.b_g2 = L.b_s2 + (L.has_shw ? L.R2 * L.ngs : 0);
+    L.b_cb = L.b_g2 + L.R2 * L.Gt;
+    L.total = L.b_cb + ((L.Gt == 0 && !L.has_shw) ? L.R2 : 0);
+    L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
+
+    if (warp == NCW) {
+        // ============================================================== producer (one thread)
+        if (lane == 0) {
+            const uint64_t pol = qf::policy_evict_first();
+            int st = 0;
+            uint32_t ph = 0;
+            for (;;) {
+                int item = (int)atomicAdd(ctrl + C_QUEUE, 1u);
+                if (qf::ld_volatile(ctrl + C_ERR) != 0u) item = L.total;
+                int kind = K_STOP, u = 0, tile = 0, tg = 0, split = 0, nk = 1, ntok = 0, e = 0;
+                if (item >= L.total) {
+                    kind = K_STOP;
+                } else if (item < L.b_s1) {
+                    kind = K_GL;
+                } else if (item < L.b_g1) {
+                    const int j = item - L.b_s1;
+                    kind = K_S1;
+                    tg = j % L.ngs;
+                    split = (j / L.ngs) % NSPLIT;
+                    tile = j / (L.ngs * NSPLIT);
+                    nk = (p.H / NSPLIT) / BF_KC;
+                    ntok = min(TG, M - TG * tg);
+                } else if (item < L.b_s2 || (item >= L.b_g2 && item < L.b_cb)) {
+                    const bool down = item >= L.b_g2;
+                    const int j = item - (down ? L.b_g2 : L.b_g1);
+                    const int R = down ? L.R2 : L.R1;
+                    u = find_u(gpre, L.U, j / R);
+                    const int ngu = gpre[u + 1] - gpre[u];
+                    const int jj = j - R * gpre[u];
+                    tile = jj / ngu;
+                    tg = jj - tile * ngu;
+                    kind = down ? K_G2 : K_G1;
+                    e = ulist[u];
+                    const int K = down ? p.I : p.H;
+                    nk = (K + W4_KC - 1) / W4_KC;
+                    ntok = min(TG, (toff[u + 1] - toff[u]) - TG * tg);
+                } else if (item < L.b_g2) {
+                    const int j = item - L.b_s2;
+                    kind = K_S2;
+                    tg = j % L.ngs;
+                    tile = j / L.ngs;
+                    nk = p.Is / BF_KC;
+                    ntok = min(TG, M - TG * tg);
+                } else {
+                    kind = K_CB;
+                    tile = item - L.b_cb;
+                }
+                bool dep_ok = true;
+                for (int kidx = 0; kidx < nk; ++kidx) {
+                    if (!qf::mbar_wait(empty + st, ph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                    uint8_t* sb = ring + st * STAGE_BYTES;
+                    uint8_t* sw = sb;
+                    uint8_t* ssc = sb + STAGE_W;
+                    uint8_t* sx = sb + STAGE_W + STAGE_S;
+                    int kc = 0;
+                    uint32_t bytes = 0;
+                    if (kind == K_G1 || kind == K_G2) {
+                        const int K = kind == K_G1 ? p.H : p.I;
+                        const int N = kind == K_G1 ? 2 * p.I : p.H;
+                        kc = min(W4_KC, K - W4_KC * kidx);
+                        bytes = 128 * kc / 2 + kc * 2 + ntok * kc * 2;
+                    } else if (kind == K_S1 || kind == K_S2) {
+                        kc = BF_KC;
+                        bytes = STAGE_W + ntok * kc * 2;
+                    }
+                    StageDesc d;
+                    d.kind = (int16_t)kind; d.u = (int16_t)u; d.tile = (int16_t)tile; d.tg = (int16_t)tg;
+                    d.split = (int16_t)split; d.kidx = (int16_t)kidx; d.nk = (int16_t)nk; d.kc = (int16_t)kc;
+                    d.ntok = (int16_t)ntok;
+                    desc[st] = d;
+                    if (kind == K_STOP) {
+                        qf::mbar_arrive(full + st);
+                        break;
+                    }
+                    qf::mbar_arrive_expect_tx(full + st, bytes);
+                    const int xrb = (kc + 8) * 2;
+                    if (kind == K_G1 || kind == K_G2) {
+                        const bool down = kind == K_G2;
+                        const int K = down ? p.I : p.H;
+                        const int N = down ? p.H : 2 * p.I;
+                        const uint8_t* wbase = (down ? p.w2 : p.w13) + (size_t)e * ((size_t)N * K / 2) +
+                                               (size_t)tile * (128 * (size_t)K / 2) + (size_t)kidx * STAGE_W;
+                        const uint16_t* sbase = (down ? p.s2 : p.s13) + (size_t)e * ((size_t)N * K / 128) +
+                                                (size_t)tile * K + (size_t)kidx * 256;
+                        qf::bulk_g2s_hint(sw, wbase, 128 * kc / 2, full + st, pol);
+                        qf::bulk_g2s_hint(ssc, sbase, kc * 2, full + st, pol);
+                        if (down && kidx == 0) {
+                            dep_ok = wait_counter(ctrl, C_DONE + u, (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])));
+                            qf::fence_proxy_async();
+                        }
+                        const int tbase = toff[u] + TG * tg;
+                        for (int j = 0; j < ntok; ++j) {
+                            const int s = tlist[tbase + j];
+                            const __nv_bfloat16* src =
+                                down ? p.hbuf + (size_t)s * p.I + W4_KC * kidx : p.x + (size_t)(s / topk) * p.H + W4_KC * kidx;
+                            qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
+                        }
+                    } else if (kind == K_S1 || kind == K_S2) {
+                        const bool down = kind == K_S2;
+                        const int K = down ? p.Is : p.H;
+                        const int k0 = down ? BF_KC * kidx : split * (p.H / NSPLIT) + BF_KC * kidx;
+                        const uint8_t* wbase = (down ? p.shw2 : p.shw13) + (size_t)tile * (128 * (size_t)K * 2) +
+                                               (size_t)(k0 / BF_KC) * STAGE_W;
+                        qf::bulk_g2s_hint(sw, wbase, STAGE_W, full + st, pol);
+                        if (down && kidx == 0) {
+                            dep_ok = wait_counter(ctrl, C_SDONE + tg, (uint32_t)L.Rs1);
+                            qf::fence_proxy_async();
+                        }
+                        for (int j = 0; j < ntok; ++j) {
+                            const int tok = TG * tg + j;
+                            const __nv_bfloat16* src = down ? p.hsh + (size_t)tok * p.Is + k0 : p.x + (size_t)tok * p.H + k0;
+                            qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
+                        }
+                    }
+                    if (++st == NST) { st = 0; ph ^= 1u; }
+                }
+                (void)dep_ok;
+                if (kind == K_STOP) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ============================================================== consumers (8 warps)
+        const int ctid = tid;   // 0..255
+        const int g = lane >> 2, t = lane & 3;
+        int st = 0;
+        uint32_t ph = 0;
+        float acc[2][4];
+        for (;;) {
+            if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
+                set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                break;
+            }
+            const StageDesc d = desc[st];
+            if (d.kind == K_STOP) break;
+            if (d.kidx == 0) {
+#pragma unroll
+                for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+                if (p.dbg != nullptr && ctid == 0 && misc[MISC_DBGN] < 32) {
+                    p.dbg[blockIdx.x * 32 + misc[MISC_DBGN]] = (long long)((qf::globaltimer() << 12) | (uint64_t)d.kind);
+                    misc[MISC_DBGN] += 1;
+                }
+            }
+            const uint8_t* sb = ring + st * STAGE_BYTES;
+            const bool two = d.ntok > 8;
+            if (d.kind == K_G1 || d.kind == K_G2) stage_w4(sb, warp, lane, d.kc, two, acc);
+            else if (d.kind == K_S1 || d.kind == K_S2) stage_bf16(sb, warp, lane, two, acc);
+            __syncwarp();
+            if (lane == 0) qf::mbar_arrive(empty + st);
+            if (++st == NST) { st = 0; ph ^= 1u; }
+            if (d.kidx != d.nk - 1) continue;
+
+            // ------------------------------------------------------------ epilogues (item complete)
+            if (d.kind == K_GL) {
+                for (int tok = warp; tok < M; tok += NCW) {
+                    const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)tok * p.H);
+                    const uint4* wr = reinterpret_cast<const uint4*>(p.wgate);
+                    float a = 0.f;
+                    for (int i = lane; i < p.H / 8; i += 32) {
+                        const uint4 xv = __ldcg(xr + i), wv = __ldg(wr + i);
+                        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            a = fmaf(bf16_lo(xx[j]), bf16_lo(ww[j]), a);
+                            a = fmaf(bf16_hi(xx[j]), bf16_hi(ww[j]), a);
+                        }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                    if (lane == 0) p.gl[tok] = a;
+                }
+                __threadfence();
+                qf::named_bar(1, CONS_THREADS);
+                if (ctid == 0) atomicExch(ctrl + C_GLF, 1u);
+            } else if (d.kind == K_G1) {
+                const int u = d.u, e = ulist[u];
+                const float gs = p.gs13 ? bf16_bits(p.gs13[e]) : 1.f;
+                const int col = 64 * d.tile + 8 * warp + g;
+                const int tbase = toff[u] + TG * d.tg;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const int jt = 8 * nt + 2 * t + i;
+                        if (jt < d.ntok) {
+                            const int s = tlist[tbase + jt];
+                            const float gv = bf16r(bf16r(acc[nt][i]) * gs), uv = bf16r(bf16r(acc[nt][2 + i]) * gs);
+                            p.hbuf[(size_t)s * p.I + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                        }
+                    }
+                __threadfence();
+                qf::named_bar(1, CONS_THREADS);
+                if (ctid == 0) atomicAdd(ctrl + C_DONE + u, 1u);
+            } else if (d.kind == K_S1) {
+                float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+                    __stcg(reinterpret_cast<float4*>(pb + (size_t)d.split * 2048 + ((warp * 2 + nt) * 32 + lane) * 4),
+                           make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+                __threadfence();
+                qf::named_bar(1, CONS_THREADS);
+                const int sc = C_SPLIT + d.tile * L.ngs + d.tg;
+                if (ctid == 0) misc[MISC_LAST] = atomicAdd(ctrl + sc, 1u) == NSPLIT - 1;
+                __syncwarp();
+                qf::named_bar(1, CONS_THREADS);
+                if (misc[MISC_LAST]) {
+                    __threadfence();
+                    float v[2][4];
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        v[nt][0] = v[nt][1] = v[nt][2] = v[nt][3] = 0.f;
+#pragma unroll
+                        for (int sp = 0; sp < NSPLIT; ++sp) {
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(
+                                pb + (size_t)sp * 2048 + ((warp * 2 + nt) * 32 + lane) * 4));
+                            v[nt][0] += q.x; v[nt][1] += q.y; v[nt][2] += q.z; v[nt][3] += q.w;
+                        }
+                    }
+                    const int col = 64 * d.tile + 8 * warp + g;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const int jt = 8 * nt + 2 * t + i;
+                            if (jt < d.ntok) {
+                                const int tok = TG * d.tg + jt;
+                                const float gv = bf16r(v[nt][i]), uv = bf16r(v[nt][2 + i]);
+                                p.hsh[(size_t)tok * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                            }
+                        }
+                    __threadfence();
+                    qf::named_bar(1, CONS_THREADS);
+                    if (ctid == 0) {
+                        ctrl[sc] = 0u;
+                        atomicAdd(ctrl + C_SDONE + d.tg, 1u);
+                    }
+                }
+            } else if (d.kind == K_G2 || d.kind == K_S2 || d.kind == K_CB) {
+                const int c = d.tile;
+                if (d.kind == K_G2) {
+                    const int u = d.u, e = ulist[u];
+                    const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
+                    const int n0 = 128 * c + 16 * warp + g;
+                    const int tbase = toff[u] + TG * d.tg;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const int jt = 8 * nt + 2 * t + i;
+                            if (jt < d.ntok) {
+                                const int s0 = tlist[tbase + jt];
+                                const int tok = s0 / topk;
+                                const float v0 = bf16r(acc[nt][i]), v1 = bf16r(acc[nt][2 + i]);
+                                for (int kp = s0 - tok * topk; kp < topk; ++kp) {
+                                    const int s = tok * topk + kp;
+                                    if (sids[s] != e) continue;
+                                    const float w = bf16r(g2 * bf16r(__ldcg(p.tw + s)));
+                                    p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v0 * w);
+                                    p.ybuf[(size_t)s * p.H + n0 + 8] = __float2bfloat16(v1 * w);
+                                }
+                            }
+                        }
+                } else if (d.kind == K_S2) {
+                    const int n0 = 128 * c + 16 * warp + g;
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                        for (int i = 0; i < 2; ++i) {
+                            const int jt = 8 * nt + 2 * t + i;
+                            if (jt < d.ntok) {
+                                const int tok = TG * d.tg + jt;
+                                p.sbuf[(size_t)tok * p.H + n0] = __float2bfloat16(acc[nt][i]);
+                                p.sbuf[(size_t)tok * p.H + n0 + 8] = __float2bfloat16(acc[nt][2 + i]);
+                            }
+                        }
+                }
+                bool last = true;
+                if (d.kind != K_CB) {
+                    __threadfence();
+                    qf::named_bar(1, CONS_THREADS);
+                    if (ctid == 0) misc[MISC_LAST] = atomicAdd(ctrl + C_CNT + c, 1u) == L.tile_target - 1u;
+                    __syncwarp();
+                    qf::named_bar(1, CONS_THREADS);
+                    last = misc[MISC_LAST] != 0;
+                }
+                if (last) {
+                    if (L.has_gate) {
+                        if (ctid == 0) wait_counter(ctrl, C_GLF, 1u);
+                        __syncwarp();
+                        qf::named_bar(1, CONS_THREADS);
+                    }
+                    __threadfence();
+                    combine_tile(p, L, sids, c, ctid);
+                    if (ctid == 0 && d.kind != K_CB) ctrl[C_CNT + c] = 0u;
+                }
+            }
+        }
+    }
+
+    // ------------------------------------------------------------------ exit: the last CTA re-arms ctrl
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        misc[MISC_FLAG] = atomicAdd(ctrl + C_EXIT, 1u) == gridDim.x - 1;
+    }
+    __syncwarp();
+    __syncthreads();
+    if (misc[MISC_FLAG]) {
+        __threadfence();
+        for (int i = tid; i < QF_MOE_CTRL_WORDS; i += MOE_THREADS)
+            if (i != C_ERR) ctrl[i] = 0u;
+    }
+}
+
+// ------------------------------------------------------------------------------------------ weight repacking
+// int4: canonical [E][N][K/8] words -> kernel layout (see moe.cu header and qwenfast_b200/formats.py).
+__device__ __forceinline__ int kernel_row_to_src(int pos, int N, int gated) {
+    if (!gated) return pos;
+    const int r = pos >> 7, w = (pos & 127) >> 4, rho = pos & 15;
+    return rho < 8 ? 64 * r + 8 * w + rho : N / 2 + 64 * r + 8 * w + (rho - 8);
+}
+
+// word o of an expert's kernel-layout matrix -> (source row, source word along K)
+__device__ __forceinline__ void w4_word_src(long long o, int N, int K, int gated, int& row, int& kw) {
+    const long long per_tile = 128LL * K / 8;
+    const int r = (int)(o / per_tile);
+    const int ot = (int)(o - r * per_tile);
+    const int st = ot / 4096;
+    const int kc = min(256, K - 256 * st);
+    const int os = ot - 4096 * st;
+    const int slab_words = (kc / 64) * 128;
+    const int w = os / slab_words;
+    const int ow = os - w * slab_words;
+    const int c = ow >> 7, L = (ow >> 2) & 31, j = ow & 3;
+    const int gg = L >> 2, t = L & 3;
+    const int rho = gg + 8 * (j & 1), b = 2 * c + (j >> 1);
+    kw = 32 * st + 4 * b + t;
+    row = kernel_row_to_src(128 * r + 16 * w + rho, N, gated);
+}
+
+__device__ __forceinline__ void w4_scale_src(long long o, int N, int K, int gated, int& row, int& grp) {
+    const int r = (int)(o / K);
+    const int ot = (int)(o - (long long)r * K);
+    const int st = ot / 256;
+    const int kc = min(256, K - 256 * st);
+    const int os = ot - 256 * st;
+    const int per_slab = (kc / 128) * 16;
+    const int w = os / per_slab;
+    const int gi = (os - w * per_slab) >> 4, ent = os & 15;
+    const int rho = (ent >> 1) + 8 * (ent & 1);
+    grp = 2 * st + gi;
+    row = kernel_row_to_src(128 * r + 16 * w + rho, N, gated);
+}
+
+__device__ __forceinline__ uint32_t nib_perm(uint32_t v, bool forward) {
+    // forward: nibble i <- k index [0,2,4,6,1,3,5,7][i]; backward: inverse
+    const int fwd[8] = {0, 2, 4, 6, 1, 3, 5, 7};
+    uint32_t o = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        if (forward) o |= ((v >> (4 * fwd[i])) & 0xFu) << (4 * i);
+        else o |= ((v >> (4 * i)) & 0xFu) << (4 * fwd[i]);
+    }
+    return o;
+}
+
+__global__ void w4_repack_kernel(const uint32_t* __restrict__ src, const uint16_t* __restrict__ ssrc,
+                                 uint32_t* __restrict__ dst, uint16_t* __restrict__ sdst, int E, int N, int K,
+                                 int gated, int unpack) {
+    const long long words = (long long)N * K / 8, ents = (long long)N * K / 128;
+    const long long total = (long long)E * words;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const long long e = i / words, o = i - e * words;
+        int row, kw;
+        w4_word_src(o, N, K, gated, row, kw);
+        const long long si = e * words + (long long)row * (K / 8) + kw;
+        if (!unpack) dst[i] = nib_perm(src[si], true);
+        else dst[si] = nib_perm(src[i], false);
+        if (o < ents) {
+            int srow, grp;
+            w4_scale_src(o, N, K, gated, srow, grp);
+            const long long ssi = e * ents + (long long)srow * (K / 128) + grp;
+            const long long di = e * ents + o;
+            if (!unpack) sdst[di] = ssrc[ssi];
+            else sdst[ssi] = ssrc[di];
+        }
+    }
+}
+
+__global__ void bf16_repack_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int N, int K,
+                                   int gated, int unpack) {
+    const long long total = (long long)N * K;
+    for (long long o = blockIdx.x * (long long)blockDim.x + threadIdx.x; o < total; o += (long long)gridDim.x * blockDim.x) {
+        const long long per_tile = 128LL * K;
+        const int r = (int)(o / per_tile);
+        const int ot = (int)(o - r * per_tile);
+        const int st = ot >> 13, os = ot & 8191;
+        const int w = os >> 10, ks = (os >> 8) & 3, L = (os >> 3) & 31, reg = (os >> 1) & 3, e2 = os & 1;
+        const int gg = L >> 2, t = L & 3, q = reg >> 1, hi = reg & 1;
+        const int k = 64 * st + 16 * ks + 4 * t + 2 * q + e2;
+        const int row = kernel_row_to_src(128 * r + 16 * w + gg + 8 * hi, N, gated);
+        const long long si = (long long)row * K + k;
+        if (!unpack) dst[o] = src[si];
+        else dst[si] = src[o];
+    }
+}
+
+}  // namespace
+
+// ================================================================================================= C ABI
+extern "C" int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64_t* hbuf_bytes, int64_t* ybuf_bytes,
+                                    int64_t* gl_numel, int64_t* ctrl_numel, int64_t* pbuf_numel,
+                                    int64_t* shbuf_bytes) {
+    QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS && H > 0 && I > 0 && topk >= 1 && topk <= QF_MAX_TOPK && Is >= 0,
+               "a16_moe_workspace: bad sizes");
+    const int ngs = (M + TG - 1) / TG;
+    if (hbuf_bytes) *hbuf_bytes = (int64_t)M * topk * I * 2;
+    if (ybuf_bytes) *ybuf_bytes = (int64_t)M * (topk + 1) * H * 2;
+    if (gl_numel) *gl_numel = M;
+    if (ctrl_numel) *ctrl_numel = QF_MOE_CTRL_WORDS;
+    if (pbuf_numel) *pbuf_numel = Is > 0 ? (int64_t)(2 * Is / 128) * ngs * NSPLIT * 2048 : 0;
+    if (shbuf_bytes) *shbuf_bytes = Is > 0 ? (int64_t)M * (Is + H) * 2 : 0;
+    return QF_OK;
+}
+
+extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* w13,
+                                 const void* s13, const void* gs13, const int32_t* w2, const void* s2, const void* gs2,
+                                 const void* w_gate, const void* shared, const void* sh_w13, const void* sh_w2,
+                                 void* hbuf, int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl,
+                                 int64_t gl_numel, int32_t* ctrl, int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel,
+                                 void* shbuf, int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk,
+                                 int Is, int phase, int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl,
+                                 qf_stream_t stream) {
+    QF_REQUIRE(x && topk_ids && topk_w && w13 && s13 && w2 && s2 && hbuf && ybuf && gl && ctrl && out,
+               "a16_moe_decode: null pointer argument");
+    QF_REQUIRE(phase == 3 || phase == 4,
+               "a16_moe_decode: phase must be 3 or 4 (whole layer); split phases 1/2 are not provided, got %d", phase);
+    QF_REQUIRE(mode == 0, "a16_moe_decode: mode %d not available (0 = full layer)", mode);
+    QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS, "a16_moe_decode: M must be in [1, %d], got %d", QF_MAX_TOKENS, M);
+    QF_REQUIRE(H >= 128 && H % 256 == 0 && H <= 8192, "a16_moe_decode: H must be a multiple of 256 in [256, 8192], got %d", H);
+    QF_REQUIRE(I >= 128 && I % 128 == 0 && I <= 8192, "a16_moe_decode: I must be a multiple of 128, got %d", I);
+    QF_REQUIRE(E >= 1 && E <= QF_MAX_EXPERTS, "a16_moe_decode: E must be in [1, %d], got %d", QF_MAX_EXPERTS, E);
+    QF_REQUIRE(topk >= 1 && topk <= QF_MAX_TOPK && topk <= E, "a16_moe_decode: topk must be in [1, %d], got %d",
+               QF_MAX_TOPK, topk);
+    QF_REQUIRE(expert_lo >= 0 && expert_lo <= expert_hi && expert_hi <= E, "a16_moe_decode: bad expert range");
+    const bool has_shw = sh_w13 != nullptr || sh_w2 != nullptr;
+    QF_REQUIRE(!(has_shw && shared), "a16_moe_decode: give either shared-expert weights or a precomputed shared output");
+    if (has_shw) {
+        QF_REQUIRE(sh_w13 && sh_w2 && pbuf && shbuf, "a16_moe_decode: shared-expert weights need sh_w13, sh_w2, pbuf, shbuf");
+        QF_REQUIRE(Is >= 64 && Is % 64 == 0 && Is <= 1024, "a16_moe_decode: Is must be a multiple of 64 in [64, 1024], got %d", Is);
+    }
+    QF_REQUIRE(!(has_shw || shared) || w_gate, "a16_moe_decode: a shared term needs w_gate");
+    int64_t need_h, need_y, need_gl, need_ctrl, need_p, need_sh;
+    qf_a16_moe_workspace(M, H, I, topk, has_shw ? Is : 0, &need_h, &need_y, &need_gl, &need_ctrl, &need_p, &need_sh);
+    QF_REQUIRE(hbuf_bytes >= need_h && ybuf_bytes >= need_y && gl_numel >= need_gl && ctrl_numel >= need_ctrl,
+               "a16_moe_decode: scratch too small (need hbuf %lld B, ybuf %lld B, gl %lld, ctrl %lld)", (long long)need_h,
+               (long long)need_y, (long long)need_gl, (long long)need_ctrl);
+    QF_REQUIRE(!has_shw || (pbuf_numel >= need_p && shbuf_bytes >= need_sh),
+               "a16_moe_decode: shared scratch too small (need pbuf %lld, shbuf %lld B)", (long long)need_p, (long long)need_sh);
+    const void* al[] = {x, w13, s13, w2, s2, hbuf, ybuf, out, w_gate, shared, sh_w13, sh_w2, pbuf, shbuf};
+    for (const void* a : al) QF_REQUIRE(a == nullptr || qf::aligned(a, 16), "a16_moe_decode: every tensor must be 16-byte aligned");
+
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaGetDevice");
+    const int sms = qf::sm_count(dev);
+    QF_REQUIRE(sms > 0, "a16_moe_decode: cannot query the SM count");
+    ce = qf::ensure_smem_attr(reinterpret_cast<const void*>(moe_persistent_kernel), MOE_SMEM);
+    if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute");
+
+    Params p;
+    p.x = static_cast<const __nv_bfloat16*>(x);
+    p.ids = topk_ids;
+    p.tw = topk_w;
+    p.w13 = reinterpret_cast<const uint8_t*>(w13);
+    p.s13 = static_cast<const uint16_t*>(s13);
+    p.gs13 = static_cast<const uint16_t*>(gs13);
+    p.w2 = reinterpret_cast<const uint8_t*>(w2);
+    p.s2 = static_cast<const uint16_t*>(s2);
+    p.gs2 = static_cast<const uint16_t*>(gs2);
+    p.wgate = static_cast<const __nv_bfloat16*>(w_gate);
+    p.shared = static_cast<const __nv_bfloat16*>(shared);
+    p.shw13 = has_shw ? static_cast<const uint8_t*>(sh_w13) : nullptr;
+    p.shw2 = has_shw ? static_cast<const uint8_t*>(sh_w2) : nullptr;
+    p.hbuf = static_cast<__nv_bfloat16*>(hbuf);
+    p.ybuf = static_cast<__nv_bfloat16*>(ybuf);
+    p.gl = gl;
+    p.ctrl = reinterpret_cast<uint32_t*>(ctrl);
+    p.pbuf = pbuf;
+    p.hsh = has_shw ? static_cast<__nv_bfloat16*>(shbuf) : nullptr;
+    p.sbuf = has_shw ? static_cast<__nv_bfloat16*>(shbuf) + (size_t)M * Is : nullptr;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.dbg = reinterpret_cast<long long*>(dbg);
+    p.M = M; p.H = H; p.I = I; p.E = E; p.topk = topk; p.Is = has_shw ? Is : 0;
+    p.mode = mode; p.elo = expert_lo; p.ehi = expert_hi;
+    ce = qf::launch_ex(moe_persistent_kernel, dim3(sms), dim3(MOE_THREADS), MOE_SMEM,
+                       reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);
+    return qf::cuda_status(ce, "a16_moe_decode: launch");
+}
+
+extern "C" int qf_moe_combine(const void*, const void*, const void*, int, void*, int, int, int, int, qf_stream_t) {
+    qf::set_error("moe_combine: expert-parallel combine not available in this build");
+    return QF_ERR_UNSUPPORTED;
+}
+
+static int repack_grid(long long n) {
+    long long b = (n + 255) / 256;
+    return (int)(b < 65535 * 8 ? (b > 0 ? b : 1) : 65535 * 8);
+}
+
+extern "C" int qf_w4_repack(const int32_t* qweight, const void* scales, int32_t* wk, void* sk, int E, int N, int K,
+                            int gated, qf_stream_t stream) {
+    QF_REQUIRE(qweight && scales && wk && sk, "w4_repack: null pointer argument");
+    QF_REQUIRE(E >= 1 && N >= 128 && N % 128 == 0 && K >= 128 && K % 128 == 0, "w4_repack: need N %% 128 == 0 and K %% 128 == 0");
+    const long long n = (long long)E * N * K / 8;
+    w4_repack_kernel<<<repack_grid(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const uint32_t*>(qweight), static_cast<const uint16_t*>(scales), reinterpret_cast<uint32_t*>(wk),
+        static_cast<uint16_t*>(sk), E, N, K, gated, 0);
+    return qf::cuda_status(cudaGetLastError(), "w4_repack: launch");
+}
+
+extern "C" int qf_w4_unpack(const int32_t* wk, const void* sk, int32_t* qweight, void* scales, int E, int N, int K,
+                            int gated, qf_stream_t stream) {
+    QF_REQUIRE(qweight && scales && wk && sk, "w4_unpack: null pointer argument");
+    QF_REQUIRE(E >= 1 && N >= 128 && N % 128 == 0 && K >= 128 && K % 128 == 0, "w4_unpack: need N %% 128 == 0 and K %% 128 == 0");
+    const long long n = (long long)E * N * K / 8;
+    w4_repack_kernel<<<repack_grid(n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const uint32_t*>(wk), static_cast<const uint16_t*>(sk), reinterpret_cast<uint32_t*>(qweight),
+        static_cast<uint16_t*>(scales), E, N, K, gated, 1);
+    return qf::cuda_status(cudaGetLastError(), "w4_unpack: launch");
+}
+
+extern "C" int qf_bf16_repack(const void* w, void* wk, int N, int K, int gated, qf_stream_t stream) {
+    QF_REQUIRE(w && wk, "bf16_repack: null pointer argument");
+    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 64 && K % 64 == 0, "bf16_repack: need N %% 128 == 0 and K %% 64 == 0");
+    bf16_repack_kernel<<<repack_grid((long long)N * K), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(w), static_cast<uint16_t*>(wk), N, K, gated, 0);
+    return qf::cuda_status(cudaGetLastError(), "bf16_repack: launch");
+}
+
+extern "C" int qf_bf16_unpack(const void* wk, void* w, int N, int K, int gated, qf_stream_t stream) {
+    QF_REQUIRE(w && wk, "bf16_unpack: null pointer argument");
+    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 64 && K % 64 == 0, "bf16_unpack: need N %% 128 == 0 and K %% 64 == 0");
+    bf16_repack_kernel<<<repack_grid((long long)N * K), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(wk), static_cast<uint16_t*>(w), N, K, gated, 1);
+    return qf::cuda_status(cudaGetLastError(), "bf16_unpack: launch");
+}

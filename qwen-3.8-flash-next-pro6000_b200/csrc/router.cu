@@ -1,0 +1,229 @@
+// MoE router for decode/verify batches (1..64 tokens): router GEMM + softmax + top-k + renormalise, one launch.
+//
+//   logits[t, e] = bf16(x[t] . w[e])          fp32 products and sums on the tensor cores
+//   p[t, e]      = softmax_e(logits[t])        fp32, max-subtracted
+//   ids[t]       = the k largest logits, lower expert id first among equal values
+//   weights[t]   = p[t, ids] / sum(p[t, ids]) when renormalising (sum > 0), else p[t, ids]
+// Selection semantics follow serve/qwenfast/qf_router.cu:3-6, 103-157 (NaN ranks as -1e30, -0 == +0).
+//
+// Layout of the work: a CTA owns 16 router rows (one m16 tile, experts as the A operand) and 16 warps split the
+// hidden dimension; tokens are the n8 operand. Each warp requests its whole weight slice before waiting on the
+// previous kernel (PDL), so the 2 MB weight stream overlaps the producer of x. Per-warp fp32 partials are summed
+// in a fixed warp order through shared memory, so the logits do not depend on timing. The last CTA to finish
+// (ticket counter, re-armed by that CTA) runs the top-k, one warp per token.
+#include "qf_common.cuh"
+
+namespace {
+
+using qf::bf16_lo;
+constexpr int RW = 16;         // warps per CTA
+constexpr int RT = RW * 32;    // threads per CTA
+constexpr int REXP = 16;       // router rows per CTA
+constexpr int MAXNT = QF_MAX_TOKENS / 8;
+
+__device__ __forceinline__ uint4 ldg_nc_v4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// order-preserving key of a logit; 0 is reserved for "already taken"
+__device__ __forceinline__ unsigned order_key(float v) {
+    const float r = (v == v) ? v : -1e30f;
+    unsigned u = __float_as_uint(r);
+    if (u == 0x80000000u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// softmax + top-k of one token row (E logits, fp32 copies of the bf16 values) by one warp.
+template <int PL>
+__device__ void topk_row(const float* __restrict__ row, int E, int topk, int renorm, float* __restrict__ wout,
+                         int* __restrict__ iout) {
+    const int lane = threadIdx.x & 31;
+    float v[PL];
+    unsigned key[PL];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int e = i * 32 + lane;
+        v[i] = e < E ? __ldcg(row + e) : -INFINITY;
+        mx = fmaxf(mx, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int e = i * 32 + lane;
+        key[i] = e < E ? order_key(v[i]) : 0u;
+        v[i] = __expf(v[i] - mx);
+        sum += v[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+
+    float my_p = 0.f, routed = 0.f;
+    int my_id = 0;
+    for (int k = 0; k < topk; ++k) {
+        unsigned bk = 0u;
+        unsigned bi = 0xffffffffu;
+#pragma unroll
+        for (int i = 0; i < PL; ++i)          // strict '>' over ascending i keeps the lowest id of this lane
+            if (key[i] > bk) { bk = key[i]; bi = (unsigned)(i * 32 + lane); }
+        const unsigned wk = __reduce_max_sync(0xffffffffu, bk);
+        const unsigned wi = __reduce_min_sync(0xffffffffu, bk == wk ? bi : 0xffffffffu);
+        const int owner = (int)(wi & 31u), slot = (int)(wi >> 5);
+        float p = 0.f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i)
+            if (lane == owner && i == slot) { p = v[i] / sum; key[i] = 0u; }
+        p = __shfl_sync(0xffffffffu, p, owner);
+        routed += p;
+        if (lane == k) { my_p = p; my_id = (int)wi; }
+    }
+    if (lane < topk) {
+        const float norm = routed > 0.f ? routed : 1.f;
+        wout[lane] = renorm ? my_p / norm : my_p;
+        iout[lane] = my_id;
+    }
+}
+
+template <int BPW>
+__global__ void __launch_bounds__(RT, 1)
+    router_topk_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                       __nv_bfloat16* __restrict__ logits, float* __restrict__ weights, int* __restrict__ ids,
+                       float* __restrict__ scratch, unsigned* __restrict__ counter, int rows, int H, int E, int topk,
+                       int renorm) {
+    extern __shared__ float red[];   // [RW][REXP][rp]
+    __shared__ unsigned s_last;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
+    const int e0 = blockIdx.x * REXP;
+    const int nblk = H / 32;
+    const int b0 = warp * BPW;
+    const int ntile = (rows + 7) >> 3, rp = ntile * 8;
+
+    // this warp's 32-k blocks of router rows e0+g and e0+g+8 (thread t holds k = 32b + 8t .. +8)
+    uint4 wa[BPW], wb[BPW];
+    const uint4* ra = reinterpret_cast<const uint4*>(w + (size_t)(e0 + g) * H) + t;
+    const uint4* rb = reinterpret_cast<const uint4*>(w + (size_t)(e0 + g + 8) * H) + t;
+#pragma unroll
+    for (int i = 0; i < BPW; ++i) {
+        if (b0 + i < nblk) {
+            wa[i] = ldg_nc_v4(ra + 4 * (b0 + i));
+            wb[i] = ldg_nc_v4(rb + 4 * (b0 + i));
+        } else {
+            wa[i] = wb[i] = make_uint4(0, 0, 0, 0);
+        }
+    }
+    qf::pdl_wait();
+    qf::pdl_launch_dependents();
+
+    float d[MAXNT][4];
+#pragma unroll
+    for (int nt = 0; nt < MAXNT; ++nt) {
+        d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+        if (nt < ntile) {
+            const int tok = nt * 8 + g;
+            const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)(tok < rows ? tok : 0) * H) + t;
+#pragma unroll
+            for (int i = 0; i < BPW; ++i) {
+                if (b0 + i < nblk) {
+                    const uint4 xv = tok < rows ? __ldcg(xr + 4 * (b0 + i)) : make_uint4(0, 0, 0, 0);
+                    qf::mma_bf16(d[nt], wa[i].x, wb[i].x, wa[i].y, wb[i].y, xv.x, xv.y);
+                    qf::mma_bf16(d[nt], wa[i].z, wb[i].z, wa[i].w, wb[i].w, xv.z, xv.w);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < MAXNT; ++nt) {
+        if (nt < ntile) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = g + ((i & 2) ? 8 : 0), tok = nt * 8 + 2 * t + (i & 1);
+                red[(warp * REXP + r) * rp + tok] = d[nt][i];
+            }
+        }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < REXP * rows; idx += RT) {
+        const int r = idx % REXP, tok = idx / REXP;
+        float s = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < RW; ++ww) s += red[(ww * REXP + r) * rp + tok];
+        const __nv_bfloat16 bv = __float2bfloat16(s);
+        logits[(size_t)tok * E + e0 + r] = bv;
+        scratch[(size_t)tok * E + e0 + r] = __bfloat162float(bv);
+    }
+
+    // ---- last CTA: softmax + top-k per token
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(counter, 1u) == gridDim.x - 1;
+    }
+    __syncwarp();
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid == 0) *counter = 0u;
+    const int pl = (E + 31) / 32;
+    for (int tok = warp; tok < rows; tok += RW) {
+        const float* row = scratch + (size_t)tok * E;
+        float* wo = weights + (size_t)tok * topk;
+        int* io = ids + (size_t)tok * topk;
+        if (pl <= 1) topk_row<1>(row, E, topk, renorm, wo, io);
+        else if (pl <= 2) topk_row<2>(row, E, topk, renorm, wo, io);
+        else if (pl <= 4) topk_row<4>(row, E, topk, renorm, wo, io);
+        else if (pl <= 8) topk_row<8>(row, E, topk, renorm, wo, io);
+        else if (pl <= 16) topk_row<16>(row, E, topk, renorm, wo, io);
+        else topk_row<32>(row, E, topk, renorm, wo, io);
+    }
+}
+
+template <int BPW>
+int launch_router(const void* x, const void* w, int rows, int H, int E, int topk, int renorm, float* weights,
+                  int32_t* ids, void* logits, float* scratch, int32_t* counter, int pdl, cudaStream_t stream) {
+    const int rp = ((rows + 7) / 8) * 8;
+    const size_t smem = (size_t)RW * REXP * rp * sizeof(float);
+    auto kern = router_topk_kernel<BPW>;
+    cudaError_t e = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), RW * REXP * QF_MAX_TOKENS * 4);
+    if (e != cudaSuccess) return qf::cuda_status(e, "router_topk: cudaFuncSetAttribute");
+    e = qf::launch_ex(kern, dim3(E / REXP), dim3(RT), smem, stream, pdl != 0,
+                      reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(w),
+                      reinterpret_cast<__nv_bfloat16*>(logits), weights, reinterpret_cast<int*>(ids), scratch,
+                      reinterpret_cast<unsigned*>(counter), rows, H, E, topk, renorm);
+    return qf::cuda_status(e, "router_topk: launch");
+}
+
+}  // namespace
+
+extern "C" int qf_router_topk(const void* x, const void* w, int rows, int hidden, int experts, int topk,
+                              int renormalize, float* topk_weights, int32_t* topk_ids, void* logits, float* scratch,
+                              int64_t scratch_numel, int32_t* counter, int pdl, qf_stream_t stream) {
+    QF_REQUIRE(x && w && topk_weights && topk_ids && logits && scratch && counter,
+               "router_topk: null pointer argument");
+    QF_REQUIRE(rows >= 1 && rows <= QF_MAX_TOKENS, "router_topk: rows must be in [1, %d], got %d", QF_MAX_TOKENS,
+               rows);
+    QF_REQUIRE(hidden >= 256 && hidden % 256 == 0 && hidden <= 4096,
+               "router_topk: hidden must be a multiple of 256 in [256, 4096], got %d", hidden);
+    QF_REQUIRE(experts >= 16 && experts % 16 == 0 && experts <= QF_MAX_EXPERTS,
+               "router_topk: experts must be a multiple of 16 in [16, %d], got %d", QF_MAX_EXPERTS, experts);
+    QF_REQUIRE(topk >= 1 && topk <= QF_MAX_TOPK && topk <= experts, "router_topk: topk must be in [1, %d], got %d",
+               QF_MAX_TOPK, topk);
+    QF_REQUIRE(scratch_numel >= (int64_t)rows * experts, "router_topk: scratch needs %lld floats, got %lld",
+               (long long)rows * experts, (long long)scratch_numel);
+    QF_REQUIRE(qf::aligned(x, 16) && qf::aligned(w, 16), "router_topk: x and w must be 16-byte aligned");
+    const int bpw = (hidden / 32 + RW - 1) / RW;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (bpw <= 1) return launch_router<1>(x, w, rows, hidden, experts, topk, renormalize, topk_weights, topk_ids,
+                                          logits, scratch, counter, pdl, st);
+    if (bpw <= 2) return launch_router<2>(x, w, rows, hidden, experts, topk, renormalize, topk_weights, topk_ids,
+                                          logits, scratch, counter, pdl, st);
+    if (bpw <= 4) return launch_router<4>(x, w, rows, hidden, experts, topk, renormalize, topk_weights, topk_ids,
+                                          logits, scratch, counter, pdl, st);
+    return launch_router<8>(x, w, rows, hidden, experts, topk, renormalize, topk_weights, topk_ids, logits, scratch,
+                            counter, pdl, st);
+}

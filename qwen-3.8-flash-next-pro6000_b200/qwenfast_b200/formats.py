@@ -1,0 +1,208 @@
+"""Weight formats: the canonical int4 expert format and the kernel-native layouts the sm_100a kernels stream.
+
+Canonical (what a checkpoint loader holds, and the synthetic configurations' definition)
+    int4 codes 0..15, zero point 8, eight codes per int32 along K with the lowest k in the low nibble:
+    ``qweight int32 [E, N, K/8]``; one bf16 scale per 128 k: ``scales bf16 [E, N, K/128]``;
+    dequantised weight ``(code - 8) * scale``.
+
+Kernel layout (one expert matrix [N, K]; ``gated`` for gate_up, where N = 2I rows are gate then up)
+    row tiles of 128 rows; each tile is a run of pipeline stages of up to 256 k (16 KB of int4); inside a stage,
+    eight 16-row slabs (one per consumer warp), each a run of 64-k chunks of 512 bytes in which lane L = 4g + t
+    owns 16 bytes: words (row g, block 2c), (row g+8, block 2c), (row g, block 2c+1), (row g+8, block 2c+1),
+    each word holding k = 32b + 8t .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i]. For gate_up, slab row
+    g < 8 is gate row 64r + 8w + g and slab row g + 8 is the matching up row, so SwiGLU pairs sit in one thread.
+    Scales follow the same tile/stage/slab order, 16 entries per (slab, 128-k group) with rows (g, g+8) adjacent.
+bf16 kernel layout (the shared expert): same tiles and slabs, stages of 64 k, four mma k-steps per slab, lane L
+    holds its four A-fragment registers (rows g, g+8; k = 16s + 4t .. +3).
+
+The CUDA entry points ``qf_w4_repack``/``qf_bf16_repack`` produce these layouts on the device; the ``*_torch``
+functions here compute the same index maps with tensor ops (any device) and are used by the CPU tests.
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+NIBBLE_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
+
+
+# ------------------------------------------------------------------------------------------ canonical helpers
+def pack_int4(codes: torch.Tensor) -> torch.Tensor:
+    """int codes [..., N, K] in 0..15 -> int32 [..., N, K/8] (lowest k in the low nibble)."""
+    c = codes.to(torch.int64).reshape(*codes.shape[:-1], codes.shape[-1] // 8, 8)
+    shifts = torch.arange(0, 32, 4, device=codes.device, dtype=torch.int64)
+    w = (c << shifts).sum(-1)
+    w = torch.where(w >= 2 ** 31, w - 2 ** 32, w)
+    return w.to(torch.int32)
+
+
+def unpack_int4(words: torch.Tensor) -> torch.Tensor:
+    shifts = torch.arange(0, 32, 4, device=words.device, dtype=torch.int32)
+    q = (words.unsqueeze(-1) >> shifts) & 0xF
+    return q.reshape(*words.shape[:-1], words.shape[-1] * 8)
+
+
+def _nibble_perm(words: torch.Tensor, forward: bool) -> torch.Tensor:
+    v = words.to(torch.int64) & 0xFFFFFFFF
+    out = torch.zeros_like(v)
+    for i, src in enumerate(NIBBLE_ORDER):
+        if forward:
+            out |= ((v >> (4 * src)) & 0xF) << (4 * i)
+        else:
+            out |= ((v >> (4 * i)) & 0xF) << (4 * src)
+    out = torch.where(out >= 2 ** 31, out - 2 ** 32, out)
+    return out.to(torch.int32)
+
+
+# ----------------------------------------------------------------------------------------------- index maps
+def kernel_row_source(N: int, gated: bool, device=None) -> torch.Tensor:
+    p = torch.arange(N, device=device, dtype=torch.int64)
+    if not gated:
+        return p
+    r, w, rho = p // 128, (p % 128) // 16, p % 16
+    return torch.where(rho < 8, 64 * r + 8 * w + rho, N // 2 + 64 * r + 8 * w + rho - 8)
+
+
+def w4_word_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
+    """Kernel-layout word o -> canonical word index row * (K/8) + kw, for one [N, K] matrix."""
+    o = torch.arange(N * K // 8, device=device, dtype=torch.int64)
+    per_tile = 128 * K // 8
+    r, ot = o // per_tile, o % per_tile
+    st = ot // 4096
+    kc = torch.clamp(K - 256 * st, max=256)
+    os_ = ot - 4096 * st
+    slab_words = (kc // 64) * 128
+    w = os_ // slab_words
+    ow = os_ - w * slab_words
+    c, lane, j = ow >> 7, (ow >> 2) & 31, ow & 3
+    g, t = lane >> 2, lane & 3
+    rho, b = g + 8 * (j & 1), 2 * c + (j >> 1)
+    kw = 32 * st + 4 * b + t
+    row = kernel_row_source(N, gated, device)[128 * r + 16 * w + rho]
+    return row * (K // 8) + kw
+
+
+def w4_scale_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
+    """Kernel-layout scale entry o -> canonical index row * (K/128) + group."""
+    o = torch.arange(N * K // 128, device=device, dtype=torch.int64)
+    r, ot = o // K, o % K
+    st = ot // 256
+    kc = torch.clamp(K - 256 * st, max=256)
+    os_ = ot - 256 * st
+    per_slab = (kc // 128) * 16
+    w = os_ // per_slab
+    gi, ent = (os_ - w * per_slab) >> 4, os_ & 15
+    rho = (ent >> 1) + 8 * (ent & 1)
+    row = kernel_row_source(N, gated, device)[128 * r + 16 * w + rho]
+    return row * (K // 128) + 2 * st + gi
+
+
+def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
+    """bf16 kernel-layout element o -> canonical index row * K + k."""
+    o = torch.arange(N * K, device=device, dtype=torch.int64)
+    per_tile = 128 * K
+    r, ot = o // per_tile, o % per_tile
+    st, os_ = ot >> 13, ot & 8191
+    w, ks, lane, reg, e2 = os_ >> 10, (os_ >> 8) & 3, (os_ >> 3) & 31, (os_ >> 1) & 3, os_ & 1
+    g, t, q, hi = lane >> 2, lane & 3, reg >> 1, reg & 1
+    k = 64 * st + 16 * ks + 4 * t + 2 * q + e2
+    row = kernel_row_source(N, gated, device)[128 * r + 16 * w + g + 8 * hi]
+    return row * K + k
+
+
+def _check_w4(qweight, scales):
+    if qweight.dtype != torch.int32 or qweight.dim() != 3:
+        raise RuntimeError("qweight must be int32 [E, N, K/8]")
+    E, N, KW = qweight.shape
+    K = KW * 8
+    if scales.dtype != torch.bfloat16 or tuple(scales.shape) != (E, N, K // 128):
+        raise RuntimeError(f"scales must be bf16 [E, N, K/128] = {(E, N, K // 128)}, got {tuple(scales.shape)}")
+    if N % 128 or K % 128:
+        raise RuntimeError(f"N and K must be multiples of 128, got N={N}, K={K}")
+    return E, N, K
+
+
+# ------------------------------------------------------------------------------------------ torch versions
+def repack_w4_torch(qweight: torch.Tensor, scales: torch.Tensor, gated: bool):
+    E, N, K = _check_w4(qweight, scales)
+    wm = w4_word_map(N, K, gated, qweight.device)
+    sm = w4_scale_map(N, K, gated, qweight.device)
+    wk = _nibble_perm(qweight.reshape(E, -1)[:, wm], True)
+    sk = scales.reshape(E, -1)[:, sm]
+    return wk.contiguous(), sk.contiguous()
+
+
+def unpack_w4_torch(wk: torch.Tensor, sk: torch.Tensor, N: int, K: int, gated: bool):
+    E = wk.shape[0]
+    wm = w4_word_map(N, K, gated, wk.device)
+    sm = w4_scale_map(N, K, gated, wk.device)
+    q = torch.empty(E, N * K // 8, dtype=torch.int32, device=wk.device)
+    q[:, wm] = _nibble_perm(wk, False)
+    s = torch.empty(E, N * K // 128, dtype=sk.dtype, device=sk.device)
+    s[:, sm] = sk
+    return q.view(E, N, K // 8), s.view(E, N, K // 128)
+
+
+def repack_bf16_torch(w: torch.Tensor, gated: bool) -> torch.Tensor:
+    N, K = w.shape
+    if N % 128 or K % 64:
+        raise RuntimeError(f"bf16 weight needs N % 128 == 0 and K % 64 == 0, got {N}x{K}")
+    return w.reshape(-1)[bf16_elem_map(N, K, gated, w.device)].contiguous()
+
+
+def unpack_bf16_torch(wk: torch.Tensor, N: int, K: int, gated: bool) -> torch.Tensor:
+    w = torch.empty(N * K, dtype=wk.dtype, device=wk.device)
+    w[bf16_elem_map(N, K, gated, wk.device)] = wk.reshape(-1)
+    return w.view(N, K)
+
+
+# ------------------------------------------------------------------------------------ device (C ABI) versions
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _req_cuda(*ts):
+    for t in ts:
+        if not t.is_cuda or not t.is_contiguous():
+            raise RuntimeError("expected contiguous CUDA tensors")
+
+
+def repack_w4(qweight: torch.Tensor, scales: torch.Tensor, gated: bool):
+    """Canonical int4 experts -> kernel layout on the GPU. Returns (wk int32 [E, N*K/8], sk bf16 [E, N*K/128])."""
+    E, N, K = _check_w4(qweight, scales)
+    _req_cuda(qweight, scales)
+    wk = torch.empty(E, N * K // 8, dtype=torch.int32, device=qweight.device)
+    sk = torch.empty(E, N * K // 128, dtype=torch.bfloat16, device=qweight.device)
+    with torch.cuda.device(qweight.device):
+        _lib.check(_lib.load().qf_w4_repack(qweight.data_ptr(), scales.data_ptr(), wk.data_ptr(), sk.data_ptr(),
+                                            E, N, K, int(gated), _stream(qweight)), "w4_repack")
+    return wk, sk
+
+
+def unpack_w4(wk: torch.Tensor, sk: torch.Tensor, N: int, K: int, gated: bool):
+    _req_cuda(wk, sk)
+    E = wk.shape[0]
+    q = torch.empty(E, N, K // 8, dtype=torch.int32, device=wk.device)
+    s = torch.empty(E, N, K // 128, dtype=torch.bfloat16, device=wk.device)
+    with torch.cuda.device(wk.device):
+        _lib.check(_lib.load().qf_w4_unpack(wk.data_ptr(), sk.data_ptr(), q.data_ptr(), s.data_ptr(), E, N, K,
+                                            int(gated), _stream(wk)), "w4_unpack")
+    return q, s
+
+
+def repack_bf16(w: torch.Tensor, gated: bool) -> torch.Tensor:
+    _req_cuda(w)
+    N, K = w.shape
+    wk = torch.empty(N * K, dtype=torch.bfloat16, device=w.device)
+    with torch.cuda.device(w.device):
+        _lib.check(_lib.load().qf_bf16_repack(w.data_ptr(), wk.data_ptr(), N, K, int(gated), _stream(w)), "bf16_repack")
+    return wk
+
+
+def unpack_bf16(wk: torch.Tensor, N: int, K: int, gated: bool) -> torch.Tensor:
+    _req_cuda(wk)
+    w = torch.empty(N, K, dtype=torch.bfloat16, device=wk.device)
+    with torch.cuda.device(wk.device):
+        _lib.check(_lib.load().qf_bf16_unpack(wk.data_ptr(), w.data_ptr(), N, K, int(gated), _stream(wk)), "bf16_unpack")
+    return w

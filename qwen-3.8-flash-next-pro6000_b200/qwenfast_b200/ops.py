@@ -1,0 +1,255 @@
+"""Torch-facing ops with the reference extension's names and argument roles (serve/qwenfast/qf_bind.cpp).
+
+Each op validates like the reference's TORCH_CHECKs (raising RuntimeError), allocates its outputs like the
+reference (``at::empty``), and enqueues the sm_100a kernel on the current CUDA stream through the C ABI. There is no
+CPU path: CPU tensors are rejected.
+"""
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .formats import repack_bf16, repack_w4
+
+BF16 = torch.bfloat16
+
+
+def _req(cond: bool, msg: str):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None or t.numel() == 0 else t.data_ptr()
+
+
+def _present(t: Optional[torch.Tensor]) -> bool:
+    return t is not None and t.numel() > 0
+
+
+def _stream(dev: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _cuda(t: torch.Tensor, name: str, op: str):
+    _req(t.is_cuda, f"{op}: {name} must be a CUDA tensor")
+
+
+# ------------------------------------------------------------------------------------------------- router
+def router_topk(x: torch.Tensor, w: torch.Tensor, topk: int, renormalize: bool, scratch: torch.Tensor,
+                counter: torch.Tensor, pdl: bool = True):
+    """(topk_weights fp32 [rows, k], topk_ids int32 [rows, k], router_logits bf16 [rows, E]).
+
+    Mirrors ``router_topk`` (serve/qwenfast/qf_router.cu:164-193): scratch fp32 >= rows * E, counter int32 [1]
+    zeroed once and re-armed by the kernel. rows 1..64."""
+    op = "router_topk"
+    _cuda(x, "x", op)
+    _req(x.dtype == BF16 and x.dim() == 2 and x.is_contiguous(), f"{op}: x must be contiguous bf16 [rows, H]")
+    _req(w.dtype == BF16 and w.dim() == 2 and w.size(1) == x.size(1) and w.is_contiguous() and w.device == x.device,
+         f"{op}: w must be contiguous bf16 [E, H] on x's device")
+    _req(scratch.dtype == torch.float32 and scratch.device == x.device, f"{op}: scratch must be fp32 on x's device")
+    _req(counter.dtype == torch.int32 and counter.numel() >= 1 and counter.device == x.device,
+         f"{op}: counter must be int32 [>=1] on x's device")
+    rows, H = x.shape
+    E = w.shape[0]
+    weights = torch.empty(rows, topk, dtype=torch.float32, device=x.device)
+    ids = torch.empty(rows, topk, dtype=torch.int32, device=x.device)
+    logits = torch.empty(rows, E, dtype=BF16, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().qf_router_topk(
+            x.data_ptr(), w.data_ptr(), rows, H, E, int(topk), int(bool(renormalize)), weights.data_ptr(),
+            ids.data_ptr(), logits.data_ptr(), scratch.data_ptr(), scratch.numel(), counter.data_ptr(), int(bool(pdl)),
+            _stream(x.device)), op)
+    return weights, ids, logits
+
+
+def router_bufs(device, rows: int = 64, experts: int = 1024):
+    """Caller-owned router scratch (reference qwenfast.py:1032-1038): fp32 [rows * experts], counter int32 [1]."""
+    return (torch.empty(rows * experts, dtype=torch.float32, device=device),
+            torch.zeros(1, dtype=torch.int32, device=device))
+
+
+# ------------------------------------------------------------------------------------------------- MoE
+def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
+    """Caller-owned scratch for ``a16_moe_decode`` (the reference's ``_a16_bufs``, qwenfast.py:1044-1059)."""
+    lib = _lib.load()
+    v = [ctypes.c_int64() for _ in range(6)]
+    _lib.check(lib.qf_a16_moe_workspace(M, H, I, topk, Is, *[ctypes.byref(a) for a in v]), "moe_workspace")
+    hb, yb, gl, ctrl, pb, sh = (a.value for a in v)
+    return dict(
+        hbuf=torch.empty(hb // 2, dtype=BF16, device=device),
+        ybuf=torch.empty(yb // 2, dtype=BF16, device=device),
+        gl=torch.empty(gl, dtype=torch.float32, device=device),
+        ctrl=torch.zeros(ctrl, dtype=torch.int32, device=device),
+        pbuf=torch.empty(max(pb, 1), dtype=torch.float32, device=device),
+        shbuf=torch.empty(max(sh // 2, 1), dtype=BF16, device=device),
+        none=torch.empty(0, dtype=BF16, device=device),
+    )
+
+
+def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, shared, hbuf, ybuf, gl, ctrl, out,
+                   phase: int = 4, dbg=None, pbuf=None, shq1=None, shs1=None, shq2=None, shs2=None, shbuf=None,
+                   pdl: bool = True, mode: int = 0, expert_range=None):
+    """Routed experts + shared expert + combine; writes ``out`` in place and returns it.
+
+    Argument roles follow ``a16_moe_decode`` (serve/qwenfast/qf_a16moe.cu:852-863). Weight format: the kernel
+    layout of ``repack_w4`` -- w13 int32 [E, 2I*H/8], s13 bf16 [E, 2I*H/128], w2 int32 [E, H*I/8],
+    s2 bf16 [E, H*I/128]; gs13 / gs2 bf16 [E] or empty (= 1). The in-kernel shared expert takes bf16 weights in the
+    kernel layout of ``repack_bf16``: shq1 = gate_up [2Is*H], shq2 = down [H*Is] (shs1 / shs2 must be empty: there
+    are no separate scales for bf16). ``shared`` is a precomputed bf16 [M, H] shared output instead (or empty).
+    Empty tensors mean "absent", as in the reference."""
+    op = "a16_moe_decode"
+    _cuda(x, "x", op)
+    M, H = x.shape
+    _req(x.dtype == BF16 and x.dim() == 2 and x.is_contiguous(), f"{op}: x must be contiguous bf16 [M, H]")
+    _req(topk_ids.dtype == torch.int32 and topk_ids.dim() == 2 and topk_ids.size(0) == M and topk_ids.is_contiguous(),
+         f"{op}: topk_ids must be contiguous int32 [M, topk]")
+    _req(topk_w.dtype == torch.float32 and tuple(topk_w.shape) == tuple(topk_ids.shape) and topk_w.is_contiguous(),
+         f"{op}: topk_w must be contiguous fp32 [M, topk]")
+    _req(w13.dtype == torch.int32 and w2.dtype == torch.int32 and w13.dim() == 2 and w2.dim() == 2,
+         f"{op}: w13 / w2 must be int32 kernel-layout [E, *] tensors (see repack_w4)")
+    E = w13.shape[0]
+    I = (w2.shape[1] * 8) // H
+    _req(w2.shape[0] == E and w13.shape[1] == 2 * I * H // 8 and w2.shape[1] * 8 == H * I,
+         f"{op}: w13 / w2 shapes do not match H={H}")
+    _req(s13.dtype == BF16 and tuple(s13.shape) == (E, 2 * I * H // 128), f"{op}: s13 must be bf16 [E, 2I*H/128]")
+    _req(s2.dtype == BF16 and tuple(s2.shape) == (E, H * I // 128), f"{op}: s2 must be bf16 [E, H*I/128]")
+    for name, g in (("gs13", gs13), ("gs2", gs2)):
+        _req(not _present(g) or (g.dtype == BF16 and g.numel() == E), f"{op}: {name} must be bf16 [E] or empty")
+    _req(not _present(shs1) and not _present(shs2), f"{op}: bf16 shared-expert weights take no separate scales")
+    has_shw = _present(shq1)
+    Is = 0
+    if has_shw:
+        _req(_present(shq2) and shq1.dtype == BF16 and shq2.dtype == BF16, f"{op}: shq1 / shq2 must be bf16")
+        Is = shq2.numel() // H
+        _req(shq1.numel() == 2 * Is * H and shq2.numel() == H * Is, f"{op}: shared-expert weight sizes do not match")
+    if _present(shared):
+        _req(shared.dtype == BF16 and shared.is_contiguous() and tuple(shared.shape) == (M, H),
+             f"{op}: shared must be contiguous bf16 [M, H]")
+    _req(out.dtype == BF16 and tuple(out.shape) == (M, H) and out.is_contiguous(), f"{op}: out must be bf16 [M, H]")
+    lo, hi = (0, E) if expert_range is None else expert_range
+    tensors = [topk_ids, topk_w, w13, s13, w2, s2, hbuf, ybuf, gl, ctrl, out]
+    _req(all(t.device == x.device for t in tensors), f"{op}: every tensor must be on x's device")
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().qf_a16_moe_decode(
+            x.data_ptr(), topk_ids.data_ptr(), topk_w.data_ptr(), w13.data_ptr(), s13.data_ptr(), _ptr(gs13),
+            w2.data_ptr(), s2.data_ptr(), _ptr(gs2), _ptr(w_gate), _ptr(shared), _ptr(shq1) if has_shw else None,
+            _ptr(shq2) if has_shw else None,
+            hbuf.data_ptr(), hbuf.numel() * hbuf.element_size(), ybuf.data_ptr(), ybuf.numel() * ybuf.element_size(),
+            gl.data_ptr(), gl.numel(), ctrl.data_ptr(), ctrl.numel(),
+            _ptr(pbuf), 0 if pbuf is None else pbuf.numel(),
+            _ptr(shbuf), 0 if shbuf is None else shbuf.numel() * shbuf.element_size(),
+            out.data_ptr(), M, H, I, E, topk_ids.shape[1], Is, int(phase), int(mode), int(lo), int(hi),
+            _ptr(dbg), int(bool(pdl)), _stream(x.device)), op)
+    return out
+
+
+def moe_error_word(ctrl: torch.Tensor) -> int:
+    """The sticky error word of a MoE control block (reads the device; synchronises)."""
+    return int(ctrl[_lib.QF_MOE_CTRL_ERR].item())
+
+
+@dataclass
+class MoELayerWeights:
+    """One MoE layer in kernel layout (routed experts + optional bf16 shared expert + router)."""
+    router: torch.Tensor            # bf16 [E, H]
+    w13: torch.Tensor               # int32 [E, 2I*H/8]
+    s13: torch.Tensor               # bf16 [E, 2I*H/128]
+    w2: torch.Tensor                # int32 [E, H*I/8]
+    s2: torch.Tensor                # bf16 [E, H*I/128]
+    w_gate: Optional[torch.Tensor]  # bf16 [H]
+    sh_w13: Optional[torch.Tensor]  # bf16 [2Is*H] kernel layout
+    sh_w2: Optional[torch.Tensor]   # bf16 [H*Is] kernel layout
+    H: int
+    I: int
+    E: int
+    Is: int
+
+    @staticmethod
+    def from_canonical(router, w13, s13, w2, s2, w_gate=None, sh_gu=None, sh_d=None) -> "MoELayerWeights":
+        """Repack canonical tensors (see formats.py) on their CUDA device."""
+        E, N13, _ = w13.shape
+        H = router.shape[1]
+        I = N13 // 2
+        wk13, sk13 = repack_w4(w13, s13, gated=True)
+        wk2, sk2 = repack_w4(w2, s2, gated=False)
+        shw13 = repack_bf16(sh_gu, gated=True) if sh_gu is not None else None
+        shw2 = repack_bf16(sh_d, gated=False) if sh_d is not None else None
+        Is = sh_d.shape[1] if sh_d is not None else 0
+        return MoELayerWeights(router.contiguous(), wk13, sk13, wk2, sk2,
+                               None if w_gate is None else w_gate.contiguous(), shw13, shw2, H, I, E, Is)
+
+
+def moe_layer_step(x: torch.Tensor, lw: MoELayerWeights, topk: int, bufs: dict, rbufs, out: torch.Tensor,
+                   renormalize: bool = True, pdl: bool = True):
+    """One decode MoE layer-step: router_topk then a16_moe_decode (the reference's ``dual`` fast path,
+    qwenfast.py:1177-1201, with the shared expert computed in-kernel). Returns (out, topk_w, topk_ids, logits)."""
+    tw, ids, logits = router_topk(x, lw.router, topk, renormalize, rbufs[0], rbufs[1], pdl)
+    a16_moe_decode(x, ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"], bufs["ybuf"],
+                   bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None,
+                   bufs["shbuf"], pdl=pdl)
+    return out, tw, ids, logits
+
+
+# ------------------------------------------------------------------------------------------------- INT8
+def w8g_gemm(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, rpw: int = 0, pdl: bool = False) -> torch.Tensor:
+    """y = x @ (q * s)^T (W8A16, group-scaled int8). Mirrors ``w8g_gemm`` (serve/qwenfast/qf_w8g.cu:303-336)."""
+    op = "w8g_gemm"
+    _cuda(x, "x", op)
+    _req(q.is_cuda and s.is_cuda and x.dtype == BF16, f"{op}: x bf16, q, s on CUDA")
+    _req(q.dtype == torch.int8 and s.dtype == BF16, f"{op}: q int8, s bf16")
+    _req(x.dim() == 2 and q.dim() == 2 and x.size(1) == q.size(1) and q.is_contiguous() and s.is_contiguous(),
+         f"{op}: shapes")
+    _req(s.dim() == 2 and s.size(0) == q.size(0) and q.size(1) % s.size(1) == 0, f"{op}: scale shape")
+    _req(x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0, f"{op}: x layout")
+    M, K = x.shape
+    N = q.shape[0]
+    group = K // s.shape[1]
+    y = torch.empty(M, N, dtype=BF16, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().qf_w8g_gemm(x.data_ptr(), x.stride(0), q.data_ptr(), s.data_ptr(), y.data_ptr(), N, M,
+                                           N, K, group, int(rpw), int(bool(pdl)), _stream(x.device)), op)
+    return y
+
+
+def w8g_unpack(q: torch.Tensor, s: torch.Tensor, w: torch.Tensor):
+    """w bf16 [rows, K] <- bf16(q * s). Mirrors ``w8g_unpack`` (serve/qwenfast/qf_w8g.cu:338-351)."""
+    op = "w8g_unpack"
+    _req(q.dtype == torch.int8 and s.dtype == BF16 and w.dtype == BF16, f"{op}: dtypes")
+    _req(q.dim() == 2 and q.is_contiguous() and s.is_contiguous() and w.is_contiguous() and w.shape == q.shape,
+         f"{op}: shapes")
+    K = q.shape[1]
+    group = K // s.shape[1]
+    _req(group * s.shape[1] == K, f"{op}: scale shape")
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.load().qf_w8g_unpack(q.data_ptr(), s.data_ptr(), w.data_ptr(), q.shape[0], K, group,
+                                             _stream(q.device)), op)
+
+
+def w8a8_gemm(x: torch.Tensor, q: torch.Tensor, sw: torch.Tensor, xq: Optional[torch.Tensor] = None,
+              sx: Optional[torch.Tensor] = None, acc_out: Optional[torch.Tensor] = None,
+              pdl: bool = True) -> torch.Tensor:
+    """W8A8: per-token int8 activations (absmax/127), per-channel fp32 weight scales, int32 accumulation.
+    Returns y bf16 [M, N]. ``xq`` int8 [M*K] / ``sx`` fp32 [M] scratch are allocated when not given; ``acc_out``
+    (int32 [M, N]) receives the exact accumulators when given."""
+    op = "w8a8_gemm"
+    _cuda(x, "x", op)
+    _req(x.dtype == BF16 and x.dim() == 2 and x.stride(1) == 1, f"{op}: x must be bf16 [M, K] with unit column stride")
+    _req(q.dtype == torch.int8 and q.dim() == 2 and q.is_contiguous() and q.size(1) == x.size(1), f"{op}: q int8 [N, K]")
+    _req(sw.dtype == torch.float32 and sw.numel() == q.size(0), f"{op}: sw fp32 [N]")
+    M, K = x.shape
+    N = q.shape[0]
+    if xq is None:
+        xq = torch.empty(M * K, dtype=torch.int8, device=x.device)
+    if sx is None:
+        sx = torch.empty(M, dtype=torch.float32, device=x.device)
+    if acc_out is not None:
+        _req(acc_out.dtype == torch.int32 and acc_out.numel() >= M * N, f"{op}: acc_out int32 [M, N]")
+    y = torch.empty(M, N, dtype=BF16, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().qf_w8a8_gemm(x.data_ptr(), x.stride(0), q.data_ptr(), sw.data_ptr(), y.data_ptr(), N,
+                                            M, N, K, xq.data_ptr(), sx.data_ptr(), None, _ptr(acc_out),
+                                            int(bool(pdl)), _stream(x.device)), op)
+    return y

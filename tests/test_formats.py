@@ -1,0 +1,44 @@
+"""Kernel-native weight layouts (host-side index maps): exact round trips and full permutations."""
+import pytest
+import torch
+
+from qwenfast_b200 import formats, synthetic
+
+
+@pytest.mark.parametrize("N,K,gated", [(256, 256, True), (256, 128, False), (1024, 2048, True), (2048, 512, False),
+                                       (384, 384, False), (128, 640, True)])
+def test_w4_round_trip(N, K, gated):
+    E = 2
+    q = synthetic.random_int4_words((E, N, K // 8), torch.Generator().manual_seed(N + K), "cpu")
+    s = synthetic.group_scales((E, N, K // 128), torch.Generator().manual_seed(1), "cpu")
+    wk, sk = formats.repack_w4_torch(q, s, gated)
+    q2, s2 = formats.unpack_w4_torch(wk, sk, N, K, gated)
+    assert torch.equal(q, q2) and torch.equal(s, s2)
+    assert torch.equal(formats.w4_word_map(N, K, gated).sort().values, torch.arange(N * K // 8))
+    assert torch.equal(formats.w4_scale_map(N, K, gated).sort().values, torch.arange(N * K // 128))
+
+
+@pytest.mark.parametrize("N,K,gated", [(1024, 2048, True), (2048, 512, False), (256, 64, True)])
+def test_bf16_round_trip(N, K, gated):
+    w = torch.randn(N, K).to(torch.bfloat16)
+    wk = formats.repack_bf16_torch(w, gated)
+    assert torch.equal(formats.unpack_bf16_torch(wk, N, K, gated), w)
+    assert torch.equal(formats.bf16_elem_map(N, K, gated).sort().values, torch.arange(N * K))
+
+
+def test_gate_up_rows_interleave_in_slabs():
+    src = formats.kernel_row_source(256, True)
+    # tile 0, slab 0: rows 0..7 are gate rows 0..7, rows 8..15 the matching up rows 128..135
+    assert src[:16].tolist() == list(range(8)) + list(range(128, 136))
+    assert src[128:136].tolist() == list(range(64, 72))
+
+
+def test_pack_unpack_int4_and_nibble_order():
+    codes = torch.randint(0, 16, (3, 5, 64))
+    words = formats.pack_int4(codes)
+    assert torch.equal(formats.unpack_int4(words).long(), codes)
+    # kernel nibble order: nibble i of a kernel word holds k = [0,2,4,6,1,3,5,7][i] of its eight
+    w = formats.pack_int4(torch.arange(8).view(1, 8))
+    p = formats._nibble_perm(w, True)
+    assert [(int(p) >> (4 * i)) & 0xF for i in range(8)] == [0, 2, 4, 6, 1, 3, 5, 7]
+    assert torch.equal(formats._nibble_perm(p, False), w)

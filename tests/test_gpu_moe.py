@@ -1,0 +1,217 @@
+"""The persistent W4A16 MoE kernel (+ shared expert + combine) vs the CPU oracle.
+
+Tolerances: bf16 outputs within max-abs 2e-2 and relative L2 1e-2 of the fp32-accumulated
+oracle that keeps the reference's bf16 rounding points (oracle.moe_ref.moe_rounded), and relative L2 1e-2 of the
+all-fp32 truth (serve/qwenfast/test_a16moe.py:139-148). The routing fed to the oracle is the kernel router's own
+ids and weights, so GEMM rounding in the router cannot flip an expert. Also checked, as in test_a16moe.py:163-178
+and :235-237: batch invariance (rows together == rows one at a time, bit for bit), back-to-back launches equal to
+synchronised ones, and the control block re-armed to zero after every launch."""
+import os
+
+import pytest
+import torch
+
+from conftest import GOLDEN
+from oracle import moe_ref
+from qwenfast_b200 import formats, ops, synthetic
+from qwenfast_b200.ops import MoELayerWeights
+
+pytestmark = pytest.mark.gpu
+BF = torch.bfloat16
+
+
+def assert_close_to_oracle(out, ref_rounded, ref_truth=None):
+    out = out.float().cpu()
+    d = out - ref_rounded.float()
+    rel = (d.norm() / ref_rounded.float().norm()).item()
+    assert d.abs().max().item() <= 2e-2 and rel <= 1e-2, (d.abs().max().item(), rel)
+    if ref_truth is not None:
+        rel_t = ((out - ref_truth).norm() / ref_truth.norm()).item()
+        assert rel_t <= 1e-2, rel_t
+
+
+def canon_cpu(L):
+    return {k: v.cpu() for k, v in L.items()}
+
+
+def layer_on(dev, L):
+    return MoELayerWeights.from_canonical(L["router"].to(dev), L["w13"].to(dev), L["s13"].to(dev), L["w2"].to(dev),
+                                          L["s2"].to(dev), L["w_gate"].to(dev) if "w_gate" in L else None,
+                                          L["sh_gu"].to(dev) if "sh_gu" in L else None,
+                                          L["sh_d"].to(dev) if "sh_d" in L else None)
+
+
+def run_moe(x, ids, tw, lw, bufs, shared=None, gs13=None, gs2=None, use_shw=True, out=None):
+    out = torch.empty_like(x) if out is None else out
+    ops.a16_moe_decode(x, ids, tw, lw.w13, lw.s13, gs13, lw.w2, lw.s2, gs2, lw.w_gate, shared, bufs["hbuf"],
+                       bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"],
+                       lw.sh_w13 if use_shw else None, None, lw.sh_w2 if use_shw else None, None, bufs["shbuf"])
+    return out
+
+
+@pytest.fixture(scope="module")
+def cfg1(cuda):
+    cfg = synthetic.CONFIGS[1]
+    L = synthetic.make_moe_layer(cfg, device=cuda)
+    lw = layer_on(cuda, L)
+    return cfg, L, lw, canon_cpu(L)
+
+
+def test_config0_against_golden(cuda):
+    cfg = synthetic.CONFIGS[0]
+    gold = torch.load(os.path.join(GOLDEN, "config0.pt"))
+    L = synthetic.make_moe_layer(cfg)
+    x = synthetic.make_tokens(cfg)
+    from tests.golden.make_golden import checksum  # noqa: E402  (same checksum as the fixture writer)
+    assert checksum(x, L["router"], L["w13"], L["s13"], L["w2"], L["s2"]) == gold["checksum"]
+    lw = layer_on(cuda, L)
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, 0, cuda)
+    out = run_moe(x.to(cuda), gold["ids"].to(cuda), gold["weights"].to(cuda), lw, bufs)
+    torch.cuda.synchronize()
+    assert_close_to_oracle(out, gold["out_rounded"], gold["out_truth"])
+    assert int(bufs["ctrl"].abs().sum().item()) == 0
+
+
+def test_config0_layer_step(cuda):
+    cfg = synthetic.CONFIGS[0]
+    L = synthetic.make_moe_layer(cfg)
+    x = synthetic.make_tokens(cfg).to(cuda)
+    lw = layer_on(cuda, L)
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, 0, cuda)
+    rb = ops.router_bufs(cuda)
+    out = torch.empty_like(x)
+    _, tw, ids, _ = ops.moe_layer_step(x, lw, cfg.topk, bufs, rb, out)
+    torch.cuda.synchronize()
+    ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), tw.cpu(), L["w13"], L["s13"], L["w2"], L["s2"])
+    assert_close_to_oracle(out, ref)
+
+
+def test_config1_full_layer(cfg1, cuda):
+    cfg, L, lw, C = cfg1
+    x = synthetic.make_tokens(cfg, device=cuda)
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+    rb = ops.router_bufs(cuda)
+    out = torch.empty_like(x)
+    _, tw, ids, _ = ops.moe_layer_step(x, lw, cfg.topk, bufs, rb, out)
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) == 0
+    xs, i_c, w_c = x.cpu(), ids.cpu(), tw.cpu()
+    ref = moe_ref.moe_rounded(xs, i_c, w_c, C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
+                              shared_w=(C["sh_gu"], C["sh_d"]))
+    tru = moe_ref.moe_truth(xs, i_c, w_c, C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
+                            shared_w=(C["sh_gu"], C["sh_d"]))
+    assert_close_to_oracle(out, ref, tru)
+    assert int(bufs["ctrl"].abs().sum().item()) == 0
+
+
+def test_config1_precomputed_shared(cfg1, cuda):
+    cfg, L, lw, C = cfg1
+    x = synthetic.make_tokens(cfg, device=cuda, seed=5)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    shared = (torch.randn(cfg.M, cfg.H, generator=g) * 0.05).to(BF)
+    w, ids, _ = ops.router_topk(x, lw.router, cfg.topk, True, *ops.router_bufs(cuda))
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, 0, cuda)
+    out = run_moe(x, ids, w, lw, bufs, shared=shared.to(cuda), use_shw=False)
+    torch.cuda.synchronize()
+    ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], shared=shared,
+                              w_gate=C["w_gate"])
+    assert_close_to_oracle(out, ref)
+
+
+def test_batch_invariance_and_back_to_back(cfg1, cuda):
+    cfg, L, lw, C = cfg1
+    x = synthetic.make_tokens(cfg, device=cuda, seed=11)
+    w, ids, _ = ops.router_topk(x, lw.router, cfg.topk, True, *ops.router_bufs(cuda))
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+    ref = run_moe(x, ids, w, lw, bufs).clone()
+    torch.cuda.synchronize()
+    outs = [run_moe(x, ids, w, lw, bufs) for _ in range(5)]            # back to back, no sync
+    single = [run_moe(x[r:r + 1].contiguous(), ids[r:r + 1].contiguous(), w[r:r + 1].contiguous(), lw, bufs)
+              for r in range(cfg.M)]
+    torch.cuda.synchronize()
+    assert all(torch.equal(o, ref) for o in outs)
+    assert torch.equal(torch.cat(single), ref)
+    assert int(bufs["ctrl"].abs().sum().item()) == 0
+
+
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16, 32, 64])
+def test_token_sweep_with_zipf_routing(cfg1, cuda, M):
+    """Config-2 style routing skew: hot experts receive more than 16 tokens (several token groups)."""
+    cfg, L, lw, C = cfg1
+    g = torch.Generator(device="cpu").manual_seed(100 + M)
+    router = synthetic.zipf_router(C["router"].float(), 1.1, g).to(BF)
+    x = synthetic.make_tokens(cfg, M=M, device=cuda, seed=100 + M)
+    w, ids, _ = ops.router_topk(x, router.to(cuda), cfg.topk, True, *ops.router_bufs(cuda))
+    bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+    out = run_moe(x, ids, w, lw, bufs)
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) == 0
+    ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
+                              shared_w=(C["sh_gu"], C["sh_d"]))
+    assert_close_to_oracle(out, ref)
+    if M == 64:
+        counts = torch.bincount(ids.cpu().flatten().long(), minlength=cfg.E)
+        assert counts.max().item() > 16, "the skewed router should give some expert several token groups"
+
+
+def test_global_scales_and_odd_shapes(cuda):
+    """I = 384 (a half-size last k stage in the down projection), top-1 and top-16, per-expert global scales."""
+    cfg = synthetic.MoEConfig("odd", 512, 32, 384, 16, 7, 0, 21)
+    L = synthetic.make_moe_layer(cfg)
+    lw = layer_on(cuda, L)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    gs13 = (torch.rand(cfg.E, generator=g) + 0.5).to(BF)
+    gs2 = (torch.rand(cfg.E, generator=g) + 0.5).to(BF)
+    for topk in (1, 16):
+        x = synthetic.make_tokens(cfg, device=cuda)
+        w, ids, _ = ops.router_topk(x, lw.router, topk, True, *ops.router_bufs(cuda))
+        bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, topk, 0, cuda)
+        out = run_moe(x, ids, w, lw, bufs, gs13=gs13.to(cuda), gs2=gs2.to(cuda))
+        torch.cuda.synchronize()
+        ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), L["w13"], L["s13"], L["w2"], L["s2"], gs13=gs13,
+                                  gs2=gs2)
+        tru = moe_ref.moe_truth(x.cpu(), ids.cpu(), w.cpu(), L["w13"], L["s13"], L["w2"], L["s2"], gs13=gs13, gs2=gs2)
+        assert_close_to_oracle(out, ref, tru)
+
+
+def test_duplicate_and_out_of_range_ids(cuda):
+    """A token that names the same expert twice gets both slots; an out-of-range id is skipped by the kernel's own
+    bounds check and reported in the control block (no memory access through it)."""
+    cfg = synthetic.CONFIGS[0]
+    L = synthetic.make_moe_layer(cfg)
+    lw = layer_on(cuda, L)
+    x = synthetic.make_tokens(cfg).to(cuda)
+    ids = torch.tensor([[3, 3, 5, 9], [1, 2, 3, 4], [15, 0, 7, 7], [8, 6, 4, 2]], dtype=torch.int32)
+    w = torch.full((4, 4), 0.25)
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, 0, cuda)
+    out = run_moe(x, ids.to(cuda), w.to(cuda), lw, bufs)
+    torch.cuda.synchronize()
+    ref = moe_ref.moe_rounded(x.cpu(), ids, w, L["w13"], L["s13"], L["w2"], L["s2"])
+    assert_close_to_oracle(out, ref)
+    assert ops.moe_error_word(bufs["ctrl"]) == 0
+    bad = ids.clone()
+    bad[1, 2] = 99
+    out2 = run_moe(x, bad.to(cuda), w.to(cuda), lw, bufs)
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) & 0x2
+    assert torch.isfinite(out2.float()).all()
+    ok_rows = [0, 2, 3]
+    assert torch.equal(out2[ok_rows].cpu(), out[ok_rows].cpu())
+    bufs["ctrl"].zero_()
+
+
+def test_repack_kernels_match_host_layout(cuda):
+    g = torch.Generator(device="cpu").manual_seed(5)
+    for (N, K, gated) in [(1024, 2048, True), (2048, 512, False), (768, 384, True)]:
+        q = synthetic.random_int4_words((3, N, K // 8), g, "cpu")
+        s = synthetic.group_scales((3, N, K // 128), g, "cpu")
+        wk, sk = formats.repack_w4(q.to(cuda), s.to(cuda), gated)
+        wt, st = formats.repack_w4_torch(q, s, gated)
+        assert torch.equal(wk.cpu(), wt) and torch.equal(sk.cpu(), st)
+        q2, s2 = formats.unpack_w4(wk, sk, N, K, gated)
+        assert torch.equal(q2.cpu(), q) and torch.equal(s2.cpu(), s)
+    for (N, K, gated) in [(1024, 2048, True), (2048, 512, False)]:
+        w = torch.randn(N, K, generator=g).to(BF)
+        wk = formats.repack_bf16(w.to(cuda), gated)
+        assert torch.equal(wk.cpu(), formats.repack_bf16_torch(w, gated))
+        assert torch.equal(formats.unpack_bf16(wk, N, K, gated).cpu(), w)

@@ -1,0 +1,79 @@
+"""INT8 dense GEMMs on the GPU vs the CPU oracle.
+
+W8A16 (w8g, reference qf_w8g.cu): relative L2 < 4e-3 against the fp32 truth x @ (q * s)^T
+(the bound of serve/qwenfast/test_w8k.py:88); w8g_unpack bit-exact.
+W8A8 (config 3): the activation quantisation (xq, sx), the int32 accumulators and the bf16 outputs are all
+bit-exact against the oracle (exact int64 accumulation, the same fp32 multiplies in the same order)."""
+import pytest
+import torch
+
+from oracle import w8_ref
+from qwenfast_b200 import ops, synthetic
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("N,K", [(2048, 2048), (1280, 2560), (2560, 640), (2560, 6144), (4096, 2048)])
+@pytest.mark.parametrize("M", [1, 2, 4, 8, 16, 64])
+def test_w8g_gemm_vs_fp32_truth(cuda, N, K, M):
+    g = torch.Generator(device="cpu").manual_seed(N + K + M)
+    w = (torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = w8_ref.w8_quant(w)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    y = ops.w8g_gemm(x.to(cuda), q.to(cuda), s.to(cuda), 0)
+    truth = x.float() @ w8_ref.w8g_dequant(q, s).T
+    err = ((y.float().cpu() - truth).norm() / truth.norm()).item()
+    assert err < 4e-3, err
+    assert torch.equal(y, ops.w8g_gemm(x.to(cuda), q.to(cuda), s.to(cuda), 0)), "deterministic"
+
+
+def test_w8g_strided_rows_and_group64(cuda):
+    g = torch.Generator(device="cpu").manual_seed(1)
+    w = (torch.randn(512, 192, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = w8_ref.w8_quant(w)                                   # K % 128 != 0 -> group 64
+    assert s.shape[1] == 3
+    xb = torch.randn(5, 256, generator=g).to(torch.bfloat16)
+    x = xb.to(cuda)[:, :192]                                    # row stride 256
+    y = ops.w8g_gemm(x, q.to(cuda), s.to(cuda), 0)
+    truth = xb[:, :192].float() @ w8_ref.w8g_dequant(q, s).T
+    assert ((y.float().cpu() - truth).norm() / truth.norm()).item() < 4e-3
+
+
+def test_w8g_unpack_exact(cuda):
+    g = torch.Generator(device="cpu").manual_seed(2)
+    w = (torch.randn(300, 1024, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = w8_ref.w8_quant(w)
+    out = torch.empty(300, 1024, dtype=torch.bfloat16, device=cuda)
+    ops.w8g_unpack(q.to(cuda), s.to(cuda), out)
+    assert torch.equal(out.cpu(), w8_ref.w8g_dequant(q, s).to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("N", synthetic.W8A8_N)
+@pytest.mark.parametrize("M", synthetic.W8A8_M)
+def test_w8a8_bit_exact(cuda, N, M):
+    K = synthetic.W8A8_K
+    q, sw = synthetic.make_w8a8(N, K, seed=N)
+    x = synthetic.make_w8a8_tokens(M, K, seed=M)
+    xq = torch.empty(M * K, dtype=torch.int8, device=cuda)
+    sx = torch.empty(M, dtype=torch.float32, device=cuda)
+    acc = torch.empty(M, N, dtype=torch.int32, device=cuda)
+    y = ops.w8a8_gemm(x.to(cuda), q.to(cuda), sw.to(cuda), xq=xq, sx=sx, acc_out=acc)
+    torch.cuda.synchronize()
+    yr, accr, xqr, sxr = w8_ref.w8a8_ref(x, q, sw)
+    assert torch.equal(sx.cpu(), sxr)
+    assert torch.equal(xq.view(M, K).cpu(), xqr)
+    assert torch.equal(acc.cpu().long(), accr)
+    assert torch.equal(y.cpu(), yr)
+
+
+def test_w8a8_zero_row_and_outliers(cuda):
+    K, N = 2048, 2048
+    q, sw = synthetic.make_w8a8(N, K, seed=9)
+    x = synthetic.make_w8a8_tokens(4, K, seed=9)
+    x[1] = 0
+    x[2, 17] = 3000.0
+    acc = torch.empty(4, N, dtype=torch.int32, device=cuda)
+    y = ops.w8a8_gemm(x.to(cuda), q.to(cuda), sw.to(cuda), acc_out=acc)
+    yr, accr, _, _ = w8_ref.w8a8_ref(x, q, sw)
+    assert torch.equal(acc.cpu().long(), accr) and torch.equal(y.cpu(), yr)
+    assert (y[1] == 0).all()

@@ -1,0 +1,50 @@
+"""The CPU oracle against outputs of the reference's own Python functions (tests/golden/make_golden.py)."""
+import os
+
+import torch
+
+from conftest import GOLDEN
+from oracle import moe_ref, router_ref, w8_ref
+
+REF = torch.load(os.path.join(GOLDEN, "reference_fns.pt"))
+
+
+def test_w8_quant_matches_reference_bit_exact():
+    for tag in ("w8_g128", "w8_g64"):
+        r = REF[tag]
+        q, s = w8_ref.w8_quant(r["w"])
+        assert torch.equal(q, r["q"]) and torch.equal(s, r["s"]), tag
+        assert r["w"].shape[1] // s.shape[1] == r["G"]
+    assert REF["w8q_equals_w8_quant"]
+
+
+def test_router_selection_matches_reference_route():
+    r = REF["route"]
+    # the reference test's route(): fp32 logits, softmax, torch.topk, renormalise (no ties in this fixture)
+    wts, ids = router_ref.topk_from_logits(r["logits"], r["ids"].shape[1], True)
+    assert torch.equal(ids, r["ids"].int())
+    torch.testing.assert_close(wts, r["w"].float(), rtol=1e-5, atol=1e-7)
+    # and our logits restate the same fp32 product
+    torch.testing.assert_close((r["x"].float() @ r["router"].float().T), r["logits"], rtol=0, atol=0)
+
+
+def test_shared_expert_matches_reference_bit_exact():
+    r = REF["shared_ref"]
+    out = w8_ref.shared_expert_w8g(r["x"], r["sq1"], r["ss1"], r["sq2"], r["ss2"])
+    assert torch.equal(out, r["out"])
+
+
+def test_moe_truth_matches_reference_truth():
+    r = REF["truth"]
+    out = moe_ref.moe_truth(r["x"], r["ids"], r["w"], r["w13"], r["s13"], r["w2"], r["s2"], shared=r["shared"],
+                            w_gate=r["wg"])
+    torch.testing.assert_close(out, r["out"], rtol=1e-6, atol=1e-6)
+
+
+def test_rounded_oracle_close_to_reference_truth():
+    r = REF["truth"]
+    out = moe_ref.moe_rounded(r["x"], r["ids"], r["w"], r["w13"], r["s13"], r["w2"], r["s2"], shared=r["shared"],
+                              w_gate=r["wg"])
+    d = out.float() - r["out"]
+    assert d.norm() / r["out"].norm() < 1e-2
+    assert d.abs().max() < 2e-2
