@@ -1,8 +1,8 @@
 // Decode-size (1..64 tokens) W4A16 routed experts + shared expert + top-k combine in ONE persistent launch.
 //
 // Reference behaviour: serve/qwenfast/qf_a16moe.cu (persistent mode :342-837, host :852-922): gemm1 (gate_up) +
-// SwiGLU, gemm2 (down) with the top-k weight, a top-k-ordered combine per 128-column tile by the last arriving
-// work item, and the sigmoid-gated shared expert. Rounding points (qf_a16moe.cu:2-4):
+// SwiGLU, gemm2 (down) with the top-k weight, a top-k-ordered combine per 128-column tile, and the sigmoid-gated
+// shared expert. Rounding points (qf_a16moe.cu:2-4):
 //   h  = bf16(silu(bf16(bf16(acc_gate) * gs13)) * bf16(bf16(acc_up) * gs13))
 //   y  = bf16(bf16(acc_down) * bf16(gs2 * bf16(topk_w)))            one slot per (token, top-k position)
 //   out = bf16(sigmoid(x . w_gate) * shared + bf16(sum_kpos y))      fp32 sum in top-k order
@@ -10,19 +10,27 @@
 // tensor cores in fp32 and then scaled once (exact products, no per-weight scale multiply).
 //
 // B200 structure
-//   * 1 CTA per SM (148), 9 warps: warp 8 lane 0 is the producer, warps 0..7 are consumers.
-//   * Work items, claimed in order from a global queue:  GL (shared gate logits) | S1 (shared gate_up, 4-way
-//     split-K) | G1 (expert u, 128-row gate_up tile, 16-token group) | S2 (shared down) | G2 (expert u, 128-row
-//     down tile, token group). An item only depends on items claimed before it, so the queue cannot deadlock.
+//   * 2 CTAs per SM (296), 9 warps each: warp 8 lane 0 is the producer, warp 8 lane 1 the signal agent, warps 0..7
+//     are consumers.
+//   * Work items, claimed in order from a global queue:
+//       GL  shared-expert gate logits          S1  shared gate_up tile, one of 4 k-splits, one 16-token group
+//       G1  expert u gate_up tile + group      S1F shared gate_up split-K sum + SwiGLU
+//       S2  shared down tile + group           G2  expert u down tile + group
+//       CB  top-k combine of one 128-column tile (+ gated shared term)
+//     An item only depends on items claimed before it, so the queue cannot deadlock.
 //   * The producer streams each item through an NST-stage shared-memory ring with 1-D bulk copies (TMA engine,
-//     mbarrier completion): per stage 16 KB of weights (128 rows x 256 k int4, or x 64 k bf16), their scales,
-//     and the matching k-slice of the item's token rows (x for gate_up, h for down). It waits (bounded) on the
-//     gate_up -> down and shared gate_up -> down dependencies itself, so consumers never spin on other CTAs.
+//     mbarrier completion): per stage 16 KB of weights (128 rows x 256 k int4, or x 64 k bf16), their scales, and
+//     the matching k-slice of the item's token rows (x for gate_up, h for down). Every cross-CTA dependency
+//     (gate_up -> down, split-K -> finalize -> shared down, all producers of a column tile -> combine) is waited on
+//     by the producer (bounded) before it fills the stage, so consumers never spin on other CTAs.
+//   * Consumers signal completed items through a CTA-local ring; the agent lane turns each record into one gpu-scope
+//     release (fence + atomic add) on the control block. Consumer warps never execute a gpu-scope fence.
 //   * Each consumer warp owns 16 weight rows of the 128-row tile: int4 -> bf16 in registers (lop3 + hsub2),
-//     mma.m16n8k16 with the weights as A and tokens as B (n = 8 or 16), fp32 group partials scaled per group.
-//     gate_up tiles interleave gate row j and up row j in one fragment, so SwiGLU runs in registers.
-//   * The routing plan (unique experts, per-expert token lists, group offsets) is rebuilt identically by every
-//     CTA from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
+//     mma.m16n8k16 with the weights as A and tokens as B (n = 8 or 16), independent partials per 32-k block,
+//     fp32 group partials scaled per group. gate_up tiles interleave gate row j and up row j in one fragment,
+//     so SwiGLU runs in registers.
+//   * The routing plan (unique experts, per-expert token lists, group offsets) is rebuilt identically by every CTA
+//     from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
 //   * Every wait is bounded (globaltimer); a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
 #include "qf_common.cuh"
 
@@ -34,10 +42,12 @@ using qf::bf16_lo;
 using qf::bf16r;
 
 constexpr int NCW = 8;                        // consumer warps
-constexpr int MOE_THREADS = (NCW + 1) * 32;   // + the producer warp
+constexpr int MOE_THREADS = (NCW + 1) * 32;   // + the producer / agent warp
 constexpr int CONS_THREADS = NCW * 32;
+constexpr int CTAS_PER_SM = 2;
 constexpr int TG = 16;                        // tokens per token group (two n8 tiles)
-constexpr int NST = 8;                        // pipeline stages
+constexpr int NST = 4;                        // pipeline stages per CTA
+constexpr int NEPI = 8;                       // completion-record ring
 constexpr int W4_KC = 256;                    // int4 k per stage
 constexpr int BF_KC = 64;                     // bf16 k per stage
 constexpr int STAGE_W = 16384;                // weight bytes of a full stage
@@ -62,10 +72,13 @@ enum : int {
 };
 static_assert(C_DONE + QF_MAX_EXPERTS <= QF_MOE_CTRL_WORDS, "ctrl layout");
 
-enum : int { K_STOP = 0, K_GL, K_S1, K_G1, K_S2, K_G2, K_CB };
+enum : int { K_STOP = 0, K_GL, K_S1, K_G1, K_S1F, K_S2, K_G2, K_CB };
 
 struct StageDesc {
     int16_t kind, u, tile, tg, split, kidx, nk, kc, ntok, pad[3];
+};
+struct EpiRec {     // one completion record: add `add` to ctrl[idx] (idx < 0: nothing; kind STOP ends the agent)
+    int idx, add;
 };
 
 struct Params {
@@ -96,18 +109,19 @@ struct Params {
 
 // shared memory map (dynamic)
 constexpr int OFF_RING = 0;
-constexpr int OFF_BAR = OFF_RING + NST * STAGE_BYTES;
-constexpr int OFF_DESC = OFF_BAR + 2 * NST * 8;
-constexpr int OFF_PLAN = OFF_DESC + NST * (int)sizeof(StageDesc);
-constexpr int PLAN_ULIST = 0;                                  // int16 [QF_MAX_EXPERTS]
-constexpr int PLAN_GPRE = PLAN_ULIST + QF_MAX_EXPERTS * 2;     // int16 [QF_MAX_EXPERTS + 1]
+constexpr int OFF_BAR = OFF_RING + NST * STAGE_BYTES;                 // full[NST], empty[NST], efull[NEPI], eempty[NEPI]
+constexpr int OFF_DESC = OFF_BAR + (2 * NST + 2 * NEPI) * 8;
+constexpr int OFF_EPI = OFF_DESC + NST * (int)sizeof(StageDesc);
+constexpr int OFF_PLAN = OFF_EPI + NEPI * (int)sizeof(EpiRec);
+constexpr int PLAN_ULIST = 0;                                         // int16 [QF_MAX_EXPERTS]
+constexpr int PLAN_GPRE = PLAN_ULIST + QF_MAX_EXPERTS * 2;            // int16 [QF_MAX_EXPERTS + 1]
 constexpr int PLAN_TOFF = PLAN_GPRE + (QF_MAX_EXPERTS + 8) * 2;
-constexpr int PLAN_TLIST = PLAN_TOFF + (QF_MAX_EXPERTS + 8) * 2;   // int16 [MAXSLOTS]
-constexpr int PLAN_SIDS = PLAN_TLIST + MAXSLOTS * 2;               // int16 [MAXSLOTS] copy of topk_ids
-constexpr int PLAN_MISC = PLAN_SIDS + MAXSLOTS * 2;                // int32 [64]
+constexpr int PLAN_TLIST = PLAN_TOFF + (QF_MAX_EXPERTS + 8) * 2;      // int16 [MAXSLOTS]
+constexpr int PLAN_SIDS = PLAN_TLIST + MAXSLOTS * 2;                  // int16 [MAXSLOTS] copy of topk_ids
+constexpr int PLAN_MISC = PLAN_SIDS + MAXSLOTS * 2;                   // int32 [64]
 constexpr int PLAN_BYTES = PLAN_MISC + 64 * 4;
 constexpr int MOE_SMEM = OFF_PLAN + PLAN_BYTES;
-static_assert(MOE_SMEM <= 227 * 1024, "shared memory budget");
+static_assert(CTAS_PER_SM * (MOE_SMEM + 1024) <= 228 * 1024, "two CTAs per SM must fit in shared memory");
 // plan-build scratch aliases the ring (the producer starts after the plan is built)
 constexpr int SCR_MASK = 0;                                        // uint64 [E]
 constexpr int SCR_EXF = SCR_MASK + QF_MAX_EXPERTS * 8;             // int16 [E] x 3 (flag, count, groups) in-chunk
@@ -115,16 +129,21 @@ constexpr int SCR_TOFFE = SCR_EXF + 3 * QF_MAX_EXPERTS * 2;        // int16 [E] 
 constexpr int SCR_CHUNK = SCR_TOFFE + QF_MAX_EXPERTS * 2;          // int32 [32] x 3 chunk totals
 static_assert(SCR_CHUNK + 3 * 32 * 4 <= NST * STAGE_BYTES, "plan scratch");
 
-enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_LAST = 4, MISC_DBGN = 5 };
+enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5 };
+
+// Errors that stop the pipeline (waits that ran out). An out-of-range expert id is reported but not fatal: the
+// slot is skipped and the rest of the layer is computed.
+constexpr uint32_t HARD_ERR = QF_MOE_ERR_TIMEOUT | QF_MOE_ERR_PIPELINE;
 
 __device__ __forceinline__ void set_err(uint32_t* ctrl, uint32_t bits) { atomicOr(ctrl + C_ERR, bits); }
+__device__ __forceinline__ bool hard_error(uint32_t* ctrl) { return (qf::ld_volatile(ctrl + C_ERR) & HARD_ERR) != 0u; }
 
-// Bounded wait until ctrl[idx] >= target. Gives up early when another CTA already recorded an error.
+// Bounded wait until ctrl[idx] >= target (acquire). Gives up early when another CTA already recorded a hard error.
 __device__ bool wait_counter(uint32_t* ctrl, int idx, uint32_t target) {
     if (qf::ld_acquire(ctrl + idx) >= target) return true;
     const uint64_t t0 = qf::globaltimer();
     while (qf::ld_acquire(ctrl + idx) < target) {
-        if (qf::ld_volatile(ctrl + C_ERR) != 0u) return false;
+        if (hard_error(ctrl)) return false;
         if (qf::globaltimer() - t0 > DEP_WAIT_NS) {
             set_err(ctrl, QF_MOE_ERR_TIMEOUT);
             return false;
@@ -136,7 +155,7 @@ __device__ bool wait_counter(uint32_t* ctrl, int idx, uint32_t target) {
 
 struct Layout {   // per-launch derived sizes, identical in every thread
     int R1, R2, Rs1, ngs, U, Gt, has_gate, has_shw;
-    int b_s1, b_g1, b_s2, b_g2, b_cb, total;
+    int b_s1, b_g1, b_s1f, b_s2, b_g2, b_cb, total;
     uint32_t tile_target;
 };
 
@@ -150,7 +169,9 @@ __device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   /
 }
 
 // ---------------------------------------------------------------------------------------------- consumer math
-// One int4 stage: this warp's 16 rows x kc k, tokens in one or two n8 tiles; per-group partials scaled into acc.
+// One int4 stage: this warp's 16 rows x kc k, tokens in one or two n8 tiles. Each 32-k block accumulates into
+// its own fragment (two chained mmas), the four block partials of a 128-k group are summed in a fixed order and
+// scaled once into acc.
 __device__ __forceinline__ void stage_w4(const uint8_t* stage, int warp, int lane, int kc, bool two,
                                          float (&acc)[2][4]) {
     const int g = lane >> 2, t = lane & 3;
@@ -163,37 +184,40 @@ __device__ __forceinline__ void stage_w4(const uint8_t* stage, int warp, int lan
 #pragma unroll
     for (int gi = 0; gi < 2; ++gi) {
         if (gi < ngrp) {
-            float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+            float d[4][2][4];
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                const uint4 wq = *reinterpret_cast<const uint4*>(ws + (2 * gi + cc) * 512);
+            for (int b = 0; b < 4; ++b)
 #pragma unroll
-                for (int hb = 0; hb < 2; ++hb) {
-                    const int b = 4 * gi + 2 * cc + hb;
-                    uint32_t P[4], Q[4];
-                    qf::dequant_w4(hb ? wq.z : wq.x, P);
-                    qf::dequant_w4(hb ? wq.w : wq.y, Q);
-                    const uint4 xv = *reinterpret_cast<const uint4*>(xs0 + b * 64);
-                    qf::mma_bf16(d0, P[0], Q[0], P[1], Q[1], xv.x, xv.y);
-                    qf::mma_bf16(d0, P[2], Q[2], P[3], Q[3], xv.z, xv.w);
-                    if (two) {
-                        const uint4 xw = *reinterpret_cast<const uint4*>(xs1 + b * 64);
-                        qf::mma_bf16(d1, P[0], Q[0], P[1], Q[1], xw.x, xw.y);
-                        qf::mma_bf16(d1, P[2], Q[2], P[3], Q[3], xw.z, xw.w);
-                    }
+                for (int nt = 0; nt < 2; ++nt) d[b][nt][0] = d[b][nt][1] = d[b][nt][2] = d[b][nt][3] = 0.f;
+            const uint4 wq0 = *reinterpret_cast<const uint4*>(ws + (2 * gi) * 512);
+            const uint4 wq1 = *reinterpret_cast<const uint4*>(ws + (2 * gi + 1) * 512);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const uint4& wq = b < 2 ? wq0 : wq1;
+                const bool hb = b & 1;
+                uint32_t P[4], Q[4];
+                qf::dequant_w4(hb ? wq.z : wq.x, P);
+                qf::dequant_w4(hb ? wq.w : wq.y, Q);
+                const uint4 xv = *reinterpret_cast<const uint4*>(xs0 + (4 * gi + b) * 64);
+                qf::mma_bf16(d[b][0], P[0], Q[0], P[1], Q[1], xv.x, xv.y);
+                qf::mma_bf16(d[b][0], P[2], Q[2], P[3], Q[3], xv.z, xv.w);
+                if (two) {
+                    const uint4 xw = *reinterpret_cast<const uint4*>(xs1 + (4 * gi + b) * 64);
+                    qf::mma_bf16(d[b][1], P[0], Q[0], P[1], Q[1], xw.x, xw.y);
+                    qf::mma_bf16(d[b][1], P[2], Q[2], P[3], Q[3], xw.z, xw.w);
                 }
             }
             const uint32_t sc = *reinterpret_cast<const uint32_t*>(ss + gi * 32);
             const float sa = bf16_lo(sc), sb = bf16_hi(sc);
-            acc[0][0] = fmaf(d0[0], sa, acc[0][0]);
-            acc[0][1] = fmaf(d0[1], sa, acc[0][1]);
-            acc[0][2] = fmaf(d0[2], sb, acc[0][2]);
-            acc[0][3] = fmaf(d0[3], sb, acc[0][3]);
-            if (two) {
-                acc[1][0] = fmaf(d1[0], sa, acc[1][0]);
-                acc[1][1] = fmaf(d1[1], sa, acc[1][1]);
-                acc[1][2] = fmaf(d1[2], sb, acc[1][2]);
-                acc[1][3] = fmaf(d1[3], sb, acc[1][3]);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                if (nt == 0 || two) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float s = (d[0][nt][i] + d[1][nt][i]) + (d[2][nt][i] + d[3][nt][i]);
+                        acc[nt][i] = fmaf(s, i < 2 ? sa : sb, acc[nt][i]);
+                    }
+                }
             }
         }
     }
@@ -206,16 +230,25 @@ __device__ __forceinline__ void stage_bf16(const uint8_t* stage, int warp, int l
     const int xrb = (BF_KC + 8) * 2;
     const uint8_t* xs0 = stage + STAGE_W + STAGE_S + g * xrb + t * 8;
     const uint8_t* xs1 = xs0 + 8 * xrb;
+    float d[4][2][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) d[ks][nt][0] = d[ks][nt][1] = d[ks][nt][2] = d[ks][nt][3] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < 4; ++ks) {
         const uint4 a = *reinterpret_cast<const uint4*>(ws + ks * 512);
         const uint2 xv = *reinterpret_cast<const uint2*>(xs0 + ks * 32);
-        qf::mma_bf16(acc[0], a.x, a.y, a.z, a.w, xv.x, xv.y);
+        qf::mma_bf16(d[ks][0], a.x, a.y, a.z, a.w, xv.x, xv.y);
         if (two) {
             const uint2 xw = *reinterpret_cast<const uint2*>(xs1 + ks * 32);
-            qf::mma_bf16(acc[1], a.x, a.y, a.z, a.w, xw.x, xw.y);
+            qf::mma_bf16(d[ks][1], a.x, a.y, a.z, a.w, xw.x, xw.y);
         }
     }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][i] += (d[0][nt][i] + d[1][nt][i]) + (d[2][nt][i] + d[3][nt][i]);
 }
 
 // Combine of one 128-column tile for all tokens: out = bf16(gate * shared + bf16(sum_kpos y)), 8 columns a thread.
@@ -264,12 +297,15 @@ __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* si
     }
 }
 
-__global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem + OFF_RING;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + NST;
+    uint64_t* efull = empty + NST;
+    uint64_t* eempty = efull + NEPI;
     StageDesc* desc = reinterpret_cast<StageDesc*>(smem + OFF_DESC);
+    EpiRec* epi = reinterpret_cast<EpiRec*>(smem + OFF_EPI);
     uint8_t* plan = smem + OFF_PLAN;
     int16_t* ulist = reinterpret_cast<int16_t*>(plan + PLAN_ULIST);
     int16_t* gpre = reinterpret_cast<int16_t*>(plan + PLAN_GPRE);
@@ -286,6 +322,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         for (int i = 0; i < NST; ++i) {
             qf::mbar_init(full + i, 1);
             qf::mbar_init(empty + i, NCW);
+        }
+        for (int i = 0; i < NEPI; ++i) {
+            qf::mbar_init(efull + i, NCW);
+            qf::mbar_init(eempty + i, 1);
         }
         qf::mbar_fence_init();
         misc[MISC_DBGN] = 0;
@@ -390,21 +430,24 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     L.Gt = misc[MISC_GT];
     L.b_s1 = L.has_gate ? 1 : 0;
     L.b_g1 = L.b_s1 + (L.has_shw ? L.Rs1 * NSPLIT * L.ngs : 0);
-    L.b_s2 = L.b_g1 + L.R1 * L.Gt;
+    L.b_s1f = L.b_g1 + L.R1 * L.Gt;
+    L.b_s2 = L.b_s1f + (L.has_shw ? L.Rs1 * L.ngs : 0);
     L.b_g2 = L.b_s2 + (L.has_shw ? L.R2 * L.ngs : 0);
     L.b_cb = L.b_g2 + L.R2 * L.Gt;
-    L.total = L.b_cb + ((L.Gt == 0 && !L.has_shw) ? L.R2 : 0);
+    L.total = L.b_cb + L.R2;
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
 
     if (warp == NCW) {
-        // ============================================================== producer (one thread)
         if (lane == 0) {
+            // ========================================================== producer (one thread)
             const uint64_t pol = qf::policy_evict_first();
             int st = 0;
             uint32_t ph = 0;
+            int next = (int)atomicAdd(ctrl + C_QUEUE, 1u);
             for (;;) {
-                int item = (int)atomicAdd(ctrl + C_QUEUE, 1u);
-                if (qf::ld_volatile(ctrl + C_ERR) != 0u) item = L.total;
+                int item = next;
+                if (hard_error(ctrl)) item = L.total;
+                if (item < L.total) next = (int)atomicAdd(ctrl + C_QUEUE, 1u);   // claim ahead; in-order per CTA
                 int kind = K_STOP, u = 0, tile = 0, tg = 0, split = 0, nk = 1, ntok = 0, e = 0;
                 if (item >= L.total) {
                     kind = K_STOP;
@@ -418,7 +461,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     tile = j / (L.ngs * NSPLIT);
                     nk = (p.H / NSPLIT) / BF_KC;
                     ntok = min(TG, M - TG * tg);
-                } else if (item < L.b_s2 || (item >= L.b_g2 && item < L.b_cb)) {
+                } else if (item < L.b_s1f || (item >= L.b_g2 && item < L.b_cb)) {
                     const bool down = item >= L.b_g2;
                     const int j = item - (down ? L.b_g2 : L.b_g1);
                     const int R = down ? L.R2 : L.R1;
@@ -432,6 +475,12 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     const int K = down ? p.I : p.H;
                     nk = (K + W4_KC - 1) / W4_KC;
                     ntok = min(TG, (toff[u + 1] - toff[u]) - TG * tg);
+                } else if (item < L.b_s2) {
+                    const int j = item - L.b_s1f;
+                    kind = K_S1F;
+                    tg = j % L.ngs;
+                    tile = j / L.ngs;
+                    ntok = min(TG, M - TG * tg);
                 } else if (item < L.b_g2) {
                     const int j = item - L.b_s2;
                     kind = K_S2;
@@ -443,7 +492,12 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     kind = K_CB;
                     tile = item - L.b_cb;
                 }
-                bool dep_ok = true;
+                // dependencies of items without copies are resolved before their (empty) stage is published
+                if (kind == K_S1F) wait_counter(ctrl, C_SPLIT + tile * L.ngs + tg, (uint32_t)NSPLIT);
+                if (kind == K_CB) {
+                    wait_counter(ctrl, C_CNT + tile, L.tile_target);
+                    if (L.has_gate) wait_counter(ctrl, C_GLF, 1u);
+                }
                 for (int kidx = 0; kidx < nk; ++kidx) {
                     if (!qf::mbar_wait(empty + st, ph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
                     uint8_t* sb = ring + st * STAGE_BYTES;
@@ -454,7 +508,6 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     uint32_t bytes = 0;
                     if (kind == K_G1 || kind == K_G2) {
                         const int K = kind == K_G1 ? p.H : p.I;
-                        const int N = kind == K_G1 ? 2 * p.I : p.H;
                         kc = min(W4_KC, K - W4_KC * kidx);
                         bytes = 128 * kc / 2 + kc * 2 + ntok * kc * 2;
                     } else if (kind == K_S1 || kind == K_S2) {
@@ -466,54 +519,74 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     d.split = (int16_t)split; d.kidx = (int16_t)kidx; d.nk = (int16_t)nk; d.kc = (int16_t)kc;
                     d.ntok = (int16_t)ntok;
                     desc[st] = d;
-                    if (kind == K_STOP) {
+                    if (bytes == 0) {
                         qf::mbar_arrive(full + st);
-                        break;
-                    }
-                    qf::mbar_arrive_expect_tx(full + st, bytes);
-                    const int xrb = (kc + 8) * 2;
-                    if (kind == K_G1 || kind == K_G2) {
-                        const bool down = kind == K_G2;
-                        const int K = down ? p.I : p.H;
-                        const int N = down ? p.H : 2 * p.I;
-                        const uint8_t* wbase = (down ? p.w2 : p.w13) + (size_t)e * ((size_t)N * K / 2) +
-                                               (size_t)tile * (128 * (size_t)K / 2) + (size_t)kidx * STAGE_W;
-                        const uint16_t* sbase = (down ? p.s2 : p.s13) + (size_t)e * ((size_t)N * K / 128) +
-                                                (size_t)tile * K + (size_t)kidx * 256;
-                        qf::bulk_g2s_hint(sw, wbase, 128 * kc / 2, full + st, pol);
-                        qf::bulk_g2s_hint(ssc, sbase, kc * 2, full + st, pol);
-                        if (down && kidx == 0) {
-                            dep_ok = wait_counter(ctrl, C_DONE + u, (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])));
-                            qf::fence_proxy_async();
-                        }
-                        const int tbase = toff[u] + TG * tg;
-                        for (int j = 0; j < ntok; ++j) {
-                            const int s = tlist[tbase + j];
-                            const __nv_bfloat16* src =
-                                down ? p.hbuf + (size_t)s * p.I + W4_KC * kidx : p.x + (size_t)(s / topk) * p.H + W4_KC * kidx;
-                            qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
-                        }
-                    } else if (kind == K_S1 || kind == K_S2) {
-                        const bool down = kind == K_S2;
-                        const int K = down ? p.Is : p.H;
-                        const int k0 = down ? BF_KC * kidx : split * (p.H / NSPLIT) + BF_KC * kidx;
-                        const uint8_t* wbase = (down ? p.shw2 : p.shw13) + (size_t)tile * (128 * (size_t)K * 2) +
-                                               (size_t)(k0 / BF_KC) * STAGE_W;
-                        qf::bulk_g2s_hint(sw, wbase, STAGE_W, full + st, pol);
-                        if (down && kidx == 0) {
-                            dep_ok = wait_counter(ctrl, C_SDONE + tg, (uint32_t)L.Rs1);
-                            qf::fence_proxy_async();
-                        }
-                        for (int j = 0; j < ntok; ++j) {
-                            const int tok = TG * tg + j;
-                            const __nv_bfloat16* src = down ? p.hsh + (size_t)tok * p.Is + k0 : p.x + (size_t)tok * p.H + k0;
-                            qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
+                    } else {
+                        qf::mbar_arrive_expect_tx(full + st, bytes);
+                        const int xrb = (kc + 8) * 2;
+                        if (kind == K_G1 || kind == K_G2) {
+                            const bool down = kind == K_G2;
+                            const int K = down ? p.I : p.H;
+                            const int N = down ? p.H : 2 * p.I;
+                            const uint8_t* wbase = (down ? p.w2 : p.w13) + (size_t)e * ((size_t)N * K / 2) +
+                                                   (size_t)tile * (128 * (size_t)K / 2) + (size_t)kidx * STAGE_W;
+                            const uint16_t* sbase = (down ? p.s2 : p.s13) + (size_t)e * ((size_t)N * K / 128) +
+                                                    (size_t)tile * K + (size_t)kidx * 256;
+                            qf::bulk_g2s_hint(sw, wbase, 128 * kc / 2, full + st, pol);
+                            qf::bulk_g2s_hint(ssc, sbase, kc * 2, full + st, pol);
+                            if (down && kidx == 0) {
+                                wait_counter(ctrl, C_DONE + u, (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])));
+                                qf::fence_proxy_async();
+                            }
+                            const int tbase = toff[u] + TG * tg;
+                            for (int j = 0; j < ntok; ++j) {
+                                const int s = tlist[tbase + j];
+                                const __nv_bfloat16* src = down ? p.hbuf + (size_t)s * p.I + W4_KC * kidx
+                                                                : p.x + (size_t)(s / topk) * p.H + W4_KC * kidx;
+                                qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
+                            }
+                        } else {
+                            const bool down = kind == K_S2;
+                            const int K = down ? p.Is : p.H;
+                            const int k0 = down ? BF_KC * kidx : split * (p.H / NSPLIT) + BF_KC * kidx;
+                            const uint8_t* wbase = (down ? p.shw2 : p.shw13) + (size_t)tile * (128 * (size_t)K * 2) +
+                                                   (size_t)(k0 / BF_KC) * STAGE_W;
+                            qf::bulk_g2s_hint(sw, wbase, STAGE_W, full + st, pol);
+                            if (down && kidx == 0) {
+                                wait_counter(ctrl, C_SDONE + tg, (uint32_t)L.Rs1);
+                                qf::fence_proxy_async();
+                            }
+                            for (int j = 0; j < ntok; ++j) {
+                                const int tok = TG * tg + j;
+                                const __nv_bfloat16* src =
+                                    down ? p.hsh + (size_t)tok * p.Is + k0 : p.x + (size_t)tok * p.H + k0;
+                                qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
+                            }
                         }
                     }
                     if (++st == NST) { st = 0; ph ^= 1u; }
                 }
-                (void)dep_ok;
                 if (kind == K_STOP) break;
+            }
+        } else if (lane == 1) {
+            // ========================================================== signal agent (one thread)
+            // Consumer warps arrive on efull[slot] after their item's global stores; this thread then makes those
+            // stores visible at gpu scope (fence) and publishes the item's counter increment.
+            int es = 0;
+            uint32_t eph = 0;
+            for (;;) {
+                if (!qf::mbar_wait(efull + es, eph, PIPE_WAIT_NS)) {
+                    set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                    break;
+                }
+                const EpiRec r = epi[es];
+                if (r.idx == -2) break;   // consumers stopped
+                if (r.idx >= 0) {
+                    __threadfence();
+                    atomicAdd(ctrl + r.idx, (uint32_t)r.add);
+                }
+                qf::mbar_arrive(eempty + es);
+                if (++es == NEPI) { es = 0; eph ^= 1u; }
             }
         }
         __syncwarp();
@@ -521,23 +594,44 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         // ============================================================== consumers (8 warps)
         const int ctid = tid;   // 0..255
         const int g = lane >> 2, t = lane & 3;
-        int st = 0;
-        uint32_t ph = 0;
+        int st = 0, es = 0;
+        uint32_t ph = 0, eph = 0;
         float acc[2][4];
+        // optional timeline: (globaltimer << 12) | tag, up to 32 per CTA (tags: item kinds, 14 plan built, 15 exit)
+        auto stamp = [&](int tag) {
+            if (p.dbg != nullptr && ctid == 0 && misc[MISC_DBGN] < 32) {
+                p.dbg[blockIdx.x * 32 + misc[MISC_DBGN]] = (long long)((qf::globaltimer() << 12) | (uint64_t)tag);
+                misc[MISC_DBGN] += 1;
+            }
+        };
+        // hand one completion record to the agent (record written by thread 0; all eight warps arrive)
+        auto signal = [&](int idx, int add) {
+            if (ctid == 0) {
+                if (!qf::mbar_wait(eempty + es, eph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                epi[es].idx = idx;
+                epi[es].add = add;
+            }
+            __syncwarp();
+            if (lane == 0) qf::mbar_arrive(efull + es);
+            if (++es == NEPI) { es = 0; eph ^= 1u; }
+        };
+        stamp(14);
         for (;;) {
             if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
                 set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                signal(-2, 0);
                 break;
             }
             const StageDesc d = desc[st];
-            if (d.kind == K_STOP) break;
+            if (d.kind == K_STOP) {
+                stamp(15);
+                signal(-2, 0);
+                break;
+            }
             if (d.kidx == 0) {
 #pragma unroll
                 for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-                if (p.dbg != nullptr && ctid == 0 && misc[MISC_DBGN] < 32) {
-                    p.dbg[blockIdx.x * 32 + misc[MISC_DBGN]] = (long long)((qf::globaltimer() << 12) | (uint64_t)d.kind);
-                    misc[MISC_DBGN] += 1;
-                }
+                stamp(d.kind);
             }
             const uint8_t* sb = ring + st * STAGE_BYTES;
             const bool two = d.ntok > 8;
@@ -567,9 +661,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
                     if (lane == 0) p.gl[tok] = a;
                 }
-                __threadfence();
-                qf::named_bar(1, CONS_THREADS);
-                if (ctid == 0) atomicExch(ctrl + C_GLF, 1u);
+                signal(C_GLF, 1);
             } else if (d.kind == K_G1) {
                 const int u = d.u, e = ulist[u];
                 const float gs = p.gs13 ? bf16_bits(p.gs13[e]) : 1.f;
@@ -586,111 +678,83 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                             p.hbuf[(size_t)s * p.I + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
                         }
                     }
-                __threadfence();
-                qf::named_bar(1, CONS_THREADS);
-                if (ctid == 0) atomicAdd(ctrl + C_DONE + u, 1u);
+                signal(C_DONE + u, 1);
             } else if (d.kind == K_S1) {
-                float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048;
+                float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048;
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt)
-                    __stcg(reinterpret_cast<float4*>(pb + (size_t)d.split * 2048 + ((warp * 2 + nt) * 32 + lane) * 4),
+                    __stcg(reinterpret_cast<float4*>(pb + ((warp * 2 + nt) * 32 + lane) * 4),
                            make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
-                __threadfence();
-                qf::named_bar(1, CONS_THREADS);
-                const int sc = C_SPLIT + d.tile * L.ngs + d.tg;
-                if (ctid == 0) misc[MISC_LAST] = atomicAdd(ctrl + sc, 1u) == NSPLIT - 1;
-                __syncwarp();
-                qf::named_bar(1, CONS_THREADS);
-                if (misc[MISC_LAST]) {
-                    __threadfence();
-                    float v[2][4];
+                signal(C_SPLIT + d.tile * L.ngs + d.tg, 1);
+            } else if (d.kind == K_S1F) {
+                const float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048;
+                float v[2][4];
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        v[nt][0] = v[nt][1] = v[nt][2] = v[nt][3] = 0.f;
+                for (int nt = 0; nt < 2; ++nt) {
+                    v[nt][0] = v[nt][1] = v[nt][2] = v[nt][3] = 0.f;
 #pragma unroll
-                        for (int sp = 0; sp < NSPLIT; ++sp) {
-                            const float4 q = __ldcg(reinterpret_cast<const float4*>(
-                                pb + (size_t)sp * 2048 + ((warp * 2 + nt) * 32 + lane) * 4));
-                            v[nt][0] += q.x; v[nt][1] += q.y; v[nt][2] += q.z; v[nt][3] += q.w;
-                        }
-                    }
-                    const int col = 64 * d.tile + 8 * warp + g;
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                        for (int i = 0; i < 2; ++i) {
-                            const int jt = 8 * nt + 2 * t + i;
-                            if (jt < d.ntok) {
-                                const int tok = TG * d.tg + jt;
-                                const float gv = bf16r(v[nt][i]), uv = bf16r(v[nt][2 + i]);
-                                p.hsh[(size_t)tok * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
-                            }
-                        }
-                    __threadfence();
-                    qf::named_bar(1, CONS_THREADS);
-                    if (ctid == 0) {
-                        ctrl[sc] = 0u;
-                        atomicAdd(ctrl + C_SDONE + d.tg, 1u);
+                    for (int sp = 0; sp < NSPLIT; ++sp) {   // fixed split order: the sum does not depend on timing
+                        const float4 q = __ldcg(reinterpret_cast<const float4*>(
+                            pb + (size_t)sp * 2048 + ((warp * 2 + nt) * 32 + lane) * 4));
+                        v[nt][0] += q.x; v[nt][1] += q.y; v[nt][2] += q.z; v[nt][3] += q.w;
                     }
                 }
-            } else if (d.kind == K_G2 || d.kind == K_S2 || d.kind == K_CB) {
+                const int col = 64 * d.tile + 8 * warp + g;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const int jt = 8 * nt + 2 * t + i;
+                        if (jt < d.ntok) {
+                            const int tok = TG * d.tg + jt;
+                            const float gv = bf16r(v[nt][i]), uv = bf16r(v[nt][2 + i]);
+                            p.hsh[(size_t)tok * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                        }
+                    }
+                signal(C_SDONE + d.tg, 1);
+            } else if (d.kind == K_G2) {
+                const int c = d.tile, u = d.u, e = ulist[u];
+                const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
+                const int n0 = 128 * c + 16 * warp + g;
+                const int tbase = toff[u] + TG * d.tg;
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        const int jt = 8 * nt + 2 * t + i;
+                        if (jt < d.ntok) {
+                            const int s0 = tlist[tbase + jt];
+                            const int tok = s0 / topk;
+                            const float v0 = bf16r(acc[nt][i]), v1 = bf16r(acc[nt][2 + i]);
+                            for (int kp = s0 - tok * topk; kp < topk; ++kp) {
+                                const int s = tok * topk + kp;
+                                if (sids[s] != e) continue;
+                                const float w = bf16r(g2 * bf16r(__ldcg(p.tw + s)));
+                                p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v0 * w);
+                                p.ybuf[(size_t)s * p.H + n0 + 8] = __float2bfloat16(v1 * w);
+                            }
+                        }
+                    }
+                signal(C_CNT + c, 1);
+            } else if (d.kind == K_S2) {
                 const int c = d.tile;
-                if (d.kind == K_G2) {
-                    const int u = d.u, e = ulist[u];
-                    const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
-                    const int n0 = 128 * c + 16 * warp + g;
-                    const int tbase = toff[u] + TG * d.tg;
+                const int n0 = 128 * c + 16 * warp + g;
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                        for (int i = 0; i < 2; ++i) {
-                            const int jt = 8 * nt + 2 * t + i;
-                            if (jt < d.ntok) {
-                                const int s0 = tlist[tbase + jt];
-                                const int tok = s0 / topk;
-                                const float v0 = bf16r(acc[nt][i]), v1 = bf16r(acc[nt][2 + i]);
-                                for (int kp = s0 - tok * topk; kp < topk; ++kp) {
-                                    const int s = tok * topk + kp;
-                                    if (sids[s] != e) continue;
-                                    const float w = bf16r(g2 * bf16r(__ldcg(p.tw + s)));
-                                    p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v0 * w);
-                                    p.ybuf[(size_t)s * p.H + n0 + 8] = __float2bfloat16(v1 * w);
-                                }
-                            }
+                    for (int i = 0; i < 2; ++i) {
+                        const int jt = 8 * nt + 2 * t + i;
+                        if (jt < d.ntok) {
+                            const int tok = TG * d.tg + jt;
+                            p.sbuf[(size_t)tok * p.H + n0] = __float2bfloat16(acc[nt][i]);
+                            p.sbuf[(size_t)tok * p.H + n0 + 8] = __float2bfloat16(acc[nt][2 + i]);
                         }
-                } else if (d.kind == K_S2) {
-                    const int n0 = 128 * c + 16 * warp + g;
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                        for (int i = 0; i < 2; ++i) {
-                            const int jt = 8 * nt + 2 * t + i;
-                            if (jt < d.ntok) {
-                                const int tok = TG * d.tg + jt;
-                                p.sbuf[(size_t)tok * p.H + n0] = __float2bfloat16(acc[nt][i]);
-                                p.sbuf[(size_t)tok * p.H + n0 + 8] = __float2bfloat16(acc[nt][2 + i]);
-                            }
-                        }
-                }
-                bool last = true;
-                if (d.kind != K_CB) {
-                    __threadfence();
-                    qf::named_bar(1, CONS_THREADS);
-                    if (ctid == 0) misc[MISC_LAST] = atomicAdd(ctrl + C_CNT + c, 1u) == L.tile_target - 1u;
-                    __syncwarp();
-                    qf::named_bar(1, CONS_THREADS);
-                    last = misc[MISC_LAST] != 0;
-                }
-                if (last) {
-                    if (L.has_gate) {
-                        if (ctid == 0) wait_counter(ctrl, C_GLF, 1u);
-                        __syncwarp();
-                        qf::named_bar(1, CONS_THREADS);
                     }
-                    __threadfence();
-                    combine_tile(p, L, sids, c, ctid);
-                    if (ctid == 0 && d.kind != K_CB) ctrl[C_CNT + c] = 0u;
-                }
+                signal(C_CNT + c, 1);
+            } else if (d.kind == K_CB) {
+                // the producer acquired every producer of this tile (and the gate logits) before publishing it
+                combine_tile(p, L, sids, d.tile, ctid);
+                signal(-1, 0);
             }
         }
     }
@@ -863,8 +927,17 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaGetDevice");
     const int sms = qf::sm_count(dev);
     QF_REQUIRE(sms > 0, "a16_moe_decode: cannot query the SM count");
+    static int per_sm_cache[64] = {0};
+    int per_sm = dev < 64 ? per_sm_cache[dev] : 0;
     ce = qf::ensure_smem_attr(reinterpret_cast<const void*>(moe_persistent_kernel), MOE_SMEM);
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute");
+    if (per_sm == 0) {
+        // every CTA of the persistent grid must be resident at once: size the grid from the occupancy
+        ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_persistent_kernel, MOE_THREADS, MOE_SMEM);
+        if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: occupancy query");
+        per_sm = per_sm < 1 ? 1 : (per_sm > CTAS_PER_SM ? CTAS_PER_SM : per_sm);
+        if (dev < 64) per_sm_cache[dev] = per_sm;
+    }
 
     Params p;
     p.x = static_cast<const __nv_bfloat16*>(x);
@@ -891,7 +964,7 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     p.dbg = reinterpret_cast<long long*>(dbg);
     p.M = M; p.H = H; p.I = I; p.E = E; p.topk = topk; p.Is = has_shw ? Is : 0;
     p.mode = mode; p.elo = expert_lo; p.ehi = expert_hi;
-    ce = qf::launch_ex(moe_persistent_kernel, dim3(sms), dim3(MOE_THREADS), MOE_SMEM,
+    ce = qf::launch_ex(moe_persistent_kernel, dim3(sms * per_sm), dim3(MOE_THREADS), MOE_SMEM,
                        reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);
     return qf::cuda_status(ce, "a16_moe_decode: launch");
 }

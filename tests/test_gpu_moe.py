@@ -21,10 +21,14 @@ BF = torch.bfloat16
 
 
 def assert_close_to_oracle(out, ref_rounded, ref_truth=None):
+    """max-abs 2e-2, widened elementwise by two bf16 ulps of the reference value (one output rounding step already
+    exceeds 2e-2 once |out| >= 4), and relative L2 1e-2."""
     out = out.float().cpu()
-    d = out - ref_rounded.float()
-    rel = (d.norm() / ref_rounded.float().norm()).item()
-    assert d.abs().max().item() <= 2e-2 and rel <= 1e-2, (d.abs().max().item(), rel)
+    ref = ref_rounded.float()
+    d = out - ref
+    rel = (d.norm() / ref.norm()).item()
+    tol = 2e-2 + 2.0 ** -6 * ref.abs()
+    assert bool((d.abs() <= tol).all()) and rel <= 1e-2, (d.abs().max().item(), rel)
     if ref_truth is not None:
         rel_t = ((out - ref_truth).norm() / ref_truth.norm()).item()
         assert rel_t <= 1e-2, rel_t
