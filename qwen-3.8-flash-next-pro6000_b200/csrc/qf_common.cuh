@@ -147,23 +147,6 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// int4 word -> four bf16x2 of the biased codes 128 + code (exact in bf16; one lop3 each). The caller cancels the
-// bias 136 = 128 + 8 on the tensor cores (see mma_bias_cancel), so no per-weight subtract is spent.
-__device__ __forceinline__ void biased_w4(uint32_t q, uint32_t (&p)[4]) {
-    const uint32_t MASK = 0x000F000Fu, MAGIC = 0x43004300u;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t s = q >> (4 * i);
-        asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(p[i]) : "r"(s), "r"(MASK), "r"(MAGIC));   // (s & MASK) | MAGIC
-    }
-}
-// d += (-136) * sum_k B[k][n] over one k16 step: with the biased codes this leaves sum_k (code - 8) * x exactly up to
-// fp32 accumulation error (the two large terms cancel; the error is ~1e-5 of the result, far below bf16 precision).
-__device__ __forceinline__ void mma_bias_cancel(float (&d)[4], uint32_t b0, uint32_t b1) {
-    const uint32_t NEG136 = 0xC308C308u;   // bf16 -136.0 in both halves
-    mma_bf16(d, NEG136, NEG136, NEG136, NEG136, b0, b1);
-}
-
 // int4 word -> four bf16x2 of (code - 8). The word's nibbles hold k = [0, 2, 4, 6, 1, 3, 5, 7] of eight
 // consecutive k (kernel layout), so the pairs come out in natural order: (k0,k1) (k2,k3) (k4,k5) (k6,k7).
 // (0x4300 | n) is the bf16 value 128 + n; subtracting 136 leaves n - 8, exactly.
