@@ -62,6 +62,15 @@ int qf_router_topk(const void* x, const void* w, int rows, int hidden, int exper
                    float* topk_weights, int32_t* topk_ids, void* logits, float* scratch, int64_t scratch_numel,
                    int32_t* counter, int pdl, qf_stream_t stream);
 
+/* Same router, for callers that cannot allocate device memory (no counterpart in the reference). Hosts such as an
+ * inference engine's plugin enqueue, whose device memory is fixed at start-up, or a launcher running during CUDA-graph
+ * capture cannot hand over scratch tensors: this variant keeps the fp32 logit scratch and the ticket counter in a
+ * static device array of the library (rows * experts <= 64 * 1024, i.e. 256 KB per GPU, held until exit) and calls no
+ * allocator. The first call on a device (device current) resolves that array's address -- make it before any stream
+ * capture. Each call clears the counter on `stream`; calls that may overlap on the GPU share the array and race. */
+int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, int experts, int topk, int renormalize,
+                           float* topk_weights, int32_t* topk_ids, void* logits, int pdl, qf_stream_t stream);
+
 /* ------------------------------------------------------------------------------------------------------------
  * Routed experts (W4A16) + shared expert + combine, one persistent launch.
  * Replaces `a16_moe_decode` (serve/qwenfast/qf_a16moe.cu:852-922, binding serve/qwenfast/qf_bind.cpp:90-97,142);

@@ -11,6 +11,8 @@
 // previous kernel (PDL), so the 2 MB weight stream overlaps the producer of x. Per-warp fp32 partials are summed
 // in a fixed warp order through shared memory, so the logits do not depend on timing. The last CTA to finish
 // (ticket counter, re-armed by that CTA) runs the top-k, one warp per token.
+#include <mutex>
+
 #include "qf_common.cuh"
 
 namespace {
@@ -226,4 +228,64 @@ extern "C" int qf_router_topk(const void* x, const void* w, int rows, int hidden
                                           logits, scratch, counter, pdl, st);
     return launch_router<8>(x, w, rows, hidden, experts, topk, renormalize, topk_weights, topk_ids, logits, scratch,
                             counter, pdl, st);
+}
+
+// ============================================================================================================
+// Router entry point that allocates nothing.
+//
+// Some hosts cannot hand this library device memory for scratch: a plugin that is enqueued by an inference engine
+// whose memory pool is sized once at start-up, or a launcher running while a CUDA graph is being captured, where a
+// cudaMalloc would either fail, synchronise the device, or invalidate the capture. For them the router's two scratch
+// buffers (the fp32 copy of the logits the top-k reads and the ticket counter of the last-CTA hand-off) live in the
+// file-scope device array below instead of in caller-owned tensors. The caller still passes x, w and the three
+// outputs. Limit: rows * experts <= 64 * 1024 (256 KB of fp32, plus one counter word); every GPU that loads the
+// library keeps this array until the process exits.
+//
+// Set-up: the first call on a device (with that device current) resolves the array's device address with
+// cudaGetSymbolAddress and caches it; make that first call before any stream capture. Each call then clears the
+// counter with cudaMemsetAsync on the caller's stream and launches the same kernel as qf_router_topk.
+// All calls on a device share the array and it keeps the last call's contents, so calls that can overlap on the
+// GPU (different streams, or no ordering between them) race with each other; order them on one stream.
+namespace {
+constexpr int NOALLOC_SCRATCH_FLOATS = QF_MAX_TOKENS * QF_MAX_EXPERTS;
+// [0, NOALLOC_SCRATCH_FLOATS): logits scratch; the next word: ticket counter
+static __device__ __align__(256) uint32_t g_router_noalloc[NOALLOC_SCRATCH_FLOATS + 64];
+
+struct NoAllocSlot {
+    bool ready;
+    float* scratch;
+    int32_t* counter;
+};
+std::mutex g_noalloc_mu;
+NoAllocSlot g_noalloc_slot[64];
+}  // namespace
+
+extern "C" int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, int experts, int topk,
+                                      int renormalize, float* topk_weights, int32_t* topk_ids, void* logits, int pdl,
+                                      qf_stream_t stream) {
+    QF_REQUIRE(rows >= 1 && experts >= 1 && (int64_t)rows * experts <= NOALLOC_SCRATCH_FLOATS,
+               "router_topk_noalloc: rows * experts must be at most %d (static scratch), got %d * %d",
+               NOALLOC_SCRATCH_FLOATS, rows, experts);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: cudaGetDevice");
+    QF_REQUIRE(dev >= 0 && dev < 64, "router_topk_noalloc: device ordinal %d out of range", dev);
+    NoAllocSlot slot;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_slot[dev].ready) {
+            void* base = nullptr;
+            e = cudaGetSymbolAddress(&base, g_router_noalloc);
+            if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: cudaGetSymbolAddress");
+            g_noalloc_slot[dev].scratch = static_cast<float*>(base);
+            g_noalloc_slot[dev].counter = reinterpret_cast<int32_t*>(static_cast<uint32_t*>(base) + NOALLOC_SCRATCH_FLOATS);
+            g_noalloc_slot[dev].ready = true;
+        }
+        slot = g_noalloc_slot[dev];
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    e = cudaMemsetAsync(slot.counter, 0, sizeof(int32_t), st);
+    if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: clearing the counter");
+    return qf_router_topk(x, w, rows, hidden, experts, topk, renormalize, topk_weights, topk_ids, logits, slot.scratch,
+                          NOALLOC_SCRATCH_FLOATS, slot.counter, pdl, stream);
 }

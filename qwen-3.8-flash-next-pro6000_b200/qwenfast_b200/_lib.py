@@ -26,6 +26,7 @@ _l = ctypes.c_int64
 SIGNATURES = {
     "qf_version": [],
     "qf_router_topk": [_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _l, _p, _i, _p],
+    "qf_router_topk_noalloc": [_p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _i, _p],
     "qf_a16_moe_workspace": [_i, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p],
     "qf_a16_moe_decode": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                           _p, _l, _p, _l, _p, _l, _p, _l, _p, _l, _p, _l,
