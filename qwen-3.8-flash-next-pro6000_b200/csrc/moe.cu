@@ -25,10 +25,15 @@
 //     by the producer (bounded) before it fills the stage, so consumers never spin on other CTAs.
 //   * Consumers signal completed items through a CTA-local ring; the agent lane turns each record into one gpu-scope
 //     release (fence + atomic add) on the control block. Consumer warps never execute a gpu-scope fence.
-//   * Each consumer warp owns 16 weight rows of the 128-row tile: int4 -> bf16 in registers (lop3 + hsub2),
-//     mma.m16n8k16 with the weights as A and tokens as B (n = 8 or 16), independent partials per 32-k block,
-//     fp32 group partials scaled per group. gate_up tiles interleave gate row j and up row j in one fragment,
-//     so SwiGLU runs in registers.
+//   * Contraction on the 5th-generation tensor cores (tcgen05). int4 tiles: every consumer thread owns one TMEM lane
+//     (= one weight row of the 128-row tile) and one 128-k half of the stage; it turns each int4 word into four
+//     bf16x2 of the biased codes (128 + code; one lop3 each) and stores them to TMEM (tcgen05.st) as the A operand.
+//     The gathered token rows are re-laid by the consumers into the canonical K-major shared-memory layout (B,
+//     N = 16). One elected thread issues tcgen05.mma kind::f16 (A in TMEM, B in SMEM, fp32 D in TMEM) per k16 step
+//     plus one against a constant -136 A tile that removes the bias, then tcgen05.commit. Each 128-k group has its
+//     own D region; its fp32 partial is read back (tcgen05.ld) and scaled once by the row's group scale.
+//     bf16 tiles (shared expert): the stage itself is the A operand (SMEM descriptor), D accumulates in TMEM over the
+//     whole item. gate_up tiles interleave gate row j (even lane) and up row j (odd lane): SwiGLU is one shuffle.
 //   * The routing plan (unique experts, per-expert token lists, group offsets) is rebuilt identically by every CTA
 //     from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
 //   * Every wait is bounded (globaltimer); a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
@@ -46,7 +51,7 @@ constexpr int MOE_THREADS = (NCW + 1) * 32;   // + the producer / agent warp
 constexpr int CONS_THREADS = NCW * 32;
 constexpr int CTAS_PER_SM = 2;
 constexpr int TG = 16;                        // tokens per token group (two n8 tiles)
-constexpr int NST = 4;                        // pipeline stages per CTA
+constexpr int NST = 3;                        // pipeline stages per CTA
 constexpr int NEPI = 8;                       // completion-record ring
 constexpr int W4_KC = 256;                    // int4 k per stage
 constexpr int BF_KC = 64;                     // bf16 k per stage
@@ -108,9 +113,11 @@ struct Params {
 };
 
 // shared memory map (dynamic)
+constexpr int BST_BYTES = TG * (W4_KC / 8) * 16;                      // B operand [k chunk][16 tokens][16 B]
 constexpr int OFF_RING = 0;
-constexpr int OFF_BAR = OFF_RING + NST * STAGE_BYTES;                 // full[NST], empty[NST], efull[NEPI], eempty[NEPI]
-constexpr int OFF_DESC = OFF_BAR + (2 * NST + 2 * NEPI) * 8;
+constexpr int OFF_BST = OFF_RING + NST * STAGE_BYTES;
+constexpr int OFF_BAR = OFF_BST + BST_BYTES;                          // full[NST], empty[NST], efull[NEPI], eempty[NEPI], mma
+constexpr int OFF_DESC = OFF_BAR + (2 * NST + 2 * NEPI + 2) * 8;
 constexpr int OFF_EPI = OFF_DESC + NST * (int)sizeof(StageDesc);
 constexpr int OFF_PLAN = OFF_EPI + NEPI * (int)sizeof(EpiRec);
 constexpr int PLAN_ULIST = 0;                                         // int16 [QF_MAX_EXPERTS]
@@ -129,7 +136,14 @@ constexpr int SCR_TOFFE = SCR_EXF + 3 * QF_MAX_EXPERTS * 2;        // int16 [E] 
 constexpr int SCR_CHUNK = SCR_TOFFE + QF_MAX_EXPERTS * 2;          // int32 [32] x 3 chunk totals
 static_assert(SCR_CHUNK + 3 * 32 * 4 <= NST * STAGE_BYTES, "plan scratch");
 
-enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5 };
+enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6 };
+
+// tensor memory map (columns of this CTA's allocation; fp32 / bf16x2 per 32-bit column, lane = tile row)
+constexpr uint32_t TM_COLS = 256;
+constexpr uint32_t TM_A = 0;       // 128 columns: A tile of one 256-k int4 stage (16 k16 steps x 8 columns)
+constexpr uint32_t TM_D = 128;     // 2 x 16 columns: fp32 partial of each 128-k group (bf16 items: running sum)
+constexpr uint32_t TM_C = 160;     // 8 columns: constant -136 A tile (bias removal)
+constexpr uint32_t IDESC = qf::idesc_bf16(128, TG);
 
 // Errors that stop the pipeline (waits that ran out). An out-of-range expert id is reported but not fatal: the
 // slot is skipped and the rest of the layer is computed.
@@ -169,86 +183,35 @@ __device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   /
 }
 
 // ---------------------------------------------------------------------------------------------- consumer math
-// One int4 stage: this warp's 16 rows x kc k, tokens in one or two n8 tiles. Each 32-k block accumulates into
-// its own fragment (two chained mmas), the four block partials of a 128-k group are summed in a fixed order and
-// scaled once into acc.
-__device__ __forceinline__ void stage_w4(const uint8_t* stage, int warp, int lane, int kc, bool two,
-                                         float (&acc)[2][4]) {
-    const int g = lane >> 2, t = lane & 3;
-    const int ngrp = kc >> 7;
-    const uint8_t* ws = stage + warp * (kc >> 6) * 512 + lane * 16;
-    const uint8_t* ss = stage + STAGE_W + warp * ngrp * 32 + g * 4;
+// Copy the stage's token rows (row-major, stride kc + 8 elements) into the canonical K-major B layout
+// [k chunk of 8][token (16)][16 bytes] (8-token core matrices: SBO = 128 B, k-chunk stride LBO = 256 B).
+__device__ __forceinline__ void reshuffle_b(const uint8_t* stage, uint8_t* bst, int kc, int ntok, int ctid) {
     const int xrb = (kc + 8) * 2;
-    const uint8_t* xs0 = stage + STAGE_W + STAGE_S + g * xrb + t * 16;
-    const uint8_t* xs1 = xs0 + 8 * xrb;
-#pragma unroll
-    for (int gi = 0; gi < 2; ++gi) {
-        if (gi < ngrp) {
-            float d[4][2][4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) d[b][nt][0] = d[b][nt][1] = d[b][nt][2] = d[b][nt][3] = 0.f;
-            const uint4 wq0 = *reinterpret_cast<const uint4*>(ws + (2 * gi) * 512);
-            const uint4 wq1 = *reinterpret_cast<const uint4*>(ws + (2 * gi + 1) * 512);
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const uint4& wq = b < 2 ? wq0 : wq1;
-                const bool hb = b & 1;
-                uint32_t P[4], Q[4];
-                qf::dequant_w4(hb ? wq.z : wq.x, P);
-                qf::dequant_w4(hb ? wq.w : wq.y, Q);
-                const uint4 xv = *reinterpret_cast<const uint4*>(xs0 + (4 * gi + b) * 64);
-                qf::mma_bf16(d[b][0], P[0], Q[0], P[1], Q[1], xv.x, xv.y);
-                qf::mma_bf16(d[b][0], P[2], Q[2], P[3], Q[3], xv.z, xv.w);
-                if (two) {
-                    const uint4 xw = *reinterpret_cast<const uint4*>(xs1 + (4 * gi + b) * 64);
-                    qf::mma_bf16(d[b][1], P[0], Q[0], P[1], Q[1], xw.x, xw.y);
-                    qf::mma_bf16(d[b][1], P[2], Q[2], P[3], Q[3], xw.z, xw.w);
-                }
-            }
-            const uint32_t sc = *reinterpret_cast<const uint32_t*>(ss + gi * 32);
-            const float sa = bf16_lo(sc), sb = bf16_hi(sc);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                if (nt == 0 || two) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float s = (d[0][nt][i] + d[1][nt][i]) + (d[2][nt][i] + d[3][nt][i]);
-                        acc[nt][i] = fmaf(s, i < 2 ? sa : sb, acc[nt][i]);
-                    }
-                }
-            }
-        }
+    const uint8_t* xs = stage + STAGE_W + STAGE_S;
+    const int nch = kc >> 3;
+    for (int idx = ctid; idx < nch * ntok; idx += CONS_THREADS) {
+        const int c = idx / ntok, n = idx - c * ntok;
+        *reinterpret_cast<uint4*>(bst + (c * TG + n) * 16) = *reinterpret_cast<const uint4*>(xs + n * xrb + c * 16);
     }
+    qf::fence_proxy_async_smem();   // the tensor cores read bst through the async proxy
 }
 
-// One bf16 stage (64 k): fragments are stored in mma order, k permuted so thread t owns k = 4t..4t+3 of a step.
-__device__ __forceinline__ void stage_bf16(const uint8_t* stage, int warp, int lane, bool two, float (&acc)[2][4]) {
-    const int g = lane >> 2, t = lane & 3;
-    const uint8_t* ws = stage + warp * 2048 + lane * 16;
-    const int xrb = (BF_KC + 8) * 2;
-    const uint8_t* xs0 = stage + STAGE_W + STAGE_S + g * xrb + t * 8;
-    const uint8_t* xs1 = xs0 + 8 * xrb;
-    float d[4][2][4];
+// Dequantise this thread's row of its 128-k half of an int4 stage into TMEM (biased codes, natural k order):
+// word w of the half (k = 8w .. 8w+7) becomes columns TM_A + 64 * half + 4w .. +4.
+__device__ __forceinline__ void stage_w4_to_tmem(const uint8_t* stage, uint32_t tmem, int half, int quarter, int lane) {
+    const int row = 32 * quarter + lane;
+    const uint8_t* ws = stage + ((half * 4) * 128 + row) * 16;
+    const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) d[ks][nt][0] = d[ks][nt][1] = d[ks][nt][2] = d[ks][nt][3] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-        const uint4 a = *reinterpret_cast<const uint4*>(ws + ks * 512);
-        const uint2 xv = *reinterpret_cast<const uint2*>(xs0 + ks * 32);
-        qf::mma_bf16(d[ks][0], a.x, a.y, a.z, a.w, xv.x, xv.y);
-        if (two) {
-            const uint2 xw = *reinterpret_cast<const uint2*>(xs1 + ks * 32);
-            qf::mma_bf16(d[ks][1], a.x, a.y, a.z, a.w, xw.x, xw.y);
-        }
+    for (int qd = 0; qd < 4; ++qd) {
+        const uint4 w = *reinterpret_cast<const uint4*>(ws + qd * 128 * 16);
+        uint32_t v[16];
+        qf::biased_w4(w.x, v + 0);
+        qf::biased_w4(w.y, v + 4);
+        qf::biased_w4(w.z, v + 8);
+        qf::biased_w4(w.w, v + 12);
+        qf::tmem_st16(tmem + lane_base + TM_A + 64 * half + 16 * qd, v);
     }
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[nt][i] += (d[0][nt][i] + d[1][nt][i]) + (d[2][nt][i] + d[3][nt][i]);
 }
 
 // Combine of one 128-column tile for all tokens: out = bf16(gate * shared + bf16(sum_kpos y)), 8 columns a thread.
@@ -300,10 +263,12 @@ __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* si
 __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* ring = smem + OFF_RING;
+    uint8_t* bst = smem + OFF_BST;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
     uint64_t* empty = full + NST;
     uint64_t* efull = empty + NST;
     uint64_t* eempty = efull + NEPI;
+    uint64_t* mma_bar = eempty + NEPI;
     StageDesc* desc = reinterpret_cast<StageDesc*>(smem + OFF_DESC);
     EpiRec* epi = reinterpret_cast<EpiRec*>(smem + OFF_EPI);
     uint8_t* plan = smem + OFF_PLAN;
@@ -327,8 +292,13 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             qf::mbar_init(efull + i, NCW);
             qf::mbar_init(eempty + i, 1);
         }
+        qf::mbar_init(mma_bar, 1);
         qf::mbar_fence_init();
         misc[MISC_DBGN] = 0;
+    }
+    if (warp == 0) {   // tensor memory: one warp allocates for the CTA (two CTAs per SM take 256 columns each)
+        qf::tmem_alloc(reinterpret_cast<uint32_t*>(misc + MISC_TMEM), TM_COLS);
+        qf::tmem_relinquish();
     }
     __syncwarp();
     // Everything below reads data of the previous kernel (topk ids, x) or the control block it may re-arm.
@@ -418,6 +388,7 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
         __syncthreads();
     }
     qf::pdl_launch_dependents();
+    const uint32_t tmem = (uint32_t)misc[MISC_TMEM];
 
     Layout L;
     L.R1 = (2 * p.I) / 128;
@@ -591,12 +562,16 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
         }
         __syncwarp();
     } else {
-        // ============================================================== consumers (8 warps)
-        const int ctid = tid;   // 0..255
-        const int g = lane >> 2, t = lane & 3;
+        // ============================================================== consumers (8 warps, 2 warpgroups)
+        const int ctid = tid;                 // 0..255
+        const int wg = warp >> 2;             // warpgroup: which 128-k half of an int4 stage this thread dequantises
+        const int quarter = warp & 3;         // TMEM lane quarter
+        const int row = 32 * quarter + lane;  // tile row (= TMEM lane) owned by this thread
+        const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+        float* red = reinterpret_cast<float*>(bst);   // [128 rows][16] partial exchange between the warpgroups
         int st = 0, es = 0;
-        uint32_t ph = 0, eph = 0;
-        float acc[2][4];
+        uint32_t ph = 0, eph = 0, mph = 0;
+        float acc[TG];
         // optional timeline: (globaltimer << 12) | tag, up to 32 per CTA (tags: item kinds, 14 plan built, 15 exit)
         auto stamp = [&](int tag) {
             if (p.dbg != nullptr && ctid == 0 && misc[MISC_DBGN] < 32) {
@@ -615,6 +590,16 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             if (lane == 0) qf::mbar_arrive(efull + es);
             if (++es == NEPI) { es = 0; eph ^= 1u; }
         };
+        // the constant -136 A tile: written once by the first warpgroup (lanes 0..127, 8 columns)
+        if (wg == 0) {
+            uint32_t v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0xC308C308u;   // bf16 -136.0 in both halves
+            qf::tmem_st8(tmem + lane_base + TM_C, v);
+            qf::tmem_wait_st();
+        }
+        qf::tc_fence_before();
+        qf::named_bar(1, CONS_THREADS);
         stamp(14);
         for (;;) {
             if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
@@ -630,19 +615,91 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             }
             if (d.kidx == 0) {
 #pragma unroll
-                for (int i = 0; i < 2; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+                for (int n = 0; n < TG; ++n) acc[n] = 0.f;
                 stamp(d.kind);
             }
-            const uint8_t* sb = ring + st * STAGE_BYTES;
-            const bool two = d.ntok > 8;
-            if (d.kind == K_G1 || d.kind == K_G2) stage_w4(sb, warp, lane, d.kc, two, acc);
-            else if (d.kind == K_S1 || d.kind == K_S2) stage_bf16(sb, warp, lane, two, acc);
-            __syncwarp();
-            if (lane == 0) qf::mbar_arrive(empty + st);
+            uint8_t* sb = ring + st * STAGE_BYTES;
+            const bool w4 = d.kind == K_G1 || d.kind == K_G2;
+            const bool bf = d.kind == K_S1 || d.kind == K_S2;
+            if (w4 || bf) {
+                const int ngrp = w4 ? (d.kc >> 7) : 0;
+                float sc = 0.f;
+                reshuffle_b(sb, bst, d.kc, d.ntok, ctid);
+                if (w4 && wg < ngrp) {
+                    stage_w4_to_tmem(sb, tmem, wg, quarter, lane);
+                    const uint16_t* ss = reinterpret_cast<const uint16_t*>(sb + STAGE_W);
+                    sc = bf16_bits(ss[row * ngrp + wg]);
+                    qf::tmem_wait_st();
+                }
+                qf::tc_fence_before();
+                if (w4) {   // the stage's bytes now live in TMEM and bst: hand the ring slot back
+                    __syncwarp();
+                    if (lane == 0) qf::mbar_arrive(empty + st);
+                }
+                qf::named_bar(1, CONS_THREADS);
+                if (ctid == 0) {
+                    qf::tc_fence_after();
+                    if (w4) {
+                        for (int j = 0; j < (d.kc >> 4); ++j) {
+                            const uint32_t dcol = tmem + TM_D + 16 * (j >> 3);
+                            const uint64_t bd = qf::smem_desc(bst + 2 * j * 256, 256, 128);
+                            qf::mma_ts(dcol, tmem + TM_C, bd, IDESC, (j & 7) != 0);
+                            qf::mma_ts(dcol, tmem + TM_A + 8 * j, bd, IDESC, 1u);
+                        }
+                    } else {
+                        for (int j = 0; j < 4; ++j)
+                            qf::mma_ss(tmem + TM_D, qf::smem_desc(sb + 2 * j * 2048, 2048, 128),
+                                       qf::smem_desc(bst + 2 * j * 256, 256, 128), IDESC, (d.kidx > 0 || j > 0));
+                    }
+                    qf::mma_commit(mma_bar);
+                }
+                __syncwarp();
+                if (!qf::mbar_wait(mma_bar, mph, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                mph ^= 1u;
+                qf::tc_fence_after();
+                if (bf) {   // the stage was the A operand: release it only now
+                    __syncwarp();
+                    if (lane == 0) qf::mbar_arrive(empty + st);
+                }
+                if (w4 && wg < ngrp) {
+                    uint32_t v[16];
+                    qf::tmem_ld16(tmem + lane_base + TM_D + 16 * wg, v);
+                    qf::tmem_wait_ld();
+#pragma unroll
+                    for (int n = 0; n < TG; ++n) acc[n] = fmaf(__uint_as_float(v[n]), sc, acc[n]);
+                }
+                qf::tc_fence_before();
+            } else {
+                __syncwarp();
+                if (lane == 0) qf::mbar_arrive(empty + st);
+            }
             if (++st == NST) { st = 0; ph ^= 1u; }
             if (d.kidx != d.nk - 1) continue;
 
             // ------------------------------------------------------------ epilogues (item complete)
+            if (w4) {   // fixed-order sum of the two warpgroups' halves into warpgroup 0
+                if (wg == 1) {
+#pragma unroll
+                    for (int n = 0; n < TG; n += 4)
+                        *reinterpret_cast<float4*>(red + row * TG + n) = make_float4(acc[n], acc[n + 1], acc[n + 2], acc[n + 3]);
+                }
+                qf::named_bar(1, CONS_THREADS);
+                if (wg == 0) {
+#pragma unroll
+                    for (int n = 0; n < TG; n += 4) {
+                        const float4 o = *reinterpret_cast<const float4*>(red + row * TG + n);
+                        acc[n] += o.x; acc[n + 1] += o.y; acc[n + 2] += o.z; acc[n + 3] += o.w;
+                    }
+                }
+                qf::named_bar(1, CONS_THREADS);
+            } else if (bf && wg == 0) {
+                uint32_t v[16];
+                qf::tmem_ld16(tmem + lane_base + TM_D, v);
+                qf::tmem_wait_ld();
+#pragma unroll
+                for (int n = 0; n < TG; ++n) acc[n] = __uint_as_float(v[n]);
+                qf::tc_fence_before();
+            }
             if (d.kind == K_GL) {
                 for (int tok = warp; tok < M; tok += NCW) {
                     const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)tok * p.H);
@@ -662,95 +719,94 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
                     if (lane == 0) p.gl[tok] = a;
                 }
                 signal(C_GLF, 1);
-            } else if (d.kind == K_G1) {
-                const int u = d.u, e = ulist[u];
-                const float gs = p.gs13 ? bf16_bits(p.gs13[e]) : 1.f;
-                const int col = 64 * d.tile + 8 * warp + g;
-                const int tbase = toff[u] + TG * d.tg;
+            } else if (d.kind == K_G1 || d.kind == K_S1F) {
+                // rows interleave gate (even lane) and up (odd lane) of intermediate column j = row / 2;
+                // even lanes finish tokens 0..7, odd lanes tokens 8..15
+                if (d.kind == K_S1F && wg == 0) {
+                    const float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048 + row * TG;
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const int jt = 8 * nt + 2 * t + i;
-                        if (jt < d.ntok) {
-                            const int s = tlist[tbase + jt];
-                            const float gv = bf16r(bf16r(acc[nt][i]) * gs), uv = bf16r(bf16r(acc[nt][2 + i]) * gs);
-                            p.hbuf[(size_t)s * p.I + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
-                        }
-                    }
-                signal(C_DONE + u, 1);
-            } else if (d.kind == K_S1) {
-                float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048;
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-                    __stcg(reinterpret_cast<float4*>(pb + ((warp * 2 + nt) * 32 + lane) * 4),
-                           make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
-                signal(C_SPLIT + d.tile * L.ngs + d.tg, 1);
-            } else if (d.kind == K_S1F) {
-                const float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048;
-                float v[2][4];
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    v[nt][0] = v[nt][1] = v[nt][2] = v[nt][3] = 0.f;
+                    for (int n = 0; n < TG; ++n) acc[n] = 0.f;
 #pragma unroll
                     for (int sp = 0; sp < NSPLIT; ++sp) {   // fixed split order: the sum does not depend on timing
-                        const float4 q = __ldcg(reinterpret_cast<const float4*>(
-                            pb + (size_t)sp * 2048 + ((warp * 2 + nt) * 32 + lane) * 4));
-                        v[nt][0] += q.x; v[nt][1] += q.y; v[nt][2] += q.z; v[nt][3] += q.w;
-                    }
-                }
-                const int col = 64 * d.tile + 8 * warp + g;
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const int jt = 8 * nt + 2 * t + i;
-                        if (jt < d.ntok) {
-                            const int tok = TG * d.tg + jt;
-                            const float gv = bf16r(v[nt][i]), uv = bf16r(v[nt][2 + i]);
-                            p.hsh[(size_t)tok * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                        for (int n = 0; n < TG; n += 4) {
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)sp * 2048 + n));
+                            acc[n] += q.x; acc[n + 1] += q.y; acc[n + 2] += q.z; acc[n + 3] += q.w;
                         }
                     }
-                signal(C_SDONE + d.tg, 1);
-            } else if (d.kind == K_G2) {
-                const int c = d.tile, u = d.u, e = ulist[u];
-                const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
-                const int n0 = 128 * c + 16 * warp + g;
-                const int tbase = toff[u] + TG * d.tg;
+                }
+                if (wg == 0) {
+                    const bool odd = lane & 1;
+                    float oth[TG];
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                    for (int n = 0; n < TG; ++n) oth[n] = __shfl_xor_sync(0xffffffffu, acc[n], 1);
+                    const int col = 64 * d.tile + (row >> 1);
+                    if (d.kind == K_G1) {
+                        const int u = d.u, e = ulist[u];
+                        const float gs = p.gs13 ? bf16_bits(p.gs13[e]) : 1.f;
+                        const int tbase = toff[u] + TG * d.tg;
 #pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const int jt = 8 * nt + 2 * t + i;
-                        if (jt < d.ntok) {
-                            const int s0 = tlist[tbase + jt];
-                            const int tok = s0 / topk;
-                            const float v0 = bf16r(acc[nt][i]), v1 = bf16r(acc[nt][2 + i]);
-                            for (int kp = s0 - tok * topk; kp < topk; ++kp) {
-                                const int s = tok * topk + kp;
-                                if (sids[s] != e) continue;
-                                const float w = bf16r(g2 * bf16r(__ldcg(p.tw + s)));
-                                p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v0 * w);
-                                p.ybuf[(size_t)s * p.H + n0 + 8] = __float2bfloat16(v1 * w);
+                        for (int i = 0; i < 8; ++i) {
+                            const int n = odd ? 8 + i : i;
+                            const float g0 = odd ? oth[8 + i] : acc[i], u0 = odd ? acc[8 + i] : oth[i];
+                            if (n < d.ntok) {
+                                const float gv = bf16r(bf16r(g0) * gs);
+                                const float uv = bf16r(bf16r(u0) * gs);
+                                p.hbuf[(size_t)tlist[tbase + n] * p.I + col] =
+                                    __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                            }
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int n = odd ? 8 + i : i;
+                            const float g0 = odd ? oth[8 + i] : acc[i], u0 = odd ? acc[8 + i] : oth[i];
+                            if (n < d.ntok) {
+                                const float gv = bf16r(g0), uv = bf16r(u0);
+                                p.hsh[(size_t)(TG * d.tg + n) * p.Is + col] =
+                                    __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
                             }
                         }
                     }
-                signal(C_CNT + c, 1);
-            } else if (d.kind == K_S2) {
-                const int c = d.tile;
-                const int n0 = 128 * c + 16 * warp + g;
+                }
+                signal(d.kind == K_G1 ? C_DONE + d.u : C_SDONE + d.tg, 1);
+            } else if (d.kind == K_S1) {
+                if (wg == 0) {
+                    float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048 + row * TG;
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt)
+                    for (int n = 0; n < TG; n += 4)
+                        __stcg(reinterpret_cast<float4*>(pb + n), make_float4(acc[n], acc[n + 1], acc[n + 2], acc[n + 3]));
+                }
+                signal(C_SPLIT + d.tile * L.ngs + d.tg, 1);
+            } else if (d.kind == K_G2) {
+                if (wg == 0) {
+                    const int u = d.u, e = ulist[u];
+                    const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
+                    const int n0 = 128 * d.tile + row;
+                    const int tbase = toff[u] + TG * d.tg;
 #pragma unroll
-                    for (int i = 0; i < 2; ++i) {
-                        const int jt = 8 * nt + 2 * t + i;
-                        if (jt < d.ntok) {
-                            const int tok = TG * d.tg + jt;
-                            p.sbuf[(size_t)tok * p.H + n0] = __float2bfloat16(acc[nt][i]);
-                            p.sbuf[(size_t)tok * p.H + n0 + 8] = __float2bfloat16(acc[nt][2 + i]);
+                    for (int n = 0; n < TG; ++n) {
+                        if (n >= d.ntok) break;
+                        const int s0 = tlist[tbase + n];
+                        const int tok = s0 / topk;
+                        const float v = bf16r(acc[n]);
+                        for (int kp = s0 - tok * topk; kp < topk; ++kp) {
+                            const int s = tok * topk + kp;
+                            if (sids[s] != e) continue;
+                            const float w = bf16r(g2 * bf16r(__ldcg(p.tw + s)));
+                            p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v * w);
                         }
                     }
-                signal(C_CNT + c, 1);
+                }
+                signal(C_CNT + d.tile, 1);
+            } else if (d.kind == K_S2) {
+                if (wg == 0) {
+                    const int n0 = 128 * d.tile + row;
+#pragma unroll
+                    for (int n = 0; n < TG; ++n)
+                        if (n < d.ntok) p.sbuf[(size_t)(TG * d.tg + n) * p.H + n0] = __float2bfloat16(acc[n]);
+                }
+                signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_CB) {
                 // the producer acquired every producer of this tile (and the gate logits) before publishing it
                 combine_tile(p, L, sids, d.tile, ctid);
@@ -761,6 +817,10 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
 
     // ------------------------------------------------------------------ exit: the last CTA re-arms ctrl
     __syncthreads();
+    if (warp == 0) {   // every mma this CTA issued has completed (each commit was waited for)
+        qf::tc_fence_after();
+        qf::tmem_dealloc(tmem, TM_COLS);
+    }
     if (tid == 0) {
         __threadfence();
         misc[MISC_FLAG] = atomicAdd(ctrl + C_EXIT, 1u) == gridDim.x - 1;
@@ -775,11 +835,16 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
 }
 
 // ------------------------------------------------------------------------------------------ weight repacking
-// int4: canonical [E][N][K/8] words -> kernel layout (see moe.cu header and qwenfast_b200/formats.py).
+// Kernel layouts (one expert matrix [N, K]; see qwenfast_b200/formats.py for the same maps in torch):
+//   row order inside a 128-row tile r: plain -> 128r + lane; gate_up ("gated") -> even lane 2j = gate row 64r + j,
+//   odd lane 2j+1 = up row N/2 + 64r + j, so a SwiGLU pair sits in neighbouring lanes of one warp.
+//   int4 stage (256 k, 16 KB): [half h (128 k)][quad q][lane (128)][4 words], word j of quad q holding
+//   k = 256st + 128h + 32q + 8j .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i]; scales [lane][h].
+//   bf16 stage (64 k, 16 KB): [k chunk c (8)][lane (128)][8 elements] = the canonical K-major no-swizzle tile.
 __device__ __forceinline__ int kernel_row_to_src(int pos, int N, int gated) {
     if (!gated) return pos;
-    const int r = pos >> 7, w = (pos & 127) >> 4, rho = pos & 15;
-    return rho < 8 ? 64 * r + 8 * w + rho : N / 2 + 64 * r + 8 * w + (rho - 8);
+    const int r = pos >> 7, rho = pos & 127;
+    return (rho & 1) ? N / 2 + 64 * r + (rho >> 1) : 64 * r + (rho >> 1);
 }
 
 // word o of an expert's kernel-layout matrix -> (source row, source word along K)
@@ -788,16 +853,10 @@ __device__ __forceinline__ void w4_word_src(long long o, int N, int K, int gated
     const int r = (int)(o / per_tile);
     const int ot = (int)(o - r * per_tile);
     const int st = ot / 4096;
-    const int kc = min(256, K - 256 * st);
     const int os = ot - 4096 * st;
-    const int slab_words = (kc / 64) * 128;
-    const int w = os / slab_words;
-    const int ow = os - w * slab_words;
-    const int c = ow >> 7, L = (ow >> 2) & 31, j = ow & 3;
-    const int gg = L >> 2, t = L & 3;
-    const int rho = gg + 8 * (j & 1), b = 2 * c + (j >> 1);
-    kw = 32 * st + 4 * b + t;
-    row = kernel_row_to_src(128 * r + 16 * w + rho, N, gated);
+    const int j = os & 3, rho = (os >> 2) & 127, hq = os >> 9;
+    kw = 32 * st + 16 * (hq >> 2) + 4 * (hq & 3) + j;
+    row = kernel_row_to_src(128 * r + rho, N, gated);
 }
 
 __device__ __forceinline__ void w4_scale_src(long long o, int N, int K, int gated, int& row, int& grp) {
@@ -806,12 +865,9 @@ __device__ __forceinline__ void w4_scale_src(long long o, int N, int K, int gate
     const int st = ot / 256;
     const int kc = min(256, K - 256 * st);
     const int os = ot - 256 * st;
-    const int per_slab = (kc / 128) * 16;
-    const int w = os / per_slab;
-    const int gi = (os - w * per_slab) >> 4, ent = os & 15;
-    const int rho = (ent >> 1) + 8 * (ent & 1);
-    grp = 2 * st + gi;
-    row = kernel_row_to_src(128 * r + 16 * w + rho, N, gated);
+    const int ngrp = kc / 128;
+    grp = 2 * st + os % ngrp;
+    row = kernel_row_to_src(128 * r + os / ngrp, N, gated);
 }
 
 __device__ __forceinline__ uint32_t nib_perm(uint32_t v, bool forward) {
@@ -857,10 +913,9 @@ __global__ void bf16_repack_kernel(const uint16_t* __restrict__ src, uint16_t* _
         const int r = (int)(o / per_tile);
         const int ot = (int)(o - r * per_tile);
         const int st = ot >> 13, os = ot & 8191;
-        const int w = os >> 10, ks = (os >> 8) & 3, L = (os >> 3) & 31, reg = (os >> 1) & 3, e2 = os & 1;
-        const int gg = L >> 2, t = L & 3, q = reg >> 1, hi = reg & 1;
-        const int k = 64 * st + 16 * ks + 4 * t + 2 * q + e2;
-        const int row = kernel_row_to_src(128 * r + 16 * w + gg + 8 * hi, N, gated);
+        const int c = os >> 10, rho = (os >> 3) & 127, el = os & 7;
+        const int k = 64 * st + 8 * c + el;
+        const int row = kernel_row_to_src(128 * r + rho, N, gated);
         const long long si = (long long)row * K + k;
         if (!unpack) dst[o] = src[si];
         else dst[si] = src[o];

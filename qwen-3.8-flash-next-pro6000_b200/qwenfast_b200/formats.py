@@ -6,14 +6,14 @@ Canonical (what a checkpoint loader holds, and the synthetic configurations' def
     dequantised weight ``(code - 8) * scale``.
 
 Kernel layout (one expert matrix [N, K]; ``gated`` for gate_up, where N = 2I rows are gate then up)
-    row tiles of 128 rows; each tile is a run of pipeline stages of up to 256 k (16 KB of int4); inside a stage,
-    eight 16-row slabs (one per consumer warp), each a run of 64-k chunks of 512 bytes in which lane L = 4g + t
-    owns 16 bytes: words (row g, block 2c), (row g+8, block 2c), (row g, block 2c+1), (row g+8, block 2c+1),
-    each word holding k = 32b + 8t .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i]. For gate_up, slab row
-    g < 8 is gate row 64r + 8w + g and slab row g + 8 is the matching up row, so SwiGLU pairs sit in one thread.
-    Scales follow the same tile/stage/slab order, 16 entries per (slab, 128-k group) with rows (g, g+8) adjacent.
-bf16 kernel layout (the shared expert): same tiles and slabs, stages of 64 k, four mma k-steps per slab, lane L
-    holds its four A-fragment registers (rows g, g+8; k = 16s + 4t .. +3).
+    128-row tiles; inside tile r, lane (row slot) p holds row 128r + p (plain) or, for gate_up, gate row 64r + p/2
+    (even p) and up row N/2 + 64r + p/2 (odd p), so a SwiGLU pair sits in neighbouring lanes of one warp.
+    int4: each tile is a run of stages of up to 256 k (16 KB); a stage is [128-k half h][quad q][lane p][4 words],
+    word j of quad q holding k = 256s + 128h + 32q + 8j .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i], so one
+    lop3 per bf16x2 pair yields natural k order and a warp's 16-byte loads are contiguous. Scales: per stage
+    [lane p][h].
+bf16 (the shared expert): stages of 64 k laid out [k chunk c of 8][lane p][8 elements] -- the canonical K-major,
+    no-swizzle tensor-core tile (8-row core matrices of 16-byte rows), used directly as the MMA's A operand.
 
 The CUDA entry points ``qf_w4_repack``/``qf_bf16_repack`` produce these layouts on the device; the ``*_torch``
 functions here compute the same index maps with tensor ops (any device) and are used by the CPU tests.
@@ -57,11 +57,12 @@ def _nibble_perm(words: torch.Tensor, forward: bool) -> torch.Tensor:
 
 # ----------------------------------------------------------------------------------------------- index maps
 def kernel_row_source(N: int, gated: bool, device=None) -> torch.Tensor:
+    """Kernel row position -> source row."""
     p = torch.arange(N, device=device, dtype=torch.int64)
     if not gated:
         return p
-    r, w, rho = p // 128, (p % 128) // 16, p % 16
-    return torch.where(rho < 8, 64 * r + 8 * w + rho, N // 2 + 64 * r + 8 * w + rho - 8)
+    r, rho = p // 128, p % 128
+    return torch.where(rho % 2 == 0, 64 * r + rho // 2, N // 2 + 64 * r + rho // 2)
 
 
 def w4_word_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
@@ -69,17 +70,10 @@ def w4_word_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     o = torch.arange(N * K // 8, device=device, dtype=torch.int64)
     per_tile = 128 * K // 8
     r, ot = o // per_tile, o % per_tile
-    st = ot // 4096
-    kc = torch.clamp(K - 256 * st, max=256)
-    os_ = ot - 4096 * st
-    slab_words = (kc // 64) * 128
-    w = os_ // slab_words
-    ow = os_ - w * slab_words
-    c, lane, j = ow >> 7, (ow >> 2) & 31, ow & 3
-    g, t = lane >> 2, lane & 3
-    rho, b = g + 8 * (j & 1), 2 * c + (j >> 1)
-    kw = 32 * st + 4 * b + t
-    row = kernel_row_source(N, gated, device)[128 * r + 16 * w + rho]
+    st, os_ = ot // 4096, ot % 4096
+    j, rho, hq = os_ & 3, (os_ >> 2) & 127, os_ >> 9
+    kw = 32 * st + 16 * (hq >> 2) + 4 * (hq & 3) + j
+    row = kernel_row_source(N, gated, device)[128 * r + rho]
     return row * (K // 8) + kw
 
 
@@ -90,12 +84,9 @@ def w4_scale_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     st = ot // 256
     kc = torch.clamp(K - 256 * st, max=256)
     os_ = ot - 256 * st
-    per_slab = (kc // 128) * 16
-    w = os_ // per_slab
-    gi, ent = (os_ - w * per_slab) >> 4, os_ & 15
-    rho = (ent >> 1) + 8 * (ent & 1)
-    row = kernel_row_source(N, gated, device)[128 * r + 16 * w + rho]
-    return row * (K // 128) + 2 * st + gi
+    ngrp = kc // 128
+    row = kernel_row_source(N, gated, device)[128 * r + os_ // ngrp]
+    return row * (K // 128) + 2 * st + os_ % ngrp
 
 
 def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
@@ -104,10 +95,9 @@ def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     per_tile = 128 * K
     r, ot = o // per_tile, o % per_tile
     st, os_ = ot >> 13, ot & 8191
-    w, ks, lane, reg, e2 = os_ >> 10, (os_ >> 8) & 3, (os_ >> 3) & 31, (os_ >> 1) & 3, os_ & 1
-    g, t, q, hi = lane >> 2, lane & 3, reg >> 1, reg & 1
-    k = 64 * st + 16 * ks + 4 * t + 2 * q + e2
-    row = kernel_row_source(N, gated, device)[128 * r + 16 * w + g + 8 * hi]
+    c, rho, el = os_ >> 10, (os_ >> 3) & 127, os_ & 7
+    k = 64 * st + 8 * c + el
+    row = kernel_row_source(N, gated, device)[128 * r + rho]
     return row * K + k
 
 

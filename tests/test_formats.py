@@ -26,11 +26,11 @@ def test_bf16_round_trip(N, K, gated):
     assert torch.equal(formats.bf16_elem_map(N, K, gated).sort().values, torch.arange(N * K))
 
 
-def test_gate_up_rows_interleave_in_slabs():
+def test_gate_up_rows_interleave_in_lanes():
     src = formats.kernel_row_source(256, True)
-    # tile 0, slab 0: rows 0..7 are gate rows 0..7, rows 8..15 the matching up rows 128..135
-    assert src[:16].tolist() == list(range(8)) + list(range(128, 136))
-    assert src[128:136].tolist() == list(range(64, 72))
+    # tile 0: even lane 2j is gate row j, odd lane 2j+1 the matching up row 128 + j; tile 1 continues at gate row 64
+    assert src[:6].tolist() == [0, 128, 1, 129, 2, 130]
+    assert src[128:132].tolist() == [64, 192, 65, 193]
 
 
 def test_pack_unpack_int4_and_nibble_order():
