@@ -41,6 +41,8 @@ enum {
  * out of range (QF_MOE_ERR_* bits); the caller clears it. */
 #define QF_MOE_CTRL_WORDS 2048
 #define QF_MOE_CTRL_ERR 3
+/* Size of the optional MoE timeline buffer (int64 entries). */
+#define QF_MOE_DBG_NUMEL (32 * 512)
 #define QF_MOE_ERR_TIMEOUT 0x1
 #define QF_MOE_ERR_BAD_EXPERT 0x2
 #define QF_MOE_ERR_PIPELINE 0x4
@@ -93,7 +95,8 @@ int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, i
  *   weighted slot outputs go to ybuf [M, topk + 1, H] with every other slot zero, slot `topk` holding the shared
  *   expert output when this shard computes it; qf_moe_combine then finishes the layer (after the caller has summed
  *   ybuf over the shards).
- * dbg: optional int64 [grid * 32] per-CTA globaltimer stamps, or NULL.
+ * dbg: optional int64 [QF_MOE_DBG_NUMEL] per-CTA globaltimer stamps (32 per CTA; CTAs beyond the first
+ *   QF_MOE_DBG_NUMEL / 32 record nothing), or NULL.
  * ------------------------------------------------------------------------------------------------------------ */
 int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64_t* hbuf_bytes, int64_t* ybuf_bytes,
                          int64_t* gl_numel, int64_t* ctrl_numel, int64_t* pbuf_numel, int64_t* shbuf_bytes);

@@ -10,30 +10,44 @@
 // tensor cores in fp32 and then scaled once (exact products, no per-weight scale multiply).
 //
 // B200 structure
-//   * 2 CTAs per SM (296), 9 warps each: warp 8 lane 0 is the producer, warp 8 lane 1 the signal agent, warps 0..7
-//     are consumers.
+//   * 2 CTAs per SM (296; the ordered queue needs no co-residency, so the grid is not cut to what the occupancy
+//     query reports), 12 warps each:
+//       warps 0..3   dequant warpgroup: stage in, token rows in, int4 -> bf16 into TMEM, hand-off to the MMA warps
+//       warps 4..7   readback warpgroup: stage partials out of TMEM, item epilogues, completion records
+//       warp 8       producer (lane 0)        warps 9, 10  MMA issuers (even / odd pipelined stages)
+//       warp 11      signal agent (lane 0)
+//     Every pipelined stage walks dequant -> MMA -> readback through NBUF job slots. Splitting dequant and
+//     readback over two warpgroups lets the two latency chains of a stage overlap instead of adding up. Roles
+//     that block on different mbarriers live in different warps: a lane suspended in mbarrier.try_wait holds up
+//     its whole warp. One thread issues a tcgen05.mma about every 60 cycles, so two issuers keep up.
 //   * Work items, claimed in order from a global queue:
 //       GL  shared-expert gate logits          S1  shared gate_up tile, one of 4 k-splits, one 16-token group
 //       G1  expert u gate_up tile + group      S1F shared gate_up split-K sum + SwiGLU
 //       S2  shared down tile + group           G2  expert u down tile + group
 //       CB  top-k combine of one 128-column tile (+ gated shared term)
 //     An item only depends on items claimed before it, so the queue cannot deadlock.
-//   * The producer streams each item through an NST-stage shared-memory ring with 1-D bulk copies (TMA engine,
-//     mbarrier completion): per stage 16 KB of weights (128 rows x 256 k int4, or x 64 k bf16), their scales, and
-//     the matching k-slice of the item's token rows (x for gate_up, h for down). Every cross-CTA dependency
-//     (gate_up -> down, split-K -> finalize -> shared down, all producers of a column tile -> combine) is waited on
-//     by the producer (bounded) before it fills the stage, so consumers never spin on other CTAs.
+//   * The producer streams each item's weights through an NST-stage shared-memory ring with 1-D bulk copies (TMA
+//     engine, mbarrier completion): per stage 8 KB of weights (128 rows x 128 k int4, or x 32 k bf16) and, for
+//     int4, the stage's 128 row scales. Every cross-CTA dependency (gate_up -> down, split-K -> finalize -> shared
+//     down, all producers of a column tile -> combine) is acquired by the producer (bounded wait) before it marks
+//     the stage full, so consumers never spin on other CTAs.
+//   * The matching k-slice of the item's token rows (x for gate_up, h for down; at most 16 rows of 256 B) is copied
+//     by the consumers themselves, one 16-byte cp.async per thread straight into the B operand, one stage ahead:
+//     small per-row bulk copies would cost the single producer thread ~60 cycles of issue each, and a plain load in
+//     flight would be waited for by the stage's own fences and release arrives.
 //   * Consumers signal completed items through a CTA-local ring; the agent lane turns each record into one gpu-scope
 //     release (fence + atomic add) on the control block. Consumer warps never execute a gpu-scope fence.
-//   * Contraction on the 5th-generation tensor cores (tcgen05). int4 tiles: every consumer thread owns one TMEM lane
-//     (= one weight row of the 128-row tile) and one 128-k half of the stage; it turns each int4 word into four
-//     bf16x2 of the biased codes (128 + code; one lop3 each) and stores them to TMEM (tcgen05.st) as the A operand.
-//     The gathered token rows are re-laid by the consumers into the canonical K-major shared-memory layout (B,
-//     N = 16). One elected thread issues tcgen05.mma kind::f16 (A in TMEM, B in SMEM, fp32 D in TMEM) per k16 step
-//     plus one against a constant -136 A tile that removes the bias, then tcgen05.commit. Each 128-k group has its
-//     own D region; its fp32 partial is read back (tcgen05.ld) and scaled once by the row's group scale.
-//     bf16 tiles (shared expert): the stage itself is the A operand (SMEM descriptor), D accumulates in TMEM over the
-//     whole item. gate_up tiles interleave gate row j (even lane) and up row j (odd lane): SwiGLU is one shuffle.
+//   * Contraction on the 5th-generation tensor cores (tcgen05), software-pipelined two stages deep. int4 stages
+//     (128 rows x 128 k, one scale group): every consumer thread owns one TMEM lane (= one weight row) and the
+//     stage's whole k; it turns each int4 word into four bf16x2 of the signed codes
+//     (code - 8: one lop3 and one bf16x2 subtract each, exact) and stores them to TMEM (tcgen05.st) as the A
+//     operand, while the token rows land in the canonical K-major shared-memory B layout (N = 16). An MMA warp
+//     issues tcgen05.mma kind::f16 per k16 step (A in TMEM, B in SMEM, fp32 D in TMEM), then tcgen05.commit.
+//     A, B and D are triple-buffered: while the tensor cores run stages s-1 and s-2, the consumers dequantise
+//     stage s, then read back (tcgen05.ld) and scale stage s-2. Each stage writes its own D and the consumers
+//     add the stages up in registers in k order (all 16 tokens of the thread's row).
+//     bf16 stages (shared expert, 32 k): the ring stage itself is the A operand (SMEM descriptor).
+//     gate_up tiles interleave gate row j (even lane) and up row j (odd lane): SwiGLU is one shuffle.
 //   * The routing plan (unique experts, per-expert token lists, group offsets) is rebuilt identically by every CTA
 //     from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
 //   * Every wait is bounded (globaltimer); a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
@@ -46,19 +60,20 @@ using qf::bf16_hi;
 using qf::bf16_lo;
 using qf::bf16r;
 
-constexpr int NCW = 8;                        // consumer warps
-constexpr int MOE_THREADS = (NCW + 1) * 32;   // + the producer / agent warp
+constexpr int NCW = 4;                        // warps per consumer warpgroup (128 threads = 128 weight rows)
+constexpr int MOE_THREADS = (2 * NCW + 4) * 32;   // dequant + readback warpgroups, producer, two MMA warps, agent
+constexpr int RB_WARP0 = NCW, PRODUCER_WARP = 2 * NCW, MMA_WARP0 = 2 * NCW + 1, AGENT_WARP = 2 * NCW + 3;
+constexpr int NBUF = 3;                       // A / B / D buffers of the pipelined stages
 constexpr int CONS_THREADS = NCW * 32;
 constexpr int CTAS_PER_SM = 2;
 constexpr int TG = 16;                        // tokens per token group (two n8 tiles)
-constexpr int NST = 3;                        // pipeline stages per CTA
+constexpr int NST = 10;                       // pipeline stages per CTA
 constexpr int NEPI = 8;                       // completion-record ring
-constexpr int W4_KC = 256;                    // int4 k per stage
-constexpr int BF_KC = 64;                     // bf16 k per stage
-constexpr int STAGE_W = 16384;                // weight bytes of a full stage
-constexpr int STAGE_S = 512;                  // scale bytes of a full int4 stage
-constexpr int STAGE_X = TG * (W4_KC + 8) * 2; // token rows of a stage (row stride kc + 8 elements)
-constexpr int STAGE_BYTES = STAGE_W + STAGE_S + STAGE_X;
+constexpr int W4_KC = 128;                    // int4 k per stage (one scale group)
+constexpr int BF_KC = 32;                     // bf16 k per stage
+constexpr int STAGE_W = 8192;                 // weight bytes of a stage (128 rows x 128 k int4 or x 32 k bf16)
+constexpr int STAGE_S = 256;                  // scale bytes of an int4 stage (one per row)
+constexpr int STAGE_BYTES = STAGE_W + STAGE_S;
 constexpr int NSPLIT = 4;                     // split-K of the shared expert's gate_up
 constexpr int MAXSLOTS = QF_MAX_TOKENS * QF_MAX_TOPK;
 constexpr uint64_t DEP_WAIT_NS = 1000000000ull;    // cross-CTA dependency waits
@@ -84,6 +99,10 @@ struct StageDesc {
 };
 struct EpiRec {     // one completion record: add `add` to ctrl[idx] (idx < 0: nothing; kind STOP ends the agent)
     int idx, add;
+};
+struct MmaJob {     // one pipelined stage (or a non-MMA item) passed from the dequant to the MMA and readback warps
+    StageDesc d;
+    int16_t ring, pad[3];
 };
 
 struct Params {
@@ -116,16 +135,19 @@ struct Params {
 constexpr int BST_BYTES = TG * (W4_KC / 8) * 16;                      // B operand [k chunk][16 tokens][16 B]
 constexpr int OFF_RING = 0;
 constexpr int OFF_BST = OFF_RING + NST * STAGE_BYTES;
-constexpr int OFF_BAR = OFF_BST + BST_BYTES;                          // full[NST], empty[NST], efull[NEPI], eempty[NEPI], mma
-constexpr int OFF_DESC = OFF_BAR + (2 * NST + 2 * NEPI + 2) * 8;
+constexpr int OFF_BAR = OFF_BST + NBUF * BST_BYTES;   // full, empty, efull, eempty, ab-ready, mma-done, d-free
+constexpr int OFF_DESC = OFF_BAR + (2 * NST + 2 * NEPI + 3 * NBUF) * 8;
 constexpr int OFF_EPI = OFF_DESC + NST * (int)sizeof(StageDesc);
-constexpr int OFF_PLAN = OFF_EPI + NEPI * (int)sizeof(EpiRec);
+constexpr int OFF_JOB = OFF_EPI + NEPI * (int)sizeof(EpiRec);
+constexpr int OFF_SCS = OFF_JOB + NBUF * (int)sizeof(MmaJob);        // float [NBUF][128] row scales of the stages
+constexpr int OFF_PLAN = OFF_SCS + NBUF * 128 * 4;
 constexpr int PLAN_ULIST = 0;                                         // int16 [QF_MAX_EXPERTS]
 constexpr int PLAN_GPRE = PLAN_ULIST + QF_MAX_EXPERTS * 2;            // int16 [QF_MAX_EXPERTS + 1]
 constexpr int PLAN_TOFF = PLAN_GPRE + (QF_MAX_EXPERTS + 8) * 2;
 constexpr int PLAN_TLIST = PLAN_TOFF + (QF_MAX_EXPERTS + 8) * 2;      // int16 [MAXSLOTS]
 constexpr int PLAN_SIDS = PLAN_TLIST + MAXSLOTS * 2;                  // int16 [MAXSLOTS] copy of topk_ids
-constexpr int PLAN_MISC = PLAN_SIDS + MAXSLOTS * 2;                   // int32 [64]
+constexpr int PLAN_DUPN = PLAN_SIDS + MAXSLOTS * 2;                   // int16 [MAXSLOTS] next slot, same token+expert
+constexpr int PLAN_MISC = PLAN_DUPN + MAXSLOTS * 2;                   // int32 [64]
 constexpr int PLAN_BYTES = PLAN_MISC + 64 * 4;
 constexpr int MOE_SMEM = OFF_PLAN + PLAN_BYTES;
 static_assert(CTAS_PER_SM * (MOE_SMEM + 1024) <= 228 * 1024, "two CTAs per SM must fit in shared memory");
@@ -140,9 +162,9 @@ enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 
 
 // tensor memory map (columns of this CTA's allocation; fp32 / bf16x2 per 32-bit column, lane = tile row)
 constexpr uint32_t TM_COLS = 256;
-constexpr uint32_t TM_A = 0;       // 128 columns: A tile of one 256-k int4 stage (16 k16 steps x 8 columns)
-constexpr uint32_t TM_D = 128;     // 2 x 16 columns: fp32 partial of each 128-k group (bf16 items: running sum)
-constexpr uint32_t TM_C = 160;     // 8 columns: constant -136 A tile (bias removal)
+constexpr uint32_t TM_A = 0;       // NBUF x 64 columns: A tiles of 128-k int4 stages (8 k16 steps x 8 columns)
+constexpr uint32_t TM_D = 192;     // NBUF x 16 columns: fp32 partial of each stage
+static_assert(TM_D + NBUF * 16 <= TM_COLS && TM_A + NBUF * 64 <= TM_D, "tensor memory map");
 constexpr uint32_t IDESC = qf::idesc_bf16(128, TG);
 
 // Errors that stop the pipeline (waits that ran out). An out-of-range expert id is reported but not fatal: the
@@ -183,34 +205,28 @@ __device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   /
 }
 
 // ---------------------------------------------------------------------------------------------- consumer math
-// Copy the stage's token rows (row-major, stride kc + 8 elements) into the canonical K-major B layout
-// [k chunk of 8][token (16)][16 bytes] (8-token core matrices: SBO = 128 B, k-chunk stride LBO = 256 B).
-__device__ __forceinline__ void reshuffle_b(const uint8_t* stage, uint8_t* bst, int kc, int ntok, int ctid) {
-    const int xrb = (kc + 8) * 2;
-    const uint8_t* xs = stage + STAGE_W + STAGE_S;
-    const int nch = kc >> 3;
-    for (int idx = ctid; idx < nch * ntok; idx += CONS_THREADS) {
-        const int c = idx / ntok, n = idx - c * ntok;
-        *reinterpret_cast<uint4*>(bst + (c * TG + n) * 16) = *reinterpret_cast<const uint4*>(xs + n * xrb + c * 16);
-    }
-    qf::fence_proxy_async_smem();   // the tensor cores read bst through the async proxy
+// Row of token n of a stage's item (its k-slice base for stage 0), or nullptr for n beyond the item's tokens.
+__device__ __forceinline__ const __nv_bfloat16* token_row(const Params& p, const StageDesc& d, const int16_t* toff,
+                                                          const int16_t* tlist, int n) {
+    if (n >= d.ntok) return nullptr;
+    if (d.kind == K_G1) return p.x + (size_t)(tlist[toff[d.u] + TG * d.tg + n] / p.topk) * p.H;
+    if (d.kind == K_G2) return p.hbuf + (size_t)tlist[toff[d.u] + TG * d.tg + n] * p.I;
+    if (d.kind == K_S1) return p.x + (size_t)(TG * d.tg + n) * p.H + d.split * (p.H / NSPLIT);
+    return p.hsh + (size_t)(TG * d.tg + n) * p.Is;   // K_S2
 }
 
-// Dequantise this thread's row of its 128-k half of an int4 stage into TMEM (biased codes, natural k order):
-// word w of the half (k = 8w .. 8w+7) becomes columns TM_A + 64 * half + 4w .. +4.
-__device__ __forceinline__ void stage_w4_to_tmem(const uint8_t* stage, uint32_t tmem, int half, int quarter, int lane) {
-    const int row = 32 * quarter + lane;
-    const uint8_t* ws = stage + ((half * 4) * 128 + row) * 16;
-    const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
+// Dequantise this thread's row of an int4 stage (w: its first 16-byte load; quads are 128 lanes apart) into
+// TMEM columns ta .. ta + 63 (signed codes, natural k order: word w, k = 8w .. +8, becomes columns 4w .. 4w + 3).
+__device__ __forceinline__ void stage_w4_to_tmem(const uint8_t* w, uint32_t ta) {
 #pragma unroll
-    for (int qd = 0; qd < 4; ++qd) {
-        const uint4 w = *reinterpret_cast<const uint4*>(ws + qd * 128 * 16);
+    for (int hq = 0; hq < 4; ++hq) {
+        const uint4 q = *reinterpret_cast<const uint4*>(w + hq * 128 * 16);
         uint32_t v[16];
-        qf::biased_w4(w.x, v + 0);
-        qf::biased_w4(w.y, v + 4);
-        qf::biased_w4(w.z, v + 8);
-        qf::biased_w4(w.w, v + 12);
-        qf::tmem_st16(tmem + lane_base + TM_A + 64 * half + 16 * qd, v);
+        qf::signed_w4(q.x, v + 0);
+        qf::signed_w4(q.y, v + 4);
+        qf::signed_w4(q.z, v + 8);
+        qf::signed_w4(q.w, v + 12);
+        qf::tmem_st16(ta + 16 * hq, v);
     }
 }
 
@@ -268,15 +284,20 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
     uint64_t* empty = full + NST;
     uint64_t* efull = empty + NST;
     uint64_t* eempty = efull + NEPI;
-    uint64_t* mma_bar = eempty + NEPI;
+    uint64_t* abr = eempty + NEPI;      // [NBUF] A/B of a pipelined stage written (8 consumer warps arrive)
+    uint64_t* mmab = abr + NBUF;        // [NBUF] the stage's mmas completed (tcgen05.commit), or the job passed on
+    uint64_t* dfree = mmab + NBUF;      // [NBUF] the readback warps are done with the job's buffers (4 warps arrive)
+    float* scs = reinterpret_cast<float*>(smem + OFF_SCS);
     StageDesc* desc = reinterpret_cast<StageDesc*>(smem + OFF_DESC);
     EpiRec* epi = reinterpret_cast<EpiRec*>(smem + OFF_EPI);
+    MmaJob* jobs = reinterpret_cast<MmaJob*>(smem + OFF_JOB);
     uint8_t* plan = smem + OFF_PLAN;
     int16_t* ulist = reinterpret_cast<int16_t*>(plan + PLAN_ULIST);
     int16_t* gpre = reinterpret_cast<int16_t*>(plan + PLAN_GPRE);
     int16_t* toff = reinterpret_cast<int16_t*>(plan + PLAN_TOFF);
     int16_t* tlist = reinterpret_cast<int16_t*>(plan + PLAN_TLIST);
     int16_t* sids = reinterpret_cast<int16_t*>(plan + PLAN_SIDS);
+    int16_t* dupn = reinterpret_cast<int16_t*>(plan + PLAN_DUPN);
     int* misc = reinterpret_cast<int*>(plan + PLAN_MISC);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -292,7 +313,11 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             qf::mbar_init(efull + i, NCW);
             qf::mbar_init(eempty + i, 1);
         }
-        qf::mbar_init(mma_bar, 1);
+        for (int i = 0; i < NBUF; ++i) {
+            qf::mbar_init(abr + i, NCW);
+            qf::mbar_init(mmab + i, 1);
+            qf::mbar_init(dfree + i, NCW);
+        }
         qf::mbar_fence_init();
         misc[MISC_DBGN] = 0;
     }
@@ -304,7 +329,7 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
     // Everything below reads data of the previous kernel (topk ids, x) or the control block it may re-arm.
     qf::pdl_wait();
 
-    // ------------------------------------------------------------------ routing plan (all 288 threads)
+    // ------------------------------------------------------------------ routing plan (all threads)
     {
         uint64_t* mask = reinterpret_cast<uint64_t*>(ring + SCR_MASK);
         int16_t* exf = reinterpret_cast<int16_t*>(ring + SCR_EXF);
@@ -329,7 +354,7 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
         if (bad) set_err(ctrl, QF_MOE_ERR_BAD_EXPERT);
         __syncthreads();
         const int nch = (E + 31) >> 5;
-        for (int c = warp; c < nch; c += NCW + 1) {
+        for (int c = warp; c < nch; c += MOE_THREADS / 32) {
             const int e = 32 * c + lane;
             const uint64_t m = e < E ? mask[e] : 0ull;
             const int f = m != 0ull, cnt = __popcll(m), ng = (cnt + TG - 1) / TG;
@@ -376,10 +401,13 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
         __syncthreads();
         for (int s = tid; s < nslots; s += MOE_THREADS) {
             const int e = sids[s];
+            dupn[s] = -1;
             if (e < 0 || e < p.elo || e >= p.ehi) continue;
             const int t = s / topk, kp = s - t * topk;
             bool first = true;
             for (int k2 = 0; k2 < kp; ++k2) first &= sids[t * topk + k2] != e;
+            for (int k2 = topk - 1; k2 > kp; --k2)   // the next slot of this token routed to the same expert
+                if (sids[t * topk + k2] == e) dupn[s] = (int16_t)(t * topk + k2);
             if (first) {
                 const int j = __popcll(mask[e] & ((1ull << t) - 1ull));
                 tlist[toffe[e] + j] = (int16_t)s;
@@ -408,7 +436,7 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
     L.total = L.b_cb + L.R2;
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
 
-    if (warp == NCW) {
+    if (warp == PRODUCER_WARP) {
         if (lane == 0) {
             // ========================================================== producer (one thread)
             const uint64_t pol = qf::policy_evict_first();
@@ -469,77 +497,65 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
                     wait_counter(ctrl, C_CNT + tile, L.tile_target);
                     if (L.has_gate) wait_counter(ctrl, C_GLF, 1u);
                 }
+                // per item: the stage descriptor (written with the item's first stage; the consumers read it once),
+                // the weight / scale sources (advanced by a constant per stage), bytes per stage, and the counter
+                // that must be acquired before the first stage is marked full (the item's inputs), if any
+                StageDesc d;
+                d.kind = (int16_t)kind; d.u = (int16_t)u; d.tile = (int16_t)tile; d.tg = (int16_t)tg;
+                d.split = (int16_t)split; d.kidx = 0; d.nk = (int16_t)nk; d.ntok = (int16_t)ntok;
+                const uint8_t* wsrc = nullptr;
+                const uint16_t* ssrc = nullptr;
+                uint32_t bytes = 0;
+                int dep_idx = -1;
+                uint32_t dep_target = 0;
+                if (kind == K_G1 || kind == K_G2) {
+                    const bool down = kind == K_G2;
+                    const int K = down ? p.I : p.H;
+                    const int N = down ? p.H : 2 * p.I;
+                    d.kc = (int16_t)W4_KC;
+                    bytes = STAGE_W + STAGE_S;
+                    wsrc = (down ? p.w2 : p.w13) + (size_t)e * ((size_t)N * K / 2) + (size_t)tile * (128 * (size_t)K / 2);
+                    ssrc = (down ? p.s2 : p.s13) + (size_t)e * ((size_t)N * K / 128) + (size_t)tile * K;
+                    if (down) { dep_idx = C_DONE + u; dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])); }
+                } else if (kind == K_S1 || kind == K_S2) {
+                    const bool down = kind == K_S2;
+                    const int K = down ? p.Is : p.H;
+                    const int k0 = down ? 0 : split * (p.H / NSPLIT);
+                    d.kc = (int16_t)BF_KC;
+                    bytes = STAGE_W;
+                    wsrc = (down ? p.shw2 : p.shw13) + (size_t)tile * (128 * (size_t)K * 2) + (size_t)(k0 / BF_KC) * STAGE_W;
+                    if (down) { dep_idx = C_SDONE + tg; dep_target = (uint32_t)L.Rs1; }
+                } else {
+                    d.kc = 0;
+                }
                 for (int kidx = 0; kidx < nk; ++kidx) {
                     if (!qf::mbar_wait(empty + st, ph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
                     uint8_t* sb = ring + st * STAGE_BYTES;
-                    uint8_t* sw = sb;
-                    uint8_t* ssc = sb + STAGE_W;
-                    uint8_t* sx = sb + STAGE_W + STAGE_S;
-                    int kc = 0;
-                    uint32_t bytes = 0;
-                    if (kind == K_G1 || kind == K_G2) {
-                        const int K = kind == K_G1 ? p.H : p.I;
-                        kc = min(W4_KC, K - W4_KC * kidx);
-                        bytes = 128 * kc / 2 + kc * 2 + ntok * kc * 2;
-                    } else if (kind == K_S1 || kind == K_S2) {
-                        kc = BF_KC;
-                        bytes = STAGE_W + ntok * kc * 2;
-                    }
-                    StageDesc d;
-                    d.kind = (int16_t)kind; d.u = (int16_t)u; d.tile = (int16_t)tile; d.tg = (int16_t)tg;
-                    d.split = (int16_t)split; d.kidx = (int16_t)kidx; d.nk = (int16_t)nk; d.kc = (int16_t)kc;
-                    d.ntok = (int16_t)ntok;
-                    desc[st] = d;
+                    if (kidx == 0) desc[st] = d;
                     if (bytes == 0) {
+                        qf::mbar_arrive(full + st);
+                    } else if (kidx == 0 && dep_idx >= 0) {
+                        // weights first; the stage is marked full (arrive) only after the item's inputs are acquired
+                        qf::mbar_expect_tx(full + st, bytes);
+                        qf::bulk_g2s_hint(sb, wsrc, STAGE_W, full + st, pol);
+                        if (ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, ssrc, STAGE_S, full + st, pol);
+                        wait_counter(ctrl, dep_idx, dep_target);
                         qf::mbar_arrive(full + st);
                     } else {
                         qf::mbar_arrive_expect_tx(full + st, bytes);
-                        const int xrb = (kc + 8) * 2;
-                        if (kind == K_G1 || kind == K_G2) {
-                            const bool down = kind == K_G2;
-                            const int K = down ? p.I : p.H;
-                            const int N = down ? p.H : 2 * p.I;
-                            const uint8_t* wbase = (down ? p.w2 : p.w13) + (size_t)e * ((size_t)N * K / 2) +
-                                                   (size_t)tile * (128 * (size_t)K / 2) + (size_t)kidx * STAGE_W;
-                            const uint16_t* sbase = (down ? p.s2 : p.s13) + (size_t)e * ((size_t)N * K / 128) +
-                                                    (size_t)tile * K + (size_t)kidx * 256;
-                            qf::bulk_g2s_hint(sw, wbase, 128 * kc / 2, full + st, pol);
-                            qf::bulk_g2s_hint(ssc, sbase, kc * 2, full + st, pol);
-                            if (down && kidx == 0) {
-                                wait_counter(ctrl, C_DONE + u, (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])));
-                                qf::fence_proxy_async();
-                            }
-                            const int tbase = toff[u] + TG * tg;
-                            for (int j = 0; j < ntok; ++j) {
-                                const int s = tlist[tbase + j];
-                                const __nv_bfloat16* src = down ? p.hbuf + (size_t)s * p.I + W4_KC * kidx
-                                                                : p.x + (size_t)(s / topk) * p.H + W4_KC * kidx;
-                                qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
-                            }
-                        } else {
-                            const bool down = kind == K_S2;
-                            const int K = down ? p.Is : p.H;
-                            const int k0 = down ? BF_KC * kidx : split * (p.H / NSPLIT) + BF_KC * kidx;
-                            const uint8_t* wbase = (down ? p.shw2 : p.shw13) + (size_t)tile * (128 * (size_t)K * 2) +
-                                                   (size_t)(k0 / BF_KC) * STAGE_W;
-                            qf::bulk_g2s_hint(sw, wbase, STAGE_W, full + st, pol);
-                            if (down && kidx == 0) {
-                                wait_counter(ctrl, C_SDONE + tg, (uint32_t)L.Rs1);
-                                qf::fence_proxy_async();
-                            }
-                            for (int j = 0; j < ntok; ++j) {
-                                const int tok = TG * tg + j;
-                                const __nv_bfloat16* src =
-                                    down ? p.hsh + (size_t)tok * p.Is + k0 : p.x + (size_t)tok * p.H + k0;
-                                qf::bulk_g2s(sx + j * xrb, src, kc * 2, full + st);
-                            }
-                        }
+                        qf::bulk_g2s_hint(sb, wsrc, STAGE_W, full + st, pol);
+                        if (ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, ssrc, STAGE_S, full + st, pol);
                     }
+                    wsrc += STAGE_W;
+                    if (ssrc != nullptr) ssrc += W4_KC;
                     if (++st == NST) { st = 0; ph ^= 1u; }
                 }
                 if (kind == K_STOP) break;
             }
-        } else if (lane == 1) {
+        }
+        __syncwarp();
+    } else if (warp == AGENT_WARP) {
+        if (lane == 0) {
             // ========================================================== signal agent (one thread)
             // Consumer warps arrive on efull[slot] after their item's global stores; this thread then makes those
             // stores visible at gpu scope (fence) and publishes the item's counter increment.
@@ -561,25 +577,190 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             }
         }
         __syncwarp();
+    } else if (warp == MMA_WARP0 || warp == MMA_WARP0 + 1) {
+        // ============================================================== MMA issuers (one lane issues)
+        // warp MMA_WARP0 + w takes the jobs s = w, w + 2, ...: slot s % NBUF, its (s / NBUF)-th use. Jobs without
+        // mmas (and the stop job) are passed on to the readback warps with a plain arrive.
+        // Descriptors advance by constants: one k16 step is 2 chunks of B (512 B, +32 in the 16-byte address
+        // field), 8 columns of an A tile in TMEM, or 2 chunks of a bf16 A stage (4096 B, +256).
+        const uint64_t bdesc0 = qf::smem_desc(bst, 256, 128);
+        const uint64_t adesc0 = qf::smem_desc(ring, 2048, 128);
+        for (uint32_t s = (uint32_t)(warp - MMA_WARP0);; s += 2) {
+            const int b = (int)(s % NBUF);
+            if (!qf::mbar_wait(abr + b, (s / NBUF) & 1u, PIPE_WAIT_NS)) {
+                set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                break;
+            }
+            const int kind = jobs[b].d.kind;
+            if (lane == 0) {
+                if (kind == K_G1 || kind == K_G2) {
+                    qf::tc_fence_after();
+                    const uint64_t bd = bdesc0 + (uint64_t)(b * (BST_BYTES >> 4));
+                    const uint32_t dcol = tmem + TM_D + 16 * b, ta = tmem + TM_A + 64 * b;
+#pragma unroll
+                    for (int j = 0; j < W4_KC / 16; ++j) qf::mma_ts(dcol, ta + 8 * j, bd + 32 * j, IDESC, j != 0);
+                    qf::mma_commit(mmab + b);
+                } else if (kind == K_S1 || kind == K_S2) {
+                    qf::tc_fence_after();
+                    const uint64_t bd = bdesc0 + (uint64_t)(b * (BST_BYTES >> 4));
+                    const uint64_t ad = adesc0 + (uint64_t)(jobs[b].ring * (STAGE_BYTES >> 4));
+                    const uint32_t dcol = tmem + TM_D + 16 * b;
+#pragma unroll
+                    for (int j = 0; j < BF_KC / 16; ++j) qf::mma_ss(dcol, ad + 256 * j, bd + 32 * j, IDESC, j != 0);
+                    qf::mma_commit(mmab + b);
+                } else {
+                    qf::mbar_arrive(mmab + b);
+                }
+            }
+            __syncwarp();
+            if (kind == K_STOP) break;
+        }
+    } else if (warp < NCW) {
+        // ============================================================== dequant warpgroup
+        const int ctid = tid;                 // 0..127
+        const int row = ctid;                 // tile row (= TMEM lane) owned by this thread
+        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+        // per-thread constant offsets: this thread's first 16-byte weight load and its scale in an int4 stage, its
+        // A columns in TMEM (slot 0)
+        const int woff = row * 16;
+        const int soff = STAGE_W + row * 2;
+        const uint32_t ta0 = tmem + lane_base + TM_A;
+        int st = 0;
+        uint32_t ph = 0;
+        uint32_t s = 0;   // jobs so far (identical in every thread of the CTA that counts them)
+        int b = 0;        // s % NBUF
+        // the slot of job s is free once the readback warps finished job s - NBUF (whose mmas had completed)
+        auto wait_free = [&]() {
+            if (s >= NBUF && !qf::mbar_wait(dfree + b, ((s / NBUF) + 1u) & 1u, PIPE_WAIT_NS))
+                set_err(ctrl, QF_MOE_ERR_PIPELINE);
+        };
+        auto next_job = [&]() {
+            ++s;
+            b = b == NBUF - 1 ? 0 : b + 1;
+        };
+        auto next_stage = [&]() {
+            if (++st == NST) { st = 0; ph ^= 1u; }
+        };
+        // stop: one stop job for each MMA warp (jobs s and s + 1); the readback warps stop at the first
+        auto push_stop = [&]() {
+            for (int i = 0; i < 2; ++i) {
+                wait_free();
+                if (ctid == 0) jobs[b].d.kind = (int16_t)K_STOP;
+                __syncwarp();
+                if (lane == 0) qf::mbar_arrive(abr + b);
+                next_job();
+            }
+        };
+        for (;;) {
+            if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
+                set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                push_stop();
+                break;
+            }
+            const StageDesc d = desc[st];
+            if (d.kind == K_STOP) {
+                push_stop();
+                break;
+            }
+            const bool w4 = d.kind == K_G1 || d.kind == K_G2;
+            if (!w4 && d.kind != K_S1 && d.kind != K_S2) {
+                // item without mmas: one job carries it to the readback warps; its (empty) ring slot is free now
+                wait_free();
+                if (ctid == 0) {
+                    jobs[b].d = d;
+                    jobs[b].ring = (int16_t)st;
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    qf::mbar_arrive(empty + st);
+                    qf::mbar_arrive(abr + b);
+                }
+                next_job();
+                next_stage();
+                continue;
+            }
+            // ---------------------------------------------------------------- pipelined item: nk stages
+            const int nk = d.nk, kc = d.kc;
+            // token chunks: int4 stages have 16 tokens x 16 chunks (two per thread: tokens t/16 and 8 + t/16,
+            // chunk t % 16), bf16 stages 16 x 4 (threads 0..63: token t/4, chunk t % 4)
+            const int lg = w4 ? 4 : 2;   // log2 of the 16-byte chunks per token row of a stage
+            const int xn = ctid >> lg, xc = ctid & ((1 << lg) - 1);
+            const bool xact = xn < TG;
+            const int xdst = (xc * TG + xn) * 16;
+            const __nv_bfloat16* xrow = token_row(p, d, toff, tlist, xn);
+            const __nv_bfloat16* xrow2 = w4 ? token_row(p, d, toff, tlist, xn + 8) : nullptr;
+            const char* xsrc = xrow != nullptr ? reinterpret_cast<const char*>(xrow + 8 * xc)
+                                               : reinterpret_cast<const char*>(p.x);
+            const char* xsrc2 = xrow2 != nullptr ? reinterpret_cast<const char*>(xrow2 + 8 * xc)
+                                                 : reinterpret_cast<const char*>(p.x);
+            const uint32_t xbytes = xrow != nullptr ? 16u : 0u;   // 0: zero-fill (token beyond the item)
+            const uint32_t xbytes2 = xrow2 != nullptr ? 16u : 0u;
+            const int xstep = xrow != nullptr ? kc * 2 : 0;
+            const int xstep2 = xrow2 != nullptr ? kc * 2 : 0;
+            bool failed = false;
+            for (int kidx = 0;;) {
+                wait_free();
+                uint8_t* bb = bst + b * BST_BYTES;
+                if (xact) qf::cp_async16(bb + xdst, xsrc, xbytes);
+                if (w4) qf::cp_async16(bb + xdst + 8 * 16, xsrc2, xbytes2);
+                if (ctid == 0) {
+                    MmaJob j;
+                    j.d = d;
+                    j.d.kidx = (int16_t)kidx;
+                    j.ring = (int16_t)st;
+                    jobs[b] = j;
+                }
+                const uint8_t* sb = ring + st * STAGE_BYTES;
+                float sc = 1.f;
+                if (w4) {
+                    stage_w4_to_tmem(sb + woff, ta0 + 64 * b);
+                    sc = bf16_bits(*reinterpret_cast<const uint16_t*>(sb + soff));
+                }
+                scs[b * 128 + row] = sc;
+                qf::cp_async_wait_all();
+                qf::fence_proxy_async_smem();   // the tensor cores read bst through the async proxy
+                if (w4) qf::tmem_wait_st();
+                qf::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if (w4) qf::mbar_arrive(empty + st);   // the stage now lives in TMEM (bf16: read by the mmas)
+                    qf::mbar_arrive(abr + b);
+                }
+                next_job();
+                next_stage();
+                if (++kidx == nk) break;
+                xsrc += xstep;
+                xsrc2 += xstep2;
+                if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
+                    set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                    failed = true;
+                    break;
+                }
+            }
+            if (failed) {
+                push_stop();
+                break;
+            }
+        }
     } else {
-        // ============================================================== consumers (8 warps, 2 warpgroups)
-        const int ctid = tid;                 // 0..255
-        const int wg = warp >> 2;             // warpgroup: which 128-k half of an int4 stage this thread dequantises
-        const int quarter = warp & 3;         // TMEM lane quarter
-        const int row = 32 * quarter + lane;  // tile row (= TMEM lane) owned by this thread
-        const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
-        float* red = reinterpret_cast<float*>(bst);   // [128 rows][16] partial exchange between the warpgroups
-        int st = 0, es = 0;
-        uint32_t ph = 0, eph = 0, mph = 0;
-        float acc[TG];
-        // optional timeline: (globaltimer << 12) | tag, up to 32 per CTA (tags: item kinds, 14 plan built, 15 exit)
+        // ============================================================== readback warpgroup
+        const int rw = warp - RB_WARP0;       // 0..3: TMEM lane quarter
+        const int ctid = tid - RB_WARP0 * 32; // 0..127
+        const int row = ctid;                 // tile row (= TMEM lane) owned by this thread
+        const uint32_t td0 = tmem + ((uint32_t)(32 * rw) << 16) + TM_D;
+        int es = 0;
+        uint32_t eph = 0;
+        uint32_t s = 0;
+        int b = 0;
+        float acc[16];   // this thread's row, tokens 0..15
+        // optional timeline: (globaltimer << 12) | tag, up to 32 per CTA (tags: item kinds, 15 exit)
         auto stamp = [&](int tag) {
-            if (p.dbg != nullptr && ctid == 0 && misc[MISC_DBGN] < 32) {
+            if (p.dbg != nullptr && ctid == 0 && blockIdx.x < QF_MOE_DBG_NUMEL / 32 && misc[MISC_DBGN] < 32) {
                 p.dbg[blockIdx.x * 32 + misc[MISC_DBGN]] = (long long)((qf::globaltimer() << 12) | (uint64_t)tag);
                 misc[MISC_DBGN] += 1;
             }
         };
-        // hand one completion record to the agent (record written by thread 0; all eight warps arrive)
+        // hand one completion record to the agent (record written by thread 0; every readback warp arrives)
         auto signal = [&](int idx, int add) {
             if (ctid == 0) {
                 if (!qf::mbar_wait(eempty + es, eph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
@@ -590,118 +771,58 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             if (lane == 0) qf::mbar_arrive(efull + es);
             if (++es == NEPI) { es = 0; eph ^= 1u; }
         };
-        // the constant -136 A tile: written once by the first warpgroup (lanes 0..127, 8 columns)
-        if (wg == 0) {
-            uint32_t v[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0xC308C308u;   // bf16 -136.0 in both halves
-            qf::tmem_st8(tmem + lane_base + TM_C, v);
-            qf::tmem_wait_st();
-        }
-        qf::tc_fence_before();
-        qf::named_bar(1, CONS_THREADS);
-        stamp(14);
         for (;;) {
-            if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
+            // job s: the dequant hand-off (job record and scales visible), then its mmas (or the pass-through)
+            const uint32_t par = (s / NBUF) & 1u;
+            if (!qf::mbar_wait(abr + b, par, PIPE_WAIT_NS) || !qf::mbar_wait(mmab + b, par, PIPE_WAIT_NS)) {
                 set_err(ctrl, QF_MOE_ERR_PIPELINE);
                 signal(-2, 0);
                 break;
             }
-            const StageDesc d = desc[st];
+            const StageDesc d = jobs[b].d;
             if (d.kind == K_STOP) {
                 stamp(15);
                 signal(-2, 0);
                 break;
             }
-            if (d.kidx == 0) {
+            const bool mma = d.kind == K_G1 || d.kind == K_G2 || d.kind == K_S1 || d.kind == K_S2;
+            if (!mma || d.kidx == 0) {
 #pragma unroll
-                for (int n = 0; n < TG; ++n) acc[n] = 0.f;
+                for (int i = 0; i < 16; ++i) acc[i] = 0.f;
                 stamp(d.kind);
             }
-            uint8_t* sb = ring + st * STAGE_BYTES;
-            const bool w4 = d.kind == K_G1 || d.kind == K_G2;
-            const bool bf = d.kind == K_S1 || d.kind == K_S2;
-            if (w4 || bf) {
-                const int ngrp = w4 ? (d.kc >> 7) : 0;
-                float sc = 0.f;
-                reshuffle_b(sb, bst, d.kc, d.ntok, ctid);
-                if (w4 && wg < ngrp) {
-                    stage_w4_to_tmem(sb, tmem, wg, quarter, lane);
-                    const uint16_t* ss = reinterpret_cast<const uint16_t*>(sb + STAGE_W);
-                    sc = bf16_bits(ss[row * ngrp + wg]);
-                    qf::tmem_wait_st();
-                }
-                qf::tc_fence_before();
-                if (w4) {   // the stage's bytes now live in TMEM and bst: hand the ring slot back
-                    __syncwarp();
-                    if (lane == 0) qf::mbar_arrive(empty + st);
-                }
-                qf::named_bar(1, CONS_THREADS);
-                if (ctid == 0) {
-                    qf::tc_fence_after();
-                    if (w4) {
-                        for (int j = 0; j < (d.kc >> 4); ++j) {
-                            const uint32_t dcol = tmem + TM_D + 16 * (j >> 3);
-                            const uint64_t bd = qf::smem_desc(bst + 2 * j * 256, 256, 128);
-                            qf::mma_ts(dcol, tmem + TM_C, bd, IDESC, (j & 7) != 0);
-                            qf::mma_ts(dcol, tmem + TM_A + 8 * j, bd, IDESC, 1u);
-                        }
-                    } else {
-                        for (int j = 0; j < 4; ++j)
-                            qf::mma_ss(tmem + TM_D, qf::smem_desc(sb + 2 * j * 2048, 2048, 128),
-                                       qf::smem_desc(bst + 2 * j * 256, 256, 128), IDESC, (d.kidx > 0 || j > 0));
-                    }
-                    qf::mma_commit(mma_bar);
-                }
-                __syncwarp();
-                if (!qf::mbar_wait(mma_bar, mph, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
-                mph ^= 1u;
+            if (mma) {
+                const float sc = scs[b * 128 + row];
                 qf::tc_fence_after();
-                if (bf) {   // the stage was the A operand: release it only now
-                    __syncwarp();
-                    if (lane == 0) qf::mbar_arrive(empty + st);
-                }
-                if (w4 && wg < ngrp) {
+                if (d.ntok > 8) {
                     uint32_t v[16];
-                    qf::tmem_ld16(tmem + lane_base + TM_D + 16 * wg, v);
+                    qf::tmem_ld16(td0 + 16 * b, v);
                     qf::tmem_wait_ld();
 #pragma unroll
-                    for (int n = 0; n < TG; ++n) acc[n] = fmaf(__uint_as_float(v[n]), sc, acc[n]);
+                    for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
+                } else {
+                    uint32_t v[8];
+                    qf::tmem_ld8(td0 + 16 * b, v);
+                    qf::tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
                 }
                 qf::tc_fence_before();
-            } else {
-                __syncwarp();
-                if (lane == 0) qf::mbar_arrive(empty + st);
             }
-            if (++st == NST) { st = 0; ph ^= 1u; }
-            if (d.kidx != d.nk - 1) continue;
+            const int rslot = jobs[b].ring;
+            __syncwarp();
+            if (lane == 0) {
+                if (d.kind == K_S1 || d.kind == K_S2) qf::mbar_arrive(empty + rslot);   // the mmas read that slot
+                qf::mbar_arrive(dfree + b);
+            }
+            ++s;
+            b = b == NBUF - 1 ? 0 : b + 1;
+            if (mma && d.kidx != d.nk - 1) continue;
 
             // ------------------------------------------------------------ epilogues (item complete)
-            if (w4) {   // fixed-order sum of the two warpgroups' halves into warpgroup 0
-                if (wg == 1) {
-#pragma unroll
-                    for (int n = 0; n < TG; n += 4)
-                        *reinterpret_cast<float4*>(red + row * TG + n) = make_float4(acc[n], acc[n + 1], acc[n + 2], acc[n + 3]);
-                }
-                qf::named_bar(1, CONS_THREADS);
-                if (wg == 0) {
-#pragma unroll
-                    for (int n = 0; n < TG; n += 4) {
-                        const float4 o = *reinterpret_cast<const float4*>(red + row * TG + n);
-                        acc[n] += o.x; acc[n + 1] += o.y; acc[n + 2] += o.z; acc[n + 3] += o.w;
-                    }
-                }
-                qf::named_bar(1, CONS_THREADS);
-            } else if (bf && wg == 0) {
-                uint32_t v[16];
-                qf::tmem_ld16(tmem + lane_base + TM_D, v);
-                qf::tmem_wait_ld();
-#pragma unroll
-                for (int n = 0; n < TG; ++n) acc[n] = __uint_as_float(v[n]);
-                qf::tc_fence_before();
-            }
+            // acc[i] = row `row`, token i
             if (d.kind == K_GL) {
-                for (int tok = warp; tok < M; tok += NCW) {
+                for (int tok = rw; tok < M; tok += NCW) {
                     const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)tok * p.H);
                     const uint4* wr = reinterpret_cast<const uint4*>(p.wgate);
                     float a = 0.f;
@@ -720,79 +841,63 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
                 }
                 signal(C_GLF, 1);
             } else if (d.kind == K_G1 || d.kind == K_S1F) {
-                // rows interleave gate (even lane) and up (odd lane) of intermediate column j = row / 2;
-                // even lanes finish tokens 0..7, odd lanes tokens 8..15
-                if (d.kind == K_S1F && wg == 0) {
+                if (d.kind == K_S1F) {
                     const float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048 + row * TG;
-#pragma unroll
-                    for (int n = 0; n < TG; ++n) acc[n] = 0.f;
 #pragma unroll
                     for (int sp = 0; sp < NSPLIT; ++sp) {   // fixed split order: the sum does not depend on timing
 #pragma unroll
-                        for (int n = 0; n < TG; n += 4) {
-                            const float4 q = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)sp * 2048 + n));
-                            acc[n] += q.x; acc[n + 1] += q.y; acc[n + 2] += q.z; acc[n + 3] += q.w;
+                        for (int i = 0; i < 16; i += 4) {
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)sp * 2048 + i));
+                            acc[i] += q.x; acc[i + 1] += q.y; acc[i + 2] += q.z; acc[i + 3] += q.w;
                         }
                     }
                 }
-                if (wg == 0) {
-                    const bool odd = lane & 1;
-                    float oth[TG];
+                // rows interleave gate (even lane) and up (odd lane) of intermediate column j = row / 2; of the
+                // 16 tokens the even lane finishes 0..7, the odd lane 8..15
+                const bool odd = lane & 1;
+                const int col = 64 * d.tile + (row >> 1);
+                float gs = 1.f;
+                int tbase = 0;
+                if (d.kind == K_G1) {
+                    const int e = ulist[d.u];
+                    gs = p.gs13 ? bf16_bits(p.gs13[e]) : 1.f;
+                    tbase = toff[d.u] + TG * d.tg;
+                }
 #pragma unroll
-                    for (int n = 0; n < TG; ++n) oth[n] = __shfl_xor_sync(0xffffffffu, acc[n], 1);
-                    const int col = 64 * d.tile + (row >> 1);
-                    if (d.kind == K_G1) {
-                        const int u = d.u, e = ulist[u];
-                        const float gs = p.gs13 ? bf16_bits(p.gs13[e]) : 1.f;
-                        const int tbase = toff[u] + TG * d.tg;
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int n = odd ? 8 + i : i;
-                            const float g0 = odd ? oth[8 + i] : acc[i], u0 = odd ? acc[8 + i] : oth[i];
-                            if (n < d.ntok) {
-                                const float gv = bf16r(bf16r(g0) * gs);
-                                const float uv = bf16r(bf16r(u0) * gs);
-                                p.hbuf[(size_t)tlist[tbase + n] * p.I + col] =
-                                    __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
-                            }
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int n = odd ? 8 + i : i;
-                            const float g0 = odd ? oth[8 + i] : acc[i], u0 = odd ? acc[8 + i] : oth[i];
-                            if (n < d.ntok) {
-                                const float gv = bf16r(g0), uv = bf16r(u0);
-                                p.hsh[(size_t)(TG * d.tg + n) * p.Is + col] =
-                                    __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
-                            }
+                for (int ii = 0; ii < 8; ++ii) {
+                    // the even lane needs its partner's up of token ii, the odd lane its partner's gate of 8 + ii
+                    const float mine = odd ? acc[8 + ii] : acc[ii];
+                    const float theirs = __shfl_xor_sync(0xffffffffu, odd ? acc[ii] : acc[8 + ii], 1);
+                    const int n = odd ? 8 + ii : ii;
+                    const float g0 = odd ? theirs : mine, u0 = odd ? mine : theirs;
+                    if (n < d.ntok) {
+                        if (d.kind == K_G1) {
+                            const float gv = bf16r(bf16r(g0) * gs), uv = bf16r(bf16r(u0) * gs);
+                            p.hbuf[(size_t)tlist[tbase + n] * p.I + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                        } else {
+                            const float gv = bf16r(g0), uv = bf16r(u0);
+                            p.hsh[(size_t)(TG * d.tg + n) * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
                         }
                     }
                 }
                 signal(d.kind == K_G1 ? C_DONE + d.u : C_SDONE + d.tg, 1);
             } else if (d.kind == K_S1) {
-                if (wg == 0) {
-                    float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048 + row * TG;
+                float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048 + row * TG;
 #pragma unroll
-                    for (int n = 0; n < TG; n += 4)
-                        __stcg(reinterpret_cast<float4*>(pb + n), make_float4(acc[n], acc[n + 1], acc[n + 2], acc[n + 3]));
-                }
+                for (int i = 0; i < 16; i += 4)
+                    __stcg(reinterpret_cast<float4*>(pb + i), make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
                 signal(C_SPLIT + d.tile * L.ngs + d.tg, 1);
             } else if (d.kind == K_G2) {
-                if (wg == 0) {
-                    const int u = d.u, e = ulist[u];
-                    const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
-                    const int n0 = 128 * d.tile + row;
-                    const int tbase = toff[u] + TG * d.tg;
+                const int u = d.u, e = ulist[u];
+                const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
+                const int n0 = 128 * d.tile + row;
+                const int tbase = toff[u] + TG * d.tg;
 #pragma unroll
-                    for (int n = 0; n < TG; ++n) {
-                        if (n >= d.ntok) break;
-                        const int s0 = tlist[tbase + n];
-                        const int tok = s0 / topk;
-                        const float v = bf16r(acc[n]);
-                        for (int kp = s0 - tok * topk; kp < topk; ++kp) {
-                            const int s = tok * topk + kp;
-                            if (sids[s] != e) continue;
+                for (int i = 0; i < 16; ++i) {
+                    if (i < d.ntok) {
+                        const float v = bf16r(acc[i]);
+                        // the token's first slot routed to e, then any later slot of the same token with e again
+                        for (int s = tlist[tbase + i]; s >= 0; s = dupn[s]) {
                             const float w = bf16r(g2 * bf16r(__ldcg(p.tw + s)));
                             p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v * w);
                         }
@@ -800,12 +905,10 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
                 }
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_S2) {
-                if (wg == 0) {
-                    const int n0 = 128 * d.tile + row;
+                const int n0 = 128 * d.tile + row;
 #pragma unroll
-                    for (int n = 0; n < TG; ++n)
-                        if (n < d.ntok) p.sbuf[(size_t)(TG * d.tg + n) * p.H + n0] = __float2bfloat16(acc[n]);
-                }
+                for (int i = 0; i < 16; ++i)
+                    if (i < d.ntok) p.sbuf[(size_t)(TG * d.tg + i) * p.H + n0] = __float2bfloat16(acc[i]);
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_CB) {
                 // the producer acquired every producer of this tile (and the gate logits) before publishing it
@@ -838,9 +941,9 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
 // Kernel layouts (one expert matrix [N, K]; see qwenfast_b200/formats.py for the same maps in torch):
 //   row order inside a 128-row tile r: plain -> 128r + lane; gate_up ("gated") -> even lane 2j = gate row 64r + j,
 //   odd lane 2j+1 = up row N/2 + 64r + j, so a SwiGLU pair sits in neighbouring lanes of one warp.
-//   int4 stage (256 k, 16 KB): [half h (128 k)][quad q][lane (128)][4 words], word j of quad q holding
-//   k = 256st + 128h + 32q + 8j .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i]; scales [lane][h].
-//   bf16 stage (64 k, 16 KB): [k chunk c (8)][lane (128)][8 elements] = the canonical K-major no-swizzle tile.
+//   int4 stage (128 k = one scale group, 8 KB): [half h (64 k)][quad q][lane (128)][4 words], word j of quad q
+//   holding k = 128st + 64h + 32q + 8j .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i]; scales [stage][lane].
+//   bf16 stage (32 k, 8 KB): [k chunk c (4)][lane (128)][8 elements] = the canonical K-major no-swizzle tile.
 __device__ __forceinline__ int kernel_row_to_src(int pos, int N, int gated) {
     if (!gated) return pos;
     const int r = pos >> 7, rho = pos & 127;
@@ -852,22 +955,18 @@ __device__ __forceinline__ void w4_word_src(long long o, int N, int K, int gated
     const long long per_tile = 128LL * K / 8;
     const int r = (int)(o / per_tile);
     const int ot = (int)(o - r * per_tile);
-    const int st = ot / 4096;
-    const int os = ot - 4096 * st;
+    const int st = ot >> 11;
+    const int os = ot & 2047;
     const int j = os & 3, rho = (os >> 2) & 127, hq = os >> 9;
-    kw = 32 * st + 16 * (hq >> 2) + 4 * (hq & 3) + j;
+    kw = 16 * st + 8 * (hq >> 1) + 4 * (hq & 1) + j;
     row = kernel_row_to_src(128 * r + rho, N, gated);
 }
 
 __device__ __forceinline__ void w4_scale_src(long long o, int N, int K, int gated, int& row, int& grp) {
     const int r = (int)(o / K);
     const int ot = (int)(o - (long long)r * K);
-    const int st = ot / 256;
-    const int kc = min(256, K - 256 * st);
-    const int os = ot - 256 * st;
-    const int ngrp = kc / 128;
-    grp = 2 * st + os % ngrp;
-    row = kernel_row_to_src(128 * r + os / ngrp, N, gated);
+    grp = ot >> 7;
+    row = kernel_row_to_src(128 * r + (ot & 127), N, gated);
 }
 
 __device__ __forceinline__ uint32_t nib_perm(uint32_t v, bool forward) {
@@ -912,9 +1011,9 @@ __global__ void bf16_repack_kernel(const uint16_t* __restrict__ src, uint16_t* _
         const long long per_tile = 128LL * K;
         const int r = (int)(o / per_tile);
         const int ot = (int)(o - r * per_tile);
-        const int st = ot >> 13, os = ot & 8191;
+        const int st = ot >> 12, os = ot & 4095;
         const int c = os >> 10, rho = (os >> 3) & 127, el = os & 7;
-        const int k = 64 * st + 8 * c + el;
+        const int k = 32 * st + 8 * c + el;
         const int row = kernel_row_to_src(128 * r + rho, N, gated);
         const long long si = (long long)row * K + k;
         if (!unpack) dst[o] = src[si];
@@ -923,6 +1022,7 @@ __global__ void bf16_repack_kernel(const uint16_t* __restrict__ src, uint16_t* _
 }
 
 }  // namespace
+
 
 // ================================================================================================= C ABI
 extern "C" int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64_t* hbuf_bytes, int64_t* ybuf_bytes,
@@ -982,17 +1082,19 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaGetDevice");
     const int sms = qf::sm_count(dev);
     QF_REQUIRE(sms > 0, "a16_moe_decode: cannot query the SM count");
-    static int per_sm_cache[64] = {0};
-    int per_sm = dev < 64 ? per_sm_cache[dev] : 0;
     ce = qf::ensure_smem_attr(reinterpret_cast<const void*>(moe_persistent_kernel), MOE_SMEM);
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute");
-    if (per_sm == 0) {
-        // every CTA of the persistent grid must be resident at once: size the grid from the occupancy
-        ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, moe_persistent_kernel, MOE_THREADS, MOE_SMEM);
-        if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: occupancy query");
-        per_sm = per_sm < 1 ? 1 : (per_sm > CTAS_PER_SM ? CTAS_PER_SM : per_sm);
-        if (dev < 64) per_sm_cache[dev] = per_sm;
+    static bool carveout_set[64] = {false};
+    if (dev >= 64 || !carveout_set[dev]) {
+        // two CTAs per SM need the largest shared-memory carveout; without the hint the driver may pick a smaller one
+        ce = cudaFuncSetAttribute(reinterpret_cast<const void*>(moe_persistent_kernel),
+                                  cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+        if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute (carveout)");
+        if (dev < 64) carveout_set[dev] = true;
     }
+    // Grid: CTAS_PER_SM per SM (registers, shared memory and the 256 tensor-memory columns each CTA allocates all
+    // fit twice). The occupancy query reports one CTA per SM for this kernel, but residency is not required for
+    // correctness: an item only waits for items claimed before it, by CTAs that are already running.
 
     Params p;
     p.x = static_cast<const __nv_bfloat16*>(x);
@@ -1019,7 +1121,7 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     p.dbg = reinterpret_cast<long long*>(dbg);
     p.M = M; p.H = H; p.I = I; p.E = E; p.topk = topk; p.Is = has_shw ? Is : 0;
     p.mode = mode; p.elo = expert_lo; p.ehi = expert_hi;
-    ce = qf::launch_ex(moe_persistent_kernel, dim3(sms * per_sm), dim3(MOE_THREADS), MOE_SMEM,
+    ce = qf::launch_ex(moe_persistent_kernel, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,
                        reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);
     return qf::cuda_status(ce, "a16_moe_decode: launch");
 }
@@ -1058,7 +1160,7 @@ extern "C" int qf_w4_unpack(const int32_t* wk, const void* sk, int32_t* qweight,
 
 extern "C" int qf_bf16_repack(const void* w, void* wk, int N, int K, int gated, qf_stream_t stream) {
     QF_REQUIRE(w && wk, "bf16_repack: null pointer argument");
-    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 64 && K % 64 == 0, "bf16_repack: need N %% 128 == 0 and K %% 64 == 0");
+    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 32 && K % 32 == 0, "bf16_repack: need N %% 128 == 0 and K %% 32 == 0");
     bf16_repack_kernel<<<repack_grid((long long)N * K), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t*>(w), static_cast<uint16_t*>(wk), N, K, gated, 0);
     return qf::cuda_status(cudaGetLastError(), "bf16_repack: launch");
@@ -1066,7 +1168,7 @@ extern "C" int qf_bf16_repack(const void* w, void* wk, int N, int K, int gated, 
 
 extern "C" int qf_bf16_unpack(const void* wk, void* w, int N, int K, int gated, qf_stream_t stream) {
     QF_REQUIRE(w && wk, "bf16_unpack: null pointer argument");
-    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 64 && K % 64 == 0, "bf16_unpack: need N %% 128 == 0 and K %% 64 == 0");
+    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 32 && K % 32 == 0, "bf16_unpack: need N %% 128 == 0 and K %% 32 == 0");
     bf16_repack_kernel<<<repack_grid((long long)N * K), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t*>(wk), static_cast<uint16_t*>(w), N, K, gated, 1);
     return qf::cuda_status(cudaGetLastError(), "bf16_unpack: launch");

@@ -88,6 +88,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
+// 16-byte asynchronous global -> shared copy (cp.async, L2 only); src_bytes 0 writes zeros and reads nothing.
+// Fences and release arrives of the issuing thread do not wait for it; cp_async_wait_all does.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Raise the phase's expected transaction bytes without arriving (the arrive comes later, e.g. after a dependency).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -99,12 +111,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait on an mbarrier phase. Returns false (and leaves the phase unconsumed) once `limit_ns` passed.
+// try_wait that suspends the thread until the phase completes or about `hint_ns` passed, so that a waiting warp
+// does not keep re-issuing barrier probes (which share the SM's memory-instruction queue with the working warps).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on an mbarrier phase. Returns false (and leaves the phase unconsumed) once about `limit_ns` passed.
+// The bound is counted in SM cycles (clock64 reads are cheap; %globaltimer reads are not), 2 per ns: at most
+// 2 x limit_ns of wall time at clocks of 1 GHz and more.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > limit_ns) return false;
+    const long long t0 = clock64();
+    const long long lim = (long long)(2 * limit_ns);
+    while (!mbar_try_wait_hint(bar, parity, 100000u)) {
+        if (clock64() - t0 > lim) return false;
     }
     return true;
 }
@@ -241,8 +269,8 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// int4 word -> four bf16x2 of the biased codes 128 + code (one lop3 each, exact). The bias is removed on the tensor
-// cores by a second mma against a constant -136 A tile (136 = 128 + the zero point 8).
+// int4 word -> four bf16x2 of the biased codes 128 + code (one lop3 each, exact); the caller removes the bias
+// (128 + the zero point 8 = 136 times the k-sum of the other operand).
 __device__ __forceinline__ void biased_w4(uint32_t q, uint32_t* p) {
     const uint32_t MASK = 0x000F000Fu, MAGIC = 0x43004300u;
 #pragma unroll
@@ -250,5 +278,20 @@ __device__ __forceinline__ void biased_w4(uint32_t q, uint32_t* p) {
         const uint32_t s = q >> (4 * i);
         asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(p[i]) : "r"(s), "r"(MASK), "r"(MAGIC));
     }
+}
+// int4 word -> four bf16x2 of the signed codes code - 8 (lop3 to 128 + code, then one bf16x2 subtract; exact).
+__device__ __forceinline__ void signed_w4(uint32_t q, uint32_t* p) {
+    biased_w4(q, p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(p[i]) : "r"(p[i]), "r"(0x43084308u));
+}
+}  // namespace qf
+
+namespace qf {
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
 }
 }  // namespace qf

@@ -8,11 +8,11 @@ Canonical (what a checkpoint loader holds, and the synthetic configurations' def
 Kernel layout (one expert matrix [N, K]; ``gated`` for gate_up, where N = 2I rows are gate then up)
     128-row tiles; inside tile r, lane (row slot) p holds row 128r + p (plain) or, for gate_up, gate row 64r + p/2
     (even p) and up row N/2 + 64r + p/2 (odd p), so a SwiGLU pair sits in neighbouring lanes of one warp.
-    int4: each tile is a run of stages of up to 256 k (16 KB); a stage is [128-k half h][quad q][lane p][4 words],
-    word j of quad q holding k = 256s + 128h + 32q + 8j .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i], so one
-    lop3 per bf16x2 pair yields natural k order and a warp's 16-byte loads are contiguous. Scales: per stage
-    [lane p][h].
-bf16 (the shared expert): stages of 64 k laid out [k chunk c of 8][lane p][8 elements] -- the canonical K-major,
+    int4: each tile is a run of stages of 128 k (one scale group, 8 KB); a stage is [64-k half h][quad q][lane p]
+    [4 words], word j of quad q holding k = 128s + 64h + 32q + 8j .. +8 with nibble i = k index
+    [0,2,4,6,1,3,5,7][i], so one lop3 per bf16x2 pair yields natural k order and a warp's 16-byte loads are
+    contiguous. Scales: per stage [lane p] (128 bf16).
+bf16 (the shared expert): stages of 32 k laid out [k chunk c of 4][lane p][8 elements] -- the canonical K-major,
     no-swizzle tensor-core tile (8-row core matrices of 16-byte rows), used directly as the MMA's A operand.
 
 The CUDA entry points ``qf_w4_repack``/``qf_bf16_repack`` produce these layouts on the device; the ``*_torch``
@@ -70,9 +70,9 @@ def w4_word_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     o = torch.arange(N * K // 8, device=device, dtype=torch.int64)
     per_tile = 128 * K // 8
     r, ot = o // per_tile, o % per_tile
-    st, os_ = ot // 4096, ot % 4096
+    st, os_ = ot // 2048, ot % 2048
     j, rho, hq = os_ & 3, (os_ >> 2) & 127, os_ >> 9
-    kw = 32 * st + 16 * (hq >> 2) + 4 * (hq & 3) + j
+    kw = 16 * st + 8 * (hq >> 1) + 4 * (hq & 1) + j
     row = kernel_row_source(N, gated, device)[128 * r + rho]
     return row * (K // 8) + kw
 
@@ -81,12 +81,9 @@ def w4_scale_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     """Kernel-layout scale entry o -> canonical index row * (K/128) + group."""
     o = torch.arange(N * K // 128, device=device, dtype=torch.int64)
     r, ot = o // K, o % K
-    st = ot // 256
-    kc = torch.clamp(K - 256 * st, max=256)
-    os_ = ot - 256 * st
-    ngrp = kc // 128
-    row = kernel_row_source(N, gated, device)[128 * r + os_ // ngrp]
-    return row * (K // 128) + 2 * st + os_ % ngrp
+    st, rho = ot // 128, ot % 128
+    row = kernel_row_source(N, gated, device)[128 * r + rho]
+    return row * (K // 128) + st
 
 
 def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
@@ -94,9 +91,9 @@ def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     o = torch.arange(N * K, device=device, dtype=torch.int64)
     per_tile = 128 * K
     r, ot = o // per_tile, o % per_tile
-    st, os_ = ot >> 13, ot & 8191
+    st, os_ = ot >> 12, ot & 4095
     c, rho, el = os_ >> 10, (os_ >> 3) & 127, os_ & 7
-    k = 64 * st + 8 * c + el
+    k = 32 * st + 8 * c + el
     row = kernel_row_source(N, gated, device)[128 * r + rho]
     return row * K + k
 
@@ -136,8 +133,8 @@ def unpack_w4_torch(wk: torch.Tensor, sk: torch.Tensor, N: int, K: int, gated: b
 
 def repack_bf16_torch(w: torch.Tensor, gated: bool) -> torch.Tensor:
     N, K = w.shape
-    if N % 128 or K % 64:
-        raise RuntimeError(f"bf16 weight needs N % 128 == 0 and K % 64 == 0, got {N}x{K}")
+    if N % 128 or K % 32:
+        raise RuntimeError(f"bf16 weight needs N % 128 == 0 and K % 32 == 0, got {N}x{K}")
     return w.reshape(-1)[bf16_elem_map(N, K, gated, w.device)].contiguous()
 
 

@@ -14,6 +14,7 @@ from . import _lib
 from .formats import repack_bf16, repack_w4
 
 BF16 = torch.bfloat16
+DBG_NUMEL = 32 * 512          # QF_MOE_DBG_NUMEL: entries of the optional MoE timeline buffer
 
 
 def _req(cond: bool, msg: str):
@@ -129,6 +130,8 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
         _req(shared.dtype == BF16 and shared.is_contiguous() and tuple(shared.shape) == (M, H),
              f"{op}: shared must be contiguous bf16 [M, H]")
     _req(out.dtype == BF16 and tuple(out.shape) == (M, H) and out.is_contiguous(), f"{op}: out must be bf16 [M, H]")
+    _req(dbg is None or (dbg.is_cuda and dbg.dtype == torch.int64 and dbg.is_contiguous() and dbg.numel() >= DBG_NUMEL),
+         f"{op}: dbg must be a contiguous int64 CUDA tensor of at least {DBG_NUMEL} entries")
     lo, hi = (0, E) if expert_range is None else expert_range
     tensors = [topk_ids, topk_w, w13, s13, w2, s2, hbuf, ybuf, gl, ctrl, out]
     _req(all(t.device == x.device for t in tensors), f"{op}: every tensor must be on x's device")

@@ -42,3 +42,18 @@ def test_pack_unpack_int4_and_nibble_order():
     p = formats._nibble_perm(w, True)
     assert [(int(p) >> (4 * i)) & 0xF for i in range(8)] == [0, 2, 4, 6, 1, 3, 5, 7]
     assert torch.equal(formats._nibble_perm(p, False), w)
+
+
+def test_stage_layout_positions():
+    # int4: a stage is 128 k x 128 rows = 2048 words [half h][quad q][lane p][word j], k = 128s + 64h + 32q + 8j
+    N, K = 128, 256
+    wm = formats.w4_word_map(N, K, False)
+    s, h, q, p, j = 1, 1, 1, 5, 2
+    o = 2048 * s + 512 * (2 * h + q) + 4 * p + j
+    assert int(wm[o]) == p * (K // 8) + (16 * s + 8 * h + 4 * q + j)
+    # scales: [stage][lane]
+    sm = formats.w4_scale_map(N, K, False)
+    assert int(sm[128 * 1 + 5]) == 5 * (K // 128) + 1
+    # bf16: a stage is 32 k x 128 rows [chunk c][lane p][8 elements], k = 32s + 8c + el
+    bm = formats.bf16_elem_map(N, 64, False)
+    assert int(bm[4096 * 1 + 1024 * 2 + 8 * 3 + 4]) == 3 * 64 + (32 + 16 + 4)
