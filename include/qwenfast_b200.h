@@ -58,7 +58,7 @@ int qf_version(void);
  *   x bf16 [rows, hidden]; w bf16 [experts, hidden]; outputs topk_weights fp32 [rows, topk],
  *   topk_ids int32 [rows, topk], logits bf16 [rows, experts];
  *   scratch fp32 >= rows*experts; counter int32[1] zeroed once (re-armed by the kernel).
- * rows 1..QF_MAX_TOKENS, hidden % 256 == 0 (<= 8192), experts % 16 == 0 (<= QF_MAX_EXPERTS), topk 1..16.
+ * rows 1..QF_MAX_TOKENS, hidden % 256 == 0 (<= 4096), experts % 16 == 0 (<= QF_MAX_EXPERTS), topk 1..16.
  * ------------------------------------------------------------------------------------------------------------ */
 int qf_router_topk(const void* x, const void* w, int rows, int hidden, int experts, int topk, int renormalize,
                    float* topk_weights, int32_t* topk_ids, void* logits, float* scratch, int64_t scratch_numel,
