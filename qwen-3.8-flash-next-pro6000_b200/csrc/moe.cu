@@ -10,47 +10,40 @@
 // tensor cores in fp32 and then scaled once (exact products, no per-weight scale multiply).
 //
 // B200 structure
-//   * 2 CTAs per SM (296; the ordered queue needs no co-residency, so the grid is not cut to what the occupancy
-//     query reports), 12 warps each:
-//       warps 0..3   dequant warpgroup: stage in, token rows in, int4 -> bf16 into TMEM, hand-off to the MMA warps
-//       warps 4..7   readback warpgroup: stage partials out of TMEM, item epilogues, completion records
-//       warp 8       producer (lane 0)        warps 9, 10  MMA issuers (even / odd pipelined stages)
-//       warp 11      signal agent (lane 0)
-//     Every pipelined stage walks dequant -> MMA -> readback through NBUF job slots. Splitting dequant and
-//     readback over two warpgroups lets the two latency chains of a stage overlap instead of adding up. Roles
-//     that block on different mbarriers live in different warps: a lane suspended in mbarrier.try_wait holds up
-//     its whole warp. One thread issues a tcgen05.mma about every 60 cycles, so two issuers keep up.
-//   * Work items, claimed in order from a global queue:
+//   * One CTA per SM (148 on B200) running NVP = 3 independent pipelines. A pipeline is 6 warps: 4 consumer warps
+//     (one warpgroup, each thread owns one weight row of a 128-row tile), a producer warp (lane 0) and an MMA warp
+//     (lane 0 issues). One more warp (lane 0) is the signal agent of all three. The pipelines share the routing plan
+//     and the tensor-memory allocation (a 160-column slice each); everything else (ring, barriers, job slots) is
+//     per pipeline. Three pipelines per SM hide the latency of each stage's hand-offs (mbarrier, TMEM store / load,
+//     tcgen05.commit), which one pipeline alone cannot: a stage is a chain of such waits around the dequantisation.
+//   * Work items, claimed in order from a global queue by each pipeline's producer:
 //       GL  shared-expert gate logits          S1  shared gate_up tile, one of 4 k-splits, one 16-token group
 //       G1  expert u gate_up tile + group      S1F shared gate_up split-K sum + SwiGLU
 //       S2  shared down tile + group           G2  expert u down tile + group
 //       CB  top-k combine of one 128-column tile (+ gated shared term)
-//     An item only depends on items claimed before it, so the queue cannot deadlock.
+//     An item only depends on items claimed before it, by pipelines that are already running, so the queue cannot
+//     deadlock for any grid size.
 //   * The producer streams each item's weights through an NST-stage shared-memory ring with 1-D bulk copies (TMA
-//     engine, mbarrier completion): per stage 8 KB of weights (128 rows x 128 k int4, or x 32 k bf16) and, for
-//     int4, the stage's 128 row scales. Every cross-CTA dependency (gate_up -> down, split-K -> finalize -> shared
-//     down, all producers of a column tile -> combine) is acquired by the producer (bounded wait) before it marks
-//     the stage full, so consumers never spin on other CTAs.
-//   * The matching k-slice of the item's token rows (x for gate_up, h for down; at most 16 rows of 256 B) is copied
-//     by the consumers themselves, one 16-byte cp.async per thread straight into the B operand, one stage ahead:
-//     small per-row bulk copies would cost the single producer thread ~60 cycles of issue each, and a plain load in
-//     flight would be waited for by the stage's own fences and release arrives.
-//   * Consumers signal completed items through a CTA-local ring; the agent lane turns each record into one gpu-scope
-//     release (fence + atomic add) on the control block. Consumer warps never execute a gpu-scope fence.
-//   * Contraction on the 5th-generation tensor cores (tcgen05), software-pipelined two stages deep. int4 stages
-//     (128 rows x 128 k, one scale group): every consumer thread owns one TMEM lane (= one weight row) and the
-//     stage's whole k; it turns each int4 word into four bf16x2 of the signed codes
-//     (code - 8: one lop3 and one bf16x2 subtract each, exact) and stores them to TMEM (tcgen05.st) as the A
-//     operand, while the token rows land in the canonical K-major shared-memory B layout (N = 16). An MMA warp
-//     issues tcgen05.mma kind::f16 per k16 step (A in TMEM, B in SMEM, fp32 D in TMEM), then tcgen05.commit.
-//     A, B and D are triple-buffered: while the tensor cores run stages s-1 and s-2, the consumers dequantise
-//     stage s, then read back (tcgen05.ld) and scale stage s-2. Each stage writes its own D and the consumers
-//     add the stages up in registers in k order (all 16 tokens of the thread's row).
+//     engine, mbarrier completion): per stage 8 KB of weights (128 rows x 128 k int4, or x 32 k bf16) and, for int4,
+//     the stage's 128 row scales. Every cross-CTA dependency (gate_up -> down, split-K -> finalize -> shared down,
+//     all producers of a column tile -> combine) is acquired by the producer (bounded wait) before it marks the
+//     stage full, so consumers never spin on other CTAs. Item bases are computed once per item.
+//   * The consumers copy the matching k-slice of the item's token rows (x for gate_up, h for down; at most 16 rows
+//     of 256 B) themselves, one 16-byte cp.async per chunk straight into the B operand, one stage ahead.
+//   * Contraction on the 5th-generation tensor cores (tcgen05), double-buffered. int4 stages (128 rows x 128 k, one
+//     scale group): every consumer thread turns its row's 16 int4 words into bf16x2 of the signed codes (code - 8:
+//     one lop3 and one bf16x2 subtract each, exact) and stores them to TMEM (tcgen05.st) as the A operand, while
+//     the token rows land in the canonical K-major shared-memory B layout (N = 16). The MMA warp issues
+//     tcgen05.mma kind::f16 per k16 step (A in TMEM, B in SMEM, fp32 D in TMEM), then tcgen05.commit. While the
+//     tensor cores run stage s, the consumers dequantise stage s+1, then read back (tcgen05.ld) and scale stage s,
+//     adding the stages up in registers in k order (all 16 tokens of the thread's row).
 //     bf16 stages (shared expert, 32 k): the ring stage itself is the A operand (SMEM descriptor).
 //     gate_up tiles interleave gate row j (even lane) and up row j (odd lane): SwiGLU is one shuffle.
+//   * Consumers signal completed items through a per-pipeline record ring; the agent turns each record into one
+//     gpu-scope release (fence + atomic add) on the control block. Consumer warps never execute a gpu-scope fence.
 //   * The routing plan (unique experts, per-expert token lists, group offsets) is rebuilt identically by every CTA
 //     from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
-//   * Every wait is bounded (globaltimer); a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
+//   * Every wait is bounded; a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
 #include "qf_common.cuh"
 
 namespace {
@@ -60,14 +53,17 @@ using qf::bf16_hi;
 using qf::bf16_lo;
 using qf::bf16r;
 
-constexpr int NCW = 4;                        // warps per consumer warpgroup (128 threads = 128 weight rows)
-constexpr int MOE_THREADS = (2 * NCW + 4) * 32;   // dequant + readback warpgroups, producer, two MMA warps, agent
-constexpr int RB_WARP0 = NCW, PRODUCER_WARP = 2 * NCW, MMA_WARP0 = 2 * NCW + 1, AGENT_WARP = 2 * NCW + 3;
-constexpr int NBUF = 3;                       // A / B / D buffers of the pipelined stages
+constexpr int NCW = 4;                        // consumer warps of a pipeline (128 threads = 128 weight rows)
+constexpr int NVP = 3;                        // pipelines per CTA
+constexpr int VP_WARPS = NCW + 2;             // consumers, producer, MMA warp
+constexpr int VP_PRODUCER = NCW, VP_MMA = NCW + 1;
+constexpr int AGENT_WARP = NVP * VP_WARPS;
+constexpr int MOE_THREADS = (NVP * VP_WARPS + 1) * 32;
+constexpr int NBUF = 2;                       // A / B / D buffers of the pipelined stages (per pipeline)
 constexpr int CONS_THREADS = NCW * 32;
-constexpr int CTAS_PER_SM = 2;
+constexpr int CTAS_PER_SM = 1;
 constexpr int TG = 16;                        // tokens per token group (two n8 tiles)
-constexpr int NST = 10;                       // pipeline stages per CTA
+constexpr int NST = 7;                        // ring stages per pipeline
 constexpr int NEPI = 8;                       // completion-record ring
 constexpr int W4_KC = 128;                    // int4 k per stage (one scale group)
 constexpr int BF_KC = 32;                     // bf16 k per stage
@@ -100,9 +96,8 @@ struct StageDesc {
 struct EpiRec {     // one completion record: add `add` to ctrl[idx] (idx < 0: nothing; kind STOP ends the agent)
     int idx, add;
 };
-struct MmaJob {     // one pipelined stage (or a non-MMA item) passed from the dequant to the MMA and readback warps
-    StageDesc d;
-    int16_t ring, pad[3];
+struct MmaJob {     // what the MMA warp issues for one pipelined stage
+    int16_t kind, ring;
 };
 
 struct Params {
@@ -131,16 +126,17 @@ struct Params {
     int M, H, I, E, topk, Is, mode, elo, ehi;
 };
 
-// shared memory map (dynamic)
+// shared memory map (dynamic): NVP pipeline blocks, then the routing plan
 constexpr int BST_BYTES = TG * (W4_KC / 8) * 16;                      // B operand [k chunk][16 tokens][16 B]
-constexpr int OFF_RING = 0;
-constexpr int OFF_BST = OFF_RING + NST * STAGE_BYTES;
-constexpr int OFF_BAR = OFF_BST + NBUF * BST_BYTES;   // full, empty, efull, eempty, ab-ready, mma-done, d-free
-constexpr int OFF_DESC = OFF_BAR + (2 * NST + 2 * NEPI + 3 * NBUF) * 8;
-constexpr int OFF_EPI = OFF_DESC + NST * (int)sizeof(StageDesc);
-constexpr int OFF_JOB = OFF_EPI + NEPI * (int)sizeof(EpiRec);
-constexpr int OFF_SCS = OFF_JOB + NBUF * (int)sizeof(MmaJob);        // float [NBUF][128] row scales of the stages
-constexpr int OFF_PLAN = OFF_SCS + NBUF * 128 * 4;
+constexpr int VO_RING = 0;
+constexpr int VO_BST = VO_RING + NST * STAGE_BYTES;
+constexpr int VO_BAR = VO_BST + NBUF * BST_BYTES;                     // full, empty, efull, eempty, ab-ready, mma-done
+constexpr int VO_DESC = VO_BAR + (2 * NST + 2 * NEPI + 2 * NBUF) * 8;
+constexpr int VO_EPI = VO_DESC + NST * (int)sizeof(StageDesc);
+constexpr int VO_JOB = VO_EPI + NEPI * (int)sizeof(EpiRec);
+constexpr int VP_BYTES = (VO_JOB + NBUF * (int)sizeof(MmaJob) + 127) & ~127;
+constexpr int OFF_PLAN = NVP * VP_BYTES;
+static_assert(VO_BST % 128 == 0 && VO_BAR % 8 == 0 && VP_BYTES % 128 == 0, "shared memory alignment");
 constexpr int PLAN_ULIST = 0;                                         // int16 [QF_MAX_EXPERTS]
 constexpr int PLAN_GPRE = PLAN_ULIST + QF_MAX_EXPERTS * 2;            // int16 [QF_MAX_EXPERTS + 1]
 constexpr int PLAN_TOFF = PLAN_GPRE + (QF_MAX_EXPERTS + 8) * 2;
@@ -150,21 +146,22 @@ constexpr int PLAN_DUPN = PLAN_SIDS + MAXSLOTS * 2;                   // int16 [
 constexpr int PLAN_MISC = PLAN_DUPN + MAXSLOTS * 2;                   // int32 [64]
 constexpr int PLAN_BYTES = PLAN_MISC + 64 * 4;
 constexpr int MOE_SMEM = OFF_PLAN + PLAN_BYTES;
-static_assert(CTAS_PER_SM * (MOE_SMEM + 1024) <= 228 * 1024, "two CTAs per SM must fit in shared memory");
+static_assert(MOE_SMEM + 1024 <= 228 * 1024, "the CTA must fit in shared memory");
 // plan-build scratch aliases the ring (the producer starts after the plan is built)
 constexpr int SCR_MASK = 0;                                        // uint64 [E]
 constexpr int SCR_EXF = SCR_MASK + QF_MAX_EXPERTS * 8;             // int16 [E] x 3 (flag, count, groups) in-chunk
 constexpr int SCR_TOFFE = SCR_EXF + 3 * QF_MAX_EXPERTS * 2;        // int16 [E] token offset per expert id
 constexpr int SCR_CHUNK = SCR_TOFFE + QF_MAX_EXPERTS * 2;          // int32 [32] x 3 chunk totals
-static_assert(SCR_CHUNK + 3 * 32 * 4 <= NST * STAGE_BYTES, "plan scratch");
+static_assert(SCR_CHUNK + 3 * 32 * 4 <= NST * STAGE_BYTES, "plan scratch (pipeline 0's ring)");
 
 enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6 };
 
 // tensor memory map (columns of this CTA's allocation; fp32 / bf16x2 per 32-bit column, lane = tile row)
-constexpr uint32_t TM_COLS = 256;
+constexpr uint32_t TM_COLS = 512;
+constexpr uint32_t TM_VP = 160;    // columns per pipeline
 constexpr uint32_t TM_A = 0;       // NBUF x 64 columns: A tiles of 128-k int4 stages (8 k16 steps x 8 columns)
-constexpr uint32_t TM_D = 192;     // NBUF x 16 columns: fp32 partial of each stage
-static_assert(TM_D + NBUF * 16 <= TM_COLS && TM_A + NBUF * 64 <= TM_D, "tensor memory map");
+constexpr uint32_t TM_D = 128;     // NBUF x 16 columns: fp32 partial of each stage
+static_assert(TM_D + NBUF * 16 <= TM_VP && TM_A + NBUF * 64 <= TM_D && NVP * TM_VP <= TM_COLS, "tensor memory map");
 constexpr uint32_t IDESC = qf::idesc_bf16(128, TG);
 
 // Errors that stop the pipeline (waits that ran out). An out-of-range expert id is reported but not fatal: the
@@ -276,21 +273,8 @@ __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* si
     }
 }
 
-__global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint8_t* ring = smem + OFF_RING;
-    uint8_t* bst = smem + OFF_BST;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    uint64_t* empty = full + NST;
-    uint64_t* efull = empty + NST;
-    uint64_t* eempty = efull + NEPI;
-    uint64_t* abr = eempty + NEPI;      // [NBUF] A/B of a pipelined stage written (8 consumer warps arrive)
-    uint64_t* mmab = abr + NBUF;        // [NBUF] the stage's mmas completed (tcgen05.commit), or the job passed on
-    uint64_t* dfree = mmab + NBUF;      // [NBUF] the readback warps are done with the job's buffers (4 warps arrive)
-    float* scs = reinterpret_cast<float*>(smem + OFF_SCS);
-    StageDesc* desc = reinterpret_cast<StageDesc*>(smem + OFF_DESC);
-    EpiRec* epi = reinterpret_cast<EpiRec*>(smem + OFF_EPI);
-    MmaJob* jobs = reinterpret_cast<MmaJob*>(smem + OFF_JOB);
     uint8_t* plan = smem + OFF_PLAN;
     int16_t* ulist = reinterpret_cast<int16_t*>(plan + PLAN_ULIST);
     int16_t* gpre = reinterpret_cast<int16_t*>(plan + PLAN_GPRE);
@@ -304,24 +288,42 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
     const int M = p.M, E = p.E, topk = p.topk, nslots = M * topk;
     uint32_t* ctrl = p.ctrl;
 
+    // this warp's pipeline block (the agent warp uses all of them)
+    const int vp = warp < AGENT_WARP ? warp / VP_WARPS : 0;
+    const int vw = warp - vp * VP_WARPS;   // role within the pipeline: 0..3 consumers, VP_PRODUCER, VP_MMA
+    uint8_t* vb = smem + vp * VP_BYTES;
+    uint8_t* ring = vb + VO_RING;
+    uint8_t* bst = vb + VO_BST;
+    uint64_t* full = reinterpret_cast<uint64_t*>(vb + VO_BAR);
+    uint64_t* empty = full + NST;
+    uint64_t* efull = empty + NST;
+    uint64_t* eempty = efull + NEPI;
+    uint64_t* abr = eempty + NEPI;      // [NBUF] A/B of a pipelined stage written (the consumer warps arrive)
+    uint64_t* mmab = abr + NBUF;        // [NBUF] the stage's mmas completed (tcgen05.commit)
+    StageDesc* desc = reinterpret_cast<StageDesc*>(vb + VO_DESC);
+    EpiRec* epi = reinterpret_cast<EpiRec*>(vb + VO_EPI);
+    MmaJob* jobs = reinterpret_cast<MmaJob*>(vb + VO_JOB);
+
     if (tid == 0) {
-        for (int i = 0; i < NST; ++i) {
-            qf::mbar_init(full + i, 1);
-            qf::mbar_init(empty + i, NCW);
-        }
-        for (int i = 0; i < NEPI; ++i) {
-            qf::mbar_init(efull + i, NCW);
-            qf::mbar_init(eempty + i, 1);
-        }
-        for (int i = 0; i < NBUF; ++i) {
-            qf::mbar_init(abr + i, NCW);
-            qf::mbar_init(mmab + i, 1);
-            qf::mbar_init(dfree + i, NCW);
+        for (int v = 0; v < NVP; ++v) {
+            uint64_t* f = reinterpret_cast<uint64_t*>(smem + v * VP_BYTES + VO_BAR);
+            for (int i = 0; i < NST; ++i) {
+                qf::mbar_init(f + i, 1);             // full
+                qf::mbar_init(f + NST + i, NCW);     // empty
+            }
+            for (int i = 0; i < NEPI; ++i) {
+                qf::mbar_init(f + 2 * NST + i, NCW);          // efull
+                qf::mbar_init(f + 2 * NST + NEPI + i, 1);     // eempty
+            }
+            for (int i = 0; i < NBUF; ++i) {
+                qf::mbar_init(f + 2 * NST + 2 * NEPI + i, NCW);        // abr
+                qf::mbar_init(f + 2 * NST + 2 * NEPI + NBUF + i, 1);   // mmab
+            }
         }
         qf::mbar_fence_init();
         misc[MISC_DBGN] = 0;
     }
-    if (warp == 0) {   // tensor memory: one warp allocates for the CTA (two CTAs per SM take 256 columns each)
+    if (warp == 0) {   // tensor memory: one warp allocates the SM's 512 columns; pipeline v uses [160 v, 160 v + 160)
         qf::tmem_alloc(reinterpret_cast<uint32_t*>(misc + MISC_TMEM), TM_COLS);
         qf::tmem_relinquish();
     }
@@ -331,12 +333,12 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
 
     // ------------------------------------------------------------------ routing plan (all threads)
     {
-        uint64_t* mask = reinterpret_cast<uint64_t*>(ring + SCR_MASK);
-        int16_t* exf = reinterpret_cast<int16_t*>(ring + SCR_EXF);
+        uint64_t* mask = reinterpret_cast<uint64_t*>(smem + SCR_MASK);
+        int16_t* exf = reinterpret_cast<int16_t*>(smem + SCR_EXF);
         int16_t* exc = exf + QF_MAX_EXPERTS;
         int16_t* exg = exc + QF_MAX_EXPERTS;
-        int16_t* toffe = reinterpret_cast<int16_t*>(ring + SCR_TOFFE);
-        int* chunk = reinterpret_cast<int*>(ring + SCR_CHUNK);
+        int16_t* toffe = reinterpret_cast<int16_t*>(smem + SCR_TOFFE);
+        int* chunk = reinterpret_cast<int*>(smem + SCR_CHUNK);
         for (int e = tid; e < E; e += MOE_THREADS) mask[e] = 0ull;
         __syncthreads();
         bool bad = false;
@@ -416,7 +418,8 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
         __syncthreads();
     }
     qf::pdl_launch_dependents();
-    const uint32_t tmem = (uint32_t)misc[MISC_TMEM];
+    const uint32_t tmem_all = (uint32_t)misc[MISC_TMEM];
+    const uint32_t tmem = tmem_all + TM_VP * (uint32_t)vp;   // this pipeline's slice
 
     Layout L;
     L.R1 = (2 * p.I) / 128;
@@ -436,7 +439,54 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
     L.total = L.b_cb + L.R2;
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
 
-    if (warp == PRODUCER_WARP) {
+
+    if (warp == AGENT_WARP) {
+        if (lane == 0) {
+            // ========================================================== signal agent (one thread, all pipelines)
+            // Consumer warps arrive on efull[slot] of their pipeline after their item's global stores; this thread
+            // makes those stores visible at gpu scope (fence) and publishes the item's counter increment. It polls
+            // the pipelines' rings without blocking (a suspended wait on one ring would hold up the others).
+            int es0 = 0, es1 = 0, es2 = 0;
+            uint32_t eph0 = 0, eph1 = 0, eph2 = 0;
+            uint32_t alive = (1u << NVP) - 1u;
+            long long idle_since = clock64();
+            const long long idle_limit = (long long)(2 * PIPE_WAIT_NS);
+            while (alive != 0u) {
+                bool any = false;
+#pragma unroll
+                for (int v = 0; v < NVP; ++v) {
+                    if (!(alive & (1u << v))) continue;
+                    int& es = v == 0 ? es0 : (v == 1 ? es1 : es2);
+                    uint32_t& eph = v == 0 ? eph0 : (v == 1 ? eph1 : eph2);
+                    uint8_t* vbv = smem + v * VP_BYTES;
+                    uint64_t* ef = reinterpret_cast<uint64_t*>(vbv + VO_BAR) + 2 * NST;
+                    if (!qf::mbar_test_wait(ef + es, eph)) continue;
+                    const EpiRec r = reinterpret_cast<const EpiRec*>(vbv + VO_EPI)[es];
+                    if (r.idx == -2) {   // this pipeline's consumers stopped
+                        alive &= ~(1u << v);
+                    } else {
+                        if (r.idx >= 0) {
+                            __threadfence();
+                            atomicAdd(ctrl + r.idx, (uint32_t)r.add);
+                        }
+                        qf::mbar_arrive(ef + NEPI + es);
+                        if (++es == NEPI) { es = 0; eph ^= 1u; }
+                    }
+                    any = true;
+                }
+                if (any) {
+                    idle_since = clock64();
+                } else {
+                    if (clock64() - idle_since > idle_limit) {
+                        set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (vw == VP_PRODUCER) {
         if (lane == 0) {
             // ========================================================== producer (one thread)
             const uint64_t pol = qf::policy_evict_first();
@@ -554,213 +604,64 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             }
         }
         __syncwarp();
-    } else if (warp == AGENT_WARP) {
-        if (lane == 0) {
-            // ========================================================== signal agent (one thread)
-            // Consumer warps arrive on efull[slot] after their item's global stores; this thread then makes those
-            // stores visible at gpu scope (fence) and publishes the item's counter increment.
-            int es = 0;
-            uint32_t eph = 0;
-            for (;;) {
-                if (!qf::mbar_wait(efull + es, eph, PIPE_WAIT_NS)) {
-                    set_err(ctrl, QF_MOE_ERR_PIPELINE);
-                    break;
-                }
-                const EpiRec r = epi[es];
-                if (r.idx == -2) break;   // consumers stopped
-                if (r.idx >= 0) {
-                    __threadfence();
-                    atomicAdd(ctrl + r.idx, (uint32_t)r.add);
-                }
-                qf::mbar_arrive(eempty + es);
-                if (++es == NEPI) { es = 0; eph ^= 1u; }
-            }
-        }
-        __syncwarp();
-    } else if (warp == MMA_WARP0 || warp == MMA_WARP0 + 1) {
-        // ============================================================== MMA issuers (one lane issues)
-        // warp MMA_WARP0 + w takes the jobs s = w, w + 2, ...: slot s % NBUF, its (s / NBUF)-th use. Jobs without
-        // mmas (and the stop job) are passed on to the readback warps with a plain arrive.
-        // Descriptors advance by constants: one k16 step is 2 chunks of B (512 B, +32 in the 16-byte address
-        // field), 8 columns of an A tile in TMEM, or 2 chunks of a bf16 A stage (4096 B, +256).
+    } else if (vw == VP_MMA) {
+        // ============================================================== MMA issuer (one lane issues)
+        // stage s uses buffer s % NBUF, its (s / NBUF)-th use. Descriptors advance by constants: one k16 step is
+        // 2 chunks of B (512 B, +32 in the 16-byte address field), 8 columns of an A tile in TMEM, or 2 chunks of a
+        // bf16 A stage (4096 B, +256).
         const uint64_t bdesc0 = qf::smem_desc(bst, 256, 128);
         const uint64_t adesc0 = qf::smem_desc(ring, 2048, 128);
-        for (uint32_t s = (uint32_t)(warp - MMA_WARP0);; s += 2) {
-            const int b = (int)(s % NBUF);
-            if (!qf::mbar_wait(abr + b, (s / NBUF) & 1u, PIPE_WAIT_NS)) {
+        for (uint32_t s = 0;; ++s) {
+            const int b = (int)(s & 1u);
+            if (!qf::mbar_wait(abr + b, (s >> 1) & 1u, PIPE_WAIT_NS)) {
                 set_err(ctrl, QF_MOE_ERR_PIPELINE);
                 break;
             }
-            const int kind = jobs[b].d.kind;
+            const MmaJob job = jobs[b];
+            if (job.kind == K_STOP) break;
             if (lane == 0) {
-                if (kind == K_G1 || kind == K_G2) {
-                    qf::tc_fence_after();
-                    const uint64_t bd = bdesc0 + (uint64_t)(b * (BST_BYTES >> 4));
-                    const uint32_t dcol = tmem + TM_D + 16 * b, ta = tmem + TM_A + 64 * b;
+                qf::tc_fence_after();
+                const uint64_t bd = bdesc0 + (uint64_t)(b * (BST_BYTES >> 4));
+                const uint32_t dcol = tmem + TM_D + 16 * b;
+                if (job.kind == K_G1 || job.kind == K_G2) {
+                    const uint32_t ta = tmem + TM_A + 64 * b;
 #pragma unroll
                     for (int j = 0; j < W4_KC / 16; ++j) qf::mma_ts(dcol, ta + 8 * j, bd + 32 * j, IDESC, j != 0);
-                    qf::mma_commit(mmab + b);
-                } else if (kind == K_S1 || kind == K_S2) {
-                    qf::tc_fence_after();
-                    const uint64_t bd = bdesc0 + (uint64_t)(b * (BST_BYTES >> 4));
-                    const uint64_t ad = adesc0 + (uint64_t)(jobs[b].ring * (STAGE_BYTES >> 4));
-                    const uint32_t dcol = tmem + TM_D + 16 * b;
+                } else {
+                    const uint64_t ad = adesc0 + (uint64_t)(job.ring * (STAGE_BYTES >> 4));
 #pragma unroll
                     for (int j = 0; j < BF_KC / 16; ++j) qf::mma_ss(dcol, ad + 256 * j, bd + 32 * j, IDESC, j != 0);
-                    qf::mma_commit(mmab + b);
-                } else {
-                    qf::mbar_arrive(mmab + b);
                 }
+                qf::mma_commit(mmab + b);
             }
             __syncwarp();
-            if (kind == K_STOP) break;
         }
-    } else if (warp < NCW) {
-        // ============================================================== dequant warpgroup
-        const int ctid = tid;                 // 0..127
-        const int row = ctid;                 // tile row (= TMEM lane) owned by this thread
-        const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
-        // per-thread constant offsets: this thread's first 16-byte weight load and its scale in an int4 stage, its
-        // A columns in TMEM (slot 0)
+    } else {
+        // ============================================================== consumers (one warpgroup per pipeline)
+        // A warp reaches only the TMEM lanes of its hardware quarter (warp index % 4): pipeline 1's consumer warps
+        // (6..9) own quarters 2, 3, 0, 1. Rows follow the quarter; ctid is just a unique index within the group.
+        const int rw = vw;                    // 0..3: consumer warp within the pipeline
+        const int q4 = warp & 3;              // TMEM lane quarter
+        const int ctid = rw * 32 + lane;      // 0..127
+        const int row = 32 * q4 + lane;       // tile row (= TMEM lane) owned by this thread
+        const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
         const int woff = row * 16;
         const int soff = STAGE_W + row * 2;
         const uint32_t ta0 = tmem + lane_base + TM_A;
-        int st = 0;
-        uint32_t ph = 0;
-        uint32_t s = 0;   // jobs so far (identical in every thread of the CTA that counts them)
-        int b = 0;        // s % NBUF
-        // the slot of job s is free once the readback warps finished job s - NBUF (whose mmas had completed)
-        auto wait_free = [&]() {
-            if (s >= NBUF && !qf::mbar_wait(dfree + b, ((s / NBUF) + 1u) & 1u, PIPE_WAIT_NS))
-                set_err(ctrl, QF_MOE_ERR_PIPELINE);
-        };
-        auto next_job = [&]() {
-            ++s;
-            b = b == NBUF - 1 ? 0 : b + 1;
-        };
-        auto next_stage = [&]() {
-            if (++st == NST) { st = 0; ph ^= 1u; }
-        };
-        // stop: one stop job for each MMA warp (jobs s and s + 1); the readback warps stop at the first
-        auto push_stop = [&]() {
-            for (int i = 0; i < 2; ++i) {
-                wait_free();
-                if (ctid == 0) jobs[b].d.kind = (int16_t)K_STOP;
-                __syncwarp();
-                if (lane == 0) qf::mbar_arrive(abr + b);
-                next_job();
-            }
-        };
-        for (;;) {
-            if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
-                set_err(ctrl, QF_MOE_ERR_PIPELINE);
-                push_stop();
-                break;
-            }
-            const StageDesc d = desc[st];
-            if (d.kind == K_STOP) {
-                push_stop();
-                break;
-            }
-            const bool w4 = d.kind == K_G1 || d.kind == K_G2;
-            if (!w4 && d.kind != K_S1 && d.kind != K_S2) {
-                // item without mmas: one job carries it to the readback warps; its (empty) ring slot is free now
-                wait_free();
-                if (ctid == 0) {
-                    jobs[b].d = d;
-                    jobs[b].ring = (int16_t)st;
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    qf::mbar_arrive(empty + st);
-                    qf::mbar_arrive(abr + b);
-                }
-                next_job();
-                next_stage();
-                continue;
-            }
-            // ---------------------------------------------------------------- pipelined item: nk stages
-            const int nk = d.nk, kc = d.kc;
-            // token chunks: int4 stages have 16 tokens x 16 chunks (two per thread: tokens t/16 and 8 + t/16,
-            // chunk t % 16), bf16 stages 16 x 4 (threads 0..63: token t/4, chunk t % 4)
-            const int lg = w4 ? 4 : 2;   // log2 of the 16-byte chunks per token row of a stage
-            const int xn = ctid >> lg, xc = ctid & ((1 << lg) - 1);
-            const bool xact = xn < TG;
-            const int xdst = (xc * TG + xn) * 16;
-            const __nv_bfloat16* xrow = token_row(p, d, toff, tlist, xn);
-            const __nv_bfloat16* xrow2 = w4 ? token_row(p, d, toff, tlist, xn + 8) : nullptr;
-            const char* xsrc = xrow != nullptr ? reinterpret_cast<const char*>(xrow + 8 * xc)
-                                               : reinterpret_cast<const char*>(p.x);
-            const char* xsrc2 = xrow2 != nullptr ? reinterpret_cast<const char*>(xrow2 + 8 * xc)
-                                                 : reinterpret_cast<const char*>(p.x);
-            const uint32_t xbytes = xrow != nullptr ? 16u : 0u;   // 0: zero-fill (token beyond the item)
-            const uint32_t xbytes2 = xrow2 != nullptr ? 16u : 0u;
-            const int xstep = xrow != nullptr ? kc * 2 : 0;
-            const int xstep2 = xrow2 != nullptr ? kc * 2 : 0;
-            bool failed = false;
-            for (int kidx = 0;;) {
-                wait_free();
-                uint8_t* bb = bst + b * BST_BYTES;
-                if (xact) qf::cp_async16(bb + xdst, xsrc, xbytes);
-                if (w4) qf::cp_async16(bb + xdst + 8 * 16, xsrc2, xbytes2);
-                if (ctid == 0) {
-                    MmaJob j;
-                    j.d = d;
-                    j.d.kidx = (int16_t)kidx;
-                    j.ring = (int16_t)st;
-                    jobs[b] = j;
-                }
-                const uint8_t* sb = ring + st * STAGE_BYTES;
-                float sc = 1.f;
-                if (w4) {
-                    stage_w4_to_tmem(sb + woff, ta0 + 64 * b);
-                    sc = bf16_bits(*reinterpret_cast<const uint16_t*>(sb + soff));
-                }
-                scs[b * 128 + row] = sc;
-                qf::cp_async_wait_all();
-                qf::fence_proxy_async_smem();   // the tensor cores read bst through the async proxy
-                if (w4) qf::tmem_wait_st();
-                qf::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    if (w4) qf::mbar_arrive(empty + st);   // the stage now lives in TMEM (bf16: read by the mmas)
-                    qf::mbar_arrive(abr + b);
-                }
-                next_job();
-                next_stage();
-                if (++kidx == nk) break;
-                xsrc += xstep;
-                xsrc2 += xstep2;
-                if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
-                    set_err(ctrl, QF_MOE_ERR_PIPELINE);
-                    failed = true;
-                    break;
-                }
-            }
-            if (failed) {
-                push_stop();
-                break;
-            }
-        }
-    } else {
-        // ============================================================== readback warpgroup
-        const int rw = warp - RB_WARP0;       // 0..3: TMEM lane quarter
-        const int ctid = tid - RB_WARP0 * 32; // 0..127
-        const int row = ctid;                 // tile row (= TMEM lane) owned by this thread
-        const uint32_t td0 = tmem + ((uint32_t)(32 * rw) << 16) + TM_D;
-        int es = 0;
-        uint32_t eph = 0;
-        uint32_t s = 0;
-        int b = 0;
-        float acc[16];   // this thread's row, tokens 0..15
-        // optional timeline: (globaltimer << 12) | tag, up to 32 per CTA (tags: item kinds, 15 exit)
+        const uint32_t td0 = tmem + lane_base + TM_D;
+        int st = 0, es = 0;
+        uint32_t ph = 0, eph = 0;
+        uint32_t mcount = 0;    // pipelined stages so far (identical in the pipeline's consumer threads)
+        uint32_t mph = 0;       // bit b: phase of mmab[b] at its next wait
+        float acc[16];          // this thread's row, tokens 0..15
+        // optional timeline (pipeline 0 only): (globaltimer << 12) | tag, up to 32 per CTA
         auto stamp = [&](int tag) {
-            if (p.dbg != nullptr && ctid == 0 && blockIdx.x < QF_MOE_DBG_NUMEL / 32 && misc[MISC_DBGN] < 32) {
+            if (p.dbg != nullptr && vp == 0 && ctid == 0 && blockIdx.x < QF_MOE_DBG_NUMEL / 32 && misc[MISC_DBGN] < 32) {
                 p.dbg[blockIdx.x * 32 + misc[MISC_DBGN]] = (long long)((qf::globaltimer() << 12) | (uint64_t)tag);
                 misc[MISC_DBGN] += 1;
             }
         };
-        // hand one completion record to the agent (record written by thread 0; every readback warp arrives)
+        // hand one completion record to the agent (record written by thread 0; every consumer warp arrives)
         auto signal = [&](int idx, int add) {
             if (ctid == 0) {
                 if (!qf::mbar_wait(eempty + es, eph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
@@ -771,53 +672,135 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
             if (lane == 0) qf::mbar_arrive(efull + es);
             if (++es == NEPI) { es = 0; eph ^= 1u; }
         };
+        // wait for the mmas of the stage in buffer bq; free its ring slot (bf16 stages: the A operand lives there)
+        // and add its partial, times sc, for this thread's tokens
+        auto retire = [&](int bq, int ring_slot, float sc, int ntok) {
+            if (!qf::mbar_wait(mmab + bq, (mph >> bq) & 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
+            mph ^= 1u << bq;
+            qf::tc_fence_after();
+            if (ring_slot >= 0) {
+                __syncwarp();
+                if (lane == 0) qf::mbar_arrive(empty + ring_slot);
+            }
+            if (ntok > 8) {
+                uint32_t v[16];
+                qf::tmem_ld16(td0 + 16 * bq, v);
+                qf::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
+            } else {
+                uint32_t v[8];
+                qf::tmem_ld8(td0 + 16 * bq, v);
+                qf::tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
+            }
+            qf::tc_fence_before();
+        };
+        // stop the MMA warp (its next stage is mcount; nothing of this pipeline is in flight)
+        auto stop_mma = [&]() {
+            const int bq = (int)(mcount & 1u);
+            if (ctid == 0) jobs[bq].kind = (int16_t)K_STOP;
+            __syncwarp();
+            if (lane == 0) qf::mbar_arrive(abr + bq);
+        };
         for (;;) {
-            // job s: the dequant hand-off (job record and scales visible), then its mmas (or the pass-through)
-            const uint32_t par = (s / NBUF) & 1u;
-            if (!qf::mbar_wait(abr + b, par, PIPE_WAIT_NS) || !qf::mbar_wait(mmab + b, par, PIPE_WAIT_NS)) {
+            if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
                 set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                stop_mma();
                 signal(-2, 0);
                 break;
             }
-            const StageDesc d = jobs[b].d;
+            const StageDesc d = desc[st];
             if (d.kind == K_STOP) {
                 stamp(15);
+                stop_mma();
                 signal(-2, 0);
                 break;
             }
-            const bool mma = d.kind == K_G1 || d.kind == K_G2 || d.kind == K_S1 || d.kind == K_S2;
-            if (!mma || d.kidx == 0) {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-                stamp(d.kind);
-            }
-            if (mma) {
-                const float sc = scs[b * 128 + row];
-                qf::tc_fence_after();
-                if (d.ntok > 8) {
-                    uint32_t v[16];
-                    qf::tmem_ld16(td0 + 16 * b, v);
-                    qf::tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
-                } else {
-                    uint32_t v[8];
-                    qf::tmem_ld8(td0 + 16 * b, v);
-                    qf::tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
+            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+            stamp(d.kind);
+            const bool w4 = d.kind == K_G1 || d.kind == K_G2;
+            if (w4 || d.kind == K_S1 || d.kind == K_S2) {
+                // ---------------------------------------------------------------- pipelined item: nk stages
+                const int nk = d.nk, ntok = d.ntok, kc = d.kc;
+                // token chunks: int4 stages have 16 tokens x 16 chunks (two per thread: tokens t/16 and 8 + t/16,
+                // chunk t % 16), bf16 stages 16 x 4 (threads 0..63: token t/4, chunk t % 4)
+                const int lg = w4 ? 4 : 2;
+                const int xn = ctid >> lg, xc = ctid & ((1 << lg) - 1);
+                const bool xact = xn < TG;
+                const int xdst = (xc * TG + xn) * 16;
+                const __nv_bfloat16* xrow = token_row(p, d, toff, tlist, xn);
+                const __nv_bfloat16* xrow2 = w4 ? token_row(p, d, toff, tlist, xn + 8) : nullptr;
+                const char* xsrc = xrow != nullptr ? reinterpret_cast<const char*>(xrow + 8 * xc)
+                                                   : reinterpret_cast<const char*>(p.x);
+                const char* xsrc2 = xrow2 != nullptr ? reinterpret_cast<const char*>(xrow2 + 8 * xc)
+                                                     : reinterpret_cast<const char*>(p.x);
+                const uint32_t xbytes = xrow != nullptr ? 16u : 0u;   // 0: zero-fill (token beyond the item)
+                const uint32_t xbytes2 = xrow2 != nullptr ? 16u : 0u;
+                const int xstep = xrow != nullptr ? kc * 2 : 0;
+                const int xstep2 = xrow2 != nullptr ? kc * 2 : 0;
+                int bcur = (int)(mcount & 1u);
+                if (xact) qf::cp_async16(bst + bcur * BST_BYTES + xdst, xsrc, xbytes);
+                if (w4) qf::cp_async16(bst + bcur * BST_BYTES + xdst + 8 * 16, xsrc2, xbytes2);
+                // the previous pipelined stage of this item (its mmas may still run): buffer, ring slot, scale
+                bool pend = false;
+                int pb = 0, pr = -1;
+                float psc = 0.f;
+                bool failed = false;
+                for (int kidx = 0;;) {
+                    // buffer bcur was last read by the mmas of stage mcount - 2, already retired
+                    const uint8_t* sb = ring + st * STAGE_BYTES;
+                    float sc = 1.f;
+                    if (w4) {
+                        stage_w4_to_tmem(sb + woff, ta0 + 64 * bcur);
+                        sc = bf16_bits(*reinterpret_cast<const uint16_t*>(sb + soff));
+                    }
+                    qf::cp_async_wait_all();
+                    qf::fence_proxy_async_smem();   // the tensor cores read bst through the async proxy
+                    if (w4) qf::tmem_wait_st();
+                    qf::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (w4) qf::mbar_arrive(empty + st);   // the stage now lives in TMEM (bf16: read by the mmas)
+                        if (ctid == 0) {
+                            MmaJob j;
+                            j.kind = (int16_t)d.kind;
+                            j.ring = (int16_t)st;
+                            jobs[bcur] = j;
+                        }
+                        qf::mbar_arrive(abr + bcur);
+                    }
+                    if (pend) retire(pb, pr, psc, ntok);
+                    pend = true; pb = bcur; pr = w4 ? -1 : st; psc = sc;
+                    ++mcount;
+                    bcur ^= 1;
+                    if (++st == NST) { st = 0; ph ^= 1u; }
+                    if (++kidx == nk) break;
+                    // buffer bcur is free again (its stage was just retired): copy the next stage's token chunks
+                    xsrc += xstep;
+                    xsrc2 += xstep2;
+                    if (xact) qf::cp_async16(bst + bcur * BST_BYTES + xdst, xsrc, xbytes);
+                    if (w4) qf::cp_async16(bst + bcur * BST_BYTES + xdst + 8 * 16, xsrc2, xbytes2);
+                    if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
+                        set_err(ctrl, QF_MOE_ERR_PIPELINE);
+                        failed = true;
+                        break;
+                    }
                 }
-                qf::tc_fence_before();
+                retire(pb, pr, psc, ntok);
+                if (failed) {   // no mma of this pipeline is in flight any more: stop the MMA warp and the agent
+                    qf::cp_async_wait_all();
+                    stop_mma();
+                    signal(-2, 0);
+                    break;
+                }
+            } else {
+                __syncwarp();
+                if (lane == 0) qf::mbar_arrive(empty + st);
+                if (++st == NST) { st = 0; ph ^= 1u; }
             }
-            const int rslot = jobs[b].ring;
-            __syncwarp();
-            if (lane == 0) {
-                if (d.kind == K_S1 || d.kind == K_S2) qf::mbar_arrive(empty + rslot);   // the mmas read that slot
-                qf::mbar_arrive(dfree + b);
-            }
-            ++s;
-            b = b == NBUF - 1 ? 0 : b + 1;
-            if (mma && d.kidx != d.nk - 1) continue;
 
             // ------------------------------------------------------------ epilogues (item complete)
             // acc[i] = row `row`, token i
@@ -922,7 +905,7 @@ __global__ void __launch_bounds__(MOE_THREADS, CTAS_PER_SM) moe_persistent_kerne
     __syncthreads();
     if (warp == 0) {   // every mma this CTA issued has completed (each commit was waited for)
         qf::tc_fence_after();
-        qf::tmem_dealloc(tmem, TM_COLS);
+        qf::tmem_dealloc(tmem_all, TM_COLS);
     }
     if (tid == 0) {
         __threadfence();
@@ -1086,15 +1069,14 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute");
     static bool carveout_set[64] = {false};
     if (dev >= 64 || !carveout_set[dev]) {
-        // two CTAs per SM need the largest shared-memory carveout; without the hint the driver may pick a smaller one
+        // the CTA needs the largest shared-memory carveout; without the hint the driver may pick a smaller one
         ce = cudaFuncSetAttribute(reinterpret_cast<const void*>(moe_persistent_kernel),
                                   cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
         if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute (carveout)");
         if (dev < 64) carveout_set[dev] = true;
     }
-    // Grid: CTAS_PER_SM per SM (registers, shared memory and the 256 tensor-memory columns each CTA allocates all
-    // fit twice). The occupancy query reports one CTA per SM for this kernel, but residency is not required for
-    // correctness: an item only waits for items claimed before it, by CTAs that are already running.
+    // Grid: one CTA per SM (three pipelines each; the CTA allocates all 512 tensor-memory columns). Residency is not
+    // required for correctness: an item only waits for items claimed before it, by pipelines that are already running.
 
     Params p;
     p.x = static_cast<const __nv_bfloat16*>(x);
