@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--zipf", type=float, default=0.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", default="")
+    ap.add_argument("--sweep-configs", default="2,3", help="which sweep records to take (comma list of 2, 3)")
     return ap.parse_args()
 
 
@@ -383,7 +384,7 @@ def run_sweep(args):
     fraction of the measured HBM bandwidth. Written to ``args.sweep`` as a JSON list; one summary line per record."""
     import torch
     from qwenfast_b200 import build as qbuild
-    from qwenfast_b200 import ops, synthetic
+    from qwenfast_b200 import formats, ops, synthetic
 
     qbuild.build()
     dev = torch.device("cuda", 0)
@@ -413,14 +414,15 @@ def run_sweep(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
+    which = {int(c) for c in args.sweep_configs.split(",") if c.strip()}
     # ---------------------------------------------------------------- config 2: M sweep, Zipf routing, 48 layers
     cfg = synthetic.CONFIGS[1]
     NL = max(args.layers, 48)
     zipf = args.zipf if args.zipf > 0 else 1.1
-    layers = build_layers(cfg, NL, dev, zipf)
+    layers = build_layers(cfg, NL, dev, zipf) if 2 in which else None
     per_e = expert_bytes(cfg.H, cfg.I)
     shared_b = (3 * cfg.H * cfg.Is + cfg.H) * 2
-    for M in (1, 2, 4, 8, 16, 32, 64):
+    for M in (1, 2, 4, 8, 16, 32, 64) if 2 in which else ():
         bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, dev)
         rb = ops.router_bufs(dev)
         xs = [synthetic.make_tokens(cfg, M=M, device=dev, seed=7000 + l) for l in range(NL)]
@@ -460,12 +462,16 @@ def run_sweep(args):
 
     # ---------------------------------------------------------------- config 3: W8A8 GEMM, K = 2048
     K = synthetic.W8A8_K
-    for N in (2048, 4096, 8192, 12288):
+    for N in (2048, 4096, 8192, 12288) if 3 in which else ():
         copies = max(2, math.ceil(400e6 / (N * K)))   # > 3x the 126 MB L2 per cycle
-        ws = [synthetic.make_w8a8(N, K, device=dev, seed=10 + c) for c in range(copies)]
+        ws = []
+        for c in range(copies):
+            q, sw = synthetic.make_w8a8(N, K, device=dev, seed=10 + c)
+            ws.append((formats.repack_w8(q), sw))   # load-time repack to the kernel layout
+            del q
         for M in (1, 2, 4, 8, 10, 16):
             x = synthetic.make_w8a8_tokens(M, K, device=dev)
-            xq = torch.empty(M * K, dtype=torch.int8, device=dev)
+            xq = torch.empty(16 * K, dtype=torch.int8, device=dev)
             sx = torch.empty(M, dtype=torch.float32, device=dev)
 
             def gemms():
@@ -473,6 +479,8 @@ def run_sweep(args):
                     ops.w8a8_gemm(x, q, sw, xq=xq, sx=sx)
 
             ms = graph_time(gemms, reps=8)
+            if ops.w8a8_take_status():
+                raise RuntimeError(f"W8A8 kernel reported a wait timeout at N={N} M={M}")
             us = ms * 1e3 / copies
             b = N * K + 4 * N + 2 * M * K + 2 * M * N
             rec = {"config": 3, "N": N, "K": K, "M": M, "us_per_gemm": us, "bytes": b,

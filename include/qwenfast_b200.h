@@ -142,13 +142,32 @@ int qf_w8g_unpack(const int8_t* q, const void* s, void* w, int64_t rows, int K, 
  * W8A8 INT8 GEMM (no counterpart kernel in the reference; the dense projections of the synthetic config 3):
  *   sx[t] = absmax(x[t]) / 127 (1 for an all-zero row); xq = rint(x / sx) clamped to [-127, 127];
  *   acc = sum_k xq * q (exact int32 on tcgen05 tensor cores); y = bf16((float(acc) * sx[t]) * sw[n]).
- *   x bf16 [M, K] (row stride ldx); q int8 [N, K]; sw fp32 [N]; y bf16 [M, N] (row stride ldy);
- *   scratch: xq int8 [M*K], sx fp32 [M], acc int32 [M*N] (split-K accumulators, zeroed by the call);
- *   acc_out: optional int32 [M, N] copy of the exact accumulators (NULL to skip).
- *   M 1..16, K % 128 == 0, N % 128 == 0.
+ *   x bf16 [M, K] (row stride ldx); q int8: the weight [N, K] in the kernel layout of qf_w8_repack; sw fp32 [N];
+ *   y bf16 [M, N] (row stride ldy). Scratch, written: xq int8 [16 * K] = the quantised activations packed as the
+ *   tensor-core operand (element (t, k) at (k / 16) * 256 + t * 16 + k % 16; rows t >= M zero), sx fp32 [M].
+ *   acc: int32 split-K fixup buffer of qf_w8a8_fixup_elems(N) elements; zero-filled before its first use, every
+ *   call leaves it zero-filled again (after a non-zero qf_w8a8_take_status, zero it again). One buffer per
+ *   stream: calls that may run concurrently need their own. acc_out: optional int32 [M, N] copy of the exact
+ *   accumulators (NULL to skip). M 1..16, N % 128 == 0, K % 128 == 0 (<= 16384).
+ *   q is load-time data: the kernel requests weight tiles before griddepcontrol.wait, so q must not be written
+ *   by the kernel directly before it in the stream (synchronise after qf_w8_repack). Two launches: the
+ *   quantisation kernel, then the GEMM under programmatic dependent launch.
  * ------------------------------------------------------------------------------------------------------------ */
 int qf_w8a8_gemm(const void* x, int64_t ldx, const int8_t* q, const float* sw, void* y, int64_t ldy, int M, int N,
                  int K, int8_t* xq, float* sx, int32_t* acc, int32_t* acc_out, int pdl, qf_stream_t stream);
+/* W8A8 weight layout (load time): canonical q int8 [N, K] row-major -> qk, contiguous 16 KB tiles
+ * [N/128][K/128][128 rows][128 bytes] with each row's 16-byte k chunk c stored at position c ^ (row % 8) (the
+ * K-major 128-byte-swizzle operand layout of the tensor cores). qf_w8_unpack is the exact inverse.
+ * (No counterpart in the reference.) N % 128 == 0, K % 128 == 0. */
+/* Sticky device status of the W8A8 kernel since the last call (synchronises the device, then clears it):
+ * 0 = every bounded wait completed; bit 0 = a weight-ring wait ran out, bit 1 = a segment
+ * (accumulator) wait ran out, bit 2 = the final tensor-core wait ran out, bit 3 = the wait for the other runs of a
+ * split weight tile ran out (the affected outputs and the fixup buffer are undefined). */
+int qf_w8a8_take_status(uint32_t* status);
+/* Elements (int32) of the W8A8 split-K fixup buffer for an N-row weight. */
+int qf_w8a8_fixup_elems(int N, int64_t* elems);
+int qf_w8_repack(const int8_t* q, int8_t* qk, int N, int K, qf_stream_t stream);
+int qf_w8_unpack(const int8_t* qk, int8_t* q, int N, int K, qf_stream_t stream);
 
 #ifdef __cplusplus
 }

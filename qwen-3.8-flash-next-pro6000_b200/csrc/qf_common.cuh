@@ -17,6 +17,15 @@ int sm_count(int device);
 // cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device); later calls only read a cache, so
 // launches made during CUDA-graph capture issue no configuration API calls.
 cudaError_t ensure_smem_attr(const void* func, int bytes);
+// W8A8 contraction on tcgen05 (w8a8tc.cu), launched under PDL of the quantisation kernel: xq = its packed token
+// operand ([K / 16][16 tokens][16 B], tokens >= M zero), sx its scales; q in the kernel layout of qf_w8_repack;
+// fix = the zero-kept split-K fixup buffer of w8a8_fixup_elems(N) int32.
+size_t w8a8_fixup_elems(int N);
+cudaError_t launch_w8a8_tc(const int8_t* xq, const float* sx, const int8_t* q, const float* sw, void* y, int ldy,
+                           int32_t* acc_out, int32_t* fix, int M, int N, int K, cudaStream_t st);
+cudaError_t w8a8_tc_take_status(unsigned* out);
+// canonical [N, K] int8 <-> the W8A8 kernel layout (unpack = 1 for the inverse)
+cudaError_t launch_w8_repack(const int8_t* src, int8_t* dst, int N, int K, int unpack, cudaStream_t st);
 
 #define QF_REQUIRE(cond, ...)                                  \
     do {                                                       \
@@ -179,6 +188,10 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 // ---- named barrier over a subset of warps (non-.aligned form: callers may arrive from divergent code)
 __device__ __forceinline__ void named_bar(int id, int threads) {
     asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// Arrive on a named barrier without waiting for it (the producer side of a one-way hand-off).
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+    asm volatile("barrier.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // ---- tensor-core fragment op (register-sourced A): D += A(16x16 bf16) * B(16x8 bf16), fp32 accumulate

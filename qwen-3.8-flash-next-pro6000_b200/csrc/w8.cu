@@ -42,14 +42,6 @@ __device__ __forceinline__ void i8x4_bf16(uint32_t w, uint32_t& lo, uint32_t& hi
     hi = __byte_perm(__float_as_uint(f2), __float_as_uint(f3), 0x7632);
 }
 
-__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                       uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 // ------------------------------------------------------------------------------------------------ W8A16 (w8g)
 template <int NT>
 __global__ void __launch_bounds__(W8_THREADS)
@@ -160,12 +152,22 @@ __global__ void w8g_unpack_kernel(const int8_t* __restrict__ q, const uint16_t* 
 }
 
 // ------------------------------------------------------------------------------------------------ W8A8
-// One CTA per token row: absmax, sx = absmax / 127 (1 when the row is all zero), xq = rint(x / sx) clamped.
-__global__ void __launch_bounds__(256) w8a8_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
-                                                         int8_t* __restrict__ xq, float* __restrict__ sx) {
+// One CTA per token row of the 16-token operand: absmax, sx = absmax / 127 (1 when the row is all zero),
+// xq = rint(x / sx) clamped, stored packed as the tensor-core operand of the W8A8 kernel: element (t, k) at
+// (k / 16) * 256 + t * 16 + k % 16 ([16-byte k chunk][16 tokens][16 B]); rows t >= M are written as zeros.
+__global__ void __launch_bounds__(256) w8a8_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M, int K,
+                                                         int8_t* __restrict__ xqp, float* __restrict__ sx) {
     __shared__ float wmax[8];
     const int m = blockIdx.x, tid = threadIdx.x;
+    // the W8A8 GEMM that follows may become resident now and prefetch its weights; it reads xq / sx only after
+    // its own griddepcontrol.wait, i.e. after this grid has completed
+    qf::pdl_launch_dependents();
     qf::pdl_wait();
+    if (m >= M) {
+        for (int k = tid * 8; k < K; k += 256 * 8)
+            *reinterpret_cast<uint2*>(xqp + (size_t)(k >> 4) * 256 + m * 16 + (k & 15)) = make_uint2(0u, 0u);
+        return;
+    }
     const __nv_bfloat16* xr = x + (size_t)m * ldx;
     float mx = 0.f;
     for (int k = tid * 8; k < K; k += 256 * 8) {
@@ -183,7 +185,6 @@ __global__ void __launch_bounds__(256) w8a8_quant_kernel(const __nv_bfloat16* __
     for (int w = 0; w < 8; ++w) amax = fmaxf(amax, wmax[w]);
     const float scale = amax > 0.f ? __fdiv_rn(amax, 127.f) : 1.f;
     if (tid == 0) sx[m] = scale;
-    qf::pdl_launch_dependents();
     for (int k = tid * 8; k < K; k += 256 * 8) {
         const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
         const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
@@ -194,70 +195,7 @@ __global__ void __launch_bounds__(256) w8a8_quant_kernel(const __nv_bfloat16* __
             const int b = max(-127, min(127, __float2int_rn(__fdiv_rn(qf::bf16_hi(vv[j]), scale))));
             packed[j >> 1] |= ((uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8)) << (16 * (j & 1));
         }
-        *reinterpret_cast<uint2*>(xq + (size_t)m * K + k) = make_uint2(packed[0], packed[1]);
-    }
-}
-
-template <int NT>
-__global__ void __launch_bounds__(W8_THREADS)
-    w8a8_kernel(const int8_t* __restrict__ xq, const float* __restrict__ sx, const int8_t* __restrict__ q,
-                const float* __restrict__ sw, __nv_bfloat16* __restrict__ y, int ldy, int32_t* __restrict__ acc_out,
-                int M, int N, int K) {
-    __shared__ int red[W8_WARPS][16][NT * 8 + 1];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t = lane & 3;
-    const int row0 = blockIdx.x * 16;
-    const size_t ra = (size_t)min(row0 + g, N - 1), rb = (size_t)min(row0 + g + 8, N - 1);
-    const int nch = K / 64, cpw = (nch + W8_WARPS - 1) / W8_WARPS;
-    const int c0 = warp * cpw, c1 = min(c0 + cpw, nch);
-    int acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0;
-    bool waited = false;
-    for (int cb = c0; cb < c1; cb += CB) {
-        uint4 wa[CB], wb[CB];
-#pragma unroll
-        for (int i = 0; i < CB; ++i) {
-            const int c = cb + i;
-            if (c < c1) {
-                wa[i] = ldg_stream(q + ra * K + 64 * c + 16 * t);
-                wb[i] = ldg_stream(q + rb * K + 64 * c + 16 * t);
-            }
-        }
-        if (!waited) { qf::pdl_wait(); waited = true; }
-#pragma unroll
-        for (int i = 0; i < CB; ++i) {
-            const int c = cb + i;
-            if (c >= c1) break;
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const int tok = nt * 8 + g;
-                const uint4 xv = tok < M ? __ldcg(reinterpret_cast<const uint4*>(xq + (size_t)tok * K + 64 * c + 16 * t))
-                                         : make_uint4(0, 0, 0, 0);
-                mma_s8(acc[nt], wa[i].x, wb[i].x, wa[i].y, wb[i].y, xv.x, xv.y);
-                mma_s8(acc[nt], wa[i].z, wb[i].z, wa[i].w, wb[i].w, xv.z, xv.w);
-            }
-        }
-    }
-    if (!waited) qf::pdl_wait();
-    qf::pdl_launch_dependents();
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        red[warp][g][nt * 8 + 2 * t] = acc[nt][0];
-        red[warp][g][nt * 8 + 2 * t + 1] = acc[nt][1];
-        red[warp][g + 8][nt * 8 + 2 * t] = acc[nt][2];
-        red[warp][g + 8][nt * 8 + 2 * t + 1] = acc[nt][3];
-    }
-    __syncthreads();
-    for (int idx = tid; idx < 16 * M; idx += W8_THREADS) {
-        const int r = idx & 15, m = idx >> 4;
-        int v = 0;
-#pragma unroll
-        for (int w = 0; w < W8_WARPS; ++w) v += red[w][r][m];
-        if (row0 + r < N) {
-            const float f = __fmul_rn(__fmul_rn(__int2float_rn(v), __ldg(sx + m)), __ldg(sw + row0 + r));
-            y[(size_t)m * ldy + row0 + r] = __float2bfloat16(f);
-            if (acc_out) acc_out[(size_t)m * N + row0 + r] = v;
-        }
+        *reinterpret_cast<uint2*>(xqp + (size_t)(k >> 4) * 256 + m * 16 + (k & 15)) = make_uint2(packed[0], packed[1]);
     }
 }
 
@@ -267,13 +205,6 @@ cudaError_t launch_w8g(const void* x, int ldx, const int8_t* q, const void* s, v
     return qf::launch_ex(w8g_kernel<NT>, dim3((N + 15) / 16), dim3(W8_THREADS), 0, st, pdl,
                          static_cast<const __nv_bfloat16*>(x), ldx, q, static_cast<const uint16_t*>(s),
                          static_cast<__nv_bfloat16*>(y), ldy, M, N, K, G);
-}
-
-template <int NT>
-cudaError_t launch_w8a8(const int8_t* xq, const float* sx, const int8_t* q, const float* sw, void* y, int ldy,
-                        int32_t* acc_out, int M, int N, int K, cudaStream_t st) {
-    return qf::launch_ex(w8a8_kernel<NT>, dim3((N + 15) / 16), dim3(W8_THREADS), 0, st, true, xq, sx, q, sw,
-                         static_cast<__nv_bfloat16*>(y), ldy, acc_out, M, N, K);
 }
 
 }  // namespace
@@ -317,23 +248,46 @@ extern "C" int qf_w8g_unpack(const int8_t* q, const void* s, void* w, int64_t ro
 extern "C" int qf_w8a8_gemm(const void* x, int64_t ldx, const int8_t* q, const float* sw, void* y, int64_t ldy, int M,
                             int N, int K, int8_t* xq, float* sx, int32_t* acc, int32_t* acc_out, int pdl,
                             qf_stream_t stream) {
-    (void)acc;
-    QF_REQUIRE(x && q && sw && y && xq && sx, "w8a8_gemm: null pointer argument");
-    QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS, "w8a8_gemm: M must be in [1, %d], got %d", QF_MAX_TOKENS, M);
-    QF_REQUIRE(N >= 1 && K >= 64 && K % 64 == 0, "w8a8_gemm: K must be a multiple of 64, got %d", K);
-    QF_REQUIRE(ldx >= K && ldx % 8 == 0 && qf::aligned(x, 16), "w8a8_gemm: x needs a row stride %% 8 == 0 and 16-byte alignment");
-    QF_REQUIRE(ldy >= N && qf::aligned(q, 16) && qf::aligned(xq, 16), "w8a8_gemm: bad y stride or unaligned q / xq");
+    QF_REQUIRE(x && q && sw && y && xq && sx && acc, "w8a8_gemm: null pointer argument");
+    QF_REQUIRE(M >= 1 && M <= 16, "w8a8_gemm: M must be in [1, 16], got %d", M);
+    QF_REQUIRE(N >= 128 && N % 128 == 0, "w8a8_gemm: N must be a multiple of 128, got %d", N);
+    QF_REQUIRE(K >= 128 && K % 128 == 0 && K <= 16384, "w8a8_gemm: K must be a multiple of 128 in [128, 16384], got %d", K);
+    QF_REQUIRE(ldx >= K && ldx % 8 == 0 && ldx <= INT32_MAX && qf::aligned(x, 16),
+               "w8a8_gemm: x needs a row stride %% 8 == 0 and 16-byte alignment");
+    QF_REQUIRE(ldy >= N && ldy <= INT32_MAX && qf::aligned(q, 16) && qf::aligned(xq, 16) && qf::aligned(acc, 16),
+               "w8a8_gemm: bad y stride or unaligned q / xq / acc");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = qf::launch_ex(w8a8_quant_kernel, dim3(M), dim3(256), 0, st, pdl != 0,
-                                  static_cast<const __nv_bfloat16*>(x), (int)ldx, K, xq, sx);
+    cudaError_t e = qf::launch_ex(w8a8_quant_kernel, dim3(16), dim3(256), 0, st, pdl != 0,
+                                  static_cast<const __nv_bfloat16*>(x), (int)ldx, M, K, xq, sx);
     if (e != cudaSuccess) return qf::cuda_status(e, "w8a8_gemm: quant launch");
-    const int nt = (M + 7) / 8;
-    switch (nt) {
-        case 1: e = launch_w8a8<1>(xq, sx, q, sw, y, (int)ldy, acc_out, M, N, K, st); break;
-        case 2: e = launch_w8a8<2>(xq, sx, q, sw, y, (int)ldy, acc_out, M, N, K, st); break;
-        case 3:
-        case 4: e = launch_w8a8<4>(xq, sx, q, sw, y, (int)ldy, acc_out, M, N, K, st); break;
-        default: e = launch_w8a8<8>(xq, sx, q, sw, y, (int)ldy, acc_out, M, N, K, st); break;
-    }
+    // tcgen05 kind::i8, stream-K over 16 KB weight tiles (w8a8tc.cu), under programmatic dependent launch of the
+    // quantisation kernel: it becomes resident and requests its first weight tiles while that one runs
+    e = qf::launch_w8a8_tc(xq, sx, q, sw, y, (int)ldy, acc_out, acc, M, N, K, st);
     return qf::cuda_status(e, "w8a8_gemm: launch");
+}
+
+extern "C" int qf_w8a8_fixup_elems(int N, int64_t* elems) {
+    QF_REQUIRE(elems && N >= 128 && N % 128 == 0, "w8a8_fixup_elems: N must be a multiple of 128, got %d", N);
+    *elems = (int64_t)qf::w8a8_fixup_elems(N);
+    return QF_OK;
+}
+
+extern "C" int qf_w8_repack(const int8_t* q, int8_t* qk, int N, int K, qf_stream_t stream) {
+    QF_REQUIRE(q && qk, "w8_repack: null pointer argument");
+    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 128 && K % 128 == 0, "w8_repack: need N %% 128 == 0 and K %% 128 == 0");
+    return qf::cuda_status(qf::launch_w8_repack(q, qk, N, K, 0, reinterpret_cast<cudaStream_t>(stream)), "w8_repack: launch");
+}
+
+extern "C" int qf_w8_unpack(const int8_t* qk, int8_t* q, int N, int K, qf_stream_t stream) {
+    QF_REQUIRE(q && qk, "w8_unpack: null pointer argument");
+    QF_REQUIRE(N >= 128 && N % 128 == 0 && K >= 128 && K % 128 == 0, "w8_unpack: need N %% 128 == 0 and K %% 128 == 0");
+    return qf::cuda_status(qf::launch_w8_repack(qk, q, N, K, 1, reinterpret_cast<cudaStream_t>(stream)), "w8_unpack: launch");
+}
+
+extern "C" int qf_w8a8_take_status(uint32_t* status) {
+    QF_REQUIRE(status, "w8a8_take_status: null pointer argument");
+    unsigned v = 0;
+    const int rc = qf::cuda_status(qf::w8a8_tc_take_status(&v), "w8a8_take_status");
+    *status = v;
+    return rc;
 }

@@ -39,6 +39,10 @@ SIGNATURES = {
     "qf_w8g_gemm": [_p, _l, _p, _p, _p, _l, _i, _i, _i, _i, _i, _i, _p],
     "qf_w8g_unpack": [_p, _p, _p, _l, _i, _i, _p],
     "qf_w8a8_gemm": [_p, _l, _p, _p, _p, _l, _i, _i, _i, _p, _p, _p, _p, _i, _p],
+    "qf_w8_repack": [_p, _p, _i, _i, _p],
+    "qf_w8a8_take_status": [_p],
+    "qf_w8a8_fixup_elems": [_i, _p],
+    "qf_w8_unpack": [_p, _p, _i, _i, _p],
 }
 
 _lib = None

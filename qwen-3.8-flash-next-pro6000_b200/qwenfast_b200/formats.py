@@ -15,8 +15,11 @@ Kernel layout (one expert matrix [N, K]; ``gated`` for gate_up, where N = 2I row
 bf16 (the shared expert): stages of 32 k laid out [k chunk c of 4][lane p][8 elements] -- the canonical K-major,
     no-swizzle tensor-core tile (8-row core matrices of 16-byte rows), used directly as the MMA's A operand.
 
-The CUDA entry points ``qf_w4_repack``/``qf_bf16_repack`` produce these layouts on the device; the ``*_torch``
-functions here compute the same index maps with tensor ops (any device) and are used by the CPU tests.
+W8A8 weights (int8 [N, K]): contiguous 16 KB tiles [N/128][K/128][128 rows][128 B], each row's 16-byte k chunk c
+    stored at position c ^ (row % 8) -- the K-major 128-byte-swizzle operand layout of the tensor cores.
+
+The CUDA entry points ``qf_w4_repack``/``qf_bf16_repack``/``qf_w8_repack`` produce these layouts on the device; the
+``*_torch`` functions here compute the same index maps with tensor ops (any device) and are used by the CPU tests.
 """
 import ctypes
 
@@ -98,6 +101,17 @@ def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     return row * K + k
 
 
+def w8_byte_map(N: int, K: int, device=None) -> torch.Tensor:
+    """W8A8 kernel layout byte o -> canonical index n * K + k: contiguous 16 KB tiles [N/128][K/128][128 rows]
+    [128 bytes], the row's 16-byte k chunk c stored at position c ^ (row % 8) (K-major 128-byte swizzle)."""
+    o = torch.arange(N * K, device=device, dtype=torch.int64)
+    tile, within = o // 16384, o % 16384
+    r, ks = tile // (K // 128), tile % (K // 128)
+    rr, pos, b = within // 128, (within // 16) % 8, within % 16
+    c = pos ^ (rr % 8)
+    return (r * 128 + rr) * K + ks * 128 + c * 16 + b
+
+
 def _check_w4(qweight, scales):
     if qweight.dtype != torch.int32 or qweight.dim() != 3:
         raise RuntimeError("qweight must be int32 [E, N, K/8]")
@@ -142,6 +156,21 @@ def unpack_bf16_torch(wk: torch.Tensor, N: int, K: int, gated: bool) -> torch.Te
     w = torch.empty(N * K, dtype=wk.dtype, device=wk.device)
     w[bf16_elem_map(N, K, gated, wk.device)] = wk.reshape(-1)
     return w.view(N, K)
+
+
+def repack_w8_torch(q: torch.Tensor) -> torch.Tensor:
+    """Canonical int8 [N, K] -> W8A8 kernel layout (same shape and dtype, bytes permuted)."""
+    N, K = q.shape
+    if N % 128 or K % 128:
+        raise RuntimeError(f"W8A8 weight needs N % 128 == 0 and K % 128 == 0, got {N}x{K}")
+    return q.reshape(-1)[w8_byte_map(N, K, q.device)].view(N, K).contiguous()
+
+
+def unpack_w8_torch(qk: torch.Tensor) -> torch.Tensor:
+    N, K = qk.shape
+    q = torch.empty(N * K, dtype=qk.dtype, device=qk.device)
+    q[w8_byte_map(N, K, qk.device)] = qk.reshape(-1)
+    return q.view(N, K)
 
 
 # ------------------------------------------------------------------------------------ device (C ABI) versions
@@ -193,3 +222,28 @@ def unpack_bf16(wk: torch.Tensor, N: int, K: int, gated: bool) -> torch.Tensor:
     with torch.cuda.device(wk.device):
         _lib.check(_lib.load().qf_bf16_unpack(wk.data_ptr(), w.data_ptr(), N, K, int(gated), _stream(wk)), "bf16_unpack")
     return w
+
+
+def repack_w8(q: torch.Tensor) -> torch.Tensor:
+    """Canonical int8 [N, K] -> the W8A8 kernel layout on the GPU (``qf_w8_repack``); same shape, bytes permuted.
+    Synchronises the current stream when done (a load-time step)."""
+    _req_cuda(q)
+    if q.dtype != torch.int8 or q.dim() != 2:
+        raise RuntimeError("q must be int8 [N, K]")
+    N, K = q.shape
+    qk = torch.empty_like(q)
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.load().qf_w8_repack(q.data_ptr(), qk.data_ptr(), N, K, _stream(q)), "w8_repack")
+        # load-time step: the GEMM requests weight tiles before its griddepcontrol.wait, so the repacked weights
+        # must be complete before any GEMM launch that could follow this kernel directly
+        torch.cuda.current_stream(q.device).synchronize()
+    return qk
+
+
+def unpack_w8(qk: torch.Tensor) -> torch.Tensor:
+    _req_cuda(qk)
+    N, K = qk.shape
+    q = torch.empty_like(qk)
+    with torch.cuda.device(qk.device):
+        _lib.check(_lib.load().qf_w8_unpack(qk.data_ptr(), q.data_ptr(), N, K, _stream(qk)), "w8_unpack")
+    return q

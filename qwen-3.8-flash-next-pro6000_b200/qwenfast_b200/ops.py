@@ -231,12 +231,30 @@ def w8g_unpack(q: torch.Tensor, s: torch.Tensor, w: torch.Tensor):
                                              _stream(q.device)), op)
 
 
+_W8A8_FIXUP = {}
+
+
+def w8a8_fixup(N: int, device, stream=None) -> torch.Tensor:
+    """The zero-kept int32 split-K fixup buffer of the W8A8 GEMM for an N-row weight, one per (device, stream, N)."""
+    dev = torch.device(device)
+    st = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    key = (dev.index, st, N)
+    buf = _W8A8_FIXUP.get(key)
+    if buf is None:
+        n = ctypes.c_int64(0)
+        _lib.check(_lib.load().qf_w8a8_fixup_elems(N, ctypes.byref(n)), "w8a8_fixup_elems")
+        buf = _W8A8_FIXUP[key] = torch.zeros(n.value, dtype=torch.int32, device=dev)
+    return buf
+
+
 def w8a8_gemm(x: torch.Tensor, q: torch.Tensor, sw: torch.Tensor, xq: Optional[torch.Tensor] = None,
               sx: Optional[torch.Tensor] = None, acc_out: Optional[torch.Tensor] = None,
-              pdl: bool = True) -> torch.Tensor:
-    """W8A8: per-token int8 activations (absmax/127), per-channel fp32 weight scales, int32 accumulation.
-    Returns y bf16 [M, N]. ``xq`` int8 [M*K] / ``sx`` fp32 [M] scratch are allocated when not given; ``acc_out``
-    (int32 [M, N]) receives the exact accumulators when given."""
+              pdl: bool = True, fixup: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """W8A8: per-token int8 activations (absmax/127), per-channel fp32 weight scales, int32 accumulation on the
+    tensor cores. ``q`` is the int8 [N, K] weight in the kernel layout of ``formats.repack_w8`` (repacked once at
+    load time). Returns y bf16 [M, N], M <= 16. ``xq`` (int8 [16*K], the packed quantised activations) / ``sx``
+    (fp32 [M]) scratch are allocated when not given; ``acc_out`` (int32 [M, N]) receives the exact accumulators
+    when given; ``fixup`` is the zero-kept split-K buffer (``w8a8_fixup``; the current stream's by default)."""
     op = "w8a8_gemm"
     _cuda(x, "x", op)
     _req(x.dtype == BF16 and x.dim() == 2 and x.stride(1) == 1, f"{op}: x must be bf16 [M, K] with unit column stride")
@@ -245,14 +263,28 @@ def w8a8_gemm(x: torch.Tensor, q: torch.Tensor, sw: torch.Tensor, xq: Optional[t
     M, K = x.shape
     N = q.shape[0]
     if xq is None:
-        xq = torch.empty(M * K, dtype=torch.int8, device=x.device)
+        xq = torch.empty(16 * K, dtype=torch.int8, device=x.device)
+    _req(xq.dtype == torch.int8 and xq.numel() >= 16 * K, f"{op}: xq int8 [16*K]")
     if sx is None:
-        sx = torch.empty(M, dtype=torch.float32, device=x.device)
+        sx = torch.empty(max(M, 1), dtype=torch.float32, device=x.device)
     if acc_out is not None:
         _req(acc_out.dtype == torch.int32 and acc_out.numel() >= M * N, f"{op}: acc_out int32 [M, N]")
+    if fixup is None and N % 128 == 0:
+        fixup = w8a8_fixup(N, x.device)
     y = torch.empty(M, N, dtype=BF16, device=x.device)
     with torch.cuda.device(x.device):
         _lib.check(_lib.load().qf_w8a8_gemm(x.data_ptr(), x.stride(0), q.data_ptr(), sw.data_ptr(), y.data_ptr(), N,
-                                            M, N, K, xq.data_ptr(), sx.data_ptr(), None, _ptr(acc_out),
+                                            M, N, K, xq.data_ptr(), sx.data_ptr(), _ptr(fixup), _ptr(acc_out),
                                             int(bool(pdl)), _stream(x.device)), op)
     return y
+
+
+def w8a8_take_status() -> int:
+    """Sticky wait-timeout bits of the W8A8 kernel since the last call (0 = clean); clears them. After a non-zero
+    status the fixup buffers may hold partial sums, so the cached ones are zeroed again."""
+    v = ctypes.c_uint32(0)
+    _lib.check(_lib.load().qf_w8a8_take_status(ctypes.byref(v)), "w8a8_take_status")
+    if v.value:
+        for buf in _W8A8_FIXUP.values():
+            buf.zero_()
+    return v.value

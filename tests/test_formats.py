@@ -57,3 +57,13 @@ def test_stage_layout_positions():
     # bf16: a stage is 32 k x 128 rows [chunk c][lane p][8 elements], k = 32s + 8c + el
     bm = formats.bf16_elem_map(N, 64, False)
     assert int(bm[4096 * 1 + 1024 * 2 + 8 * 3 + 4]) == 3 * 64 + (32 + 16 + 4)
+
+
+@pytest.mark.parametrize("N,K", [(128, 128), (256, 2048), (384, 640)])
+def test_w8_layout_round_trip_and_swizzle(N, K):
+    q = torch.randint(-127, 128, (N, K), dtype=torch.int8)
+    qk = formats.repack_w8_torch(q)
+    assert torch.equal(formats.unpack_w8_torch(qk), q)
+    assert torch.equal(formats.w8_byte_map(N, K).sort().values, torch.arange(N * K))
+    # tile (0, 0): row 3's chunk 1 (k = 16..31) sits at position 1 ^ 3 = 2 of the row
+    assert torch.equal(qk.reshape(-1)[3 * 128 + 2 * 16: 3 * 128 + 3 * 16], q[3, 16:32])

@@ -8,7 +8,7 @@ import pytest
 import torch
 
 from oracle import w8_ref
-from qwenfast_b200 import ops, synthetic
+from qwenfast_b200 import formats, ops, synthetic
 
 pytestmark = pytest.mark.gpu
 
@@ -54,16 +54,21 @@ def test_w8a8_bit_exact(cuda, N, M):
     K = synthetic.W8A8_K
     q, sw = synthetic.make_w8a8(N, K, seed=N)
     x = synthetic.make_w8a8_tokens(M, K, seed=M)
-    xq = torch.empty(M * K, dtype=torch.int8, device=cuda)
+    xq = torch.empty(16 * K, dtype=torch.int8, device=cuda)
     sx = torch.empty(M, dtype=torch.float32, device=cuda)
     acc = torch.empty(M, N, dtype=torch.int32, device=cuda)
-    y = ops.w8a8_gemm(x.to(cuda), q.to(cuda), sw.to(cuda), xq=xq, sx=sx, acc_out=acc)
+    qk = formats.repack_w8(q.to(cuda))
+    y = ops.w8a8_gemm(x.to(cuda), qk, sw.to(cuda), xq=xq, sx=sx, acc_out=acc)
     torch.cuda.synchronize()
     yr, accr, xqr, sxr = w8_ref.w8a8_ref(x, q, sw)
     assert torch.equal(sx.cpu(), sxr)
-    assert torch.equal(xq.view(M, K).cpu(), xqr)
+    # packed operand: element (t, k) at (k / 16) * 256 + t * 16 + k % 16, rows t >= M zero
+    xq16 = xq.view(K // 16, 16, 16).permute(1, 0, 2).reshape(16, K).cpu()
+    assert torch.equal(xq16[:M], xqr)
+    assert not xq16[M:].any()
     assert torch.equal(acc.cpu().long(), accr)
     assert torch.equal(y.cpu(), yr)
+    assert ops.w8a8_take_status() == 0
 
 
 def test_w8a8_zero_row_and_outliers(cuda):
@@ -73,7 +78,36 @@ def test_w8a8_zero_row_and_outliers(cuda):
     x[1] = 0
     x[2, 17] = 3000.0
     acc = torch.empty(4, N, dtype=torch.int32, device=cuda)
-    y = ops.w8a8_gemm(x.to(cuda), q.to(cuda), sw.to(cuda), acc_out=acc)
+    y = ops.w8a8_gemm(x.to(cuda), formats.repack_w8(q.to(cuda)), sw.to(cuda), acc_out=acc)
     yr, accr, _, _ = w8_ref.w8a8_ref(x, q, sw)
     assert torch.equal(acc.cpu().long(), accr) and torch.equal(y.cpu(), yr)
     assert (y[1] == 0).all()
+
+
+def test_w8_repack_matches_torch_and_round_trips(cuda):
+    q, _ = synthetic.make_w8a8(384, 640, seed=5)
+    qk = formats.repack_w8(q.to(cuda))
+    assert torch.equal(qk.cpu(), formats.repack_w8_torch(q))
+    assert torch.equal(formats.unpack_w8(qk).cpu(), q)
+
+
+def test_w8a8_rejects_large_m(cuda):
+    q, sw = synthetic.make_w8a8(256, 256, seed=6)
+    x = synthetic.make_w8a8_tokens(17, 256, seed=6)
+    with pytest.raises(RuntimeError, match="M must be"):
+        ops.w8a8_gemm(x.to(cuda), formats.repack_w8(q.to(cuda)), sw.to(cuda))
+
+
+@pytest.mark.parametrize("N,K,M", [(384, 640, 3), (128, 16384, 2), (1280, 4096, 16), (256, 128, 1),
+                                   (16384, 2048, 4), (2560, 8192, 5)])
+def test_w8a8_shapes_split_k(cuda, N, K, M):
+    """The stream-K partition: odd k-tile counts, the largest K (128 runs share one tile), runs that cross tile
+    boundaries with full M, runs longer than a tile, a single tile."""
+    q, sw = synthetic.make_w8a8(N, K, seed=N + K)
+    x = synthetic.make_w8a8_tokens(M, K, seed=M + 7)
+    acc = torch.empty(M, N, dtype=torch.int32, device=cuda)
+    y = ops.w8a8_gemm(x.to(cuda), formats.repack_w8(q.to(cuda)), sw.to(cuda), acc_out=acc)
+    yr, accr, _, _ = w8_ref.w8a8_ref(x, q, sw)
+    assert torch.equal(acc.cpu().long(), accr)
+    assert torch.equal(y.cpu(), yr)
+    assert ops.w8a8_take_status() == 0
