@@ -83,18 +83,24 @@ def moe_rounded(x, topk_ids, topk_w, w13, s13, w2, s2, gs13=None, gs2=None,
         acc2 = h @ dequant_int4(w2[e], s2[e]).T
         tw = bf16r(g2 * bf16r(topk_w[toks, kps].float()))
         y[toks, kps] = bf16r(bf16r(acc2) * tw[:, None])
-    acc = y[:, 0].clone()
-    for kp in range(1, k):
-        acc = acc + y[:, kp]
-    routed = bf16r(acc)
     if shared_w is not None:
         shared = shared_expert_bf16(x, *shared_w)
-    if shared is not None:
-        gate = torch.sigmoid(shared_gate_logits(x, w_gate))
-        out = (gate[:, None] * shared.float() + routed).to(torch.bfloat16)
-    else:
-        out = routed.to(torch.bfloat16)
+    out = combine_slots(x, y, shared, w_gate)
     return (out, y.to(torch.bfloat16)) if return_slots else out
+
+
+def combine_slots(x, y, shared=None, w_gate=None):
+    """The combine (qf_a16moe.cu:449-461): fp32 sum of the slot outputs y [M, k, H] in top-k order, rounded to bf16,
+    then ``bf16(sigmoid(x . w_gate) * shared + routed)`` when a shared term is given."""
+    y = y.float()
+    acc = y[:, 0].clone()
+    for kp in range(1, y.shape[1]):
+        acc = acc + y[:, kp]
+    routed = bf16r(acc)
+    if shared is None:
+        return routed.to(torch.bfloat16)
+    gate = torch.sigmoid(shared_gate_logits(x, w_gate))
+    return (gate[:, None] * shared.float() + routed).to(torch.bfloat16)
 
 
 def moe_truth(x, topk_ids, topk_w, w13, s13, w2, s2, gs13=None, gs2=None,

@@ -124,6 +124,7 @@ struct Params {
     __nv_bfloat16* out;
     long long* dbg;
     int M, H, I, E, topk, Is, mode, elo, ehi;
+    int wofs;   // expert id of the first expert in w13 / s13 / w2 / s2 / gs13 / gs2 (mode 1: elo)
 };
 
 // shared memory map (dynamic): NVP pipeline blocks, then the routing plan
@@ -227,6 +228,61 @@ __device__ __forceinline__ void stage_w4_to_tmem(const uint8_t* w, uint32_t ta) 
     }
 }
 
+// Shared-expert gate logit of one token, x[t] . w_gate in fp32: lane-strided fma chain over 16-byte chunks, then an
+// xor-tree warp sum (every lane returns it). One definition for the layer kernel and the expert-parallel combine,
+// so both produce the same bits.
+__device__ __forceinline__ float gate_logit(const __nv_bfloat16* xrow, const __nv_bfloat16* wgate, int H, int lane) {
+    const uint4* xr = reinterpret_cast<const uint4*>(xrow);
+    const uint4* wr = reinterpret_cast<const uint4*>(wgate);
+    float a = 0.f;
+    for (int i = lane; i < H / 8; i += 32) {
+        const uint4 xv = __ldcg(xr + i), wv = __ldg(wr + i);
+        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            a = fmaf(bf16_lo(xx[j]), bf16_lo(ww[j]), a);
+            a = fmaf(bf16_hi(xx[j]), bf16_hi(ww[j]), a);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    return a;
+}
+
+// Add 8 bf16 slot values (one 16-byte word) to the fp32 column sums.
+__device__ __forceinline__ void add8(float (&a)[8], uint4 v) {
+    const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        a[2 * j] += bf16_lo(vv[j]);
+        a[2 * j + 1] += bf16_hi(vv[j]);
+    }
+}
+// out = bf16(gate * shared + bf16(a)) for 8 columns (gate applied when has_gate), where a = the fp32 sum of the
+// routed slots in top-k order: the reference's combine rounding points (qf_a16moe.cu:449-461).
+__device__ __forceinline__ uint4 finish8(const float (&a)[8], bool has_gate, float gl, uint4 sv) {
+    float r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = bf16r(a[j]);
+    if (has_gate) {
+        const float gate = 1.f / (1.f + __expf(-gl));
+        const uint32_t ss[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            r[2 * j] = fmaf(gate, bf16_lo(ss[j]), r[2 * j]);
+            r[2 * j + 1] = fmaf(gate, bf16_hi(ss[j]), r[2 * j + 1]);
+        }
+    }
+    uint4 o;
+    uint32_t* op = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        __nv_bfloat162 b2 = __floats2bfloat162_rn(r[2 * j], r[2 * j + 1]);
+        op[j] = *reinterpret_cast<uint32_t*>(&b2);
+    }
+    return o;
+}
+
 // Combine of one 128-column tile for all tokens: out = bf16(gate * shared + bf16(sum_kpos y)), 8 columns a thread.
 __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int ctid) {
     const int H = p.H, topk = p.topk;
@@ -239,37 +295,37 @@ __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* si
             const int s = t * topk + kp;
             const int e = sids[s];
             if (e < 0 || e < p.elo || e >= p.ehi) continue;
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n));
-            const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                a[2 * j] += bf16_lo(vv[j]);
-                a[2 * j + 1] += bf16_hi(vv[j]);
-            }
+            add8(a, __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n)));
         }
-        float r[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) r[j] = bf16r(a[j]);
+        uint4 sv = make_uint4(0u, 0u, 0u, 0u);
+        float gl = 0.f;
         if (L.has_gate) {
-            const float gate = 1.f / (1.f + __expf(-__ldcg(p.gl + t)));
-            uint4 sv;
+            gl = __ldcg(p.gl + t);
             if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
             else sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
-            const uint32_t ss[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                r[2 * j] = fmaf(gate, bf16_lo(ss[j]), r[2 * j]);
-                r[2 * j + 1] = fmaf(gate, bf16_hi(ss[j]), r[2 * j + 1]);
-            }
         }
-        uint4 o;
-        uint32_t* op = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            __nv_bfloat162 b2 = __floats2bfloat162_rn(r[2 * j], r[2 * j + 1]);
-            op[j] = *reinterpret_cast<uint32_t*>(&b2);
+        *reinterpret_cast<uint4*>(p.out + (size_t)t * H + n) = finish8(a, L.has_gate != 0, gl, sv);
+    }
+}
+
+// Expert-parallel shard (mode 1), one 128-column tile: make ybuf the shard's exact contribution to the slot sum --
+// zeros in every slot this shard does not own (other shards' experts, invalid ids), and the shared expert's output
+// in rows M * topk + t when this shard computes it (zeros otherwise). The routed slots of local experts were
+// written by the down-projection epilogues.
+__device__ void shard_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int ctid) {
+    const int H = p.H, topk = p.topk;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    for (int q = ctid; q < p.M * 16; q += CONS_THREADS) {
+        const int t = q >> 4, n = 128 * c + 8 * (q & 15);
+        for (int kp = 0; kp < topk; ++kp) {
+            const int s = t * topk + kp;
+            const int e = sids[s];
+            if (e < 0 || e < p.elo || e >= p.ehi) *reinterpret_cast<uint4*>(p.ybuf + (size_t)s * H + n) = zero;
         }
-        *reinterpret_cast<uint4*>(p.out + (size_t)t * H + n) = o;
+        uint4 sv = zero;
+        if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
+        else if (p.shared != nullptr) sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
+        *reinterpret_cast<uint4*>(p.ybuf + (size_t)(p.M * topk + t) * H + n) = sv;
     }
 }
 
@@ -564,8 +620,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     const int N = down ? p.H : 2 * p.I;
                     d.kc = (int16_t)W4_KC;
                     bytes = STAGE_W + STAGE_S;
-                    wsrc = (down ? p.w2 : p.w13) + (size_t)e * ((size_t)N * K / 2) + (size_t)tile * (128 * (size_t)K / 2);
-                    ssrc = (down ? p.s2 : p.s13) + (size_t)e * ((size_t)N * K / 128) + (size_t)tile * K;
+                    wsrc = (down ? p.w2 : p.w13) + (size_t)(e - p.wofs) * ((size_t)N * K / 2) + (size_t)tile * (128 * (size_t)K / 2);
+                    ssrc = (down ? p.s2 : p.s13) + (size_t)(e - p.wofs) * ((size_t)N * K / 128) + (size_t)tile * K;
                     if (down) { dep_idx = C_DONE + u; dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])); }
                 } else if (kind == K_S1 || kind == K_S2) {
                     const bool down = kind == K_S2;
@@ -806,20 +862,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             // acc[i] = row `row`, token i
             if (d.kind == K_GL) {
                 for (int tok = rw; tok < M; tok += NCW) {
-                    const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)tok * p.H);
-                    const uint4* wr = reinterpret_cast<const uint4*>(p.wgate);
-                    float a = 0.f;
-                    for (int i = lane; i < p.H / 8; i += 32) {
-                        const uint4 xv = __ldcg(xr + i), wv = __ldg(wr + i);
-                        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            a = fmaf(bf16_lo(xx[j]), bf16_lo(ww[j]), a);
-                            a = fmaf(bf16_hi(xx[j]), bf16_hi(ww[j]), a);
-                        }
-                    }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                    const float a = gate_logit(p.x + (size_t)tok * p.H, p.wgate, p.H, lane);
                     if (lane == 0) p.gl[tok] = a;
                 }
                 signal(C_GLF, 1);
@@ -843,7 +886,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 int tbase = 0;
                 if (d.kind == K_G1) {
                     const int e = ulist[d.u];
-                    gs = p.gs13 ? bf16_bits(p.gs13[e]) : 1.f;
+                    gs = p.gs13 ? bf16_bits(p.gs13[e - p.wofs]) : 1.f;
                     tbase = toff[d.u] + TG * d.tg;
                 }
 #pragma unroll
@@ -872,7 +915,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 signal(C_SPLIT + d.tile * L.ngs + d.tg, 1);
             } else if (d.kind == K_G2) {
                 const int u = d.u, e = ulist[u];
-                const float g2 = p.gs2 ? bf16_bits(p.gs2[e]) : 1.f;
+                const float g2 = p.gs2 ? bf16_bits(p.gs2[e - p.wofs]) : 1.f;
                 const int n0 = 128 * d.tile + row;
                 const int tbase = toff[u] + TG * d.tg;
 #pragma unroll
@@ -895,7 +938,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_CB) {
                 // the producer acquired every producer of this tile (and the gate logits) before publishing it
-                combine_tile(p, L, sids, d.tile, ctid);
+                if (p.mode == 0) combine_tile(p, L, sids, d.tile, ctid);
+                else shard_tile(p, L, sids, d.tile, ctid);
                 signal(-1, 0);
             }
         }
@@ -1004,6 +1048,37 @@ __global__ void bf16_repack_kernel(const uint16_t* __restrict__ src, uint16_t* _
     }
 }
 
+// Expert-parallel finish, one CTA per token: ybuf = the shards' slot buffers summed (each slot has exactly one
+// owner, so the sum is exact), laid out as in mode 1; out = the mode-0 combine of it, bit for bit (same gate logit
+// and combine arithmetic; the zero slots of other shards add exactly nothing).
+constexpr int COMBINE_THREADS = 256;
+__global__ void __launch_bounds__(COMBINE_THREADS) moe_combine_kernel(const __nv_bfloat16* __restrict__ ybuf,
+                                                                      const __nv_bfloat16* __restrict__ x,
+                                                                      const __nv_bfloat16* __restrict__ wgate,
+                                                                      bool has_shared, __nv_bfloat16* __restrict__ out,
+                                                                      int M, int H, int topk) {
+    __shared__ float s_gl;
+    const int t = blockIdx.x, tid = threadIdx.x;
+    qf::pdl_wait();
+    if (has_shared && tid < 32) {
+        const float a = gate_logit(x + (size_t)t * H, wgate, H, tid);
+        if (tid == 0) s_gl = a;
+    }
+    __syncthreads();
+    qf::pdl_launch_dependents();
+    const float gl = has_shared ? s_gl : 0.f;
+    for (int n = 8 * tid; n < H; n += 8 * COMBINE_THREADS) {
+        float a[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] = 0.f;
+        for (int kp = 0; kp < topk; ++kp)
+            add8(a, __ldcg(reinterpret_cast<const uint4*>(ybuf + (size_t)(t * topk + kp) * H + n)));
+        const uint4 sv = has_shared ? __ldcg(reinterpret_cast<const uint4*>(ybuf + (size_t)(M * topk + t) * H + n))
+                                    : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(out + (size_t)t * H + n) = finish8(a, has_shared, gl, sv);
+    }
+}
+
 }  // namespace
 
 
@@ -1035,7 +1110,8 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
                "a16_moe_decode: null pointer argument");
     QF_REQUIRE(phase == 3 || phase == 4,
                "a16_moe_decode: phase must be 3 or 4 (whole layer); split phases 1/2 are not provided, got %d", phase);
-    QF_REQUIRE(mode == 0, "a16_moe_decode: mode %d not available (0 = full layer)", mode);
+    QF_REQUIRE(mode == 0 || mode == 1, "a16_moe_decode: mode must be 0 (full layer) or 1 (expert-parallel shard), got %d",
+               mode);
     QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS, "a16_moe_decode: M must be in [1, %d], got %d", QF_MAX_TOKENS, M);
     QF_REQUIRE(H >= 128 && H % 256 == 0 && H <= 8192, "a16_moe_decode: H must be a multiple of 256 in [256, 8192], got %d", H);
     QF_REQUIRE(I >= 128 && I % 128 == 0 && I <= 8192, "a16_moe_decode: I must be a multiple of 128, got %d", I);
@@ -1103,14 +1179,27 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     p.dbg = reinterpret_cast<long long*>(dbg);
     p.M = M; p.H = H; p.I = I; p.E = E; p.topk = topk; p.Is = has_shw ? Is : 0;
     p.mode = mode; p.elo = expert_lo; p.ehi = expert_hi;
+    p.wofs = mode == 1 ? expert_lo : 0;
     ce = qf::launch_ex(moe_persistent_kernel, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,
                        reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);
     return qf::cuda_status(ce, "a16_moe_decode: launch");
 }
 
-extern "C" int qf_moe_combine(const void*, const void*, const void*, int, void*, int, int, int, int, qf_stream_t) {
-    qf::set_error("moe_combine: expert-parallel combine not available in this build");
-    return QF_ERR_UNSUPPORTED;
+extern "C" int qf_moe_combine(const void* ybuf, const void* x, const void* w_gate, int has_shared, void* out, int M,
+                              int H, int topk, int pdl, qf_stream_t stream) {
+    QF_REQUIRE(ybuf && x && out, "moe_combine: null pointer argument");
+    QF_REQUIRE(!has_shared || w_gate, "moe_combine: a shared term needs w_gate");
+    QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS, "moe_combine: M must be in [1, %d], got %d", QF_MAX_TOKENS, M);
+    QF_REQUIRE(H >= 128 && H % 128 == 0 && H <= 8192, "moe_combine: H must be a multiple of 128 in [128, 8192], got %d", H);
+    QF_REQUIRE(topk >= 1 && topk <= QF_MAX_TOPK, "moe_combine: topk must be in [1, %d], got %d", QF_MAX_TOPK, topk);
+    QF_REQUIRE(qf::aligned(ybuf, 16) && qf::aligned(x, 16) && qf::aligned(out, 16) && (!w_gate || qf::aligned(w_gate, 16)),
+               "moe_combine: ybuf, x, w_gate and out need 16-byte alignment");
+    const cudaError_t e = qf::launch_ex(moe_combine_kernel, dim3(M), dim3(COMBINE_THREADS), 0,
+                                        reinterpret_cast<cudaStream_t>(stream), pdl != 0,
+                                        static_cast<const __nv_bfloat16*>(ybuf), static_cast<const __nv_bfloat16*>(x),
+                                        static_cast<const __nv_bfloat16*>(w_gate), has_shared != 0,
+                                        static_cast<__nv_bfloat16*>(out), M, H, topk);
+    return qf::cuda_status(e, "moe_combine: launch");
 }
 
 static int repack_grid(long long n) {

@@ -92,7 +92,7 @@ def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
 
 def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, shared, hbuf, ybuf, gl, ctrl, out,
                    phase: int = 4, dbg=None, pbuf=None, shq1=None, shs1=None, shq2=None, shs2=None, shbuf=None,
-                   pdl: bool = True, mode: int = 0, expert_range=None):
+                   pdl: bool = True, mode: int = 0, expert_range=None, num_experts: Optional[int] = None):
     """Routed experts + shared expert + combine; writes ``out`` in place and returns it.
 
     Argument roles follow ``a16_moe_decode`` (serve/qwenfast/qf_a16moe.cu:852-863). Weight format: the kernel
@@ -100,7 +100,12 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     s2 bf16 [E, H*I/128]; gs13 / gs2 bf16 [E] or empty (= 1). The in-kernel shared expert takes bf16 weights in the
     kernel layout of ``repack_bf16``: shq1 = gate_up [2Is*H], shq2 = down [H*Is] (shs1 / shs2 must be empty: there
     are no separate scales for bf16). ``shared`` is a precomputed bf16 [M, H] shared output instead (or empty).
-    Empty tensors mean "absent", as in the reference."""
+    Empty tensors mean "absent", as in the reference.
+
+    ``mode=1`` is one expert-parallel shard: the weights hold only experts ``expert_range = (lo, hi)`` of
+    ``num_experts`` (the router's expert count), and instead of ``out`` the kernel leaves the shard's exact slot
+    contribution in ``ybuf`` (``[M*topk + M, H]``: routed slots, then the shared rows); the shards' ``ybuf`` summed
+    and passed to ``moe_combine`` give the mode-0 output bit for bit."""
     op = "a16_moe_decode"
     _cuda(x, "x", op)
     M, H = x.shape
@@ -111,7 +116,7 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
          f"{op}: topk_w must be contiguous fp32 [M, topk]")
     _req(w13.dtype == torch.int32 and w2.dtype == torch.int32 and w13.dim() == 2 and w2.dim() == 2,
          f"{op}: w13 / w2 must be int32 kernel-layout [E, *] tensors (see repack_w4)")
-    E = w13.shape[0]
+    E = w13.shape[0]          # experts held in w13 / w2 (the shard's, in mode 1)
     I = (w2.shape[1] * 8) // H
     _req(w2.shape[0] == E and w13.shape[1] == 2 * I * H // 8 and w2.shape[1] * 8 == H * I,
          f"{op}: w13 / w2 shapes do not match H={H}")
@@ -132,7 +137,11 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     _req(out.dtype == BF16 and tuple(out.shape) == (M, H) and out.is_contiguous(), f"{op}: out must be bf16 [M, H]")
     _req(dbg is None or (dbg.is_cuda and dbg.dtype == torch.int64 and dbg.is_contiguous() and dbg.numel() >= DBG_NUMEL),
          f"{op}: dbg must be a contiguous int64 CUDA tensor of at least {DBG_NUMEL} entries")
-    lo, hi = (0, E) if expert_range is None else expert_range
+    E_all = E if num_experts is None else int(num_experts)
+    lo, hi = (0, E_all) if expert_range is None else (int(expert_range[0]), int(expert_range[1]))
+    _req(mode in (0, 1), f"{op}: mode must be 0 or 1")
+    _req(mode == 0 or hi - lo == E, f"{op}: mode 1 takes the weights of experts [lo, hi) only ({hi - lo} != {E})")
+    _req(mode == 1 or E == E_all, f"{op}: mode 0 takes every expert's weights")
     tensors = [topk_ids, topk_w, w13, s13, w2, s2, hbuf, ybuf, gl, ctrl, out]
     _req(all(t.device == x.device for t in tensors), f"{op}: every tensor must be on x's device")
     with torch.cuda.device(x.device):
@@ -144,8 +153,26 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
             gl.data_ptr(), gl.numel(), ctrl.data_ptr(), ctrl.numel(),
             _ptr(pbuf), 0 if pbuf is None else pbuf.numel(),
             _ptr(shbuf), 0 if shbuf is None else shbuf.numel() * shbuf.element_size(),
-            out.data_ptr(), M, H, I, E, topk_ids.shape[1], Is, int(phase), int(mode), int(lo), int(hi),
+            out.data_ptr(), M, H, I, E_all, topk_ids.shape[1], Is, int(phase), int(mode), int(lo), int(hi),
             _ptr(dbg), int(bool(pdl)), _stream(x.device)), op)
+    return out
+
+
+def moe_combine(ybuf: torch.Tensor, x: torch.Tensor, w_gate: Optional[torch.Tensor], has_shared: bool,
+                out: torch.Tensor, topk: int, pdl: bool = True) -> torch.Tensor:
+    """Expert-parallel finish: ``out`` = the layer output from the shards' summed slot buffers (``ybuf`` as left by
+    mode-1 ``a16_moe_decode``, summed over the shards). The gate logit is recomputed from ``x`` and ``w_gate``."""
+    op = "moe_combine"
+    _cuda(x, "x", op)
+    M, H = x.shape
+    _req(x.dtype == BF16 and x.is_contiguous() and ybuf.dtype == BF16 and ybuf.is_contiguous(), f"{op}: bf16 tensors")
+    _req(ybuf.numel() >= M * (topk + 1) * H, f"{op}: ybuf must hold [M*topk + M, H]")
+    _req(out.dtype == BF16 and tuple(out.shape) == (M, H) and out.is_contiguous(), f"{op}: out must be bf16 [M, H]")
+    _req(not has_shared or (w_gate is not None and w_gate.numel() == H), f"{op}: a shared term needs w_gate [H]")
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().qf_moe_combine(ybuf.data_ptr(), x.data_ptr(), _ptr(w_gate) if has_shared else None,
+                                              int(bool(has_shared)), out.data_ptr(), M, H, int(topk), int(bool(pdl)),
+                                              _stream(x.device)), op)
     return out
 
 
