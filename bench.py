@@ -204,7 +204,7 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
     from qwenfast_b200 import build as qbuild
-    from qwenfast_b200 import ops, synthetic
+    from qwenfast_b200 import ep, ops, synthetic
 
     rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -215,18 +215,30 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
     cfg = synthetic.CONFIGS[1]
     M, NL = args.M, args.layers
+    # N > 1: expert parallelism -- the same layers on every rank (same seeds), each rank holding E/N experts of
+    # each, the tokens replicated, one all-reduce of the slot buffer per layer-step (strong scaling of one step)
+    epar = world > 1
     layers = build_layers(cfg, NL, dev, args.zipf)
+    shards = [ep.shard_weights(lw, rank, world) for lw in layers] if epar else layers
+    lo, hi = ep.shard_range(cfg.E, rank, world)
     bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, dev)
     rb = ops.router_bufs(dev)
     # independent N(0, 1) tokens per layer (chaining outputs into the next layer would correlate the tokens and
     # shrink the number of distinct experts below the configuration's)
-    xs = [synthetic.make_tokens(cfg, M=M, device=dev, seed=1000 * rank + l) for l in range(NL)]
+    xs = [synthetic.make_tokens(cfg, M=M, device=dev, seed=1000 + l) for l in range(NL)]
     outs = [torch.empty_like(xs[0]) for _ in range(NL)]
     x0 = xs[0]
 
-    def step(l, pdl=True):
-        _, tw, ids, _ = ops.moe_layer_step(xs[l], layers[l], cfg.topk, bufs, rb, outs[l], pdl=pdl)
+    def layer_step(x, l, out, pdl=True):
+        if epar:
+            _, tw, ids = ep.ep_layer_step(x, shards[l], cfg.topk, bufs, rb, out, rank, world, has_shared=True,
+                                          pdl=pdl)
+        else:
+            _, tw, ids, _ = ops.moe_layer_step(x, layers[l], cfg.topk, bufs, rb, out, pdl=pdl)
         return tw, ids
+
+    def step(l, pdl=True):
+        return layer_step(xs[l], l, outs[l], pdl)
 
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
@@ -249,10 +261,18 @@ def run_ours(args):
     g_moe = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_moe):
         for l in range(NL):
-            lw = layers[l]
+            lw = shards[l]
             ops.a16_moe_decode(xs[l], ids_list[l], tw_list[l], lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate,
                                None, bufs["hbuf"], bufs["ybuf"], bufs["gl"], bufs["ctrl"], outs[l], 4, None,
-                               bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None, bufs["shbuf"])
+                               bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None, bufs["shbuf"],
+                               mode=1 if epar else 0, expert_range=(lo, hi), num_experts=cfg.E)
+    g_coll = None
+    if epar:
+        slots = bufs["ybuf"][: ep.slot_rows(M, cfg.topk) * cfg.H]
+        g_coll = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_coll):
+            for l in range(NL):
+                ep.reduce_slots(slots)
     g_router = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_router):
         for l in range(NL):
@@ -280,13 +300,21 @@ def run_ours(args):
     for _ in range(warm_reps):
         g_full.replay()
     torch.cuda.synchronize()
+    # soak ~1 s under the same load first, so clocks settle and the sampler sees the timed regime; every rank
+    # replays the same number of times (the graph holds collectives under expert parallelism)
+    t0 = time.perf_counter()
+    g_full.replay()
+    torch.cuda.synchronize()
+    dt = torch.tensor([time.perf_counter() - t0], device=dev)
+    if world > 1:
+        dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+    n_soak = max(1, min(2000, math.ceil(1.0 / max(float(dt.item()), 1e-6))))
     with ClockSampler(local) as clk:
-        # soak ~1 s under the same load first, so clocks settle and the sampler sees the timed regime
-        t0 = time.perf_counter()
-        while time.perf_counter() - t0 < 1.0:
-            for _ in range(8):
-                g_full.replay()
-            torch.cuda.synchronize()
+        for i in range(n_soak):
+            g_full.replay()
+            if i % 8 == 7:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
         ms_full = timed(g_full, reps)
     steps = reps * NL
     us_step = ms_full * 1e3 / steps
@@ -296,21 +324,36 @@ def run_ours(args):
     for _ in range(warm_reps):
         g_router.replay()
     us_router = timed(g_router, reps) * 1e3 / steps
+    us_coll = None
+    if g_coll is not None:
+        for _ in range(warm_reps):
+            g_coll.replay()
+        us_coll = timed(g_coll, reps) * 1e3 / steps
     torch.cuda.synchronize()
     err = ops.moe_error_word(bufs["ctrl"])
     if err:
         raise RuntimeError(f"MoE kernel reported error word {err:#x}")
 
-    # algorithmic bytes (counted from the routing each layer actually produced)
+    # algorithmic bytes (counted from the routing each layer actually produced); with expert parallelism the MoE
+    # kernel of this rank streams its own distinct experts (and the shared expert on rank 0)
     per_e = expert_bytes(cfg.H, cfg.I)
     U = [int(torch.unique(ids_list[l]).numel()) for l in range(NL)]
+    U_loc = [int(torch.unique(ids_list[l][(ids_list[l] >= lo) & (ids_list[l] < hi)]).numel()) for l in range(NL)]
     shared_b = (3 * cfg.H * cfg.Is + cfg.H) * 2
     act_b = 2 * M * cfg.H * 2
     moe_b = [u * per_e + shared_b + act_b for u in U]
+    loc_b = [u * per_e + (shared_b if rank == 0 else 0) + act_b for u in U_loc]
     router_b = cfg.E * cfg.H * 2 + M * cfg.H * 2
     step_b = statistics.mean(moe_b) + router_b
     peak, peak_kind = load_peaks()
-    achieved = statistics.mean(moe_b) / (us_moe * 1e-6) / 1e9
+    achieved = statistics.mean(loc_b) / (us_moe * 1e-6) / 1e9
+    rank_frac = None
+    if epar:
+        # per-rank HBM fraction of the local MoE kernel (each rank's own kernel time, not the max)
+        mine = torch.tensor([achieved / peak], device=dev)
+        allf = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allf, mine)
+        rank_frac = [round(float(t.item()), 4) for t in allf]
 
     # end to end through the public ops: pinned host x in, result out, every step
     xh = x0.cpu().pin_memory()
@@ -319,7 +362,7 @@ def run_ours(args):
     od = torch.empty_like(x0)
     for l in range(NL):
         xd.copy_(xh, non_blocking=True)
-        ops.moe_layer_step(xd, layers[l], cfg.topk, bufs, rb, od)
+        layer_step(xd, l, od)
         oh.copy_(od, non_blocking=True)
     torch.cuda.synchronize()
     n_e2e = min(args.steps, 4 * NL)
@@ -329,7 +372,7 @@ def run_ours(args):
     ev0.record()
     for i in range(n_e2e):
         xd.copy_(xh, non_blocking=True)
-        ops.moe_layer_step(xd, layers[i % NL], cfg.topk, bufs, rb, od)
+        layer_step(xd, i % NL, od)
         oh.copy_(od, non_blocking=True)
     ev1.record()
     torch.cuda.synchronize()
@@ -349,32 +392,36 @@ def run_ours(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": us_step, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warm_reps * NL,
-            "ms_per_step": us_step / 1e3, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": us_step / 1e3, "higher_is_better": False, "scaling": "strong" if epar else "weak",
+            "vs_baseline": None,
             "dtype": "bf16 activations, int4 experts, fp32 accumulate", "data": "synthetic",
             "config": {"workload": f"config1 decode MoE layer-step (router top-10 + 512-expert W4A16 + bf16 shared "
-                                   f"expert + combine), M={M}",
+                                   f"expert + combine), M={M}" + (f", expert-parallel over {world} GPUs "
+                                                                  f"({cfg.E // world} experts each, NCCL all-reduce "
+                                                                  f"of the slot buffer)" if epar else ""),
                        "H": cfg.H, "E": cfg.E, "I": cfg.I, "topk": cfg.topk, "Is": cfg.Is, "M": M,
                        "layers_cycled": NL, "zipf_s": args.zipf,
                        "l2": f"weights cycled over {NL} layers (~{statistics.mean(moe_b) * NL / 1e9:.1f} GB touched "
                              f"per cycle) > 126 MB L2; no flush",
-                       "parallelism": "replicas" if world > 1 else "single GPU", "graph": "CUDA graph + PDL"},
+                       "parallelism": f"ep{world}" if epar else "single GPU", "graph": "CUDA graph + PDL"},
             "hbm_gbs_step": step_b / (us_step * 1e-6) / 1e9,
             "unique_experts_mean": statistics.mean(U),
             "us_moe_kernel": us_moe, "us_router_kernel": us_router,
+            "us_collective": us_coll, "rank_hbm_frac": rank_frac,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "kernel": "moe_persistent_kernel",
-                         "bytes_per_launch": statistics.mean(moe_b),
+                         "bytes_per_launch": statistics.mean(loc_b),
                          "traffic": load_traffic("moe_persistent_kernel")},
             "e2e": {"value": us_e2e, "unit": UNIT, "h2d_bytes_per_step": M * cfg.H * 2,
                     "d2h_bytes_per_step": M * cfg.H * 2, "steps": n_e2e},
-            "gpu_launches": 2 * steps,
+            "gpu_launches": (3 if epar else 2) * steps,
             "clocks": clk.summary(),
         }
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
-        del g_full, g_moe, g_router
+        del g_full, g_moe, g_router, g_coll
         dist.destroy_process_group()
 
 
