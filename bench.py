@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", default="")
     ap.add_argument("--sweep-configs", default="2,3", help="which sweep records to take (comma list of 2, 3)")
+    ap.add_argument("--sweep-n", default="2048,4096,8192,12288", help="config-3 weight row counts N to sweep")
     return ap.parse_args()
 
 
@@ -509,7 +510,7 @@ def run_sweep(args):
 
     # ---------------------------------------------------------------- config 3: W8A8 GEMM, K = 2048
     K = synthetic.W8A8_K
-    for N in (2048, 4096, 8192, 12288) if 3 in which else ():
+    for N in [int(n) for n in args.sweep_n.split(",") if n.strip()] if 3 in which else ():
         copies = max(2, math.ceil(400e6 / (N * K)))   # > 3x the 126 MB L2 per cycle
         ws = []
         for c in range(copies):

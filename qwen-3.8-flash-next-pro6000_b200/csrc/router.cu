@@ -69,19 +69,32 @@ __device__ void topk_row(const float* __restrict__ row, int E, int topk, int ren
     float my_p = 0.f, routed = 0.f;
     int my_id = 0;
     for (int k = 0; k < topk; ++k) {
-        unsigned bk = 0u;
-        unsigned bi = 0xffffffffu;
+        // lane-local best by a pairwise tournament (depth log2 PL instead of a PL-long chain); the higher slot of a
+        // pair wins only with a strictly larger key, so the lowest id among equal keys survives
+        unsigned tk[PL];
+        int ti[PL];
 #pragma unroll
-        for (int i = 0; i < PL; ++i)          // strict '>' over ascending i keeps the lowest id of this lane
-            if (key[i] > bk) { bk = key[i]; bi = (unsigned)(i * 32 + lane); }
+        for (int i = 0; i < PL; ++i) { tk[i] = key[i]; ti[i] = i; }
+#pragma unroll
+        for (int w = 1; w < PL; w <<= 1) {
+#pragma unroll
+            for (int i = 0; i + w < PL; i += 2 * w) {
+                const bool hi = tk[i + w] > tk[i];
+                tk[i] = hi ? tk[i + w] : tk[i];
+                ti[i] = hi ? ti[i + w] : ti[i];
+            }
+        }
+        const unsigned bk = tk[0], bi = bk != 0u ? (unsigned)(ti[0] * 32 + lane) : 0xffffffffu;
         const unsigned wk = __reduce_max_sync(0xffffffffu, bk);
         const unsigned wi = __reduce_min_sync(0xffffffffu, bk == wk ? bi : 0xffffffffu);
         const int owner = (int)(wi & 31u), slot = (int)(wi >> 5);
-        float p = 0.f;
+        float sel = 0.f;
 #pragma unroll
-        for (int i = 0; i < PL; ++i)
-            if (lane == owner && i == slot) { p = v[i] / sum; key[i] = 0u; }
-        p = __shfl_sync(0xffffffffu, p, owner);
+        for (int i = 0; i < PL; ++i) {
+            sel = i == slot ? v[i] : sel;
+            key[i] = (lane == owner && i == slot) ? 0u : key[i];
+        }
+        const float p = __shfl_sync(0xffffffffu, sel, owner) / sum;
         routed += p;
         if (lane == k) { my_p = p; my_id = (int)wi; }
     }
@@ -123,18 +136,29 @@ __global__ void __launch_bounds__(RT, 1)
     qf::pdl_launch_dependents();
 
     float d[MAXNT][4];
+    // token tiles two at a time: their x fragments are all requested before the first mma uses one
 #pragma unroll
-    for (int nt = 0; nt < MAXNT; ++nt) {
-        d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
-        if (nt < ntile) {
-            const int tok = nt * 8 + g;
-            const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)(tok < rows ? tok : 0) * H) + t;
+    for (int np = 0; np < MAXNT; np += 2) {
+        if (np < ntile) {
+            uint4 xv[2][BPW];
 #pragma unroll
-            for (int i = 0; i < BPW; ++i) {
-                if (b0 + i < nblk) {
-                    const uint4 xv = tok < rows ? __ldcg(xr + 4 * (b0 + i)) : make_uint4(0, 0, 0, 0);
-                    qf::mma_bf16(d[nt], wa[i].x, wb[i].x, wa[i].y, wb[i].y, xv.x, xv.y);
-                    qf::mma_bf16(d[nt], wa[i].z, wb[i].z, wa[i].w, wb[i].w, xv.z, xv.w);
+            for (int h = 0; h < 2; ++h) {
+                const int tok = (np + h) * 8 + g;
+                const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)(tok < rows ? tok : 0) * H) + t;
+#pragma unroll
+                for (int i = 0; i < BPW; ++i)
+                    xv[h][i] = (tok < rows && b0 + i < nblk) ? __ldcg(xr + 4 * (b0 + i)) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int nt = np + h;
+                d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+#pragma unroll
+                for (int i = 0; i < BPW; ++i) {
+                    if (b0 + i < nblk) {
+                        qf::mma_bf16(d[nt], wa[i].x, wb[i].x, wa[i].y, wb[i].y, xv[h][i].x, xv[h][i].y);
+                        qf::mma_bf16(d[nt], wa[i].z, wb[i].z, wa[i].w, wb[i].w, xv[h][i].z, xv[h][i].w);
+                    }
                 }
             }
         }
