@@ -235,13 +235,24 @@ __device__ __forceinline__ float gate_logit(const __nv_bfloat16* xrow, const __n
     const uint4* xr = reinterpret_cast<const uint4*>(xrow);
     const uint4* wr = reinterpret_cast<const uint4*>(wgate);
     float a = 0.f;
-    for (int i = lane; i < H / 8; i += 32) {
-        const uint4 xv = __ldcg(xr + i), wv = __ldg(wr + i);
-        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    // two chunks' loads in flight at a time (one memory round trip per two), the fma chain in chunk order
+    for (int i0 = lane; i0 < H / 8; i0 += 2 * 32) {
+        uint4 xv[2], wv[2];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            a = fmaf(bf16_lo(xx[j]), bf16_lo(ww[j]), a);
-            a = fmaf(bf16_hi(xx[j]), bf16_hi(ww[j]), a);
+        for (int b = 0; b < 2; ++b) {
+            const int i = i0 + 32 * b;
+            xv[b] = i < H / 8 ? __ldcg(xr + i) : make_uint4(0u, 0u, 0u, 0u);
+            wv[b] = i < H / 8 ? __ldg(wr + i) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            if (i0 + 32 * b >= H / 8) break;
+            const uint32_t xx[4] = {xv[b].x, xv[b].y, xv[b].z, xv[b].w}, ww[4] = {wv[b].x, wv[b].y, wv[b].z, wv[b].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a = fmaf(bf16_lo(xx[j]), bf16_lo(ww[j]), a);
+                a = fmaf(bf16_hi(xx[j]), bf16_hi(ww[j]), a);
+            }
         }
     }
 #pragma unroll
@@ -291,11 +302,20 @@ __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* si
         float a[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) a[j] = 0.f;
-        for (int kp = 0; kp < topk; ++kp) {
-            const int s = t * topk + kp;
-            const int e = sids[s];
-            if (e < 0 || e < p.elo || e >= p.ehi) continue;
-            add8(a, __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n)));
+        // four slots' loads in flight at a time, then the sums in top-k order (one round trip per four slots)
+        for (int k0 = 0; k0 < topk; k0 += 4) {
+            uint4 v[4];
+            bool live[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int kp = k0 + b, s = t * topk + kp;
+                const int e = kp < topk ? sids[s] : -1;
+                live[b] = e >= 0 && e >= p.elo && e < p.ehi;
+                if (live[b]) v[b] = __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n));
+            }
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+                if (live[b]) add8(a, v[b]);
         }
         uint4 sv = make_uint4(0u, 0u, 0u, 0u);
         float gl = 0.f;
@@ -1071,8 +1091,15 @@ __global__ void __launch_bounds__(COMBINE_THREADS) moe_combine_kernel(const __nv
         float a[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) a[j] = 0.f;
-        for (int kp = 0; kp < topk; ++kp)
-            add8(a, __ldcg(reinterpret_cast<const uint4*>(ybuf + (size_t)(t * topk + kp) * H + n)));
+        for (int k0 = 0; k0 < topk; k0 += 8) {   // eight slots' loads in flight, sums in top-k order
+            uint4 v[8];
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+                if (k0 + b < topk) v[b] = __ldcg(reinterpret_cast<const uint4*>(ybuf + (size_t)(t * topk + k0 + b) * H + n));
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+                if (k0 + b < topk) add8(a, v[b]);
+        }
         const uint4 sv = has_shared ? __ldcg(reinterpret_cast<const uint4*>(ybuf + (size_t)(M * topk + t) * H + n))
                                     : make_uint4(0u, 0u, 0u, 0u);
         *reinterpret_cast<uint4*>(out + (size_t)t * H + n) = finish8(a, has_shared, gl, sv);
