@@ -71,6 +71,8 @@ constexpr int STAGE_W = 8192;                 // weight bytes of a stage (128 ro
 constexpr int STAGE_S = 256;                  // scale bytes of an int4 stage (one per row)
 constexpr int STAGE_BYTES = STAGE_W + STAGE_S;
 constexpr int NSPLIT = 4;                     // split-K of the shared expert's gate_up
+constexpr int G1_SPLIT = 2;                   // k halves of a routed gate_up item (finished by the later half) when
+                                              // all halves fit in one wave of pipelines (small M)
 constexpr int MAXSLOTS = QF_MAX_TOKENS * QF_MAX_TOPK;
 constexpr uint64_t DEP_WAIT_NS = 1000000000ull;    // cross-CTA dependency waits
 constexpr uint64_t PIPE_WAIT_NS = 4000000000ull;   // ring waits (longer: they cover the dependency waits)
@@ -135,7 +137,8 @@ constexpr int VO_BAR = VO_BST + NBUF * BST_BYTES;                     // full, e
 constexpr int VO_DESC = VO_BAR + (2 * NST + 2 * NEPI + 2 * NBUF) * 8;
 constexpr int VO_EPI = VO_DESC + NST * (int)sizeof(StageDesc);
 constexpr int VO_JOB = VO_EPI + NEPI * (int)sizeof(EpiRec);
-constexpr int VP_BYTES = (VO_JOB + NBUF * (int)sizeof(MmaJob) + 127) & ~127;
+constexpr int VO_FLAG = VO_JOB + NBUF * (int)sizeof(MmaJob);         // int: this group finishes the item
+constexpr int VP_BYTES = (VO_FLAG + 4 + 127) & ~127;
 constexpr int OFF_PLAN = NVP * VP_BYTES;
 static_assert(VO_BST % 128 == 0 && VO_BAR % 8 == 0 && VP_BYTES % 128 == 0, "shared memory alignment");
 constexpr int PLAN_ULIST = 0;                                         // int16 [QF_MAX_EXPERTS]
@@ -191,6 +194,8 @@ struct Layout {   // per-launch derived sizes, identical in every thread
     int R1, R2, Rs1, ngs, U, Gt, has_gate, has_shw;
     int b_s1, b_g1, b_s1f, b_s2, b_g2, b_cb, total;
     uint32_t tile_target;
+    int g1s;                          // gate_up k splits this launch: G1_SPLIT or 1
+    size_t g1_cnt_off, g1_part_off;   // pbuf (floats): gate_up half counters (uint32), then half partials
 };
 
 __device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   // largest u with gpre[u] <= key
@@ -207,7 +212,7 @@ __device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   /
 __device__ __forceinline__ const __nv_bfloat16* token_row(const Params& p, const StageDesc& d, const int16_t* toff,
                                                           const int16_t* tlist, int n) {
     if (n >= d.ntok) return nullptr;
-    if (d.kind == K_G1) return p.x + (size_t)(tlist[toff[d.u] + TG * d.tg + n] / p.topk) * p.H;
+    if (d.kind == K_G1) return p.x + (size_t)(tlist[toff[d.u] + TG * d.tg + n] / p.topk) * p.H + d.split * (p.H / G1_SPLIT);
     if (d.kind == K_G2) return p.hbuf + (size_t)tlist[toff[d.u] + TG * d.tg + n] * p.I;
     if (d.kind == K_S1) return p.x + (size_t)(TG * d.tg + n) * p.H + d.split * (p.H / NSPLIT);
     return p.hsh + (size_t)(TG * d.tg + n) * p.Is;   // K_S2
@@ -508,12 +513,19 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     L.Gt = misc[MISC_GT];
     L.b_s1 = L.has_gate ? 1 : 0;
     L.b_g1 = L.b_s1 + (L.has_shw ? L.Rs1 * NSPLIT * L.ngs : 0);
-    L.b_s1f = L.b_g1 + L.R1 * L.Gt;
+    // split the gate_up items only when every half still fits in one wave of pipelines: then the halves shorten
+    // the critical path; with more items the split only adds the hand-off of the partials. The test uses the
+    // bound M * topk on the token groups, not this launch's count, so that a shard (mode 1) decides exactly as
+    // the whole layer does and the sums keep the same association.
+    L.g1s = G1_SPLIT * L.R1 * M * p.topk <= (int)gridDim.x * NVP ? G1_SPLIT : 1;
+    L.b_s1f = L.b_g1 + L.R1 * L.Gt * L.g1s;
     L.b_s2 = L.b_s1f + (L.has_shw ? L.Rs1 * L.ngs : 0);
     L.b_g2 = L.b_s2 + (L.has_shw ? L.R2 * L.ngs : 0);
     L.b_cb = L.b_g2 + L.R2 * L.Gt;
     L.total = L.b_cb + L.R2;
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
+    L.g1_cnt_off = L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0;
+    L.g1_part_off = L.g1_cnt_off + (((size_t)M * p.topk * L.R1 + 3) & ~(size_t)3);
 
 
     if (warp == AGENT_WARP) {
@@ -589,16 +601,19 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 } else if (item < L.b_s1f || (item >= L.b_g2 && item < L.b_cb)) {
                     const bool down = item >= L.b_g2;
                     const int j = item - (down ? L.b_g2 : L.b_g1);
-                    const int R = down ? L.R2 : L.R1;
+                    // gate_up: (tile, k half) pairs, the two halves of a tile next to each other in the queue
+                    const int R = down ? L.R2 : L.R1 * L.g1s;
                     u = find_u(gpre, L.U, j / R);
                     const int ngu = gpre[u + 1] - gpre[u];
                     const int jj = j - R * gpre[u];
-                    tile = jj / ngu;
-                    tg = jj - tile * ngu;
+                    const int th = jj / ngu;
+                    tg = jj - th * ngu;
+                    tile = down ? th : th / L.g1s;
+                    split = down ? 0 : th % L.g1s;
                     kind = down ? K_G2 : K_G1;
                     e = ulist[u];
                     const int K = down ? p.I : p.H;
-                    nk = (K + W4_KC - 1) / W4_KC;
+                    nk = (K + W4_KC - 1) / W4_KC / (down ? 1 : L.g1s);
                     ntok = min(TG, (toff[u + 1] - toff[u]) - TG * tg);
                 } else if (item < L.b_s2) {
                     const int j = item - L.b_s1f;
@@ -640,8 +655,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     const int N = down ? p.H : 2 * p.I;
                     d.kc = (int16_t)W4_KC;
                     bytes = STAGE_W + STAGE_S;
-                    wsrc = (down ? p.w2 : p.w13) + (size_t)(e - p.wofs) * ((size_t)N * K / 2) + (size_t)tile * (128 * (size_t)K / 2);
-                    ssrc = (down ? p.s2 : p.s13) + (size_t)(e - p.wofs) * ((size_t)N * K / 128) + (size_t)tile * K;
+                    wsrc = (down ? p.w2 : p.w13) + (size_t)(e - p.wofs) * ((size_t)N * K / 2) + (size_t)tile * (128 * (size_t)K / 2) +
+                           (size_t)split * nk * STAGE_W;
+                    ssrc = (down ? p.s2 : p.s13) + (size_t)(e - p.wofs) * ((size_t)N * K / 128) + (size_t)tile * K +
+                           (size_t)split * nk * W4_KC;
                     if (down) { dep_idx = C_DONE + u; dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])); }
                 } else if (kind == K_S1 || kind == K_S2) {
                     const bool down = kind == K_S2;
@@ -887,6 +904,43 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 }
                 signal(C_GLF, 1);
             } else if (d.kind == K_G1 || d.kind == K_S1F) {
+                if (d.kind == K_G1 && L.g1s > 1) {
+                    // one k half of the tile: publish this half's partials, count it; the half counted second
+                    // adds the other half's partials (a + b: the same bits whichever half comes second) and runs
+                    // the SwiGLU epilogue. The counter is left at zero for the next launch.
+                    const int unit = (gpre[d.u] + d.tg) * L.R1 + d.tile;
+                    uint32_t* cnt = reinterpret_cast<uint32_t*>(p.pbuf + L.g1_cnt_off) + unit;
+                    float* parts = p.pbuf + L.g1_part_off + (size_t)unit * G1_SPLIT * 2048;
+                    float* mine = parts + (size_t)d.split * 2048 + row * TG;
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4)
+                        __stcg(reinterpret_cast<float4*>(mine + i), make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
+                    __threadfence();
+                    qf::named_bar(1 + vp, CONS_THREADS);
+                    volatile int* gflag = reinterpret_cast<volatile int*>(vb + VO_FLAG);
+                    if (ctid == 0) {
+                        const bool last = atomicAdd(cnt, 1u) == (uint32_t)(L.g1s - 1);
+                        if (last) {
+                            __threadfence();
+                            *cnt = 0u;
+                        }
+                        *gflag = last ? 1 : 0;
+                    }
+                    qf::named_bar(1 + vp, CONS_THREADS);
+                    const bool last = *gflag != 0;
+                    qf::named_bar(1 + vp, CONS_THREADS);   // every thread has read the flag before its next use
+                    if (!last) continue;
+#pragma unroll
+                    for (int sp = 0; sp < G1_SPLIT; ++sp) {
+                        if (sp == d.split || sp >= L.g1s) continue;
+                        const float* other = parts + (size_t)sp * 2048 + row * TG;
+#pragma unroll
+                        for (int i = 0; i < 16; i += 4) {
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(other + i));
+                            acc[i] += q.x; acc[i + 1] += q.y; acc[i + 2] += q.z; acc[i + 3] += q.w;
+                        }
+                    }
+                }
                 if (d.kind == K_S1F) {
                     const float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048 + row * TG;
 #pragma unroll
@@ -1120,7 +1174,13 @@ extern "C" int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64
     if (ybuf_bytes) *ybuf_bytes = (int64_t)M * (topk + 1) * H * 2;
     if (gl_numel) *gl_numel = M;
     if (ctrl_numel) *ctrl_numel = QF_MOE_CTRL_WORDS;
-    if (pbuf_numel) *pbuf_numel = Is > 0 ? (int64_t)(2 * Is / 128) * ngs * NSPLIT * 2048 : 0;
+    if (pbuf_numel) {
+        // shared expert split-K partials, then the gate_up k-half counters and partials (at most M * topk token
+        // groups of routed experts, 2I / 128 tiles each)
+        const int64_t sh = Is > 0 ? (int64_t)(2 * Is / 128) * ngs * NSPLIT * 2048 : 0;
+        const int64_t units = (int64_t)M * topk * (2 * I / 128);
+        *pbuf_numel = sh + ((units + 3) & ~(int64_t)3) + units * G1_SPLIT * 2048;
+    }
     if (shbuf_bytes) *shbuf_bytes = Is > 0 ? (int64_t)M * (Is + H) * 2 : 0;
     return QF_OK;
 }
@@ -1158,8 +1218,9 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     QF_REQUIRE(hbuf_bytes >= need_h && ybuf_bytes >= need_y && gl_numel >= need_gl && ctrl_numel >= need_ctrl,
                "a16_moe_decode: scratch too small (need hbuf %lld B, ybuf %lld B, gl %lld, ctrl %lld)", (long long)need_h,
                (long long)need_y, (long long)need_gl, (long long)need_ctrl);
-    QF_REQUIRE(!has_shw || (pbuf_numel >= need_p && shbuf_bytes >= need_sh),
-               "a16_moe_decode: shared scratch too small (need pbuf %lld, shbuf %lld B)", (long long)need_p, (long long)need_sh);
+    QF_REQUIRE(pbuf && pbuf_numel >= need_p && (!has_shw || shbuf_bytes >= need_sh),
+               "a16_moe_decode: pbuf / shared scratch too small (need pbuf %lld, shbuf %lld B)", (long long)need_p,
+               (long long)need_sh);
     const void* al[] = {x, w13, s13, w2, s2, hbuf, ybuf, out, w_gate, shared, sh_w13, sh_w2, pbuf, shbuf};
     for (const void* a : al) QF_REQUIRE(a == nullptr || qf::aligned(a, 16), "a16_moe_decode: every tensor must be 16-byte aligned");
 

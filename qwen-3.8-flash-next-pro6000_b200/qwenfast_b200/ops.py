@@ -84,7 +84,7 @@ def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
         ybuf=torch.empty(yb // 2, dtype=BF16, device=device),
         gl=torch.empty(gl, dtype=torch.float32, device=device),
         ctrl=torch.zeros(ctrl, dtype=torch.int32, device=device),
-        pbuf=torch.empty(max(pb, 1), dtype=torch.float32, device=device),
+        pbuf=torch.zeros(max(pb, 1), dtype=torch.float32, device=device),   # holds counters: zeroed once
         shbuf=torch.empty(max(sh // 2, 1), dtype=BF16, device=device),
         none=torch.empty(0, dtype=BF16, device=device),
     )

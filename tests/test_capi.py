@@ -49,7 +49,7 @@ def test_moe_rejects_bad_arguments(lib):
     p = ctypes.c_void_p(256)
     # x, ids, w, w13, s13, gs13, w2, s2, gs2, w_gate, shared (absent), sh_w13, sh_w2 + scratch + out
     head = [p] * 10 + [None, p, p]
-    args = head + [p, 1 << 30, p, 1 << 30, p, 64, p, 2048, p, 1 << 20, p, 1 << 30, p]
+    args = head + [p, 1 << 30, p, 1 << 30, p, 64, p, 2048, p, 1 << 26, p, 1 << 30, p]
     ok_dims = [10, 2048, 512, 512, 10, 512]
     st = lib.qf_a16_moe_decode(*args, 10, 2048, 512, 512, 10, 512, 1, 0, 0, 512, None, 1, None)
     assert st == -1 and b"phase" in lib.qf_last_error()
@@ -57,7 +57,7 @@ def test_moe_rejects_bad_arguments(lib):
     assert st == -1 and b"M must" in lib.qf_last_error()
     st = lib.qf_a16_moe_decode(*args, *ok_dims, 4, 0, 0, 513, None, 1, None)
     assert st == -1 and b"expert range" in lib.qf_last_error()
-    small = head + [p, 16, p, 1 << 30, p, 64, p, 2048, p, 1 << 20, p, 1 << 30, p]
+    small = head + [p, 16, p, 1 << 30, p, 64, p, 2048, p, 1 << 26, p, 1 << 30, p]
     st = lib.qf_a16_moe_decode(*small, *ok_dims, 4, 0, 0, 512, None, 1, None)
     assert st == -1 and b"scratch" in lib.qf_last_error()
     unaligned = [ctypes.c_void_p(258)] + head[1:] + args[13:]
@@ -78,4 +78,5 @@ def test_workspace_sizes(lib):
     assert lib.qf_a16_moe_workspace(10, 2048, 512, 10, 512, *[ctypes.byref(a) for a in v]) == 0
     hb, yb, gl, ctrl, pb, sh = (a.value for a in v)
     assert hb == 10 * 10 * 512 * 2 and yb == 10 * 11 * 2048 * 2 and gl == 10 and ctrl == 2048
-    assert pb == (2 * 512 // 128) * 1 * 4 * 2048 and sh == 10 * (512 + 2048) * 2
+    units = 10 * 10 * (2 * 512 // 128)   # gate_up k-half counters and partials: M * topk groups x 2I / 128 tiles
+    assert pb == (2 * 512 // 128) * 1 * 4 * 2048 + units + units * 2 * 2048 and sh == 10 * (512 + 2048) * 2
