@@ -20,7 +20,7 @@
 //       GL  shared-expert gate logits          S1  shared gate_up tile, one of 4 k-splits, one 16-token group
 //       G1  expert u gate_up tile + group      S1F shared gate_up split-K sum + SwiGLU
 //       S2  shared down tile + group           G2  expert u down tile + group
-//       CB  top-k combine of one 128-column tile (+ gated shared term)
+//       CB  top-k combine of one 128-column tile for 8 tokens (+ gated shared term)
 //     An item only depends on items claimed before it, by pipelines that are already running, so the queue cannot
 //     deadlock for any grid size.
 //   * The producer streams each item's weights through an NST-stage shared-memory ring with 1-D bulk copies (TMA
@@ -74,6 +74,8 @@ constexpr int NSPLIT = 4;                     // split-K of the shared expert's 
 constexpr int G1_SPLIT = 2;                   // k halves of a routed gate_up item (finished by the later half) when
                                               // all halves fit in one wave of pipelines (small M)
 constexpr int MAXSLOTS = QF_MAX_TOKENS * QF_MAX_TOPK;
+constexpr int CB_TOK = 8;                     // tokens of a combine item (x 16 column chunks = one per thread)
+constexpr int CB_BATCH = 4;                   // slot loads a combine thread keeps in flight (registers)
 constexpr uint64_t DEP_WAIT_NS = 1000000000ull;    // cross-CTA dependency waits
 constexpr uint64_t PIPE_WAIT_NS = 4000000000ull;   // ring waits (longer: they cover the dependency waits)
 
@@ -147,7 +149,8 @@ constexpr int PLAN_TOFF = PLAN_GPRE + (QF_MAX_EXPERTS + 8) * 2;
 constexpr int PLAN_TLIST = PLAN_TOFF + (QF_MAX_EXPERTS + 8) * 2;      // int16 [MAXSLOTS]
 constexpr int PLAN_SIDS = PLAN_TLIST + MAXSLOTS * 2;                  // int16 [MAXSLOTS] copy of topk_ids
 constexpr int PLAN_DUPN = PLAN_SIDS + MAXSLOTS * 2;                   // int16 [MAXSLOTS] next slot, same token+expert
-constexpr int PLAN_MISC = PLAN_DUPN + MAXSLOTS * 2;                   // int32 [64]
+constexpr int PLAN_TW = PLAN_DUPN + MAXSLOTS * 2;                     // fp32 [MAXSLOTS] bf16-rounded topk_weights
+constexpr int PLAN_MISC = PLAN_TW + MAXSLOTS * 4;                     // int32 [64]
 constexpr int PLAN_BYTES = PLAN_MISC + 64 * 4;
 constexpr int MOE_SMEM = OFF_PLAN + PLAN_BYTES;
 static_assert(MOE_SMEM + 1024 <= 228 * 1024, "the CTA must fit in shared memory");
@@ -191,7 +194,7 @@ __device__ bool wait_counter(uint32_t* ctrl, int idx, uint32_t target) {
 }
 
 struct Layout {   // per-launch derived sizes, identical in every thread
-    int R1, R2, Rs1, ngs, U, Gt, has_gate, has_shw;
+    int R1, R2, Rs1, ngs, ngc, U, Gt, has_gate, has_shw;
     int b_s1, b_g1, b_s1f, b_s2, b_g2, b_cb, total;
     uint32_t tile_target;
     int g1s;                          // gate_up k splits this launch: G1_SPLIT or 1
@@ -299,59 +302,58 @@ __device__ __forceinline__ uint4 finish8(const float (&a)[8], bool has_gate, flo
     return o;
 }
 
-// Combine of one 128-column tile for all tokens: out = bf16(gate * shared + bf16(sum_kpos y)), 8 columns a thread.
-__device__ void combine_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int ctid) {
+// Combine of one 128-column tile for tokens CB_TOK g .. CB_TOK g + CB_TOK - 1: out = bf16(gate * shared +
+// bf16(sum_kpos y)); a thread owns one (token, 8 columns). The shared row, the gate logit and CB_BATCH slots are
+// requested before the first add (one L2 round trip per CB_BATCH slots); the sum runs in top-k order.
+__device__ void combine_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int g, int ctid) {
     const int H = p.H, topk = p.topk;
-    for (int q = ctid; q < p.M * 16; q += CONS_THREADS) {
-        const int t = q >> 4, n = 128 * c + 8 * (q & 15);
-        float a[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) a[j] = 0.f;
-        // four slots' loads in flight at a time, then the sums in top-k order (one round trip per four slots)
-        for (int k0 = 0; k0 < topk; k0 += 4) {
-            uint4 v[4];
-            bool live[4];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int kp = k0 + b, s = t * topk + kp;
-                const int e = kp < topk ? sids[s] : -1;
-                live[b] = e >= 0 && e >= p.elo && e < p.ehi;
-                if (live[b]) v[b] = __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n));
-            }
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-                if (live[b]) add8(a, v[b]);
-        }
-        uint4 sv = make_uint4(0u, 0u, 0u, 0u);
-        float gl = 0.f;
-        if (L.has_gate) {
-            gl = __ldcg(p.gl + t);
-            if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
-            else sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
-        }
-        *reinterpret_cast<uint4*>(p.out + (size_t)t * H + n) = finish8(a, L.has_gate != 0, gl, sv);
+    const int t = CB_TOK * g + (ctid >> 4), n = 128 * c + 8 * (ctid & 15);
+    if (t >= p.M) return;
+    uint4 sv = make_uint4(0u, 0u, 0u, 0u);
+    float gl = 0.f;
+    if (L.has_gate) {
+        gl = __ldcg(p.gl + t);
+        if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
+        else sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
     }
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[j] = 0.f;
+    for (int k0 = 0; k0 < topk; k0 += CB_BATCH) {
+        uint4 v[CB_BATCH];
+        bool live[CB_BATCH];
+#pragma unroll
+        for (int b = 0; b < CB_BATCH; ++b) {
+            const int kp = k0 + b, s = t * topk + kp;
+            const int e = kp < topk ? sids[s] : -1;
+            live[b] = e >= 0 && e >= p.elo && e < p.ehi;
+            if (live[b]) v[b] = __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n));
+        }
+#pragma unroll
+        for (int b = 0; b < CB_BATCH; ++b)
+            if (live[b]) add8(a, v[b]);
+    }
+    *reinterpret_cast<uint4*>(p.out + (size_t)t * H + n) = finish8(a, L.has_gate != 0, gl, sv);
 }
 
-// Expert-parallel shard (mode 1), one 128-column tile: make ybuf the shard's exact contribution to the slot sum --
-// zeros in every slot this shard does not own (other shards' experts, invalid ids), and the shared expert's output
-// in rows M * topk + t when this shard computes it (zeros otherwise). The routed slots of local experts were
-// written by the down-projection epilogues.
-__device__ void shard_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int ctid) {
+// Expert-parallel shard (mode 1), one 128-column tile, tokens CB_TOK g ..: make ybuf the shard's exact contribution
+// to the slot sum -- zeros in every slot this shard does not own (other shards' experts, invalid ids), and the
+// shared expert's output in rows M * topk + t when this shard computes it (zeros otherwise). The routed slots of
+// local experts were written by the down-projection epilogues.
+__device__ void shard_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int g, int ctid) {
     const int H = p.H, topk = p.topk;
+    const int t = CB_TOK * g + (ctid >> 4), n = 128 * c + 8 * (ctid & 15);
+    if (t >= p.M) return;
     const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-    for (int q = ctid; q < p.M * 16; q += CONS_THREADS) {
-        const int t = q >> 4, n = 128 * c + 8 * (q & 15);
-        for (int kp = 0; kp < topk; ++kp) {
-            const int s = t * topk + kp;
-            const int e = sids[s];
-            if (e < 0 || e < p.elo || e >= p.ehi) *reinterpret_cast<uint4*>(p.ybuf + (size_t)s * H + n) = zero;
-        }
-        uint4 sv = zero;
-        if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
-        else if (p.shared != nullptr) sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
-        *reinterpret_cast<uint4*>(p.ybuf + (size_t)(p.M * topk + t) * H + n) = sv;
+    uint4 sv = zero;
+    if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
+    else if (p.shared != nullptr) sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
+    for (int kp = 0; kp < topk; ++kp) {
+        const int s = t * topk + kp;
+        const int e = sids[s];
+        if (e < 0 || e < p.elo || e >= p.ehi) *reinterpret_cast<uint4*>(p.ybuf + (size_t)s * H + n) = zero;
     }
+    *reinterpret_cast<uint4*>(p.ybuf + (size_t)(p.M * topk + t) * H + n) = sv;
 }
 
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __grid_constant__ Params p) {
@@ -363,6 +365,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     int16_t* tlist = reinterpret_cast<int16_t*>(plan + PLAN_TLIST);
     int16_t* sids = reinterpret_cast<int16_t*>(plan + PLAN_SIDS);
     int16_t* dupn = reinterpret_cast<int16_t*>(plan + PLAN_DUPN);
+    float* tws = reinterpret_cast<float*>(plan + PLAN_TW);
     int* misc = reinterpret_cast<int*>(plan + PLAN_MISC);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -411,6 +414,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     __syncwarp();
     // Everything below reads data of the previous kernel (topk ids, x) or the control block it may re-arm.
     qf::pdl_wait();
+    // each producer claims its first item now: the atomic's round trip overlaps the routing plan
+    int first_item = 0;
+    if (warp < AGENT_WARP && vw == VP_PRODUCER && lane == 0) first_item = (int)atomicAdd(ctrl + C_QUEUE, 1u);
 
     // ------------------------------------------------------------------ routing plan (all threads)
     {
@@ -425,6 +431,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         bool bad = false;
         for (int s = tid; s < nslots; s += MOE_THREADS) {
             const int e = p.ids[s];
+            tws[s] = bf16r(p.tw[s]);   // the down epilogues read the slot weights from here, not from L2
             if (e < 0 || e >= E) {
                 bad = true;
                 sids[s] = -1;
@@ -509,6 +516,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     L.has_gate = (p.shared != nullptr || L.has_shw) ? 1 : 0;
     L.Rs1 = L.has_shw ? (2 * p.Is) / 128 : 0;
     L.ngs = (M + TG - 1) / TG;
+    L.ngc = (M + CB_TOK - 1) / CB_TOK;
     L.U = misc[MISC_U];
     L.Gt = misc[MISC_GT];
     L.b_s1 = L.has_gate ? 1 : 0;
@@ -522,7 +530,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     L.b_s2 = L.b_s1f + (L.has_shw ? L.Rs1 * L.ngs : 0);
     L.b_g2 = L.b_s2 + (L.has_shw ? L.R2 * L.ngs : 0);
     L.b_cb = L.b_g2 + L.R2 * L.Gt;
-    L.total = L.b_cb + L.R2;
+    L.total = L.b_cb + L.R2 * L.ngc;
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
     L.g1_cnt_off = L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0;
     L.g1_part_off = L.g1_cnt_off + (((size_t)M * p.topk * L.R1 + 3) & ~(size_t)3);
@@ -580,7 +588,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             const uint64_t pol = qf::policy_evict_first();
             int st = 0;
             uint32_t ph = 0;
-            int next = (int)atomicAdd(ctrl + C_QUEUE, 1u);
+            int next = first_item;
             for (;;) {
                 int item = next;
                 if (hard_error(ctrl)) item = L.total;
@@ -630,7 +638,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     ntok = min(TG, M - TG * tg);
                 } else {
                     kind = K_CB;
-                    tile = item - L.b_cb;
+                    const int j = item - L.b_cb;   // (column tile, group of CB_TOK tokens), tile-major
+                    tile = j / L.ngc;
+                    tg = j - tile * L.ngc;
                 }
                 // dependencies of items without copies are resolved before their (empty) stage is published
                 if (kind == K_S1F) wait_counter(ctrl, C_SPLIT + tile * L.ngs + tg, (uint32_t)NSPLIT);
@@ -790,8 +800,42 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             }
             qf::tc_fence_before();
         };
+        // this thread's token chunks of an item's stages: int4 stages have 16 tokens x 16 chunks (two per thread:
+        // tokens t/16 and 8 + t/16, chunk t % 16), bf16 stages 16 x 4 (threads 0..63: token t/4, chunk t % 4);
+        // sources advance by one stage's k per stage, a token beyond the item reads zeros (zero-fill copy)
+        struct XChunks {
+            const char* src0;
+            const char* src1;
+            uint32_t n0, n1;
+            int step0, step1, dst;
+            bool act, two;
+        };
+        auto xchunks = [&](const StageDesc& dd) {
+            XChunks c;
+            const bool w4d = dd.kind == K_G1 || dd.kind == K_G2;
+            const int lg = w4d ? 4 : 2;
+            const int xn = ctid >> lg, xc = ctid & ((1 << lg) - 1);
+            c.act = xn < TG;
+            c.two = w4d;
+            c.dst = (xc * TG + xn) * 16;
+            const __nv_bfloat16* r0 = token_row(p, dd, toff, tlist, xn);
+            const __nv_bfloat16* r1 = w4d ? token_row(p, dd, toff, tlist, xn + 8) : nullptr;
+            c.src0 = r0 != nullptr ? reinterpret_cast<const char*>(r0 + 8 * xc) : reinterpret_cast<const char*>(p.x);
+            c.src1 = r1 != nullptr ? reinterpret_cast<const char*>(r1 + 8 * xc) : reinterpret_cast<const char*>(p.x);
+            c.n0 = r0 != nullptr ? 16u : 0u;
+            c.n1 = r1 != nullptr ? 16u : 0u;
+            c.step0 = r0 != nullptr ? dd.kc * 2 : 0;
+            c.step1 = r1 != nullptr ? dd.kc * 2 : 0;
+            return c;
+        };
+        auto xissue = [&](const XChunks& c, int b) {
+            if (c.act) qf::cp_async16(bst + b * BST_BYTES + c.dst, c.src0, c.n0);
+            if (c.two) qf::cp_async16(bst + b * BST_BYTES + c.dst + 8 * 16, c.src1, c.n1);
+        };
+        bool pre = false;   // this thread already copied the current item's first token chunks
         // stop the MMA warp (its next stage is mcount; nothing of this pipeline is in flight)
         auto stop_mma = [&]() {
+            qf::cp_async_wait_all();
             const int bq = (int)(mcount & 1u);
             if (ctid == 0) jobs[bq].kind = (int16_t)K_STOP;
             __syncwarp();
@@ -817,26 +861,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             const bool w4 = d.kind == K_G1 || d.kind == K_G2;
             if (w4 || d.kind == K_S1 || d.kind == K_S2) {
                 // ---------------------------------------------------------------- pipelined item: nk stages
-                const int nk = d.nk, ntok = d.ntok, kc = d.kc;
-                // token chunks: int4 stages have 16 tokens x 16 chunks (two per thread: tokens t/16 and 8 + t/16,
-                // chunk t % 16), bf16 stages 16 x 4 (threads 0..63: token t/4, chunk t % 4)
-                const int lg = w4 ? 4 : 2;
-                const int xn = ctid >> lg, xc = ctid & ((1 << lg) - 1);
-                const bool xact = xn < TG;
-                const int xdst = (xc * TG + xn) * 16;
-                const __nv_bfloat16* xrow = token_row(p, d, toff, tlist, xn);
-                const __nv_bfloat16* xrow2 = w4 ? token_row(p, d, toff, tlist, xn + 8) : nullptr;
-                const char* xsrc = xrow != nullptr ? reinterpret_cast<const char*>(xrow + 8 * xc)
-                                                   : reinterpret_cast<const char*>(p.x);
-                const char* xsrc2 = xrow2 != nullptr ? reinterpret_cast<const char*>(xrow2 + 8 * xc)
-                                                     : reinterpret_cast<const char*>(p.x);
-                const uint32_t xbytes = xrow != nullptr ? 16u : 0u;   // 0: zero-fill (token beyond the item)
-                const uint32_t xbytes2 = xrow2 != nullptr ? 16u : 0u;
-                const int xstep = xrow != nullptr ? kc * 2 : 0;
-                const int xstep2 = xrow2 != nullptr ? kc * 2 : 0;
+                const int nk = d.nk, ntok = d.ntok;
+                XChunks xc = xchunks(d);
                 int bcur = (int)(mcount & 1u);
-                if (xact) qf::cp_async16(bst + bcur * BST_BYTES + xdst, xsrc, xbytes);
-                if (w4) qf::cp_async16(bst + bcur * BST_BYTES + xdst + 8 * 16, xsrc2, xbytes2);
+                if (!pre) xissue(xc, bcur);
+                pre = false;
                 // the previous pipelined stage of this item (its mmas may still run): buffer, ring slot, scale
                 bool pend = false;
                 int pb = 0, pr = -1;
@@ -870,12 +899,23 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     ++mcount;
                     bcur ^= 1;
                     if (++st == NST) { st = 0; ph ^= 1u; }
-                    if (++kidx == nk) break;
+                    if (++kidx == nk) {
+                        // buffer bcur is free (its stage was just retired) and is the next item's first buffer: if
+                        // that item's first stage is already in the ring, copy its first token chunks now, so that
+                        // the copy's L2 round trip overlaps this item's last retire and epilogue
+                        if (qf::mbar_test_wait(full + st, ph)) {
+                            const StageDesc dn = desc[st];
+                            if (dn.kind == K_G1 || dn.kind == K_G2 || dn.kind == K_S1 || dn.kind == K_S2) {
+                                xissue(xchunks(dn), bcur);
+                                pre = true;
+                            }
+                        }
+                        break;
+                    }
                     // buffer bcur is free again (its stage was just retired): copy the next stage's token chunks
-                    xsrc += xstep;
-                    xsrc2 += xstep2;
-                    if (xact) qf::cp_async16(bst + bcur * BST_BYTES + xdst, xsrc, xbytes);
-                    if (w4) qf::cp_async16(bst + bcur * BST_BYTES + xdst + 8 * 16, xsrc2, xbytes2);
+                    xc.src0 += xc.step0;
+                    xc.src1 += xc.step1;
+                    xissue(xc, bcur);
                     if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
                         set_err(ctrl, QF_MOE_ERR_PIPELINE);
                         failed = true;
@@ -998,7 +1038,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                         const float v = bf16r(acc[i]);
                         // the token's first slot routed to e, then any later slot of the same token with e again
                         for (int s = tlist[tbase + i]; s >= 0; s = dupn[s]) {
-                            const float w = bf16r(g2 * bf16r(__ldcg(p.tw + s)));
+                            const float w = bf16r(g2 * tws[s]);
                             p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v * w);
                         }
                     }
@@ -1012,8 +1052,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_CB) {
                 // the producer acquired every producer of this tile (and the gate logits) before publishing it
-                if (p.mode == 0) combine_tile(p, L, sids, d.tile, ctid);
-                else shard_tile(p, L, sids, d.tile, ctid);
+                if (p.mode == 0) combine_tile(p, L, sids, d.tile, d.tg, ctid);
+                else shard_tile(p, L, sids, d.tile, d.tg, ctid);
                 signal(-1, 0);
             }
         }
