@@ -151,7 +151,9 @@ constexpr int PLAN_SIDS = PLAN_TLIST + MAXSLOTS * 2;                  // int16 [
 constexpr int PLAN_DUPN = PLAN_SIDS + MAXSLOTS * 2;                   // int16 [MAXSLOTS] next slot, same token+expert
 constexpr int PLAN_TW = PLAN_DUPN + MAXSLOTS * 2;                     // fp32 [MAXSLOTS] bf16-rounded topk_weights
 constexpr int PLAN_MISC = PLAN_TW + MAXSLOTS * 4;                     // int32 [64]
-constexpr int PLAN_BYTES = PLAN_MISC + 64 * 4;
+constexpr int PLAN_LAYOUT = PLAN_MISC + 64 * 4;                       // Layout (per-launch sizes, one copy per CTA)
+constexpr int PLAN_LAYOUT_BYTES = 256;
+constexpr int PLAN_BYTES = PLAN_LAYOUT + PLAN_LAYOUT_BYTES;
 constexpr int MOE_SMEM = OFF_PLAN + PLAN_BYTES;
 static_assert(MOE_SMEM + 1024 <= 228 * 1024, "the CTA must fit in shared memory");
 // plan-build scratch aliases the ring (the producer starts after the plan is built)
@@ -161,7 +163,7 @@ constexpr int SCR_TOFFE = SCR_EXF + 3 * QF_MAX_EXPERTS * 2;        // int16 [E] 
 constexpr int SCR_CHUNK = SCR_TOFFE + QF_MAX_EXPERTS * 2;          // int32 [32] x 3 chunk totals
 static_assert(SCR_CHUNK + 3 * 32 * 4 <= NST * STAGE_BYTES, "plan scratch (pipeline 0's ring)");
 
-enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6 };
+enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6, MISC_DUPS = 7 };
 
 // tensor memory map (columns of this CTA's allocation; fp32 / bf16x2 per 32-bit column, lane = tile row)
 constexpr uint32_t TM_COLS = 512;
@@ -200,6 +202,36 @@ struct Layout {   // per-launch derived sizes, identical in every thread
     int g1s;                          // gate_up k splits this launch: G1_SPLIT or 1
     size_t g1_cnt_off, g1_part_off;   // pbuf (floats): gate_up half counters (uint32), then half partials
 };
+static_assert(sizeof(Layout) <= PLAN_LAYOUT_BYTES && PLAN_LAYOUT % 8 == 0, "Layout slot in the plan");
+
+// The per-launch sizes: computed once per CTA (after the routing plan has counted U and Gt) into shared memory,
+// read from there by every role, so that they do not occupy registers of the pipelines' loops.
+__device__ void make_layout(Layout& L, const Params& p, int M, int U, int Gt, int grid) {
+    L.R1 = (2 * p.I) / 128;
+    L.R2 = p.H / 128;
+    L.has_shw = p.shw13 != nullptr;
+    L.has_gate = (p.shared != nullptr || L.has_shw) ? 1 : 0;
+    L.Rs1 = L.has_shw ? (2 * p.Is) / 128 : 0;
+    L.ngs = (M + TG - 1) / TG;
+    L.ngc = (M + CB_TOK - 1) / CB_TOK;
+    L.U = U;
+    L.Gt = Gt;
+    L.b_s1 = L.has_gate ? 1 : 0;
+    L.b_g1 = L.b_s1 + (L.has_shw ? L.Rs1 * NSPLIT * L.ngs : 0);
+    // split the gate_up items only when every half still fits in one wave of pipelines: then the halves shorten
+    // the critical path; with more items the split only adds the hand-off of the partials. The test uses the
+    // bound M * topk on the token groups, not this launch's count, so that a shard (mode 1) decides exactly as
+    // the whole layer does and the sums keep the same association.
+    L.g1s = G1_SPLIT * L.R1 * M * p.topk <= grid * NVP ? G1_SPLIT : 1;
+    L.b_s1f = L.b_g1 + L.R1 * L.Gt * L.g1s;
+    L.b_s2 = L.b_s1f + (L.has_shw ? L.Rs1 * L.ngs : 0);
+    L.b_g2 = L.b_s2 + (L.has_shw ? L.R2 * L.ngs : 0);
+    L.b_cb = L.b_g2 + L.R2 * L.Gt;
+    L.total = L.b_cb + L.R2 * L.ngc;
+    L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
+    L.g1_cnt_off = L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0;
+    L.g1_part_off = L.g1_cnt_off + (((size_t)M * p.topk * L.R1 + 3) & ~(size_t)3);
+}
 
 __device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   // largest u with gpre[u] <= key
     int lo = 0, hi = U - 1;
@@ -227,12 +259,13 @@ __device__ __forceinline__ void stage_w4_to_tmem(const uint8_t* w, uint32_t ta) 
 #pragma unroll
     for (int hq = 0; hq < 4; ++hq) {
         const uint4 q = *reinterpret_cast<const uint4*>(w + hq * 128 * 16);
-        uint32_t v[16];
+        uint32_t v[8];
         qf::signed_w4(q.x, v + 0);
         qf::signed_w4(q.y, v + 4);
-        qf::signed_w4(q.z, v + 8);
-        qf::signed_w4(q.w, v + 12);
-        qf::tmem_st16(ta + 16 * hq, v);
+        qf::tmem_st8(ta + 16 * hq, v);
+        qf::signed_w4(q.z, v + 0);
+        qf::signed_w4(q.w, v + 4);
+        qf::tmem_st8(ta + 16 * hq + 8, v);
     }
 }
 
@@ -411,7 +444,13 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         qf::tmem_alloc(reinterpret_cast<uint32_t*>(misc + MISC_TMEM), TM_COLS);
         qf::tmem_relinquish();
     }
-    __syncwarp();
+    // the plan's expert bitmasks live in shared scratch only: cleared before the wait on the previous kernel
+    {
+        uint64_t* mask = reinterpret_cast<uint64_t*>(smem + SCR_MASK);
+        for (int e = tid; e < E; e += MOE_THREADS) mask[e] = 0ull;
+        if (tid == 0) misc[MISC_DUPS] = 0;
+    }
+    __syncthreads();
     // Everything below reads data of the previous kernel (topk ids, x) or the control block it may re-arm.
     qf::pdl_wait();
     // each producer claims its first item now: the atomic's round trip overlaps the routing plan
@@ -426,9 +465,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         int16_t* exg = exc + QF_MAX_EXPERTS;
         int16_t* toffe = reinterpret_cast<int16_t*>(smem + SCR_TOFFE);
         int* chunk = reinterpret_cast<int*>(smem + SCR_CHUNK);
-        for (int e = tid; e < E; e += MOE_THREADS) mask[e] = 0ull;
-        __syncthreads();
-        bool bad = false;
+        bool bad = false, dup = false;
         for (int s = tid; s < nslots; s += MOE_THREADS) {
             const int e = p.ids[s];
             tws[s] = bf16r(p.tw[s]);   // the down epilogues read the slot weights from here, not from L2
@@ -439,9 +476,12 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             }
             sids[s] = (int16_t)e;
             if (e < p.elo || e >= p.ehi) continue;
-            atomicOr(reinterpret_cast<unsigned long long*>(mask + e), 1ull << (s / topk));
+            const unsigned long long bit = 1ull << (s / topk);
+            // a token that names one expert in two slots (never from the router; possible through the op's API)
+            dup |= (atomicOr(reinterpret_cast<unsigned long long*>(mask + e), bit) & bit) != 0ull;
         }
         if (bad) set_err(ctrl, QF_MOE_ERR_BAD_EXPERT);
+        if (dup) misc[MISC_DUPS] = 1;
         __syncthreads();
         const int nch = (E + 31) >> 5;
         for (int c = warp; c < nch; c += MOE_THREADS / 32) {
@@ -487,17 +527,22 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         if (tid == 0) {
             toff[misc[MISC_U]] = (int16_t)misc[MISC_NTOK];
             gpre[misc[MISC_U]] = (int16_t)misc[MISC_GT];
+            make_layout(*reinterpret_cast<Layout*>(plan + PLAN_LAYOUT), p, M, misc[MISC_U], misc[MISC_GT],
+                        (int)gridDim.x);
         }
         __syncthreads();
+        const bool any_dup = misc[MISC_DUPS] != 0;
         for (int s = tid; s < nslots; s += MOE_THREADS) {
             const int e = sids[s];
             dupn[s] = -1;
             if (e < 0 || e < p.elo || e >= p.ehi) continue;
             const int t = s / topk, kp = s - t * topk;
             bool first = true;
-            for (int k2 = 0; k2 < kp; ++k2) first &= sids[t * topk + k2] != e;
-            for (int k2 = topk - 1; k2 > kp; --k2)   // the next slot of this token routed to the same expert
-                if (sids[t * topk + k2] == e) dupn[s] = (int16_t)(t * topk + k2);
+            if (any_dup) {
+                for (int k2 = 0; k2 < kp; ++k2) first &= sids[t * topk + k2] != e;
+                for (int k2 = topk - 1; k2 > kp; --k2)   // the next slot of this token routed to the same expert
+                    if (sids[t * topk + k2] == e) dupn[s] = (int16_t)(t * topk + k2);
+            }
             if (first) {
                 const int j = __popcll(mask[e] & ((1ull << t) - 1ull));
                 tlist[toffe[e] + j] = (int16_t)s;
@@ -509,31 +554,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     const uint32_t tmem_all = (uint32_t)misc[MISC_TMEM];
     const uint32_t tmem = tmem_all + TM_VP * (uint32_t)vp;   // this pipeline's slice
 
-    Layout L;
-    L.R1 = (2 * p.I) / 128;
-    L.R2 = p.H / 128;
-    L.has_shw = p.shw13 != nullptr;
-    L.has_gate = (p.shared != nullptr || L.has_shw) ? 1 : 0;
-    L.Rs1 = L.has_shw ? (2 * p.Is) / 128 : 0;
-    L.ngs = (M + TG - 1) / TG;
-    L.ngc = (M + CB_TOK - 1) / CB_TOK;
-    L.U = misc[MISC_U];
-    L.Gt = misc[MISC_GT];
-    L.b_s1 = L.has_gate ? 1 : 0;
-    L.b_g1 = L.b_s1 + (L.has_shw ? L.Rs1 * NSPLIT * L.ngs : 0);
-    // split the gate_up items only when every half still fits in one wave of pipelines: then the halves shorten
-    // the critical path; with more items the split only adds the hand-off of the partials. The test uses the
-    // bound M * topk on the token groups, not this launch's count, so that a shard (mode 1) decides exactly as
-    // the whole layer does and the sums keep the same association.
-    L.g1s = G1_SPLIT * L.R1 * M * p.topk <= (int)gridDim.x * NVP ? G1_SPLIT : 1;
-    L.b_s1f = L.b_g1 + L.R1 * L.Gt * L.g1s;
-    L.b_s2 = L.b_s1f + (L.has_shw ? L.Rs1 * L.ngs : 0);
-    L.b_g2 = L.b_s2 + (L.has_shw ? L.R2 * L.ngs : 0);
-    L.b_cb = L.b_g2 + L.R2 * L.Gt;
-    L.total = L.b_cb + L.R2 * L.ngc;
-    L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
-    L.g1_cnt_off = L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0;
-    L.g1_part_off = L.g1_cnt_off + (((size_t)M * p.topk * L.R1 + 3) & ~(size_t)3);
+    const Layout& L = *reinterpret_cast<const Layout*>(plan + PLAN_LAYOUT);
 
 
     if (warp == AGENT_WARP) {
