@@ -2,13 +2,15 @@
 """Benchmark of the decode MoE layer-step on B200: router top-k + W4A16 routed experts + shared expert + combine.
 
 Default workload: H=2048, 512 experts, top-10 renormalised, I=512 int4 group-128 experts,
-bf16 shared expert (Is=512), M=10 tokens. A "step" is one layer-step (router_topk + a16_moe_decode, two kernels);
+bf16 shared expert (Is=512), M=10 tokens. A "step" is one layer-step: router + routed experts + shared expert +
+combine in one launch (the fused layer-step of ops.moe_layer_step; us_router_kernel times the separate router op);
 the timed loop replays a CUDA graph over L distinct synthetic layers (default 16, 13.6 GB of weights), so every
 step streams its experts from HBM (each step touches ~157 MB, a full cycle ~2.5 GB >> 126 MB L2).
 
 Output: one JSON line (rank 0). value = microseconds per layer-step (lower is better); roofline = the MoE kernel's
 algorithmic bytes per launch / its CUDA-event launch time vs the measured HBM copy bandwidth; e2e = the same step
-through the public ops with pinned-host x in and out copied back every step; cpu_baseline = the CPU oracle (a port
+through the public ops with x in pinned host memory and out written to pinned host memory every step (one GPU: read
+and written by the launch itself; expert parallelism: copy-engine transfers); cpu_baseline = the CPU oracle (a port
 of the reference's torch dequant-and-matmul path) on this host.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--M 10] [--layers 16]
@@ -356,15 +358,24 @@ def run_ours(args):
         dist.all_gather(allf, mine)
         rank_frac = [round(float(t.item()), 4) for t in allf]
 
-    # end to end through the public ops: pinned host x in, result out, every step
+    # end to end through the public ops: pinned host x in, result out, every step. One GPU: the fused layer-step
+    # reads x from pinned host memory itself (staged to device memory inside the launch) and writes out to pinned
+    # host memory; expert parallelism: copy-engine transfers around the step.
     xh = x0.cpu().pin_memory()
     oh = torch.empty_like(xh).pin_memory()
     xd = torch.empty_like(x0)
     od = torch.empty_like(x0)
+
+    def e2e_step(l):
+        if epar:
+            xd.copy_(xh, non_blocking=True)
+            layer_step(xd, l, od)
+            oh.copy_(od, non_blocking=True)
+        else:
+            ops.moe_layer_step(xh, layers[l], cfg.topk, bufs, rb, oh, x_stage=xd)
+
     for l in range(NL):
-        xd.copy_(xh, non_blocking=True)
-        layer_step(xd, l, od)
-        oh.copy_(od, non_blocking=True)
+        e2e_step(l)
     torch.cuda.synchronize()
     n_e2e = min(args.steps, 4 * NL)
     if world > 1:
@@ -372,9 +383,7 @@ def run_ours(args):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record()
     for i in range(n_e2e):
-        xd.copy_(xh, non_blocking=True)
-        layer_step(xd, i % NL, od)
-        oh.copy_(od, non_blocking=True)
+        e2e_step(i % NL)
     ev1.record()
     torch.cuda.synchronize()
     e2e_ms = ev0.elapsed_time(ev1)
@@ -415,7 +424,9 @@ def run_ours(args):
                          "traffic": load_traffic("moe_persistent_kernel")},
             "e2e": {"value": us_e2e, "unit": UNIT, "h2d_bytes_per_step": M * cfg.H * 2,
                     "d2h_bytes_per_step": M * cfg.H * 2, "steps": n_e2e},
-            "gpu_launches": (3 if epar else 2) * steps,
+            # ours per step: the fused layer-step launch (+ the combine under expert parallelism; the all-reduce is
+            # NCCL's)
+            "gpu_launches": (2 if epar else 1) * steps,
             "clocks": clk.summary(),
         }
         if cpu:

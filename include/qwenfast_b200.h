@@ -110,6 +110,28 @@ int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_
                       void* out, int M, int H, int I, int E, int topk, int Is, int phase, int mode, int expert_lo,
                       int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream);
 
+/* One decode MoE layer-step with the router inside the same launch (no counterpart in the reference, whose `dual`
+ * path -- serve/overlays/sglang/srt/qwenfast.py:1177-1201 -- calls router_topk and then a16_moe_decode; this entry
+ * gives the caller the outputs of both): every CTA computes bf16 logits of E / SMs router rows, a grid barrier on
+ * ctrl follows, then every CTA runs the router's softmax / top-k / renormalise (the routine of qf_router_topk) on
+ * all rows and the layer continues as qf_a16_moe_decode (phase 4). router_w bf16 [E, H] (H % 256 == 0, <= 4096,
+ * 16-byte aligned); outputs topk_w fp32 [M, topk], topk_ids int32 [M, topk], logits bf16 [M, E]. The logits are
+ * fp32 dot products in this kernel's own order, rounded to bf16 (within one bf16 ulp of qf_router_topk's); ids and
+ * weights follow from them exactly as in qf_router_topk. Other arguments as qf_a16_moe_decode; ctrl also holds the
+ * barrier's counter (re-armed by the kernel). All CTAs of the launch must become resident (one per SM): the barrier's
+ * wait is bounded (~1 s), after which the sticky error word is set and the items stop.
+ * x_stage: NULL (x is device memory), or a device buffer bf16 [M, H], 16-byte aligned: then x is pinned host memory
+ *   (page-locked, mapped into the device's address space, as cudaHostAlloc gives under unified addressing) that the
+ *   kernel itself copies into x_stage (each CTA a slice, then a second grid barrier) instead of a copy-engine transfer;
+ *   out may likewise be pinned host memory (the combine writes it directly). */
+int qf_moe_layer_decode(const void* x, void* x_stage, const void* router_w, int renormalize, float* topk_w, int32_t* topk_ids,
+                        void* logits, const int32_t* w13, const void* s13, const void* gs13, const int32_t* w2,
+                        const void* s2, const void* gs2, const void* w_gate, const void* shared, const void* sh_w13,
+                        const void* sh_w2, void* hbuf, int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl,
+                        int64_t gl_numel, int32_t* ctrl, int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel,
+                        void* shbuf, int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk, int Is,
+                        int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream);
+
 /* Expert-parallel finish: out = the mode-0 combine of a ybuf [M, topk + 1, H] summed over the shards.
  * gl fp32 [M] is recomputed from x and w_gate when w_gate is given (has_shared != 0). */
 int qf_moe_combine(const void* ybuf, const void* x, const void* w_gate, int has_shared, void* out, int M, int H,

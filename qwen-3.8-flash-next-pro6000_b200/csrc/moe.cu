@@ -45,6 +45,7 @@
 //     from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
 //   * Every wait is bounded; a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
 #include "qf_common.cuh"
+#include "topk.cuh"
 
 namespace {
 
@@ -85,6 +86,8 @@ enum : int {
     C_EXIT = 1,
     C_GLF = 2,
     C_ERR = QF_MOE_CTRL_ERR,
+    C_RBAR = 4,     // fused router: CTAs whose logits are stored (grid barrier)
+    C_XBAR = 5,     // fused router with host input: CTAs whose slice of x is in device memory (grid barrier)
     C_CNT = 8,      // [64] column-tile arrivals
     C_SDONE = 72,   // [4] finished shared gate_up tiles per token group
     C_SPLIT = 80,   // [64] split-K arrivals per (shared tile, token group)
@@ -127,6 +130,12 @@ struct Params {
     __nv_bfloat16* sbuf;
     __nv_bfloat16* out;
     long long* dbg;
+    const __nv_bfloat16* rw;   // fused router: router weight [E, H]; nullptr when topk ids / weights are inputs
+    __nv_bfloat16* logits;     // fused router outputs: logits bf16 [M, E], ids int32 [M, topk], weights fp32 [M, topk]
+    int* ids_out;
+    float* tw_out;
+    int renorm;
+    const __nv_bfloat16* xsrc;   // fused router: x in pinned (mapped) host memory, copied into x by the kernel, or nullptr
     int M, H, I, E, topk, Is, mode, elo, ehi;
     int wofs;   // expert id of the first expert in w13 / s13 / w2 / s2 / gs13 / gs2 (mode 1: elo)
 };
@@ -161,7 +170,12 @@ constexpr int SCR_MASK = 0;                                        // uint64 [E]
 constexpr int SCR_EXF = SCR_MASK + QF_MAX_EXPERTS * 8;             // int16 [E] x 3 (flag, count, groups) in-chunk
 constexpr int SCR_TOFFE = SCR_EXF + 3 * QF_MAX_EXPERTS * 2;        // int16 [E] token offset per expert id
 constexpr int SCR_CHUNK = SCR_TOFFE + QF_MAX_EXPERTS * 2;          // int32 [32] x 3 chunk totals
-static_assert(SCR_CHUNK + 3 * 32 * 4 <= NST * STAGE_BYTES, "plan scratch (pipeline 0's ring)");
+constexpr int SCR_RIDS = SCR_CHUNK + 3 * 32 * 4;                   // int32 [MAXSLOTS] fused router: selected ids
+constexpr int SCR_RTW = SCR_RIDS + MAXSLOTS * 4;                    // fp32 [MAXSLOTS] fused router: their weights
+static_assert(SCR_RTW + MAXSLOTS * 4 <= NST * STAGE_BYTES, "plan scratch (pipeline 0's ring)");
+// fused router: this CTA's router rows live in pipeline 1's ring (idle until the plan is done)
+constexpr int RROWS_BYTES = NST * STAGE_BYTES;
+constexpr int RPC_MAX = 8;                                          // router rows per CTA
 
 enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6, MISC_DUPS = 7 };
 
@@ -181,18 +195,36 @@ __device__ __forceinline__ void set_err(uint32_t* ctrl, uint32_t bits) { atomicO
 __device__ __forceinline__ bool hard_error(uint32_t* ctrl) { return (qf::ld_volatile(ctrl + C_ERR) & HARD_ERR) != 0u; }
 
 // Bounded wait until ctrl[idx] >= target (acquire). Gives up early when another CTA already recorded a hard error.
+// Bounded spin until ctrl[idx] >= target (acquire). The bound is counted in SM cycles (2 per ns: at most ~1 s at
+// the B200's clocks); the sticky error word and the bound are checked every 16 polls, so that a poll costs one L2
+// round trip.
 __device__ bool wait_counter(uint32_t* ctrl, int idx, uint32_t target) {
     if (qf::ld_acquire(ctrl + idx) >= target) return true;
-    const uint64_t t0 = qf::globaltimer();
-    while (qf::ld_acquire(ctrl + idx) < target) {
-        if (hard_error(ctrl)) return false;
-        if (qf::globaltimer() - t0 > DEP_WAIT_NS) {
-            set_err(ctrl, QF_MOE_ERR_TIMEOUT);
-            return false;
+    const long long t0 = clock64();
+    const long long lim = (long long)(2 * DEP_WAIT_NS);
+    for (uint32_t it = 1;; ++it) {
+        __nanosleep(32);
+        if (qf::ld_acquire(ctrl + idx) >= target) return true;
+        if ((it & 15u) == 0u) {
+            if (hard_error(ctrl)) return false;
+            if (clock64() - t0 > lim) {
+                set_err(ctrl, QF_MOE_ERR_TIMEOUT);
+                return false;
+            }
         }
-        __nanosleep(64);
     }
-    return true;
+}
+
+// Every CTA of the launch arrives, then waits (bounded) for all: writes before the barrier are visible to loads at
+// L2 level (ld.cg / cp.async.cg) after it. The counter is re-armed at the launch's exit.
+__device__ void grid_barrier(uint32_t* ctrl, int idx) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(ctrl + idx, 1u);
+        wait_counter(ctrl, idx, gridDim.x);   // a timeout sets the sticky error; the items then stop
+    }
+    __syncthreads();
 }
 
 struct Layout {   // per-launch derived sizes, identical in every thread
@@ -444,6 +476,18 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         qf::tmem_alloc(reinterpret_cast<uint32_t*>(misc + MISC_TMEM), TM_COLS);
         qf::tmem_relinquish();
     }
+    // fused router: this CTA's router rows (load-time constants) are requested before the wait on the previous
+    // kernel; CTA c owns rows [c rpc, c rpc + rpc)
+    const bool fused = p.rw != nullptr;
+    const int rpc = fused ? (E + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+    const int r0 = (int)blockIdx.x * rpc;
+    const int nrows = fused ? max(0, min(E, r0 + rpc) - r0) : 0;
+    uint8_t* rrows = smem + VP_BYTES;
+    if (nrows > 0) {
+        const int chunks = nrows * (p.H / 8);
+        const char* src = reinterpret_cast<const char*>(p.rw + (size_t)r0 * p.H);
+        for (int c = tid; c < chunks; c += MOE_THREADS) qf::cp_async16(rrows + 16 * c, src + 16 * c, 16u);
+    }
     // the plan's expert bitmasks live in shared scratch only: cleared before the wait on the previous kernel
     {
         uint64_t* mask = reinterpret_cast<uint64_t*>(smem + SCR_MASK);
@@ -456,6 +500,71 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     // each producer claims its first item now: the atomic's round trip overlaps the routing plan
     int first_item = 0;
     if (warp < AGENT_WARP && vw == VP_PRODUCER && lane == 0) first_item = (int)atomicAdd(ctrl + C_QUEUE, 1u);
+    int* rids = reinterpret_cast<int*>(smem + SCR_RIDS);
+    float* rtw = reinterpret_cast<float*>(smem + SCR_RTW);
+    if (fused && p.xsrc != nullptr) {
+        // the layer input is in pinned host memory: each CTA copies its slice into the device copy p.x (one PCIe
+        // round trip), then a grid barrier; every later read of x goes to the device copy
+        const int nch = M * p.H / 8;
+        const int per = (nch + (int)gridDim.x - 1) / (int)gridDim.x;
+        const int c1 = min(nch, ((int)blockIdx.x + 1) * per);
+        const uint4* src = reinterpret_cast<const uint4*>(p.xsrc);
+        uint4* dst = reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(p.x));
+        for (int c = (int)blockIdx.x * per + tid; c < c1; c += MOE_THREADS) __stcg(dst + c, __ldcv(src + c));
+        grid_barrier(ctrl, C_XBAR);
+    }
+    if (fused) {
+        // ---------------------------------------------------------------- fused router (serve/qwenfast/qf_router.cu)
+        // logits[t, e] = bf16(x[t] . w[e]) for this CTA's rows: one warp per token, lanes over 16-byte k chunks
+        // (fp32 fma in chunk order, then a butterfly sum); then a grid barrier, and every CTA selects the top-k
+        // of every token itself (the same routine as the router kernel), so the plan needs no ids from memory
+        qf::cp_async_wait_all();
+        __syncthreads();
+        const int nc = p.H / 8;
+        for (int t = warp; t < M; t += MOE_THREADS / 32) {
+            float a[RPC_MAX];
+#pragma unroll
+            for (int r = 0; r < RPC_MAX; ++r) a[r] = 0.f;
+            const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)t * p.H);
+            for (int c0 = 0; c0 < nc; c0 += 8 * 32) {   // eight chunks per lane in flight
+                uint4 xv[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int c = c0 + 32 * j + lane;
+                    xv[j] = c < nc ? __ldcg(xr + c) : make_uint4(0u, 0u, 0u, 0u);
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int c = c0 + 32 * j + lane;
+                    if (c >= nc) continue;
+                    const uint32_t xw[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+#pragma unroll
+                    for (int r = 0; r < RPC_MAX; ++r) {
+                        if (r >= nrows) continue;
+                        const uint4 wv = *reinterpret_cast<const uint4*>(rrows + ((size_t)r * nc + c) * 16);
+                        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            a[r] = fmaf(__uint_as_float(ww[i] << 16), __uint_as_float(xw[i] << 16), a[r]);
+                            a[r] = fmaf(__uint_as_float(ww[i] & 0xffff0000u), __uint_as_float(xw[i] & 0xffff0000u), a[r]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < RPC_MAX; ++r) {
+                if (r >= nrows) continue;
+                float v = a[r];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0) p.logits[(size_t)t * E + r0 + r] = __float2bfloat16(v);
+            }
+        }
+        grid_barrier(ctrl, C_RBAR);
+        for (int t = warp; t < M; t += MOE_THREADS / 32)
+            qf::topk_row_any(p.logits + (size_t)t * E, E, topk, p.renorm, rtw + t * topk, rids + t * topk);
+        __syncthreads();
+    }
 
     // ------------------------------------------------------------------ routing plan (all threads)
     {
@@ -467,8 +576,13 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         int* chunk = reinterpret_cast<int*>(smem + SCR_CHUNK);
         bool bad = false, dup = false;
         for (int s = tid; s < nslots; s += MOE_THREADS) {
-            const int e = p.ids[s];
-            tws[s] = bf16r(p.tw[s]);   // the down epilogues read the slot weights from here, not from L2
+            const int e = fused ? rids[s] : p.ids[s];
+            const float twv = fused ? rtw[s] : p.tw[s];
+            tws[s] = bf16r(twv);   // the down epilogues read the slot weights from here, not from L2
+            if (fused && blockIdx.x == 0) {   // the fused router's outputs for the caller
+                p.ids_out[s] = e;
+                p.tw_out[s] = twv;
+            }
             if (e < 0 || e >= E) {
                 bad = true;
                 sids[s] = -1;
@@ -1246,14 +1360,21 @@ extern "C" int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64
     return QF_OK;
 }
 
-extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* w13,
-                                 const void* s13, const void* gs13, const int32_t* w2, const void* s2, const void* gs2,
-                                 const void* w_gate, const void* shared, const void* sh_w13, const void* sh_w2,
-                                 void* hbuf, int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl,
-                                 int64_t gl_numel, int32_t* ctrl, int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel,
-                                 void* shbuf, int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk,
-                                 int Is, int phase, int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl,
-                                 qf_stream_t stream) {
+namespace {
+struct FusedRouter {   // the router inputs and outputs of qf_moe_layer_decode
+    const void* w;
+    int renorm;
+    void* logits;
+    void* x_stage;   // device copy of x when x is in pinned host memory, or nullptr
+};
+
+int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* w13, const void* s13,
+               const void* gs13, const int32_t* w2, const void* s2, const void* gs2, const void* w_gate,
+               const void* shared, const void* sh_w13, const void* sh_w2, void* hbuf, int64_t hbuf_bytes, void* ybuf,
+               int64_t ybuf_bytes, float* gl, int64_t gl_numel, int32_t* ctrl, int64_t ctrl_numel, float* pbuf,
+               int64_t pbuf_numel, void* shbuf, int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk,
+               int Is, int phase, int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream,
+               const FusedRouter* fr) {
     QF_REQUIRE(x && topk_ids && topk_w && w13 && s13 && w2 && s2 && hbuf && ybuf && gl && ctrl && out,
                "a16_moe_decode: null pointer argument");
     QF_REQUIRE(phase == 3 || phase == 4,
@@ -1290,6 +1411,16 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaGetDevice");
     const int sms = qf::sm_count(dev);
     QF_REQUIRE(sms > 0, "a16_moe_decode: cannot query the SM count");
+    if (fr != nullptr) {
+        QF_REQUIRE(fr->w && fr->logits, "moe_layer_decode: null router weight or logits");
+        QF_REQUIRE(qf::aligned(fr->w, 16), "moe_layer_decode: the router weight must be 16-byte aligned");
+        QF_REQUIRE(H % 256 == 0 && H <= 4096, "moe_layer_decode: H must be a multiple of 256 <= 4096, got %d", H);
+        const int rpc = (E + sms - 1) / sms;
+        QF_REQUIRE(rpc <= RPC_MAX && (int64_t)rpc * H * 2 <= RROWS_BYTES,
+                   "moe_layer_decode: %d router rows per CTA of %d do not fit (E %d, H %d)", rpc, sms, E, H);
+        QF_REQUIRE(fr->x_stage == nullptr || qf::aligned(fr->x_stage, 16),
+                   "moe_layer_decode: x_stage must be 16-byte aligned");
+    }
     ce = qf::ensure_smem_attr(reinterpret_cast<const void*>(moe_persistent_kernel), MOE_SMEM);
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute");
     static bool carveout_set[64] = {false};
@@ -1329,9 +1460,49 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
     p.M = M; p.H = H; p.I = I; p.E = E; p.topk = topk; p.Is = has_shw ? Is : 0;
     p.mode = mode; p.elo = expert_lo; p.ehi = expert_hi;
     p.wofs = mode == 1 ? expert_lo : 0;
+    p.rw = fr ? static_cast<const __nv_bfloat16*>(fr->w) : nullptr;
+    p.logits = fr ? static_cast<__nv_bfloat16*>(fr->logits) : nullptr;
+    p.ids_out = fr ? const_cast<int*>(topk_ids) : nullptr;
+    p.tw_out = fr ? const_cast<float*>(topk_w) : nullptr;
+    p.renorm = fr ? (fr->renorm != 0) : 0;
+    p.xsrc = nullptr;
+    if (fr && fr->x_stage) {   // x is pinned host memory (read by the kernel through its mapping); x_stage its copy
+        p.xsrc = p.x;
+        p.x = static_cast<const __nv_bfloat16*>(fr->x_stage);
+    }
     ce = qf::launch_ex(moe_persistent_kernel, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,
                        reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);
     return qf::cuda_status(ce, "a16_moe_decode: launch");
+}
+}  // namespace
+
+extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* w13,
+                                 const void* s13, const void* gs13, const int32_t* w2, const void* s2, const void* gs2,
+                                 const void* w_gate, const void* shared, const void* sh_w13, const void* sh_w2,
+                                 void* hbuf, int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl,
+                                 int64_t gl_numel, int32_t* ctrl, int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel,
+                                 void* shbuf, int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk,
+                                 int Is, int phase, int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl,
+                                 qf_stream_t stream) {
+    return moe_launch(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, shared, sh_w13, sh_w2, hbuf,
+                      hbuf_bytes, ybuf, ybuf_bytes, gl, gl_numel, ctrl, ctrl_numel, pbuf, pbuf_numel, shbuf,
+                      shbuf_bytes, out, M, H, I, E, topk, Is, phase, mode, expert_lo, expert_hi, dbg, pdl, stream,
+                      nullptr);
+}
+
+extern "C" int qf_moe_layer_decode(const void* x, void* x_stage, const void* router_w, int renormalize, float* topk_w,
+                                   int32_t* topk_ids, void* logits, const int32_t* w13, const void* s13,
+                                   const void* gs13, const int32_t* w2, const void* s2, const void* gs2,
+                                   const void* w_gate, const void* shared, const void* sh_w13, const void* sh_w2,
+                                   void* hbuf, int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl,
+                                   int64_t gl_numel, int32_t* ctrl, int64_t ctrl_numel, float* pbuf,
+                                   int64_t pbuf_numel, void* shbuf, int64_t shbuf_bytes, void* out, int M, int H,
+                                   int I, int E, int topk, int Is, int mode, int expert_lo, int expert_hi,
+                                   int64_t* dbg, int pdl, qf_stream_t stream) {
+    const FusedRouter fr{router_w, renormalize, logits, x_stage};
+    return moe_launch(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, shared, sh_w13, sh_w2, hbuf,
+                      hbuf_bytes, ybuf, ybuf_bytes, gl, gl_numel, ctrl, ctrl_numel, pbuf, pbuf_numel, shbuf,
+                      shbuf_bytes, out, M, H, I, E, topk, Is, 4, mode, expert_lo, expert_hi, dbg, pdl, stream, &fr);
 }
 
 extern "C" int qf_moe_combine(const void* ybuf, const void* x, const void* w_gate, int has_shared, void* out, int M,

@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "qf_common.cuh"
+#include "topk.cuh"
 
 namespace {
 
@@ -29,86 +30,6 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const uint4* p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "l"(p));
     return v;
-}
-
-// Ranking of one logit, larger is better: bits 10..26 the order-preserving key of the value (top 17 bits of the
-// monotone uint32 image of the float; NaN ranks as -1e30, -0 as +0), bits 0..9 1023 - expert id, so that among
-// equal values the lower id wins and one unsigned max picks the winner. The logits are bf16 values (fp32 copies), so
-// 17 bits order them exactly: a bf16 value's image has its low 16 bits all equal, and the image of -1e30 (not a
-// bf16 value) falls strictly between those of its two bf16 neighbours. 0 means "no candidate".
-constexpr float RANK_NAN_AS = -1e30f;
-__device__ __forceinline__ uint32_t image17(float v) {
-    const float r = (v == v) ? v : RANK_NAN_AS;
-    uint32_t u = __float_as_uint(r);
-    if (u == 0x80000000u) u = 0u;
-    return ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) >> 15;
-}
-__device__ __forceinline__ uint32_t rank_of(float v, int e) { return (image17(v) << 10) | (uint32_t)(1023 - e); }
-// the logit a rank was made from (NaN for the NaN stand-in)
-__device__ __forceinline__ float logit_of(uint32_t rank) {
-    const uint32_t k17 = rank >> 10;
-    if (k17 == image17(RANK_NAN_AS)) return __uint_as_float(0x7fc00000u);
-    const uint32_t img = (k17 << 15) | ((k17 & 1u) ? 0x7fffu : 0u);
-    return __uint_as_float((img & 0x80000000u) ? (img & 0x7fffffffu) : ~img);
-}
-
-// softmax + top-k of one token row (E logits, fp32 copies of the bf16 values) by one warp. Each round takes the
-// warp-wide largest rank (a lane-local max tree, then one redux) and clears it; lane k keeps round k's winner. The
-// probabilities are formed afterwards, all lanes at once: p_k = exp(logit_k - max) / sum, the same operands as a
-// softmax over the row, and the renormalising sum runs over p_0, p_1, ... in selection order.
-template <int PL>
-__device__ void topk_row(const float* __restrict__ row, int E, int topk, int renorm, float* __restrict__ wout,
-                         int* __restrict__ iout) {
-    const int lane = threadIdx.x & 31;
-    float v[PL];
-    uint32_t rk[PL];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < PL; ++i) {
-        const int e = i * 32 + lane;
-        v[i] = e < E ? __ldcg(row + e) : -INFINITY;
-        mx = fmaxf(mx, v[i]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < PL; ++i) {
-        const int e = i * 32 + lane;
-        rk[i] = e < E ? rank_of(v[i], e) : 0u;
-        sum += __expf(v[i] - mx);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-
-    uint32_t mine = 0u;
-    for (int k = 0; k < topk; ++k) {
-        uint32_t t[PL];
-#pragma unroll
-        for (int i = 0; i < PL; ++i) t[i] = rk[i];
-#pragma unroll
-        for (int w = 1; w < PL; w <<= 1) {
-#pragma unroll
-            for (int i = 0; i + w < PL; i += 2 * w) t[i] = max(t[i], t[i + w]);
-        }
-        const uint32_t win = __reduce_max_sync(0xffffffffu, t[0]);
-#pragma unroll
-        for (int i = 0; i < PL; ++i) rk[i] = rk[i] == win ? 0u : rk[i];
-        mine = lane == k ? win : mine;
-    }
-    float p = 0.f;
-    int id = -1;
-    if (lane < topk && mine != 0u) {
-        id = 1023 - (int)(mine & 1023u);
-        p = __expf(logit_of(mine) - mx) / sum;
-    }
-    float routed = 0.f;
-    for (int k = 0; k < topk; ++k) routed += __shfl_sync(0xffffffffu, p, k);
-    if (lane < topk) {
-        const float norm = routed > 0.f ? routed : 1.f;
-        wout[lane] = renorm ? p / norm : p;
-        iout[lane] = id;
-    }
 }
 
 template <int BPW>
@@ -201,18 +122,9 @@ __global__ void __launch_bounds__(RT, 1)
     if (!s_last) return;
     __threadfence();
     if (tid == 0) *counter = 0u;
-    const int pl = (E + 31) / 32;
-    for (int tok = warp; tok < rows; tok += RW) {
-        const float* row = scratch + (size_t)tok * E;
-        float* wo = weights + (size_t)tok * topk;
-        int* io = ids + (size_t)tok * topk;
-        if (pl <= 1) topk_row<1>(row, E, topk, renorm, wo, io);
-        else if (pl <= 2) topk_row<2>(row, E, topk, renorm, wo, io);
-        else if (pl <= 4) topk_row<4>(row, E, topk, renorm, wo, io);
-        else if (pl <= 8) topk_row<8>(row, E, topk, renorm, wo, io);
-        else if (pl <= 16) topk_row<16>(row, E, topk, renorm, wo, io);
-        else topk_row<32>(row, E, topk, renorm, wo, io);
-    }
+    for (int tok = warp; tok < rows; tok += RW)
+        qf::topk_row_any(scratch + (size_t)tok * E, E, topk, renorm, weights + (size_t)tok * topk,
+                         ids + (size_t)tok * topk);
 }
 
 template <int BPW>

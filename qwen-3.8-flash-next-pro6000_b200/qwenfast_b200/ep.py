@@ -2,8 +2,8 @@
 
 Partition (the plan for the reference's single-GPU layer, ``serve/qwenfast/qf_a16moe.cu:852-922``, spread over
 G GPUs): rank r holds the contiguous experts ``[r*E/G, (r+1)*E/G)``; the tokens and the router are replicated.
-Every rank runs the router itself (identical ids everywhere: the kernel is deterministic), then the MoE kernel in
-shard mode on its local experts. Each (token, top-k position) slot has exactly one owner, so the shards' slot
+Every rank runs the router itself (identical ids everywhere: the kernels are deterministic), inside its MoE launch
+(fused router) or as its own launch, then the MoE kernel in shard mode on its local experts. Each (token, top-k position) slot has exactly one owner, so the shards' slot
 buffers sum exactly (every other rank contributes zeros); one all-reduce over NCCL / NVLink gives every rank the
 full slot buffer and the combine kernel finishes the layer -- the same bits as one GPU. The shared expert runs on
 one rank (``shared_rank``), whose slot buffer carries its output.
@@ -52,19 +52,27 @@ def reduce_slots(slots: torch.Tensor, group=None) -> torch.Tensor:
 
 def ep_layer_step(x: torch.Tensor, shard: ops.MoELayerWeights, topk: int, bufs: dict, rbufs, out: torch.Tensor,
                   rank: int, world: int, has_shared: Optional[bool] = None, group=None, renormalize: bool = True,
-                  pdl: bool = True):
-    """One expert-parallel decode layer-step on this rank: router (replicated), local experts (shard mode),
-    all-reduce of the slot buffer, combine. ``shard`` comes from ``shard_weights``; ``has_shared`` says whether the
-    layer has a shared expert (on any rank; default: this rank holds w_gate). Returns (out, topk_w, topk_ids)."""
+                  pdl: bool = True, fused: bool = True):
+    """One expert-parallel decode layer-step on this rank: router (replicated; inside the MoE launch when
+    ``fused``), local experts (shard mode), all-reduce of the slot buffer, combine. ``shard`` comes from
+    ``shard_weights``; ``has_shared`` says whether the layer has a shared expert (on any rank; default: this rank
+    holds w_gate). Returns (out, topk_w, topk_ids)."""
     M, H = x.shape
     lo, hi = shard_range(shard.E, rank, world)
     if has_shared is None:
         has_shared = shard.w_gate is not None
-    tw, ids, _ = ops.router_topk(x, shard.router, topk, renormalize, rbufs[0], rbufs[1], pdl)
+    route = {}
+    if fused:
+        tw = torch.empty(M, topk, dtype=torch.float32, device=x.device)
+        ids = torch.empty(M, topk, dtype=torch.int32, device=x.device)
+        route = dict(router_w=shard.router, renormalize=renormalize,
+                     logits=torch.empty(M, shard.E, dtype=torch.bfloat16, device=x.device))
+    else:
+        tw, ids, _ = ops.router_topk(x, shard.router, topk, renormalize, rbufs[0], rbufs[1], pdl)
     ops.a16_moe_decode(x, ids, tw, shard.w13, shard.s13, None, shard.w2, shard.s2, None, shard.w_gate, None,
                        bufs["hbuf"], bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"],
                        shard.sh_w13, None, shard.sh_w2, None, bufs["shbuf"], pdl=pdl, mode=1, expert_range=(lo, hi),
-                       num_experts=shard.E)
+                       num_experts=shard.E, **route)
     slots = bufs["ybuf"][: slot_rows(M, topk) * H]
     if world > 1:
         reduce_slots(slots, group)

@@ -92,7 +92,9 @@ def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
 
 def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, shared, hbuf, ybuf, gl, ctrl, out,
                    phase: int = 4, dbg=None, pbuf=None, shq1=None, shs1=None, shq2=None, shs2=None, shbuf=None,
-                   pdl: bool = True, mode: int = 0, expert_range=None, num_experts: Optional[int] = None):
+                   pdl: bool = True, mode: int = 0, expert_range=None, num_experts: Optional[int] = None,
+                   router_w: Optional[torch.Tensor] = None, renormalize: bool = True,
+                   logits: Optional[torch.Tensor] = None, x_stage: Optional[torch.Tensor] = None):
     """Routed experts + shared expert + combine; writes ``out`` in place and returns it.
 
     Argument roles follow ``a16_moe_decode`` (serve/qwenfast/qf_a16moe.cu:852-863). Weight format: the kernel
@@ -105,9 +107,26 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     ``mode=1`` is one expert-parallel shard: the weights hold only experts ``expert_range = (lo, hi)`` of
     ``num_experts`` (the router's expert count), and instead of ``out`` the kernel leaves the shard's exact slot
     contribution in ``ybuf`` (``[M*topk + M, H]``: routed slots, then the shared rows); the shards' ``ybuf`` summed
-    and passed to ``moe_combine`` give the mode-0 output bit for bit."""
-    op = "a16_moe_decode"
-    _cuda(x, "x", op)
+    and passed to ``moe_combine`` give the mode-0 output bit for bit.
+
+    With ``router_w`` (bf16 [E, H]) the router runs inside the same launch (C ABI ``qf_moe_layer_decode``):
+    ``topk_ids`` / ``topk_w`` and ``logits`` (bf16 [M, E]) are then outputs, written by the kernel. With it,
+    ``x_stage`` (CUDA bf16 [M, H]) means ``x`` is a pinned host tensor that the kernel copies into ``x_stage`` itself,
+    and ``out`` may be a pinned host tensor as well (written by the kernel)."""
+    op = "a16_moe_decode" if router_w is None else "moe_layer_decode"
+    if x_stage is None:
+        _cuda(x, "x", op)
+        dev = x.device
+    else:
+        _req(router_w is not None, f"{op}: x_stage needs the fused router (router_w)")
+        _req(not x.is_cuda and x.is_pinned(), f"{op}: with x_stage, x must be a pinned host tensor")
+        _cuda(x_stage, "x_stage", op)
+        _req(x_stage.dtype == BF16 and x_stage.is_contiguous() and x_stage.shape == x.shape,
+             f"{op}: x_stage must be contiguous bf16 shaped like x")
+        dev = x_stage.device
+    host_out = not out.is_cuda
+    _req(not host_out or (x_stage is not None and out.is_pinned()),
+         f"{op}: out must be a CUDA tensor (or a pinned host tensor, with x_stage)")
     M, H = x.shape
     _req(x.dtype == BF16 and x.dim() == 2 and x.is_contiguous(), f"{op}: x must be contiguous bf16 [M, H]")
     _req(topk_ids.dtype == torch.int32 and topk_ids.dim() == 2 and topk_ids.size(0) == M and topk_ids.is_contiguous(),
@@ -142,8 +161,29 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     _req(mode in (0, 1), f"{op}: mode must be 0 or 1")
     _req(mode == 0 or hi - lo == E, f"{op}: mode 1 takes the weights of experts [lo, hi) only ({hi - lo} != {E})")
     _req(mode == 1 or E == E_all, f"{op}: mode 0 takes every expert's weights")
-    tensors = [topk_ids, topk_w, w13, s13, w2, s2, hbuf, ybuf, gl, ctrl, out]
-    _req(all(t.device == x.device for t in tensors), f"{op}: every tensor must be on x's device")
+    tensors = [topk_ids, topk_w, w13, s13, w2, s2, hbuf, ybuf, gl, ctrl] + ([] if host_out else [out])
+    _req(all(t.device == dev for t in tensors), f"{op}: every tensor must be on x's device")
+    if router_w is not None:
+        _req(router_w.dtype == BF16 and router_w.is_contiguous() and tuple(router_w.shape) == (E_all, H)
+             and router_w.device == dev, f"{op}: router_w must be contiguous bf16 [E, H] on x's device")
+        _req(logits is not None and logits.dtype == BF16 and logits.is_contiguous()
+             and tuple(logits.shape) == (M, E_all) and logits.device == dev,
+             f"{op}: logits must be a contiguous bf16 [M, E] tensor on x's device")
+        _req(int(phase) in (3, 4), f"{op}: phase must be 3 or 4")
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().qf_moe_layer_decode(
+                x.data_ptr(), _ptr(x_stage), router_w.data_ptr(), int(bool(renormalize)), topk_w.data_ptr(),
+                topk_ids.data_ptr(),
+                logits.data_ptr(), w13.data_ptr(), s13.data_ptr(), _ptr(gs13), w2.data_ptr(), s2.data_ptr(),
+                _ptr(gs2), _ptr(w_gate), _ptr(shared), _ptr(shq1) if has_shw else None,
+                _ptr(shq2) if has_shw else None,
+                hbuf.data_ptr(), hbuf.numel() * hbuf.element_size(), ybuf.data_ptr(),
+                ybuf.numel() * ybuf.element_size(), gl.data_ptr(), gl.numel(), ctrl.data_ptr(), ctrl.numel(),
+                _ptr(pbuf), 0 if pbuf is None else pbuf.numel(),
+                _ptr(shbuf), 0 if shbuf is None else shbuf.numel() * shbuf.element_size(),
+                out.data_ptr(), M, H, I, E_all, topk_ids.shape[1], Is, int(mode), int(lo), int(hi),
+                _ptr(dbg), int(bool(pdl)), _stream(dev)), op)
+        return out
     with torch.cuda.device(x.device):
         _lib.check(_lib.load().qf_a16_moe_decode(
             x.data_ptr(), topk_ids.data_ptr(), topk_w.data_ptr(), w13.data_ptr(), s13.data_ptr(), _ptr(gs13),
@@ -213,13 +253,29 @@ class MoELayerWeights:
 
 
 def moe_layer_step(x: torch.Tensor, lw: MoELayerWeights, topk: int, bufs: dict, rbufs, out: torch.Tensor,
-                   renormalize: bool = True, pdl: bool = True):
-    """One decode MoE layer-step: router_topk then a16_moe_decode (the reference's ``dual`` fast path,
-    qwenfast.py:1177-1201, with the shared expert computed in-kernel). Returns (out, topk_w, topk_ids, logits)."""
-    tw, ids, logits = router_topk(x, lw.router, topk, renormalize, rbufs[0], rbufs[1], pdl)
+                   renormalize: bool = True, pdl: bool = True, fused: bool = True,
+                   x_stage: Optional[torch.Tensor] = None):
+    """One decode MoE layer-step: the reference's ``dual`` fast path (qwenfast.py:1177-1201: router_topk, then
+    a16_moe_decode with the shared expert computed in-kernel). ``fused`` (default) runs the router inside the MoE
+    launch (``qf_moe_layer_decode``); ``fused=False`` launches ``router_topk`` (scratch ``rbufs``) and then
+    ``a16_moe_decode``. Host I/O (fused only): ``x`` and ``out`` pinned host tensors and ``x_stage`` a CUDA
+    bf16 [M, H] buffer -- the kernel reads x from host memory and writes out there, no copy-engine transfers.
+    Returns (out, topk_w, topk_ids, logits)."""
+    M = x.shape[0]
+    dev = x.device if x_stage is None else x_stage.device
+    if not fused:
+        tw, ids, logits = router_topk(x, lw.router, topk, renormalize, rbufs[0], rbufs[1], pdl)
+        a16_moe_decode(x, ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
+                       bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"], lw.sh_w13, None,
+                       lw.sh_w2, None, bufs["shbuf"], pdl=pdl)
+        return out, tw, ids, logits
+    tw = torch.empty(M, topk, dtype=torch.float32, device=dev)
+    ids = torch.empty(M, topk, dtype=torch.int32, device=dev)
+    logits = torch.empty(M, lw.E, dtype=BF16, device=dev)
     a16_moe_decode(x, ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"], bufs["ybuf"],
                    bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None,
-                   bufs["shbuf"], pdl=pdl)
+                   bufs["shbuf"], pdl=pdl, router_w=lw.router, renormalize=renormalize, logits=logits,
+                   x_stage=x_stage)
     return out, tw, ids, logits
 
 
