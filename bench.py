@@ -260,15 +260,20 @@ def run_ours(args):
         tws = [step(l) for l in range(NL)]
     ids_list = [t[1] for t in tws]
     tw_list = [t[0] for t in tws]
-    # MoE-kernel-only graph over the same routing (for the per-launch kernel time of the roofline)
+    # kernel-only graph of the layer-step launches (router inside, no collective or combine): the per-launch time of
+    # the roofline's kernel
+    r_tw = torch.empty(M, cfg.topk, dtype=torch.float32, device=dev)
+    r_ids = torch.empty(M, cfg.topk, dtype=torch.int32, device=dev)
+    r_lg = torch.empty(M, cfg.E, dtype=torch.bfloat16, device=dev)
     g_moe = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_moe):
         for l in range(NL):
             lw = shards[l]
-            ops.a16_moe_decode(xs[l], ids_list[l], tw_list[l], lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate,
+            ops.a16_moe_decode(xs[l], r_ids, r_tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate,
                                None, bufs["hbuf"], bufs["ybuf"], bufs["gl"], bufs["ctrl"], outs[l], 4, None,
                                bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None, bufs["shbuf"],
-                               mode=1 if epar else 0, expert_range=(lo, hi), num_experts=cfg.E)
+                               mode=1 if epar else 0, expert_range=(lo, hi), num_experts=cfg.E,
+                               router_w=lw.router, logits=r_lg)
     g_coll = None
     if epar:
         slots = bufs["ybuf"][: ep.slot_rows(M, cfg.topk) * cfg.H]
@@ -349,7 +354,9 @@ def run_ours(args):
     router_b = cfg.E * cfg.H * 2 + M * cfg.H * 2
     step_b = statistics.mean(moe_b) + router_b
     peak, peak_kind = load_peaks()
-    achieved = statistics.mean(loc_b) / (us_moe * 1e-6) / 1e9
+    # the layer-step launch streams its experts, the shared expert (rank 0), the activations and the router weights
+    launch_b = statistics.mean(loc_b) + router_b
+    achieved = launch_b / (us_moe * 1e-6) / 1e9
     rank_frac = None
     if epar:
         # per-rank HBM fraction of the local MoE kernel (each rank's own kernel time, not the max)
@@ -419,8 +426,8 @@ def run_ours(args):
             "us_moe_kernel": us_moe, "us_router_kernel": us_router,
             "us_collective": us_coll, "rank_hbm_frac": rank_frac,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "kernel": "moe_persistent_kernel",
-                         "bytes_per_launch": statistics.mean(loc_b),
+                         "peak_kind": peak_kind, "kernel": "moe_persistent_kernel (layer-step launch, router inside)",
+                         "bytes_per_launch": launch_b,
                          "traffic": load_traffic("moe_persistent_kernel")},
             "e2e": {"value": us_e2e, "unit": UNIT, "h2d_bytes_per_step": M * cfg.H * 2,
                     "d2h_bytes_per_step": M * cfg.H * 2, "steps": n_e2e},
