@@ -176,6 +176,8 @@ static_assert(SCR_RTW + MAXSLOTS * 4 <= NST * STAGE_BYTES, "plan scratch (pipeli
 // fused router: this CTA's router rows live in pipeline 1's ring (idle until the plan is done)
 constexpr int RROWS_BYTES = NST * STAGE_BYTES;
 constexpr int RPC_MAX = 8;                                          // router rows per CTA
+// fused router: token tiles of x in pipeline 2's ring (idle until the plan is done); H <= 4096 gives >= 7 tokens
+static_assert(RROWS_BYTES >= 4096 * 2 * 7, "x tile of the fused router");
 
 enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6, MISC_DUPS = 7 };
 
@@ -421,6 +423,60 @@ __device__ void shard_tile(const Params& p, const Layout& L, const int16_t* sids
     *reinterpret_cast<uint4*>(p.ybuf + (size_t)(p.M * topk + t) * H + n) = sv;
 }
 
+// ------------------------------------------------------------------------------------------------ fused router
+// logits[t, e] = bf16(x[t] . w[e]) for this CTA's router rows (already requested into rrows), a grid barrier, then
+// this CTA's own top-k of every token into rids / rtw (serve/qwenfast/qf_router.cu). Not inlined: it runs once per
+// launch, and as a separate function its registers do not compete with the pipelines' loops.
+__device__ __noinline__ void fused_router(const Params& p, uint8_t* smem, const uint8_t* rrows, int r0, int nrows,
+                                          int* rids, float* rtw) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int M = p.M, E = p.E, topk = p.topk;
+    uint32_t* ctrl = p.ctrl;
+    // logits: one warp per (token, row) pair, lanes over 16-byte k chunks (fp32 fma in chunk order, then a butterfly
+    // sum); then a grid barrier, and every CTA selects the top-k of every token itself (the same routine as the
+    // router kernel), so the plan needs no ids from memory
+    qf::cp_async_wait_all();
+    __syncthreads();
+    // x is staged in shared memory by token tiles (pipeline 2's ring, idle until the plan is done), then one warp
+    // per (token, row) pair reads both operands from shared memory; a small loop body (this code runs once per
+    // launch, with its instructions fetched cold) and few registers
+    const int nc = p.H / 8;
+    uint8_t* xs = smem + 2 * VP_BYTES;
+    const int tile_tok = min(M, RROWS_BYTES / (p.H * 2));
+    for (int t0 = 0; t0 < M; t0 += tile_tok) {
+        const int nt = min(tile_tok, M - t0);
+        const char* xsrc = reinterpret_cast<const char*>(p.x + (size_t)t0 * p.H);
+        for (int c = tid; c < nt * nc; c += MOE_THREADS) qf::cp_async16(xs + 16 * c, xsrc + 16 * c, 16u);
+        qf::cp_async_wait_all();
+        __syncthreads();
+#pragma unroll 1
+        for (int pr = warp; pr < nt * nrows; pr += MOE_THREADS / 32) {
+            const int tt = pr / nrows, r = pr - tt * nrows;
+            const uint4* xr = reinterpret_cast<const uint4*>(xs) + (size_t)tt * nc;
+            const uint4* wr = reinterpret_cast<const uint4*>(rrows) + (size_t)r * nc;
+            float a = 0.f;
+#pragma unroll 2
+            for (int c = lane; c < nc; c += 32) {
+                const uint4 xv = xr[c], wv = wr[c];
+                const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    a = fmaf(__uint_as_float(ww[i] << 16), __uint_as_float(xw[i] << 16), a);
+                    a = fmaf(__uint_as_float(ww[i] & 0xffff0000u), __uint_as_float(xw[i] & 0xffff0000u), a);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+            if (lane == 0) p.logits[(size_t)(t0 + tt) * E + r0 + r] = __float2bfloat16(a);
+        }
+        __syncthreads();   // the tile's x is consumed before the next tile overwrites it
+    }
+    grid_barrier(ctrl, C_RBAR);
+    for (int t = warp; t < M; t += MOE_THREADS / 32)
+        qf::topk_row_any(p.logits + (size_t)t * E, E, topk, p.renorm, rtw + t * topk, rids + t * topk);
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint8_t* plan = smem + OFF_PLAN;
@@ -513,58 +569,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         for (int c = (int)blockIdx.x * per + tid; c < c1; c += MOE_THREADS) __stcg(dst + c, __ldcv(src + c));
         grid_barrier(ctrl, C_XBAR);
     }
-    if (fused) {
-        // ---------------------------------------------------------------- fused router (serve/qwenfast/qf_router.cu)
-        // logits[t, e] = bf16(x[t] . w[e]) for this CTA's rows: one warp per token, lanes over 16-byte k chunks
-        // (fp32 fma in chunk order, then a butterfly sum); then a grid barrier, and every CTA selects the top-k
-        // of every token itself (the same routine as the router kernel), so the plan needs no ids from memory
-        qf::cp_async_wait_all();
-        __syncthreads();
-        const int nc = p.H / 8;
-        for (int t = warp; t < M; t += MOE_THREADS / 32) {
-            float a[RPC_MAX];
-#pragma unroll
-            for (int r = 0; r < RPC_MAX; ++r) a[r] = 0.f;
-            const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)t * p.H);
-            for (int c0 = 0; c0 < nc; c0 += 8 * 32) {   // eight chunks per lane in flight
-                uint4 xv[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int c = c0 + 32 * j + lane;
-                    xv[j] = c < nc ? __ldcg(xr + c) : make_uint4(0u, 0u, 0u, 0u);
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int c = c0 + 32 * j + lane;
-                    if (c >= nc) continue;
-                    const uint32_t xw[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
-#pragma unroll
-                    for (int r = 0; r < RPC_MAX; ++r) {
-                        if (r >= nrows) continue;
-                        const uint4 wv = *reinterpret_cast<const uint4*>(rrows + ((size_t)r * nc + c) * 16);
-                        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            a[r] = fmaf(__uint_as_float(ww[i] << 16), __uint_as_float(xw[i] << 16), a[r]);
-                            a[r] = fmaf(__uint_as_float(ww[i] & 0xffff0000u), __uint_as_float(xw[i] & 0xffff0000u), a[r]);
-                        }
-                    }
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < RPC_MAX; ++r) {
-                if (r >= nrows) continue;
-                float v = a[r];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0) p.logits[(size_t)t * E + r0 + r] = __float2bfloat16(v);
-            }
-        }
-        grid_barrier(ctrl, C_RBAR);
-        for (int t = warp; t < M; t += MOE_THREADS / 32)
-            qf::topk_row_any(p.logits + (size_t)t * E, E, topk, p.renorm, rtw + t * topk, rids + t * topk);
-        __syncthreads();
-    }
+    if (fused) fused_router(p, smem, rrows, r0, nrows, rids, rtw);
 
     // ------------------------------------------------------------------ routing plan (all threads)
     {
