@@ -916,8 +916,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             if (++es == NEPI) { es = 0; eph ^= 1u; }
         };
         // wait for the mmas of the stage in buffer bq; free its ring slot (bf16 stages: the A operand lives there)
-        // and add its partial, times sc, for this thread's tokens
-        auto retire = [&](int bq, int ring_slot, float sc, int ntok) {
+        // and add its partial, times sc, for all 16 token columns (columns beyond the item's tokens hold zeros: their
+        // B rows were zero-filled)
+        auto retire = [&](int bq, int ring_slot, float sc) {
             if (!qf::mbar_wait(mmab + bq, (mph >> bq) & 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
             mph ^= 1u << bq;
             qf::tc_fence_after();
@@ -925,19 +926,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 __syncwarp();
                 if (lane == 0) qf::mbar_arrive(empty + ring_slot);
             }
-            if (ntok > 8) {
-                uint32_t v[16];
-                qf::tmem_ld16(td0 + 16 * bq, v);
-                qf::tmem_wait_ld();
+            uint32_t v[16];
+            qf::tmem_ld16(td0 + 16 * bq, v);
+            qf::tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
-            } else {
-                uint32_t v[8];
-                qf::tmem_ld8(td0 + 16 * bq, v);
-                qf::tmem_wait_ld();
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
-            }
+            for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
             qf::tc_fence_before();
         };
         // this thread's token chunks of an item's stages: int4 stages have 16 tokens x 16 chunks (two per thread:
@@ -1001,7 +994,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             const bool w4 = d.kind == K_G1 || d.kind == K_G2;
             if (w4 || d.kind == K_S1 || d.kind == K_S2) {
                 // ---------------------------------------------------------------- pipelined item: nk stages
-                const int nk = d.nk, ntok = d.ntok;
+                const int nk = d.nk;
                 XChunks xc = xchunks(d);
                 int bcur = (int)(mcount & 1u);
                 if (!pre) xissue(xc, bcur);
@@ -1034,7 +1027,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                         }
                         qf::mbar_arrive(abr + bcur);
                     }
-                    if (pend) retire(pb, pr, psc, ntok);
+                    if (pend) retire(pb, pr, psc);
                     pend = true; pb = bcur; pr = w4 ? -1 : st; psc = sc;
                     ++mcount;
                     bcur ^= 1;
@@ -1062,7 +1055,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                         break;
                     }
                 }
-                retire(pb, pr, psc, ntok);
+                retire(pb, pr, psc);
                 if (failed) {   // no mma of this pipeline is in flight any more: stop the MMA warp and the agent
                     qf::cp_async_wait_all();
                     stop_mma();
