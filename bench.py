@@ -520,6 +520,9 @@ def run_sweep(args):
                "us_per_layer_step": us_step, "us_moe_kernel": us_moe, "moe_bytes": moe_b,
                "achieved_gbs": moe_b / (us_moe * 1e-6) / 1e9, "peak_gbs": peak, "peak_kind": peak_kind}
         rec["frac"] = rec["achieved_gbs"] / peak
+        # the layer-step is one launch (router inside): its bytes add the router weights and the router's x read
+        rec["step_bytes"] = moe_b + cfg.E * cfg.H * 2 + M * cfg.H * 2
+        rec["step_frac"] = rec["step_bytes"] / (us_step * 1e-6) / 1e9 / peak
         records.append(rec)
         print(json.dumps(rec), flush=True)
         del bufs, xs, outs
