@@ -234,7 +234,10 @@ struct Layout {   // per-launch derived sizes, identical in every thread
     int b_s1, b_g1, b_s1f, b_s2, b_g2, b_cb, total;
     uint32_t tile_target;
     int g1s;                          // gate_up k splits this launch: G1_SPLIT or 1
-    size_t g1_cnt_off, g1_part_off;   // pbuf (floats): gate_up half counters (uint32), then half partials
+    // pbuf (floats): [0, sh_off) the zero-kept gate_up half counters (uint32), sized for QF_MAX_TOKENS so that their
+    // place does not depend on M (one workspace sized for the largest M serves every smaller M); then the shared
+    // gate_up split-K partials, then the gate_up half partials
+    size_t sh_off, g1_part_off;
 };
 static_assert(sizeof(Layout) <= PLAN_LAYOUT_BYTES && PLAN_LAYOUT % 8 == 0, "Layout slot in the plan");
 
@@ -263,8 +266,8 @@ __device__ void make_layout(Layout& L, const Params& p, int M, int U, int Gt, in
     L.b_cb = L.b_g2 + L.R2 * L.Gt;
     L.total = L.b_cb + L.R2 * L.ngc;
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
-    L.g1_cnt_off = L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0;
-    L.g1_part_off = L.g1_cnt_off + (((size_t)M * p.topk * L.R1 + 3) & ~(size_t)3);
+    L.sh_off = ((size_t)QF_MAX_TOKENS * p.topk * L.R1 + 3) & ~(size_t)3;
+    L.g1_part_off = L.sh_off + (L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0);
 }
 
 __device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   // largest u with gpre[u] <= key
@@ -1082,7 +1085,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     // adds the other half's partials (a + b: the same bits whichever half comes second) and runs
                     // the SwiGLU epilogue. The counter is left at zero for the next launch.
                     const int unit = (gpre[d.u] + d.tg) * L.R1 + d.tile;
-                    uint32_t* cnt = reinterpret_cast<uint32_t*>(p.pbuf + L.g1_cnt_off) + unit;
+                    uint32_t* cnt = reinterpret_cast<uint32_t*>(p.pbuf) + unit;
                     float* parts = p.pbuf + L.g1_part_off + (size_t)unit * G1_SPLIT * 2048;
                     float* mine = parts + (size_t)d.split * 2048 + row * TG;
 #pragma unroll
@@ -1115,7 +1118,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     }
                 }
                 if (d.kind == K_S1F) {
-                    const float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048 + row * TG;
+                    const float* pb = p.pbuf + L.sh_off + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048 + row * TG;
 #pragma unroll
                     for (int sp = 0; sp < NSPLIT; ++sp) {   // fixed split order: the sum does not depend on timing
 #pragma unroll
@@ -1155,7 +1158,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 }
                 signal(d.kind == K_G1 ? C_DONE + d.u : C_SDONE + d.tg, 1);
             } else if (d.kind == K_S1) {
-                float* pb = p.pbuf + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048 + row * TG;
+                float* pb = p.pbuf + L.sh_off + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048 + row * TG;
 #pragma unroll
                 for (int i = 0; i < 16; i += 4)
                     __stcg(reinterpret_cast<float4*>(pb + i), make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
@@ -1348,11 +1351,14 @@ extern "C" int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64
     if (gl_numel) *gl_numel = M;
     if (ctrl_numel) *ctrl_numel = QF_MOE_CTRL_WORDS;
     if (pbuf_numel) {
-        // shared expert split-K partials, then the gate_up k-half counters and partials (at most M * topk token
-        // groups of routed experts, 2I / 128 tiles each)
+        // the zero-kept gate_up k-half counters (sized for QF_MAX_TOKENS: their place does not depend on M), the
+        // shared expert's split-K partials, the gate_up k-half partials (at most M * topk token groups of routed
+        // experts, 2I / 128 tiles each). Everything after the counters grows with M, so a workspace sized for the
+        // largest M serves every smaller M.
+        const int64_t cnt = ((int64_t)QF_MAX_TOKENS * topk * (2 * I / 128) + 3) & ~(int64_t)3;
         const int64_t sh = Is > 0 ? (int64_t)(2 * Is / 128) * ngs * NSPLIT * 2048 : 0;
         const int64_t units = (int64_t)M * topk * (2 * I / 128);
-        *pbuf_numel = sh + ((units + 3) & ~(int64_t)3) + units * G1_SPLIT * 2048;
+        *pbuf_numel = cnt + sh + units * G1_SPLIT * 2048;
     }
     if (shbuf_bytes) *shbuf_bytes = Is > 0 ? (int64_t)M * (Is + H) * 2 : 0;
     return QF_OK;

@@ -78,5 +78,10 @@ def test_workspace_sizes(lib):
     assert lib.qf_a16_moe_workspace(10, 2048, 512, 10, 512, *[ctypes.byref(a) for a in v]) == 0
     hb, yb, gl, ctrl, pb, sh = (a.value for a in v)
     assert hb == 10 * 10 * 512 * 2 and yb == 10 * 11 * 2048 * 2 and gl == 10 and ctrl == 2048
-    units = 10 * 10 * (2 * 512 // 128)   # gate_up k-half counters and partials: M * topk groups x 2I / 128 tiles
-    assert pb == (2 * 512 // 128) * 1 * 4 * 2048 + units + units * 2 * 2048 and sh == 10 * (512 + 2048) * 2
+    units = 10 * 10 * (2 * 512 // 128)   # gate_up k-half partials: M * topk token groups x 2I / 128 tiles
+    cnt = 64 * 10 * (2 * 512 // 128)     # their zero-kept counters, sized for 64 tokens (the same place for any M)
+    s1 = (2 * 512 // 128) * 1 * 4 * 2048  # shared gate_up: 4 k splits of 2Is / 128 tiles x token groups x 128 x 16
+    assert pb == cnt + s1 + units * 2 * 2048 and sh == 10 * (512 + 2048) * 2
+    assert lib.qf_a16_moe_workspace(32, 2048, 512, 10, 512, *[ctypes.byref(a) for a in v]) == 0
+    units = 32 * 10 * (2 * 512 // 128)   # two token groups
+    assert v[4].value == cnt + (2 * 512 // 128) * 2 * 4 * 2048 + units * 2 * 2048

@@ -123,6 +123,9 @@ def test_config1_precomputed_shared(cfg1, cuda):
 
 
 def test_batch_invariance_and_back_to_back(cfg1, cuda):
+    """Back-to-back launches equal a synchronised one; rows give the same bits in any batch of the same gate_up
+    split regime (test_a16moe.py:163-178): at config 1, M = 10 (one chain per gate_up tile) against two batches of
+    5, and M = 2 (k halves) against single rows; across the regimes, within the oracle tolerance."""
     cfg, L, lw, C = cfg1
     x = synthetic.make_tokens(cfg, device=cuda, seed=11)
     w, ids, _ = ops.router_topk(x, lw.router, cfg.topk, True, *ops.router_bufs(cuda))
@@ -130,11 +133,59 @@ def test_batch_invariance_and_back_to_back(cfg1, cuda):
     ref = run_moe(x, ids, w, lw, bufs).clone()
     torch.cuda.synchronize()
     outs = [run_moe(x, ids, w, lw, bufs) for _ in range(5)]            # back to back, no sync
-    single = [run_moe(x[r:r + 1].contiguous(), ids[r:r + 1].contiguous(), w[r:r + 1].contiguous(), lw, bufs)
-              for r in range(cfg.M)]
+
+    def rows(r0, r1):
+        return run_moe(x[r0:r1].contiguous(), ids[r0:r1].contiguous(), w[r0:r1].contiguous(), lw, bufs)
+
+    assert not gate_up_split(10, cfg.I, cfg.topk) and not gate_up_split(5, cfg.I, cfg.topk)
+    assert gate_up_split(2, cfg.I, cfg.topk) and gate_up_split(1, cfg.I, cfg.topk)
+    halves = torch.cat([rows(0, 5), rows(5, 10)])
+    pair = rows(0, 2)
+    single = torch.cat([rows(r, r + 1) for r in range(cfg.M)])
     torch.cuda.synchronize()
     assert all(torch.equal(o, ref) for o in outs)
-    assert torch.equal(torch.cat(single), ref)
+    assert torch.equal(halves, ref)
+    assert torch.equal(single[:2], pair)
+    oracle = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"],
+                                 w_gate=C["w_gate"], shared_w=(C["sh_gu"], C["sh_d"]))
+    assert_close_to_oracle(single, oracle)
+    assert int(bufs["ctrl"].abs().sum().item()) == 0
+
+
+def gate_up_split(M, I, topk):
+    """Whether a launch of M tokens splits its gate_up items into two k halves (every half fits one wave of the
+    three pipelines per SM): the kernel's rule. Within one regime results are batch-invariant bit for bit; across
+    the two the fp32 association of the gate_up sums differs (half + half vs one chain)."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    return 2 * (2 * I // 128) * M * topk <= 3 * sms
+
+
+@pytest.mark.parametrize("M", [3, 20, 60])
+def test_odd_shared_shape_and_workspace_reuse(cuda, M):
+    """H = 768 and a shared expert of Is = 192 (six 32-k stages per split-K item and per down item), two and four
+    token groups at M = 20 / 60. The rows are then run one at a time on the same workspace (sized for M rows: its
+    zero-kept counters sit at the same place for every M): equal to the batch bit for bit where both launches
+    make the same gate_up split choice, within the oracle tolerance where they do not (M = 60)."""
+    cfg = synthetic.MoEConfig("odd-shared", 768, 32, 128, 4, M, 192, 40 + M)
+    L = synthetic.make_moe_layer(cfg)
+    lw = layer_on(cuda, L)
+    x = synthetic.make_tokens(cfg, device=cuda)
+    w, ids, _ = ops.router_topk(x, lw.router, cfg.topk, True, *ops.router_bufs(cuda))
+    bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+    out = run_moe(x, ids, w, lw, bufs)
+    single = torch.cat([run_moe(x[r:r + 1].contiguous(), ids[r:r + 1].contiguous(), w[r:r + 1].contiguous(), lw, bufs)
+                        for r in range(M)])
+    again = run_moe(x, ids, w, lw, bufs)
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) == 0
+    C = canon_cpu(L)
+    ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
+                              shared_w=(C["sh_gu"], C["sh_d"]))
+    assert_close_to_oracle(out, ref)
+    assert_close_to_oracle(single, ref)
+    assert torch.equal(again, out)
+    if gate_up_split(M, cfg.I, cfg.topk) == gate_up_split(1, cfg.I, cfg.topk):
+        assert torch.equal(single, out)
     assert int(bufs["ctrl"].abs().sum().item()) == 0
 
 
