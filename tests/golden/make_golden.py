@@ -2,7 +2,9 @@
 
 1. ``reference_fns.pt`` -- outputs of the reference's OWN Python functions, run on seeded CPU inputs:
    * ``w8_quant``  from serve/overlays/sglang/srt/qwenfast.py:301-315 (INT8 group quantisation),
-   * ``w8q``, ``route``, ``shared_ref``, ``truth`` from serve/qwenfast/test_a16moe.py:61-86, 139-148.
+   * ``w8q``, ``route``, ``shared_ref``, ``truth`` from serve/qwenfast/test_a16moe.py:61-86, 139-148,
+   * the NVFP4 format: the module-level ``E2M1`` table and ``deq`` (test_a16moe.py:134-137), and ``truth`` once more
+     with that real ``deq`` on NVFP4 experts (``nvfp4_deq``, ``nvfp4_truth``).
    The functions are extracted from the reference sources with ``ast`` (their modules import sglang and load a
    CUDA extension at import time, neither of which exists here) and executed in a namespace that supplies the
    globals they read (top-k ``K``, sizes ``I``/``Hd``, device ``dev`` = cpu). ``truth`` dequantises through a global
@@ -29,12 +31,16 @@ sys.path.insert(0, os.path.join(REPO, "qwen-3.8-flash-next-pro6000_b200"))
 
 
 def extract(path, names):
+    """Source of the top-level functions (or single-name assignments) called ``names`` in a Python file."""
     src = open(path).read()
     tree = ast.parse(src)
     out = {}
     for node in tree.body:
         if isinstance(node, ast.FunctionDef) and node.name in names:
             out[node.name] = ast.get_source_segment(src, node)
+        elif (isinstance(node, ast.Assign) and len(node.targets) == 1 and isinstance(node.targets[0], ast.Name)
+              and node.targets[0].id in names):
+            out[node.targets[0].id] = ast.get_source_segment(src, node)
     missing = set(names) - set(out)
     if missing:
         raise SystemExit(f"{path}: functions {sorted(missing)} not found")
@@ -101,6 +107,22 @@ def main():
     canon = dict(w13=w13, s13=s13, w2=w2, s2=s2_, g13=torch.ones(E, 2), g2=torch.ones(E))
     out = ns["truth"](dict(canon=canon, wg=wg), x, tw, ids, shared)
     res["truth"] = dict(x=x, ids=ids, w=tw, w13=w13, s13=s13, w2=w2, s2=s2_, wg=wg, shared=shared, out=out)
+
+    # (5) NVFP4: the reference's own E2M1 table and deq, and its truth on NVFP4 experts
+    from oracle import nvfp4_ref
+    n_src = extract(os.path.join(ref, "serve/qwenfast/test_a16moe.py"), ["E2M1", "deq", "truth"])
+    ns4 = dict(torch=torch, dev="cpu", E=E, Hd=Hd, I=I, K=K)
+    for name in ("E2M1", "deq", "truth"):
+        exec(compile(n_src[name], "<reference>", "exec"), ns4)
+    wp, sf = nvfp4_ref.random_nvfp4((48, 256), g)
+    res["nvfp4_deq"] = dict(wp=wp, sf=sf, g=0.25, out=ns4["deq"](wp, sf, 0.25))
+    w13f, s13f = nvfp4_ref.random_nvfp4((E, 2 * I, Hd), g)
+    w2f, s2f = nvfp4_ref.random_nvfp4((E, Hd, I), g)
+    g13f = torch.rand(E, 2, generator=g) * 2 + 0.5
+    g2f = torch.rand(E, generator=g) * 2 + 0.5
+    canon4 = dict(w13=w13f, s13=s13f, w2=w2f, s2=s2f, g13=g13f, g2=g2f)
+    out4 = ns4["truth"](dict(canon=canon4, wg=wg), x, tw, ids, shared)
+    res["nvfp4_truth"] = dict(x=x, ids=ids, w=tw, **canon4, wg=wg, shared=shared, out=out4)
     torch.save(res, os.path.join(HERE, "reference_fns.pt"))
 
     # config 0 oracle outputs (inputs are regenerated from the seed; checksums guard the generator)

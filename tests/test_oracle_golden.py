@@ -48,3 +48,30 @@ def test_rounded_oracle_close_to_reference_truth():
     d = out.float() - r["out"]
     assert d.norm() / r["out"].norm() < 1e-2
     assert d.abs().max() < 2e-2
+
+
+def test_nvfp4_dequant_matches_reference_deq():
+    """The NVFP4 restatement (oracle/nvfp4_ref.py) against the reference's own E2M1 table and deq
+    (serve/qwenfast/test_a16moe.py:134-137), bit for bit."""
+    from oracle import nvfp4_ref
+    r = REF["nvfp4_deq"]
+    assert torch.equal(nvfp4_ref.dequant_nvfp4(r["wp"], r["sf"], r["g"]), r["out"])
+
+
+def test_nvfp4_truth_matches_reference_truth():
+    """The fp32 layer truth on NVFP4 experts against the reference's truth run with its own deq."""
+    from oracle import nvfp4_ref
+    r = REF["nvfp4_truth"]
+    out = nvfp4_ref.truth(r["x"], r["ids"], r["w"], r["w13"], r["s13"], r["g13"], r["w2"], r["s2"], r["g2"],
+                          w_gate=r["wg"], shared=r["shared"])
+    torch.testing.assert_close(out, r["out"], rtol=1e-6, atol=1e-6)
+
+
+def test_nvfp4_group_products_are_exact_in_bf16():
+    """Every e2m1 value times every finite E4M3 scale is a bf16 value: a group dequantises exactly with one bf16
+    multiply, and the global 1 / g can wait for the epilogue."""
+    from oracle import nvfp4_ref
+    sf = torch.arange(256, dtype=torch.int32).to(torch.uint8).view(torch.float8_e4m3fn).float()
+    sf = sf[torch.isfinite(sf)]
+    prod = nvfp4_ref.e2m1_values()[:, None] * sf[None, :]
+    assert torch.equal(prod.to(torch.bfloat16).float(), prod)
