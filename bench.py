@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--sweep", default="")
     ap.add_argument("--sweep-configs", default="2,3", help="which sweep records to take (comma list of 2, 3)")
     ap.add_argument("--sweep-n", default="2048,4096,8192,12288", help="config-3 weight row counts N to sweep")
+    ap.add_argument("--timeline", default="", help="write the per-CTA item timeline of config-1 layer-steps here")
+    ap.add_argument("--timeline-m", default="1,10", help="token counts of the timeline")
     return ap.parse_args()
 
 
@@ -564,10 +566,108 @@ def run_sweep(args):
         json.dump(records, f, indent=1)
 
 
+KIND_NAMES = {1: "GL", 2: "S1", 3: "G1", 4: "S1F", 5: "S2", 6: "G2", 7: "CB"}
+
+
+def decode_timeline(dbg, sms):
+    """The MoE kernel's timeline buffer (include/qwenfast_b200.h, ``dbg``) -> per-phase summary in us, relative to
+    the earliest CTA entry: router + routing plan (median consumer start), per item kind the count, the span of
+    starts, the median / max time from an item's start to its last stage retired, and when the last pipeline
+    stopped."""
+    d = dbg.view(-1, 32)[:sms].tolist()
+    U = lambda v: (v & ((1 << 64) - 1)) >> 12
+    t0 = min(U(row[31]) for row in d if row[31] != 0)
+    ev = []
+    for c, row in enumerate(d):
+        for v in row[:31]:
+            if v:
+                tag = v & 0xFFF
+                ev.append(((U(v) - t0) / 1e3, c, (tag >> 5) & 3, tag & 31))
+    ev.sort()
+    open_items, dur, starts = {}, {}, {}
+    for t, c, vp, code in ev:
+        if 1 <= code <= 7:
+            open_items[(c, vp)] = (code, t)
+            starts.setdefault(code, []).append(t)
+        elif 17 <= code <= 23 and open_items.get((c, vp), (0,))[0] == code - 16:
+            dur.setdefault(code - 16, []).append((t - open_items.pop((c, vp))[1], t))
+    med = lambda v: sorted(v)[len(v) // 2]
+    out = dict(consumers_start_us=round(med([t for t, _, _, code in ev if code == 30]), 2),
+               last_stop_us=round(max(t for t, _, _, code in ev if code == 31), 2), kinds={})
+    for k, st in sorted(starts.items()):
+        dd = dur.get(k, [])
+        out["kinds"][KIND_NAMES[k]] = dict(
+            n=len(st), first_start_us=round(min(st), 2), last_start_us=round(max(st), 2),
+            stages_us_median=round(med([a for a, _ in dd]), 2) if dd else None,
+            stages_us_max=round(max(a for a, _ in dd), 2) if dd else None,
+            last_stages_done_us=round(max(b for _, b in dd), 2) if dd else None)
+    return out
+
+
+def run_timeline(args):
+    """Per-item timeline of the config-1 layer-step (router inside) at each M of ``--timeline-m``: the kernel's
+    globaltimer stamps (every pipeline: item start, stages retired, start / stop), taken on one launch per run
+    inside a CUDA graph of 8 layer-steps over 8 different layers (weights from HBM), without programmatic launch so
+    that each launch starts after the previous one ended. Four runs per M; written to ``args.timeline`` (JSON) with a
+    summary line per run."""
+    import torch
+    from qwenfast_b200 import ops, synthetic
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = synthetic.CONFIGS[1]
+    NL = 8
+    layers = build_layers(cfg, NL, dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    res = {}
+    for M in [int(m) for m in args.timeline_m.split(",") if m.strip()]:
+        xs = [synthetic.make_tokens(cfg, M=M, device=dev, seed=200 + i) for i in range(NL)]
+        bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, dev)
+        out = torch.empty(M, cfg.H, dtype=torch.bfloat16, device=dev)
+        tw = torch.empty(M, cfg.topk, dtype=torch.float32, device=dev)
+        ids = torch.empty(M, cfg.topk, dtype=torch.int32, device=dev)
+        lg = torch.empty(M, cfg.E, dtype=torch.bfloat16, device=dev)
+        dbg = torch.zeros(ops.DBG_NUMEL, dtype=torch.int64, device=dev)
+
+        def seq():
+            for i, lw in enumerate(layers):
+                ops.a16_moe_decode(xs[i], ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None,
+                                   bufs["hbuf"], bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, 4,
+                                   dbg if i == NL // 2 else None, bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None,
+                                   bufs["shbuf"], pdl=False, router_w=lw.router, logits=lg)
+
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                seq()
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            seq()
+        runs = []
+        for _ in range(4):
+            g.replay()
+            dbg.zero_()
+            g.replay()
+            torch.cuda.synchronize()
+            runs.append(decode_timeline(dbg.cpu(), sms))
+        if ops.moe_error_word(bufs["ctrl"]) != 0:
+            raise RuntimeError("timeline: the MoE kernel reported an error")
+        res[M] = runs
+        for r in runs:
+            print(json.dumps(dict(M=M, **r)), flush=True)
+        del g
+    with open(args.timeline, "w") as f:
+        json.dump(res, f, indent=1)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.timeline:
+        run_timeline(args)
     elif args.sweep:
         run_sweep(args)
     else:

@@ -96,8 +96,11 @@ int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, i
  *   weighted slot outputs go to ybuf [M, topk + 1, H] with every other slot zero, slot `topk` holding the shared
  *   expert output when this shard computes it; qf_moe_combine then finishes the layer (after the caller has summed
  *   ybuf over the shards).
- * dbg: optional int64 [QF_MOE_DBG_NUMEL] per-CTA globaltimer stamps (32 per CTA; CTAs beyond the first
- *   QF_MOE_DBG_NUMEL / 32 record nothing), or NULL.
+ * dbg: optional int64 [QF_MOE_DBG_NUMEL] timeline, or NULL: 32 entries per CTA (CTAs beyond the first
+ *   QF_MOE_DBG_NUMEL / 32 record nothing), each (globaltimer ns << 12) | tag as a 64-bit pattern; entry 31 is the
+ *   CTA's entry (tag 0xFFF), entries 0..30 in order of recording: tag bits 0-4 the event (1..7 an item of that kind
+ *   starts -- GL, S1, G1, S1F, S2, G2, CB --, 16 + kind its stages are done, 30 the pipeline's consumers start, 31
+ *   they stop), bits 5-6 the pipeline.
  * ------------------------------------------------------------------------------------------------------------ */
 int qf_a16_moe_workspace(int M, int H, int I, int topk, int Is, int64_t* hbuf_bytes, int64_t* ybuf_bytes,
                          int64_t* gl_numel, int64_t* ctrl_numel, int64_t* pbuf_numel, int64_t* shbuf_bytes);

@@ -179,6 +179,7 @@ constexpr int RPC_MAX = 8;                                          // router ro
 // fused router: token tiles of x in pipeline 2's ring (idle until the plan is done); H <= 4096 gives >= 7 tokens
 static_assert(RROWS_BYTES >= 4096 * 2 * 7, "x tile of the fused router");
 
+enum : int { DBG_CONSUMERS = 30, DBG_STOP = 31, DBG_ENTRY = 0xFFF };   // timeline events (dbg)
 enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6, MISC_DUPS = 7 };
 
 // tensor memory map (columns of this CTA's allocation; fp32 / bf16x2 per 32-bit column, lane = tile row)
@@ -482,6 +483,8 @@ __device__ __noinline__ void fused_router(const Params& p, uint8_t* smem, const 
 
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
+    if (p.dbg != nullptr && threadIdx.x == 0 && blockIdx.x < QF_MOE_DBG_NUMEL / 32)   // timeline: CTA entry
+        p.dbg[blockIdx.x * 32 + 31] = (long long)((qf::globaltimer() << 12) | (uint64_t)DBG_ENTRY);
     uint8_t* plan = smem + OFF_PLAN;
     int16_t* ulist = reinterpret_cast<int16_t*>(plan + PLAN_ULIST);
     int16_t* gpre = reinterpret_cast<int16_t*>(plan + PLAN_GPRE);
@@ -900,13 +903,17 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         uint32_t mcount = 0;    // pipelined stages so far (identical in the pipeline's consumer threads)
         uint32_t mph = 0;       // bit b: phase of mmab[b] at its next wait
         float acc[16];          // this thread's row, tokens 0..15
-        // optional timeline (pipeline 0 only): (globaltimer << 12) | tag, up to 32 per CTA
+        // optional timeline: (globaltimer << 12) | tag in the CTA's first 31 entries, tag = event | pipeline << 5;
+        // events: 1..7 an item of that kind starts (its first stage is in the ring), 16 + kind its stages are done,
+        // DBG_CONSUMERS the pipeline's consumers start (routing plan built), DBG_STOP they stop
         auto stamp = [&](int tag) {
-            if (p.dbg != nullptr && vp == 0 && ctid == 0 && blockIdx.x < QF_MOE_DBG_NUMEL / 32 && misc[MISC_DBGN] < 32) {
-                p.dbg[blockIdx.x * 32 + misc[MISC_DBGN]] = (long long)((qf::globaltimer() << 12) | (uint64_t)tag);
-                misc[MISC_DBGN] += 1;
+            if (p.dbg != nullptr && ctid == 0 && blockIdx.x < QF_MOE_DBG_NUMEL / 32) {
+                const int i = atomicAdd(&misc[MISC_DBGN], 1);
+                if (i < 31)
+                    p.dbg[blockIdx.x * 32 + i] = (long long)((qf::globaltimer() << 12) | (uint64_t)(tag | (vp << 5)));
             }
         };
+        stamp(DBG_CONSUMERS);
         // hand one completion record to the agent (record written by thread 0; every consumer warp arrives)
         auto signal = [&](int idx, int add) {
             if (ctid == 0) {
@@ -986,7 +993,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             }
             const StageDesc d = desc[st];
             if (d.kind == K_STOP) {
-                stamp(15);
+                stamp(DBG_STOP);
                 stop_mma();
                 signal(-2, 0);
                 break;
@@ -1059,6 +1066,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     }
                 }
                 retire(pb, pr, psc);
+                stamp(16 + d.kind);
                 if (failed) {   // no mma of this pipeline is in flight any more: stop the MMA warp and the agent
                     qf::cp_async_wait_all();
                     stop_mma();

@@ -270,3 +270,23 @@ def test_repack_kernels_match_host_layout(cuda):
         wk = formats.repack_bf16(w.to(cuda), gated)
         assert torch.equal(wk.cpu(), formats.repack_bf16_torch(w, gated))
         assert torch.equal(formats.unpack_bf16(wk, N, K, gated).cpu(), w)
+
+
+def test_checkpoint_on_device(cuda, tmp_path):
+    """The repack exactness check with the CUDA unpack kernels, and a saved layer loaded onto the GPU that runs the
+    same layer-step bits as the layer it was saved from."""
+    from qwenfast_b200 import checkpoint
+    cfg = synthetic.MoEConfig("ckpt-gpu", 2048, 32, 512, 4, 6, 512, 77)
+    L = synthetic.make_moe_layer(cfg)
+    lw = layer_on(cuda, L)
+    checkpoint.verify_layer(lw, L, experts_per_block=8)
+    path = os.path.join(tmp_path, "layer.safetensors")
+    checkpoint.save_layer(path, lw)
+    lw2 = checkpoint.load_layer(path, device=cuda)
+    x = synthetic.make_tokens(cfg, device=cuda)
+    outs = []
+    for w in (lw, lw2):
+        bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+        outs.append(ops.moe_layer_step(x, w, cfg.topk, bufs, ops.router_bufs(cuda), torch.empty_like(x))[0])
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
