@@ -87,7 +87,8 @@ int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, i
  *   sh_w13, sh_w2: bf16 shared expert weights (gate_up [2*Is, H] and down [H, Is]) in the kernel layout made by
  *              qf_bf16_repack (gated = 1 / 0), or NULL; Is = their intermediate size (0 when absent);
  *   scratch (caller-owned, sizes from qf_a16_moe_workspace): hbuf, ybuf, gl, ctrl (zeroed once), pbuf (required;
- *              zeroed once: it holds counters the kernel re-arms), shbuf;
+ *              zeroed once: it holds counters the kernel re-arms), shbuf; scratch sized for some M serves every
+ *              smaller M of the same layer shape (the re-armed counters sit at places that do not depend on M);
  *   out bf16 [M, H].
  * out[t] = bf16(sigmoid(x[t].w_gate) * shared[t] + bf16(sum over top-k positions, in order, of
  *          bf16(bf16(expert_out) * bf16(gs2 * bf16(topk_w)))))  -- the reference's rounding points.
