@@ -5,6 +5,7 @@ reference (``at::empty``), and enqueues the sm_100a kernel on the current CUDA s
 CPU path: CPU tensors are rejected.
 """
 import ctypes
+import weakref
 from dataclasses import dataclass
 from typing import Optional
 
@@ -73,6 +74,38 @@ def router_bufs(device, rows: int = 64, experts: int = 1024):
 
 
 # ------------------------------------------------------------------------------------------------- MoE
+_W8_SHARED = {}
+
+
+def shared_w8_as_bf16(sq1, ss1, sq2, ss2, H: int, op: str = "a16_moe_decode"):
+    """The shared expert given as the reference passes it to its MoE op (qwenfast.py:1092-1113, 1196-1200): INT8
+    gate_up sq1 [2Is, H] and down sq2 [H, Is] with bf16 group scales ss1 / ss2 (``w8_quant`` format, group 128 or
+    64) -> the kernel-layout bf16 weights the MoE kernel streams, ``bf16(q * s)`` dequantised on the device
+    (``w8g_unpack``) and repacked. Done once per weight tensor: the result is cached for as long as ``sq1`` lives, so
+    only the first call allocates (make it before any graph capture). The weights are then rounded to bf16 (relative
+    2^-9 per weight) where the reference's w8g arithmetic applies the scale to fp32 group sums -- within the layer's
+    tolerance (tested against that arithmetic)."""
+    for name, q, sc in (("shq1 / shs1", sq1, ss1), ("shq2 / shs2", sq2, ss2)):
+        _req(q is not None and sc is not None and q.dtype == torch.int8 and q.dim() == 2 and q.is_contiguous()
+             and sc.dtype == BF16 and sc.dim() == 2 and sc.is_contiguous() and sc.size(0) == q.size(0)
+             and q.size(1) % sc.size(1) == 0 and q.size(1) // sc.size(1) in (64, 128) and q.is_cuda and sc.is_cuda,
+             f"{op}: INT8 shared-expert weights {name} must be int8 [N, K] with bf16 group scales [N, K/128]")
+    Is = sq2.size(1)
+    _req(tuple(sq1.shape) == (2 * Is, H) and tuple(sq2.shape) == (H, Is),
+         f"{op}: INT8 shared-expert weights must be gate_up [2Is, H] and down [H, Is]")
+    key = (sq1.data_ptr(), ss1.data_ptr(), sq2.data_ptr(), ss2.data_ptr(), H, Is)
+    hit = _W8_SHARED.get(key)
+    if hit is not None and all(r() is t for r, t in zip(hit[0], (sq1, ss1, sq2, ss2))):
+        return hit[1], hit[2]
+    w1 = torch.empty(2 * Is, H, dtype=BF16, device=sq1.device)
+    w2 = torch.empty(H, Is, dtype=BF16, device=sq1.device)
+    w8g_unpack(sq1, ss1, w1)
+    w8g_unpack(sq2, ss2, w2)
+    wk1, wk2 = repack_bf16(w1, gated=True), repack_bf16(w2, gated=False)
+    _W8_SHARED[key] = (tuple(weakref.ref(t) for t in (sq1, ss1, sq2, ss2)), wk1, wk2)
+    return wk1, wk2
+
+
 def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
     """Caller-owned scratch for ``a16_moe_decode`` (the reference's ``_a16_bufs``, qwenfast.py:1044-1059)."""
     lib = _lib.load()
@@ -100,8 +133,9 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     Argument roles follow ``a16_moe_decode`` (serve/qwenfast/qf_a16moe.cu:852-863). Weight format: the kernel
     layout of ``repack_w4`` -- w13 int32 [E, 2I*H/8], s13 bf16 [E, 2I*H/128], w2 int32 [E, H*I/8],
     s2 bf16 [E, H*I/128]; gs13 / gs2 bf16 [E] or empty (= 1). The in-kernel shared expert takes bf16 weights in the
-    kernel layout of ``repack_bf16``: shq1 = gate_up [2Is*H], shq2 = down [H*Is] (shs1 / shs2 must be empty: there
-    are no separate scales for bf16). ``shared`` is a precomputed bf16 [M, H] shared output instead (or empty).
+    kernel layout of ``repack_bf16``: shq1 = gate_up [2Is*H], shq2 = down [H*Is], shs1 / shs2 empty -- or, as the
+    reference passes it, INT8 weights shq1 [2Is, H] / shq2 [H, Is] with bf16 group scales shs1 / shs2 (converted
+    once, see ``shared_w8_as_bf16``). ``shared`` is a precomputed bf16 [M, H] shared output instead (or empty).
     Empty tensors mean "absent", as in the reference.
 
     ``mode=1`` is one expert-parallel shard: the weights hold only experts ``expert_range = (lo, hi)`` of
@@ -143,7 +177,10 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     _req(s2.dtype == BF16 and tuple(s2.shape) == (E, H * I // 128), f"{op}: s2 must be bf16 [E, H*I/128]")
     for name, g in (("gs13", gs13), ("gs2", gs2)):
         _req(not _present(g) or (g.dtype == BF16 and g.numel() == E), f"{op}: {name} must be bf16 [E] or empty")
-    _req(not _present(shs1) and not _present(shs2), f"{op}: bf16 shared-expert weights take no separate scales")
+    if _present(shs1) or _present(shs2):
+        # the reference's in-kernel shared expert: group-scaled INT8 weights (w8_quant format)
+        shq1, shq2 = shared_w8_as_bf16(shq1, shs1, shq2, shs2, H, op)
+        shs1 = shs2 = None
     has_shw = _present(shq1)
     Is = 0
     if has_shw:

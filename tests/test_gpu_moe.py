@@ -290,3 +290,35 @@ def test_checkpoint_on_device(cuda, tmp_path):
         outs.append(ops.moe_layer_step(x, w, cfg.topk, bufs, ops.router_bufs(cuda), torch.empty_like(x))[0])
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1])
+
+
+def test_int8_shared_expert_as_the_reference_passes_it(cfg1, cuda):
+    """The shared expert given as INT8 weights with bf16 group scales (the reference's in-kernel shared expert,
+    serve/overlays/sglang/srt/qwenfast.py:1092-1113, passed as shq1, shs1, shq2, shs2): against the oracle of that
+    w8g arithmetic (test_a16moe.py:68-73) within the layer tolerance; converted once per weight tensor."""
+    from oracle import w8_ref
+    cfg, L, lw, C = cfg1
+    sq1, ss1 = w8_ref.w8_quant(C["sh_gu"])
+    sq2, ss2 = w8_ref.w8_quant(C["sh_d"])
+    dq = [t.to(cuda) for t in (sq1, ss1, sq2, ss2)]
+    x = synthetic.make_tokens(cfg, device=cuda, seed=21)
+    w, ids, _ = ops.router_topk(x, lw.router, cfg.topk, True, *ops.router_bufs(cuda))
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+    outs = []
+    for _ in range(2):
+        out = torch.empty_like(x)
+        ops.a16_moe_decode(x, ids, w, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
+                           bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"], *dq, bufs["shbuf"])
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and ops.moe_error_word(bufs["ctrl"]) == 0
+    key_hits = [v for k, v in ops._W8_SHARED.items() if k[0] == dq[0].data_ptr()]
+    assert len(key_hits) == 1                              # converted once
+    shared = w8_ref.shared_expert_w8g(x.cpu(), sq1, ss1, sq2, ss2)
+    ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], shared=shared,
+                              w_gate=C["w_gate"])
+    assert_close_to_oracle(outs[0], ref)
+    with pytest.raises(RuntimeError, match="INT8 shared-expert"):
+        ops.a16_moe_decode(x, ids, w, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
+                           bufs["ybuf"], bufs["gl"], bufs["ctrl"], torch.empty_like(x), 4, None, bufs["pbuf"],
+                           dq[0], dq[1][:, :8].contiguous(), dq[2], dq[3], bufs["shbuf"])
