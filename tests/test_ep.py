@@ -91,3 +91,40 @@ def test_expert_parallel_combine_is_exact(world, tmp_path):
         assert torch.equal(got["ids"], ids)
         assert torch.equal(got["out"], ref)
         assert int(got["owned"].max()) <= 1       # no slot has two owners
+
+
+def _fail_worker(rank, world, port, result_dir, how):
+    """Rank 1 fails between steps -- it exits (``how == "exits"``) or stays alive without joining the exchange
+    (``"stalls"``); rank 0 runs the slot exchange and must get an error within the process group's timeout."""
+    import datetime
+    import sys
+    import time
+    for p in (ROOT, os.path.join(ROOT, "qwen-3.8-flash-next-pro6000_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import torch.distributed as dist
+    from qwenfast_b200 import ep as epm
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=4))
+    if rank == 1:
+        if how == "stalls":
+            time.sleep(10)
+        os._exit(0)
+    t0 = time.time()
+    err = None
+    try:
+        epm.reduce_slots(torch.ones(epm.slot_rows(2, 4), 64))
+    except Exception as e:   # gloo reports the lost peer or the timeout as a RuntimeError
+        err = f"{type(e).__name__}: {e}"
+    torch.save({"error": err, "elapsed": time.time() - t0}, os.path.join(result_dir, "rank0.pt"))
+    os._exit(0)
+
+
+@pytest.mark.parametrize("how", ["exits", "stalls"])
+def test_a_failed_rank_is_reported_not_waited_for(how, tmp_path):
+    """Failure detection on the host (gloo, CPU): the surviving rank's exchange raises instead of hanging."""
+    mp.start_processes(_fail_worker, args=(2, _free_port(), str(tmp_path), how), nprocs=2, join=True,
+                       start_method="spawn")
+    got = torch.load(os.path.join(tmp_path, "rank0.pt"))
+    assert got["error"] is not None
+    assert got["elapsed"] < 30, got
