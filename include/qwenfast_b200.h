@@ -96,7 +96,9 @@ int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, i
  * mode 0: full layer. mode 1: expert-parallel shard -- only experts in [expert_lo, expert_hi) are computed; their
  *   weighted slot outputs go to ybuf [M, topk + 1, H] with every other slot zero, slot `topk` holding the shared
  *   expert output when this shard computes it; qf_moe_combine then finishes the layer (after the caller has summed
- *   ybuf over the shards).
+ *   ybuf over the shards). mode 2: diagnostic of the failure path -- the full layer, except that one producer first
+ *   waits for a control word that nothing increments: the bounded wait runs out (about one second), the launch
+ *   drains and leaves QF_MOE_ERR_TIMEOUT in ctrl[QF_MOE_CTRL_ERR] (its outputs are then undefined).
  * dbg: optional int64 [QF_MOE_DBG_NUMEL] timeline, or NULL: 32 entries per CTA (CTAs beyond the first
  *   QF_MOE_DBG_NUMEL / 32 record nothing), each (globaltimer ns << 12) | tag as a 64-bit pattern; entry 31 is the
  *   CTA's entry (tag 0xFFF), entries 0..30 in order of recording: tag bits 0-4 the event (1..7 an item of that kind

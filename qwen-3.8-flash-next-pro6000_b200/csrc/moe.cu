@@ -88,6 +88,7 @@ enum : int {
     C_ERR = QF_MOE_CTRL_ERR,
     C_RBAR = 4,     // fused router: CTAs whose logits are stored (grid barrier)
     C_XBAR = 5,     // fused router with host input: CTAs whose slice of x is in device memory (grid barrier)
+    C_NEVER = 6,    // diagnostic mode 2: a word nothing increments (a dependency that never arrives)
     C_CNT = 8,      // [64] column-tile arrivals
     C_SDONE = 72,   // [4] finished shared gate_up tiles per token group
     C_SPLIT = 80,   // [64] split-K arrivals per (shared tile, token group)
@@ -735,7 +736,14 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             int st = 0;
             uint32_t ph = 0;
             int next = first_item;
+            // diagnostic mode 2: CTA 0's first producer waits, before its first item, for a dependency that never
+            // arrives; the bounded wait runs out, records QF_MOE_ERR_TIMEOUT and the launch drains
+            bool never = p.mode == 2 && blockIdx.x == 0 && vp == 0;
             for (;;) {
+                if (never) {
+                    never = false;
+                    wait_counter(ctrl, C_NEVER, 1u);
+                }
                 int item = next;
                 if (hard_error(ctrl)) item = L.total;
                 if (item < L.total) next = (int)atomicAdd(ctrl + C_QUEUE, 1u);   // claim ahead; in-order per CTA
@@ -1196,7 +1204,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_CB) {
                 // the producer acquired every producer of this tile (and the gate logits) before publishing it
-                if (p.mode == 0) combine_tile(p, L, sids, d.tile, d.tg, ctid);
+                if (p.mode != 1) combine_tile(p, L, sids, d.tile, d.tg, ctid);
                 else shard_tile(p, L, sids, d.tile, d.tg, ctid);
                 signal(-1, 0);
             }
@@ -1391,7 +1399,8 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
                "a16_moe_decode: null pointer argument");
     QF_REQUIRE(phase == 3 || phase == 4,
                "a16_moe_decode: phase must be 3 or 4 (whole layer); split phases 1/2 are not provided, got %d", phase);
-    QF_REQUIRE(mode == 0 || mode == 1, "a16_moe_decode: mode must be 0 (full layer) or 1 (expert-parallel shard), got %d",
+    QF_REQUIRE(mode == 0 || mode == 1 || mode == 2,
+               "a16_moe_decode: mode must be 0 (full layer), 1 (expert-parallel shard) or 2 (diagnostic), got %d",
                mode);
     QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS, "a16_moe_decode: M must be in [1, %d], got %d", QF_MAX_TOKENS, M);
     QF_REQUIRE(H >= 128 && H % 256 == 0 && H <= 8192, "a16_moe_decode: H must be a multiple of 256 in [256, 8192], got %d", H);

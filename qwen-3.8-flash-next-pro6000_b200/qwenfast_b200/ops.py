@@ -195,7 +195,7 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
          f"{op}: dbg must be a contiguous int64 CUDA tensor of at least {DBG_NUMEL} entries")
     E_all = E if num_experts is None else int(num_experts)
     lo, hi = (0, E_all) if expert_range is None else (int(expert_range[0]), int(expert_range[1]))
-    _req(mode in (0, 1), f"{op}: mode must be 0 or 1")
+    _req(mode in (0, 1, 2), f"{op}: mode must be 0, 1 or 2")
     _req(mode == 0 or hi - lo == E, f"{op}: mode 1 takes the weights of experts [lo, hi) only ({hi - lo} != {E})")
     _req(mode == 1 or E == E_all, f"{op}: mode 0 takes every expert's weights")
     tensors = [topk_ids, topk_w, w13, s13, w2, s2, hbuf, ybuf, gl, ctrl] + ([] if host_out else [out])

@@ -322,3 +322,33 @@ def test_int8_shared_expert_as_the_reference_passes_it(cfg1, cuda):
         ops.a16_moe_decode(x, ids, w, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
                            bufs["ybuf"], bufs["gl"], bufs["ctrl"], torch.empty_like(x), 4, None, bufs["pbuf"],
                            dq[0], dq[1][:, :8].contiguous(), dq[2], dq[3], bufs["shbuf"])
+
+
+def test_bounded_wait_runs_out_and_is_reported(cfg1, cuda):
+    """Failure detection without a GPU fault: diagnostic mode 2 makes one producer wait for a dependency that never
+    arrives. The wait gives up at its bound (about one second), the launch drains and returns, the sticky error word
+    holds QF_MOE_ERR_TIMEOUT, and once the caller has zeroed the control block and pbuf again the next launch on the
+    same context is correct."""
+    import time
+    from qwenfast_b200 import _lib
+    cfg, L, lw, C = cfg1
+    x = synthetic.make_tokens(cfg, device=cuda, seed=31)
+    w, ids, _ = ops.router_topk(x, lw.router, cfg.topk, True, *ops.router_bufs(cuda))
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ops.a16_moe_decode(x, ids, w, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
+                       bufs["ybuf"], bufs["gl"], bufs["ctrl"], torch.empty_like(x), 4, None, bufs["pbuf"], lw.sh_w13,
+                       None, lw.sh_w2, None, bufs["shbuf"], mode=2)
+    torch.cuda.synchronize()
+    elapsed = time.time() - t0
+    assert ops.moe_error_word(bufs["ctrl"]) & _lib.QF_MOE_ERR_TIMEOUT
+    assert 0.2 < elapsed < 30, elapsed
+    bufs["ctrl"].zero_()
+    bufs["pbuf"].zero_()
+    out = run_moe(x, ids, w, lw, bufs)
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) == 0
+    ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
+                              shared_w=(C["sh_gu"], C["sh_d"]))
+    assert_close_to_oracle(out, ref)
