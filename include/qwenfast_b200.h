@@ -116,6 +116,23 @@ int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const float* topk_
                       void* out, int M, int H, int I, int E, int topk, int Is, int phase, int mode, int expert_lo,
                       int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream);
 
+/* The same layer on NVFP4 experts -- the reference's own expert format (qf_a16moe.cu:43-57 dequantisation,
+ * serve/qwenfast/test_a16moe.py:134-137): e2m1 codes with one E4M3 scale per 16 k and a per-expert global value.
+ *   w13 / w2: the codes (canonical uint8 [E, N, K/2], even k in the low nibble, read as int32 [E, N, K/8]) in the
+ *             int4 kernel layout (qf_w4_repack on those words, or qwenfast_b200.formats.repack_nvfp4);
+ *   f13 / f2: the E4M3 scales (canonical [E, N, K/16]) in the scale layout of formats.repack_nvfp4: per 128-row tile
+ *             and 128-k stage, [kernel row (128)][8 groups];
+ *   gs13 / gs2: bf16 [E] per-expert multipliers (the reference's 1 / global scale), or NULL (= 1).
+ * The group scales are folded into the dequantised bf16 weights (e2m1 x E4M3 is exact in bf16); the rounding
+ * points, the shared expert, the combine and every other argument are those of qf_a16_moe_decode. H, I % 128 == 0. */
+int qf_a16_moe_decode_nvfp4(const void* x, const int32_t* topk_ids, const float* topk_w, const int32_t* w13,
+                            const void* f13, const void* gs13, const int32_t* w2, const void* f2, const void* gs2,
+                            const void* w_gate, const void* shared, const void* sh_w13, const void* sh_w2, void* hbuf,
+                            int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl, int64_t gl_numel,
+                            int32_t* ctrl, int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel, void* shbuf,
+                            int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk, int Is, int phase,
+                            int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream);
+
 /* One decode MoE layer-step with the router inside the same launch (no counterpart in the reference, whose `dual`
  * path -- serve/overlays/sglang/srt/qwenfast.py:1177-1201 -- calls router_topk and then a16_moe_decode; this entry
  * gives the caller the outputs of both): every CTA computes bf16 logits of E / SMs router rows, a grid barrier on

@@ -54,7 +54,7 @@ def shared_gate_logits(x: torch.Tensor, w_gate: torch.Tensor) -> torch.Tensor:
 
 
 def moe_rounded(x, topk_ids, topk_w, w13, s13, w2, s2, gs13=None, gs2=None,
-                shared=None, w_gate=None, shared_w=None, expert_range=None, return_slots=False):
+                shared=None, w_gate=None, shared_w=None, expert_range=None, return_slots=False, dequant=None):
     """The routed-expert layer with the kernel's rounding points.
 
     x bf16 [M, H]; topk_ids int [M, k]; topk_w fp32 [M, k]; w13 int32 [E, 2I, H/8]; s13 bf16 [E, 2I, H/128];
@@ -63,10 +63,12 @@ def moe_rounded(x, topk_ids, topk_w, w13, s13, w2, s2, gs13=None, gs2=None,
     either needs ``w_gate`` bf16 [H].  ``expert_range=(lo, hi)`` keeps only the slots whose expert is in range
     (the expert-parallel shard of one rank; the other slots are zero).
     Returns out bf16 [M, H] (and the per-slot y bf16 [M, k, H] when ``return_slots``).
+    ``dequant(w, s)`` -> fp32 [N, K] replaces the int4 dequantisation for another expert format (NVFP4: the codes and
+    E4M3 scales, with the per-expert global multiplier passed as gs13 / gs2, as the reference's kernel applies it).
     """
     M, H = x.shape
     k = topk_ids.shape[1]
-    I = w2.shape[2] * 8
+    deq = dequant_int4 if dequant is None else dequant
     xf = x.float()
     ids = topk_ids.long()
     y = torch.zeros(M, k, H)
@@ -76,11 +78,13 @@ def moe_rounded(x, topk_ids, topk_w, w13, s13, w2, s2, gs13=None, gs2=None,
         toks, kps = torch.nonzero(ids == e, as_tuple=True)
         g13 = 1.0 if gs13 is None else float(gs13[e].float())
         g2 = torch.tensor(1.0) if gs2 is None else gs2[e].float()
-        acc = xf[toks] @ dequant_int4(w13[e], s13[e]).T
+        w_gu = deq(w13[e], s13[e])
+        I = w_gu.shape[0] // 2
+        acc = xf[toks] @ w_gu.T
         g = bf16r(bf16r(acc[:, :I]) * g13)
         u = bf16r(bf16r(acc[:, I:]) * g13)
         h = bf16r(g / (1.0 + torch.exp(-g)) * u)
-        acc2 = h @ dequant_int4(w2[e], s2[e]).T
+        acc2 = h @ deq(w2[e], s2[e]).T
         tw = bf16r(g2 * bf16r(topk_w[toks, kps].float()))
         y[toks, kps] = bf16r(bf16r(acc2) * tw[:, None])
     if shared_w is not None:

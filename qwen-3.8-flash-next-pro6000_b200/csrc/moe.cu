@@ -139,6 +139,8 @@ struct Params {
     const __nv_bfloat16* xsrc;   // fused router: x in pinned (mapped) host memory, copied into x by the kernel, or nullptr
     int M, H, I, E, topk, Is, mode, elo, ehi;
     int wofs;   // expert id of the first expert in w13 / s13 / w2 / s2 / gs13 / gs2 (mode 1: elo)
+    const uint8_t* f13;   // NVFP4 experts (FMT 1): E4M3 group-16 scales in the layout of formats.nvfp4_scale_map
+    const uint8_t* f2;
 };
 
 // shared memory map (dynamic): NVP pipeline blocks, then the routing plan
@@ -304,6 +306,25 @@ __device__ __forceinline__ void stage_w4_to_tmem(const uint8_t* w, uint32_t ta) 
         qf::tmem_st8(ta + 16 * hq, v);
         qf::signed_w4(q.z, v + 0);
         qf::signed_w4(q.w, v + 4);
+        qf::tmem_st8(ta + 16 * hq + 8, v);
+    }
+}
+
+// NVFP4: this thread's row of a stage (e2m1 codes in the int4 word layout) -> TMEM columns ta .. ta + 63 as bf16
+// code * group scale (exact); sc = the row's eight E4M3 scales of the stage (group g = byte g: word j of quad q
+// covers k 32q + 8j .. +8, group 2q + j / 2).
+__device__ __forceinline__ void stage_nvfp4_to_tmem(const uint8_t* w, uint32_t ta, uint2 sc) {
+#pragma unroll
+    for (int hq = 0; hq < 4; ++hq) {
+        const uint4 q = *reinterpret_cast<const uint4*>(w + hq * 128 * 16);
+        const uint32_t sw = (hq < 2 ? sc.x : sc.y) >> (16 * (hq & 1));
+        const uint32_t s0 = qf::e4m3_scale_bf16x2(sw & 0xFFu), s1 = qf::e4m3_scale_bf16x2((sw >> 8) & 0xFFu);
+        uint32_t v[8];
+        qf::nvfp4_w4(q.x, s0, v + 0);
+        qf::nvfp4_w4(q.y, s0, v + 4);
+        qf::tmem_st8(ta + 16 * hq, v);
+        qf::nvfp4_w4(q.z, s1, v + 0);
+        qf::nvfp4_w4(q.w, s1, v + 4);
         qf::tmem_st8(ta + 16 * hq + 8, v);
     }
 }
@@ -482,6 +503,10 @@ __device__ __noinline__ void fused_router(const Params& p, uint8_t* smem, const 
     __syncthreads();
 }
 
+// FMT 0: int4 experts (code - 8, one bf16 scale per 128 k, applied to each stage's fp32 partial). FMT 1: NVFP4 experts
+// (e2m1 codes with one E4M3 scale per 16 k, folded into the dequantised weights; the per-expert global multiplier
+// is gs13 / gs2, as for int4).
+template <int FMT>
 __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __grid_constant__ Params p) {
     extern __shared__ __align__(128) uint8_t smem[];
     if (p.dbg != nullptr && threadIdx.x == 0 && blockIdx.x < QF_MOE_DBG_NUMEL / 32)   // timeline: CTA entry
@@ -818,11 +843,19 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     const int K = down ? p.I : p.H;
                     const int N = down ? p.H : 2 * p.I;
                     d.kc = (int16_t)W4_KC;
-                    bytes = STAGE_W + STAGE_S;
                     wsrc = (down ? p.w2 : p.w13) + (size_t)(e - p.wofs) * ((size_t)N * K / 2) + (size_t)tile * (128 * (size_t)K / 2) +
                            (size_t)split * nk * STAGE_W;
-                    ssrc = (down ? p.s2 : p.s13) + (size_t)(e - p.wofs) * ((size_t)N * K / 128) + (size_t)tile * K +
-                           (size_t)split * nk * W4_KC;
+                    if constexpr (FMT == 0) {
+                        bytes = STAGE_W + STAGE_S;
+                        ssrc = (down ? p.s2 : p.s13) + (size_t)(e - p.wofs) * ((size_t)N * K / 128) + (size_t)tile * K +
+                               (size_t)split * nk * W4_KC;
+                    } else {
+                        // the item's E4M3 scales (1 KB per stage, contiguous) into L2; the consumers load them
+                        bytes = STAGE_W;
+                        qf::prefetch_l2((down ? p.f2 : p.f13) + (size_t)(e - p.wofs) * ((size_t)N * K / 16) +
+                                            (size_t)tile * (8 * (size_t)K) + (size_t)split * nk * 1024,
+                                        (uint32_t)nk * 1024u);
+                    }
                     if (down) { dep_idx = C_DONE + u; dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])); }
                 } else if (kind == K_S1 || kind == K_S2) {
                     const bool down = kind == K_S2;
@@ -1022,13 +1055,30 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 int pb = 0, pr = -1;
                 float psc = 0.f;
                 bool failed = false;
+                // NVFP4: this row's E4M3 scales of the item's stages (1 KB per stage), one stage loaded ahead
+                const uint8_t* fsrc = nullptr;
+                uint2 scl = make_uint2(0u, 0u);
+                if constexpr (FMT == 1) {
+                    if (w4) {
+                        const bool down = d.kind == K_G2;
+                        const int K = down ? p.I : p.H, N = down ? p.H : 2 * p.I;
+                        fsrc = (down ? p.f2 : p.f13) + (size_t)(ulist[d.u] - p.wofs) * ((size_t)N * K / 16) +
+                               (size_t)d.tile * (8 * (size_t)K) + (size_t)d.split * d.nk * 1024 + row * 8;
+                        scl = __ldg(reinterpret_cast<const uint2*>(fsrc));
+                    }
+                }
                 for (int kidx = 0;;) {
                     // buffer bcur was last read by the mmas of stage mcount - 2, already retired
                     const uint8_t* sb = ring + st * STAGE_BYTES;
                     float sc = 1.f;
                     if (w4) {
-                        stage_w4_to_tmem(sb + woff, ta0 + 64 * bcur);
-                        sc = bf16_bits(*reinterpret_cast<const uint16_t*>(sb + soff));
+                        if constexpr (FMT == 0) {
+                            stage_w4_to_tmem(sb + woff, ta0 + 64 * bcur);
+                            sc = bf16_bits(*reinterpret_cast<const uint16_t*>(sb + soff));
+                        } else {
+                            stage_nvfp4_to_tmem(sb + woff, ta0 + 64 * bcur, scl);
+                            if (kidx + 1 < nk) scl = __ldg(reinterpret_cast<const uint2*>(fsrc + (size_t)(kidx + 1) * 1024));
+                        }
                     }
                     qf::cp_async_wait_all();
                     qf::fence_proxy_async_smem();   // the tensor cores read bst through the async proxy
@@ -1394,7 +1444,7 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
                int64_t ybuf_bytes, float* gl, int64_t gl_numel, int32_t* ctrl, int64_t ctrl_numel, float* pbuf,
                int64_t pbuf_numel, void* shbuf, int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk,
                int Is, int phase, int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream,
-               const FusedRouter* fr) {
+               const FusedRouter* fr, int fmt = 0) {
     QF_REQUIRE(x && topk_ids && topk_w && w13 && s13 && w2 && s2 && hbuf && ybuf && gl && ctrl && out,
                "a16_moe_decode: null pointer argument");
     QF_REQUIRE(phase == 3 || phase == 4,
@@ -1442,15 +1492,19 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
         QF_REQUIRE(fr->x_stage == nullptr || qf::aligned(fr->x_stage, 16),
                    "moe_layer_decode: x_stage must be 16-byte aligned");
     }
-    ce = qf::ensure_smem_attr(reinterpret_cast<const void*>(moe_persistent_kernel), MOE_SMEM);
+    if (fmt == 1) {
+        QF_REQUIRE(I % 128 == 0 && H % 128 == 0, "a16_moe_decode_nvfp4: H and I must be multiples of 128");
+    }
+    void (*kern)(Params) = fmt == 1 ? moe_persistent_kernel<1> : moe_persistent_kernel<0>;
+    ce = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), MOE_SMEM);
     if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute");
-    static bool carveout_set[64] = {false};
-    if (dev >= 64 || !carveout_set[dev]) {
+    static bool carveout_set[2][64] = {{false}};
+    if (dev >= 64 || !carveout_set[fmt][dev]) {
         // the CTA needs the largest shared-memory carveout; without the hint the driver may pick a smaller one
-        ce = cudaFuncSetAttribute(reinterpret_cast<const void*>(moe_persistent_kernel),
-                                  cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+        ce = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  (int)cudaSharedmemCarveoutMaxShared);
         if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute (carveout)");
-        if (dev < 64) carveout_set[dev] = true;
+        if (dev < 64) carveout_set[fmt][dev] = true;
     }
     // Grid: one CTA per SM (three pipelines each; the CTA allocates all 512 tensor-memory columns). Residency is not
     // required for correctness: an item only waits for items claimed before it, by pipelines that are already running.
@@ -1481,6 +1535,12 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
     p.M = M; p.H = H; p.I = I; p.E = E; p.topk = topk; p.Is = has_shw ? Is : 0;
     p.mode = mode; p.elo = expert_lo; p.ehi = expert_hi;
     p.wofs = mode == 1 ? expert_lo : 0;
+    p.f13 = p.f2 = nullptr;
+    if (fmt == 1) {   // s13 / s2 are the E4M3 group-16 scales
+        p.f13 = static_cast<const uint8_t*>(s13);
+        p.f2 = static_cast<const uint8_t*>(s2);
+        p.s13 = p.s2 = nullptr;
+    }
     p.rw = fr ? static_cast<const __nv_bfloat16*>(fr->w) : nullptr;
     p.logits = fr ? static_cast<__nv_bfloat16*>(fr->logits) : nullptr;
     p.ids_out = fr ? const_cast<int*>(topk_ids) : nullptr;
@@ -1491,7 +1551,7 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
         p.xsrc = p.x;
         p.x = static_cast<const __nv_bfloat16*>(fr->x_stage);
     }
-    ce = qf::launch_ex(moe_persistent_kernel, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,
+    ce = qf::launch_ex(kern, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,
                        reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);
     return qf::cuda_status(ce, "a16_moe_decode: launch");
 }
@@ -1509,6 +1569,21 @@ extern "C" int qf_a16_moe_decode(const void* x, const int32_t* topk_ids, const f
                       hbuf_bytes, ybuf, ybuf_bytes, gl, gl_numel, ctrl, ctrl_numel, pbuf, pbuf_numel, shbuf,
                       shbuf_bytes, out, M, H, I, E, topk, Is, phase, mode, expert_lo, expert_hi, dbg, pdl, stream,
                       nullptr);
+}
+
+extern "C" int qf_a16_moe_decode_nvfp4(const void* x, const int32_t* topk_ids, const float* topk_w,
+                                       const int32_t* w13, const void* f13, const void* gs13, const int32_t* w2,
+                                       const void* f2, const void* gs2, const void* w_gate, const void* shared,
+                                       const void* sh_w13, const void* sh_w2, void* hbuf, int64_t hbuf_bytes, void* ybuf,
+                                       int64_t ybuf_bytes, float* gl, int64_t gl_numel, int32_t* ctrl,
+                                       int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel, void* shbuf,
+                                       int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk, int Is,
+                                       int phase, int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl,
+                                       qf_stream_t stream) {
+    return moe_launch(x, topk_ids, topk_w, w13, f13, gs13, w2, f2, gs2, w_gate, shared, sh_w13, sh_w2, hbuf,
+                      hbuf_bytes, ybuf, ybuf_bytes, gl, gl_numel, ctrl, ctrl_numel, pbuf, pbuf_numel, shbuf,
+                      shbuf_bytes, out, M, H, I, E, topk, Is, phase, mode, expert_lo, expert_hi, dbg, pdl, stream,
+                      nullptr, 1);
 }
 
 extern "C" int qf_moe_layer_decode(const void* x, void* x_stage, const void* router_w, int renormalize, float* topk_w,

@@ -323,3 +323,38 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
                  : "memory");
 }
 }  // namespace qf
+
+namespace qf {
+// Bring [src, src + bytes) into L2 ahead of its use (bulk prefetch through the copy engine; nothing is written to
+// shared memory). src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// NVFP4 (e2m1 codes with one E4M3 scale per 16 k) -> bf16, exactly.
+// An E4M3 byte's fields placed at the low end of a bf16's exponent and mantissa (sign at bit 15, the 7 exponent and
+// mantissa bits at 4..10) read as a bf16 of 2^-120 times its value -- a bf16 subnormal for an E4M3 subnormal -- so one
+// multiply by 2^120 gives the scale (exact). The result is the scale in both halves.
+__device__ __forceinline__ uint32_t e4m3_scale_bf16x2(uint32_t b) {
+    const uint32_t bits = ((b & 0x80u) << 8) | ((b & 0x7Fu) << 4);
+    uint32_t s;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(s) : "r"(bits | (bits << 16)), "r"(0x7B807B80u));   // 2^120
+    return s;
+}
+// One word of eight e2m1 codes (nibble i = k index [0,2,4,6,1,3,5,7][i], the int4 kernel layout) -> four bf16x2 of
+// the weights code * scale (scale: a bf16x2 from e4m3_scale_bf16x2), pair j = k 2j (low half), 2j + 1 (high half).
+// The code's sign goes to bit 15 and its exponent and mantissa bits to 6..8: a bf16 of 2^-126 times the code's value
+// (0.5 a bf16 subnormal); times 2^126, then times the scale -- both exact (e2m1 x E4M3 has at most 6 significant
+// bits).
+__device__ __forceinline__ void nvfp4_w4(uint32_t q, uint32_t scale, uint32_t* p) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t a = (6 - 4 * j) >= 0 ? (q << (6 - 4 * j)) : (q >> (4 * j - 6));   // exponent, mantissa -> 6..8
+        const uint32_t b = q << (12 - 4 * j);                                              // sign -> 15
+        const uint32_t bits = (a & 0x01C001C0u) | (b & 0x80008000u);
+        uint32_t v;
+        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(v) : "r"(bits), "r"(0x7E807E80u));   // 2^126
+        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(p[j]) : "r"(v), "r"(scale));
+    }
+}
+}  // namespace qf

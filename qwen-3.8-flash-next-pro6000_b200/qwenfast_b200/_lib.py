@@ -31,6 +31,9 @@ SIGNATURES = {
     "qf_a16_moe_decode": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                           _p, _l, _p, _l, _p, _l, _p, _l, _p, _l, _p, _l,
                           _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p],
+    "qf_a16_moe_decode_nvfp4": [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                _p, _l, _p, _l, _p, _l, _p, _l, _p, _l, _p, _l,
+                                _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p],
     "qf_moe_layer_decode": [_p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                             _p, _l, _p, _l, _p, _l, _p, _l, _p, _l, _p, _l,
                             _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p],

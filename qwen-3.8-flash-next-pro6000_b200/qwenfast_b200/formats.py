@@ -89,6 +89,19 @@ def w4_scale_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     return row * (K // 128) + st
 
 
+def nvfp4_scale_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
+    """NVFP4 kernel-layout scale byte o -> canonical index row * (K/16) + group, for one [N, K] matrix: per 128-row
+    tile r and 128-k stage st, [lane p (128)][group g (8)] -- each kernel row's eight E4M3 scales of the stage
+    together, so one 8-byte load gives a thread its row's scales."""
+    o = torch.arange(N * K // 16, device=device, dtype=torch.int64)
+    per_tile = 128 * K // 16
+    r, ot = o // per_tile, o % per_tile
+    st, os_ = ot // 1024, ot % 1024
+    rho, g = os_ // 8, os_ % 8
+    row = kernel_row_source(N, gated, device)[128 * r + rho]
+    return row * (K // 16) + 8 * st + g
+
+
 def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     """bf16 kernel-layout element o -> canonical index row * K + k."""
     o = torch.arange(N * K, device=device, dtype=torch.int64)
@@ -143,6 +156,34 @@ def unpack_w4_torch(wk: torch.Tensor, sk: torch.Tensor, N: int, K: int, gated: b
     s = torch.empty(E, N * K // 128, dtype=sk.dtype, device=sk.device)
     s[:, sm] = sk
     return q.view(E, N, K // 8), s.view(E, N, K // 128)
+
+
+def repack_nvfp4(wp: torch.Tensor, sf: torch.Tensor, gated: bool):
+    """Canonical NVFP4 experts (the reference's checkpoint format: codes uint8 [E, N, K/2], even k in the low
+    nibble; E4M3 scales [E, N, K/16]) -> the kernel layout on the tensors' device: the codes in the int4 layout
+    (int32 [E, N*K/8], read as eight codes per word with the lowest k in the low nibble), the scales uint8
+    [E, N*K/16] per ``nvfp4_scale_map``. Returns (wk, sk)."""
+    if wp.dtype != torch.uint8 or wp.dim() != 3 or sf.dtype != torch.float8_e4m3fn:
+        raise RuntimeError("NVFP4 experts need codes uint8 [E, N, K/2] and float8_e4m3fn scales [E, N, K/16]")
+    E, N, K2 = wp.shape
+    K = 2 * K2
+    if tuple(sf.shape) != (E, N, K // 16) or N % 128 or K % 128:
+        raise RuntimeError(f"NVFP4 scales must be [E, N, K/16] = {(E, N, K // 16)} with N, K multiples of 128")
+    words = wp.contiguous().view(torch.int32).view(E, N, K // 8)
+    wm = w4_word_map(N, K, gated, wp.device)
+    wk = _nibble_perm(words.reshape(E, -1)[:, wm], True)
+    sk = sf.contiguous().view(torch.uint8).reshape(E, -1)[:, nvfp4_scale_map(N, K, gated, wp.device)]
+    return wk.contiguous(), sk.contiguous()
+
+
+def unpack_nvfp4(wk: torch.Tensor, sk: torch.Tensor, N: int, K: int, gated: bool):
+    """Inverse of ``repack_nvfp4`` (exact): (codes uint8 [E, N, K/2], scales float8_e4m3fn [E, N, K/16])."""
+    E = wk.shape[0]
+    words = torch.empty(E, N * K // 8, dtype=torch.int32, device=wk.device)
+    words[:, w4_word_map(N, K, gated, wk.device)] = _nibble_perm(wk, False)
+    sf = torch.empty(E, N * K // 16, dtype=torch.uint8, device=sk.device)
+    sf[:, nvfp4_scale_map(N, K, gated, sk.device)] = sk
+    return words.view(torch.uint8).view(E, N, K // 2), sf.view(torch.float8_e4m3fn).view(E, N, K // 16)
 
 
 def repack_bf16_torch(w: torch.Tensor, gated: bool) -> torch.Tensor:

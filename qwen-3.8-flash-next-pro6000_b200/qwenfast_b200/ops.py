@@ -127,7 +127,8 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
                    phase: int = 4, dbg=None, pbuf=None, shq1=None, shs1=None, shq2=None, shs2=None, shbuf=None,
                    pdl: bool = True, mode: int = 0, expert_range=None, num_experts: Optional[int] = None,
                    router_w: Optional[torch.Tensor] = None, renormalize: bool = True,
-                   logits: Optional[torch.Tensor] = None, x_stage: Optional[torch.Tensor] = None):
+                   logits: Optional[torch.Tensor] = None, x_stage: Optional[torch.Tensor] = None,
+                   fmt: str = "int4"):
     """Routed experts + shared expert + combine; writes ``out`` in place and returns it.
 
     Argument roles follow ``a16_moe_decode`` (serve/qwenfast/qf_a16moe.cu:852-863). Weight format: the kernel
@@ -146,7 +147,11 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     With ``router_w`` (bf16 [E, H]) the router runs inside the same launch (C ABI ``qf_moe_layer_decode``):
     ``topk_ids`` / ``topk_w`` and ``logits`` (bf16 [M, E]) are then outputs, written by the kernel. With it,
     ``x_stage`` (CUDA bf16 [M, H]) means ``x`` is a pinned host tensor that the kernel copies into ``x_stage`` itself,
-    and ``out`` may be a pinned host tensor as well (written by the kernel)."""
+    and ``out`` may be a pinned host tensor as well (written by the kernel).
+
+    ``fmt="nvfp4"``: the experts are NVFP4 (the reference's own format) in the layout of ``formats.repack_nvfp4`` --
+    w13 / w2 the e2m1 codes (int32, int4 kernel layout), s13 / s2 the E4M3 group-16 scales (uint8 [E, N*K/16]),
+    gs13 / gs2 the per-expert multipliers 1 / g (C ABI ``qf_a16_moe_decode_nvfp4``; routing given, not fused)."""
     op = "a16_moe_decode" if router_w is None else "moe_layer_decode"
     if x_stage is None:
         _cuda(x, "x", op)
@@ -173,8 +178,16 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     I = (w2.shape[1] * 8) // H
     _req(w2.shape[0] == E and w13.shape[1] == 2 * I * H // 8 and w2.shape[1] * 8 == H * I,
          f"{op}: w13 / w2 shapes do not match H={H}")
-    _req(s13.dtype == BF16 and tuple(s13.shape) == (E, 2 * I * H // 128), f"{op}: s13 must be bf16 [E, 2I*H/128]")
-    _req(s2.dtype == BF16 and tuple(s2.shape) == (E, H * I // 128), f"{op}: s2 must be bf16 [E, H*I/128]")
+    _req(fmt in ("int4", "nvfp4"), f"{op}: fmt must be 'int4' or 'nvfp4'")
+    if fmt == "nvfp4":
+        _req(router_w is None and x_stage is None, f"{op}: NVFP4 experts take the routing as input (no fused router)")
+        _req(s13.dtype == torch.uint8 and tuple(s13.shape) == (E, 2 * I * H // 16) and s13.is_contiguous(),
+             f"{op}: NVFP4 s13 must be the E4M3 scales uint8 [E, 2I*H/16] (formats.repack_nvfp4)")
+        _req(s2.dtype == torch.uint8 and tuple(s2.shape) == (E, H * I // 16) and s2.is_contiguous(),
+             f"{op}: NVFP4 s2 must be the E4M3 scales uint8 [E, H*I/16] (formats.repack_nvfp4)")
+    else:
+        _req(s13.dtype == BF16 and tuple(s13.shape) == (E, 2 * I * H // 128), f"{op}: s13 must be bf16 [E, 2I*H/128]")
+        _req(s2.dtype == BF16 and tuple(s2.shape) == (E, H * I // 128), f"{op}: s2 must be bf16 [E, H*I/128]")
     for name, g in (("gs13", gs13), ("gs2", gs2)):
         _req(not _present(g) or (g.dtype == BF16 and g.numel() == E), f"{op}: {name} must be bf16 [E] or empty")
     if _present(shs1) or _present(shs2):
@@ -221,8 +234,9 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
                 out.data_ptr(), M, H, I, E_all, topk_ids.shape[1], Is, int(mode), int(lo), int(hi),
                 _ptr(dbg), int(bool(pdl)), _stream(dev)), op)
         return out
+    entry = _lib.load().qf_a16_moe_decode_nvfp4 if fmt == "nvfp4" else _lib.load().qf_a16_moe_decode
     with torch.cuda.device(x.device):
-        _lib.check(_lib.load().qf_a16_moe_decode(
+        _lib.check(entry(
             x.data_ptr(), topk_ids.data_ptr(), topk_w.data_ptr(), w13.data_ptr(), s13.data_ptr(), _ptr(gs13),
             w2.data_ptr(), s2.data_ptr(), _ptr(gs2), _ptr(w_gate), _ptr(shared), _ptr(shq1) if has_shw else None,
             _ptr(shq2) if has_shw else None,

@@ -67,3 +67,28 @@ def test_w8_layout_round_trip_and_swizzle(N, K):
     assert torch.equal(formats.w8_byte_map(N, K).sort().values, torch.arange(N * K))
     # tile (0, 0): row 3's chunk 1 (k = 16..31) sits at position 1 ^ 3 = 2 of the row
     assert torch.equal(qk.reshape(-1)[3 * 128 + 2 * 16: 3 * 128 + 3 * 16], q[3, 16:32])
+
+
+def test_nvfp4_kernel_layout():
+    """NVFP4 experts (the reference's format) in the kernel layout: exact round trip, and each position holds what
+    the kernel reads there -- a thread of lane p in tile r reads stage st's word (quad q, word j) at
+    [st][q][p][j] (nibble i = k 32q + 8j + [0,2,4,6,1,3,5,7][i]) and its eight group scales at [st][p][0..8)."""
+    from oracle import nvfp4_ref
+    g = torch.Generator().manual_seed(5)
+    E, N, K = 2, 256, 384
+    for gated in (True, False):
+        wp, sf = nvfp4_ref.random_nvfp4((E, N, K), g)
+        wk, sk = formats.repack_nvfp4(wp, sf, gated)
+        wp2, sf2 = formats.unpack_nvfp4(wk, sk, N, K, gated)
+        assert torch.equal(wp2, wp) and torch.equal(sf2.view(torch.uint8), sf.view(torch.uint8))
+        codes = nvfp4_ref.unpack_e2m1(wp)                      # [E, N, K]
+        src = formats.kernel_row_source(N, gated)
+        perm = formats.NIBBLE_ORDER
+        for e, r, st, q, p, j in ((0, 0, 0, 0, 0, 0), (1, 1, 2, 3, 127, 3), (0, 1, 1, 2, 77, 1), (1, 0, 2, 1, 6, 2)):
+            word = int(wk[e, r * (128 * K // 8) + st * 2048 + q * 512 + p * 4 + j]) & 0xFFFFFFFF
+            row = int(src[128 * r + p])
+            for i in range(8):
+                assert (word >> (4 * i)) & 15 == int(codes[e, row, 128 * st + 32 * q + 8 * j + perm[i]])
+            for gi in range(8):
+                got = int(sk[e, r * (128 * K // 16) + st * 1024 + p * 8 + gi])
+                assert got == int(sf.view(torch.uint8)[e, row, 8 * st + gi])
