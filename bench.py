@@ -48,7 +48,8 @@ def parse():
     ap.add_argument("--zipf", type=float, default=0.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", default="")
-    ap.add_argument("--sweep-configs", default="2,3", help="which sweep records to take (comma list of 2, 3)")
+    ap.add_argument("--sweep-configs", default="2,3",
+                    help="which sweep records to take (comma list of 2, 3, nvfp4)")
     ap.add_argument("--sweep-n", default="2048,4096,8192,12288", help="config-3 weight row counts N to sweep")
     ap.add_argument("--timeline", default="", help="write the per-CTA item timeline of config-1 layer-steps here")
     ap.add_argument("--timeline-m", default="1,10", help="token counts of the timeline")
@@ -482,7 +483,7 @@ def run_sweep(args):
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / reps
 
-    which = {int(c) for c in args.sweep_configs.split(",") if c.strip()}
+    which = {int(c) if c.strip().isdigit() else c.strip() for c in args.sweep_configs.split(",") if c.strip()}
     # ---------------------------------------------------------------- config 2: M sweep, Zipf routing, 48 layers
     cfg = synthetic.CONFIGS[1]
     NL = max(args.layers, 48)
@@ -530,6 +531,59 @@ def run_sweep(args):
         del bufs, xs, outs
     del layers
     torch.cuda.empty_cache()
+
+    # ---------------------------------------------------------------- config-1 shapes on NVFP4 experts
+    if "nvfp4" in which:
+        NL4 = 16
+        lay4 = []
+        for l in range(NL4):
+            wp, sf, g13 = synthetic.make_nvfp4_experts(cfg.E, 2 * cfg.I, cfg.H, device=dev, seed=500 + l)
+            wk13, sk13 = formats.repack_nvfp4(wp, sf, gated=True)
+            wp, sf, g2 = synthetic.make_nvfp4_experts(cfg.E, cfg.H, cfg.I, device=dev, seed=900 + l)
+            wk2, sk2 = formats.repack_nvfp4(wp, sf, gated=False)
+            del wp, sf
+            L = synthetic.make_moe_layer(synthetic.MoEConfig("nvfp4-shared", cfg.H, 16, 128, 4, 1, cfg.Is, 1300 + l),
+                                         device=dev)   # the router and the bf16 shared expert only
+            router = (torch.randn(cfg.E, cfg.H, device=dev, generator=torch.Generator(device=dev).manual_seed(l))
+                      * 0.02).to(torch.bfloat16)
+            lay4.append(dict(w13=wk13, s13=sk13, w2=wk2, s2=sk2, gs13=(1.0 / g13).to(torch.bfloat16),
+                             gs2=(1.0 / g2).to(torch.bfloat16), router=router, w_gate=L["w_gate"],
+                             sh13=formats.repack_bf16(L["sh_gu"], gated=True),
+                             sh2=formats.repack_bf16(L["sh_d"], gated=False)))
+            del L
+        per_e4 = (2 * cfg.I * cfg.H + cfg.H * cfg.I) // 2 + (2 * cfg.I * cfg.H + cfg.H * cfg.I) // 16
+        for M in (1, 10):
+            bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, dev)
+            rb = ops.router_bufs(dev)
+            xs = [synthetic.make_tokens(cfg, M=M, device=dev, seed=8000 + l) for l in range(NL4)]
+            routes = [ops.router_topk(xs[l], lay4[l]["router"], cfg.topk, True, *rb) for l in range(NL4)]
+            outs = [torch.empty_like(xs[0]) for _ in range(NL4)]
+
+            def nvfp4_layers():
+                for l, q in enumerate(lay4):
+                    tw, ids, _ = routes[l]
+                    ops.a16_moe_decode(xs[l], ids, tw, q["w13"], q["s13"], q["gs13"], q["w2"], q["s2"], q["gs2"],
+                                       q["w_gate"], None, bufs["hbuf"], bufs["ybuf"], bufs["gl"], bufs["ctrl"],
+                                       outs[l], 4, None, bufs["pbuf"], q["sh13"], None, q["sh2"], None,
+                                       bufs["shbuf"], fmt="nvfp4")
+
+            ms4 = graph_time(nvfp4_layers, reps=8)
+            err = ops.moe_error_word(bufs["ctrl"])
+            if err:
+                raise RuntimeError(f"NVFP4 MoE kernel reported error word {err:#x} at M={M}")
+            U = [int(torch.unique(routes[l][1]).numel()) for l in range(NL4)]
+            b4 = statistics.mean(u * per_e4 + shared_b + 2 * M * cfg.H * 2 for u in U)
+            us4 = ms4 * 1e3 / NL4
+            rec = {"config": "1-nvfp4", "M": M, "layers": NL4, "unique_experts_mean": statistics.mean(U),
+                   "us_moe_kernel": us4, "moe_bytes": b4, "achieved_gbs": b4 / (us4 * 1e-6) / 1e9,
+                   "peak_gbs": peak, "peak_kind": peak_kind,
+                   "note": "NVFP4 experts (e2m1 + E4M3 group-16 scales), routing given, bf16 shared expert"}
+            rec["frac"] = rec["achieved_gbs"] / peak
+            records.append(rec)
+            print(json.dumps(rec), flush=True)
+            del bufs, xs, outs, routes
+        del lay4
+        torch.cuda.empty_cache()
 
     # ---------------------------------------------------------------- config 3: W8A8 GEMM, K = 2048
     K = synthetic.W8A8_K

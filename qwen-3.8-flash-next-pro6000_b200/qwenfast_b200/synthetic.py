@@ -54,6 +54,17 @@ def group_scales(shape, g, device) -> torch.Tensor:
     return (torch.randn(shape, generator=g, device=device).abs() * 0.01 + 1e-4).to(torch.bfloat16)
 
 
+def make_nvfp4_experts(E: int, N: int, K: int, device="cpu", seed: int = 0):
+    """Synthetic NVFP4 experts (the reference's checkpoint format): uniform e2m1 codes uint8 [E, N, K/2], E4M3 group-16
+    scales |N(0, 1)| * 2 + 1/64 [E, N, K/16], per-expert global values g in [100, 300) (the weight is
+    e2m1 * scale / g)."""
+    g = _gen(device, seed)
+    wp = torch.randint(0, 256, (E, N, K // 2), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+    sf = (torch.randn(E, N, K // 16, generator=g, device=device).abs() * 2 + 1.0 / 64).to(torch.float8_e4m3fn)
+    gv = torch.rand(E, generator=g, device=device) * 200 + 100
+    return wp, sf, gv
+
+
 def make_moe_layer(cfg: MoEConfig, device="cpu", seed=None, zipf_s: float = 0.0) -> dict:
     """Canonical weights of one MoE layer. ``zipf_s > 0`` skews the router (config 2)."""
     g = _gen(device, cfg.seed if seed is None else seed)
