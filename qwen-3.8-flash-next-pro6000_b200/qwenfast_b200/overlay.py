@@ -174,9 +174,16 @@ def _a16_weights(block):
                                                 "w2_weight", "w2_weight_scale", "w2_weight_scale_2"))
 
 
+def _a16_format(block) -> str:
+    """"nvfp4" when the routed experts carry E4M3 group-16 scales (uint8, ``formats.repack_nvfp4``), else "int4"."""
+    s13 = _a16_weights(block)[1]
+    return "nvfp4" if s13 is not None and s13.dtype == torch.uint8 else "int4"
+
+
 def _a16_ok(block, x: torch.Tensor) -> bool:
-    """The routed experts qualify for the W4A16 kernel (qwenfast.py:1074-1089): int32 kernel-layout int4 weights of
-    E experts, bf16 group-128 scales, optional bf16 [E] global scales, and the shared-expert gate (bf16 [H], no
+    """The routed experts qualify for the W4A16 kernel (qwenfast.py:1074-1089): int32 kernel-layout codes of E
+    experts with either bf16 group-128 scales (int4) or E4M3 group-16 scales (NVFP4, the reference's format, as uint8
+    from ``formats.repack_nvfp4``), optional bf16 [E] global multipliers, and the shared-expert gate (bf16 [H], no
     bias)."""
     w13, s13, g13, w2, s2, g2 = _a16_weights(block)
     sg = getattr(block, "shared_expert_gate", None)
@@ -192,10 +199,11 @@ def _a16_ok(block, x: torch.Tensor) -> bool:
     if w2 is None or w2.dim() != 2 or w2.shape[0] != E:
         return False
     I = w2.shape[1] * 8 // H
+    sdt, grp = (torch.uint8, 16) if _a16_format(block) == "nvfp4" else (BF16, 128)
     return (
         1 <= M <= _lib.QF_MAX_TOKENS and I >= 128 and I % 128 == 0 and w2.shape[1] * 8 == H * I
-        and shaped(w13, torch.int32, (E, 2 * I * H // 8)) and shaped(s13, BF16, (E, 2 * I * H // 128))
-        and shaped(w2, torch.int32, (E, H * I // 8)) and shaped(s2, BF16, (E, H * I // 128))
+        and shaped(w13, torch.int32, (E, 2 * I * H // 8)) and shaped(s13, sdt, (E, 2 * I * H // grp))
+        and shaped(w2, torch.int32, (E, H * I // 8)) and shaped(s2, sdt, (E, H * I // grp))
         and (g13 is None or (g13.dtype == BF16 and g13.numel() == E))
         and (g2 is None or (g2.dtype == BF16 and g2.numel() == E))
         and sg is not None and getattr(sg, "weight", None) is not None and sg.weight.numel() == H
@@ -290,6 +298,16 @@ def dual(block, hidden_states: torch.Tensor, orig=None, lora_active: bool = Fals
         I = w2.shape[1] * 8 // H
         b = _a16_bufs(x.device, H, I, cfg.top_k, sh[2] if sh is not None else 0)
         out = torch.empty_like(x)
+        if _a16_format(block) == "nvfp4":   # the reference's order: the router op, then the MoE op
+            scratch, counter = _router_bufs(x.device)
+            tw, ids, logits = ops.router_topk(x, block.gate.weight, cfg.top_k, bool(cfg.renormalize), scratch,
+                                              counter, True)
+            ops.a16_moe_decode(x, ids, tw, w13, s13, g13, w2, s2, g2, block.shared_expert_gate.weight.view(-1),
+                               shared, b["hbuf"], b["ybuf"], b["gl"], b["ctrl"], out, 4, None, b["pbuf"],
+                               sh[0] if sh is not None else None, None, sh[1] if sh is not None else None, None,
+                               b["shbuf"], fmt="nvfp4")
+            block._qf_topk = TopKOutput(tw, ids, logits)
+            return out, None
         tw = torch.empty(M, cfg.top_k, dtype=torch.float32, device=x.device)
         ids = torch.empty(M, cfg.top_k, dtype=torch.int32, device=x.device)
         logits = torch.empty(M, E, dtype=BF16, device=x.device)

@@ -152,3 +152,45 @@ def test_dual_precomputed_shared_and_stock_experts(cuda, cfg1_layer):
     t = block.experts.calls[0]
     assert torch.equal(t.topk_ids, ids) and torch.equal(t.topk_weights, w) and block._qf_topk is t
     assert routed.shape == x.shape and sh.shape == x.shape
+
+
+def test_dual_nvfp4_experts(cuda):
+    """The block with NVFP4 experts (the reference's format, repacked by formats.repack_nvfp4): ``dual`` runs the
+    router op and then the NVFP4 MoE op, as the reference's dual does; the result equals that op called directly and
+    the oracle within tolerance."""
+    from oracle import nvfp4_ref
+    from qwenfast_b200 import formats
+    E, H, I, topk, M, Is = 64, 2048, 512, 10, 10, 512
+    wp13, sf13, g13 = synthetic.make_nvfp4_experts(E, 2 * I, H, seed=1)
+    wp2, sf2, g2 = synthetic.make_nvfp4_experts(E, H, I, seed=2)
+    cfg = synthetic.MoEConfig("nvfp4-block", H, E, 128, topk, M, Is, 3)
+    L = synthetic.make_moe_layer(cfg)                       # router, shared expert, gate
+    block, _ = _block(cfg, {**L, "w13": L["w13"], "s13": L["s13"], "w2": L["w2"], "s2": L["s2"]}, cuda,
+                      kernel_experts=False)
+    wk13, sk13 = formats.repack_nvfp4(wp13.to(cuda), sf13.to(cuda), gated=True)
+    wk2, sk2 = formats.repack_nvfp4(wp2.to(cuda), sf2.to(cuda), gated=False)
+    gs13, gs2 = (1.0 / g13).to(BF).to(cuda), (1.0 / g2).to(BF).to(cuda)
+    ex = block.experts
+    ex.w13_weight, ex.w13_weight_scale, ex.w13_weight_scale_2 = wk13, sk13, gs13
+    ex.w2_weight, ex.w2_weight_scale, ex.w2_weight_scale_2 = wk2, sk2, gs2
+    x = synthetic.make_tokens(cfg, device=cuda, seed=4)
+    assert overlay._a16_format(block) == "nvfp4" and overlay._a16_ok(block, x)
+    out, sh = overlay.dual(block, x)
+    torch.cuda.synchronize()
+    r = block._qf_topk
+    assert sh is None and not block.experts.calls
+    w, ids, _ = ops.router_topk(x, block.gate.weight, topk, True, *ops.router_bufs(cuda))
+    assert torch.equal(ids, r.topk_ids) and torch.equal(w, r.topk_weights)
+    bufs = ops.moe_workspace(M, H, I, topk, Is, cuda)
+    direct = torch.empty_like(x)
+    shk = block._qf_a16sh
+    ops.a16_moe_decode(x, ids, w, wk13, sk13, gs13, wk2, sk2, gs2, block.shared_expert_gate.weight.view(-1), None,
+                       bufs["hbuf"], bufs["ybuf"], bufs["gl"], bufs["ctrl"], direct, 4, None, bufs["pbuf"], shk[0],
+                       None, shk[1], None, bufs["shbuf"], fmt="nvfp4")
+    torch.cuda.synchronize()
+    assert torch.equal(out, direct)
+    deq = lambda wp, sf: nvfp4_ref.dequant_nvfp4(wp, sf, 1.0)
+    ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), wp13, sf13, wp2, sf2, gs13=gs13.cpu(), gs2=gs2.cpu(),
+                              dequant=deq, w_gate=L["w_gate"], shared_w=(L["sh_gu"], L["sh_d"]))
+    d = out.float().cpu() - ref.float()
+    assert bool((d.abs() <= 2e-2 + 2.0 ** -6 * ref.float().abs()).all()) and (d.norm() / ref.float().norm()) <= 1e-2

@@ -139,3 +139,16 @@ def test_a16_shared_gate_on_host():
     assert overlay._a16_shared(b) is None and b._qf_a16sh is None
     b = _block()
     assert overlay._a16_shared(b) is None                 # CPU weights: nothing is repacked here
+
+
+def test_a16_ok_accepts_nvfp4_experts():
+    """NVFP4 experts (E4M3 group-16 scales as uint8, the reference's format) qualify with their own scale shapes."""
+    b = _block()
+    E, H, I = 32, 256, 128
+    b.experts.w13_weight_scale = torch.zeros(E, 2 * I * H // 16, dtype=torch.uint8)
+    b.experts.w2_weight_scale = torch.zeros(E, H * I // 16, dtype=torch.uint8)
+    x = torch.zeros(4, 256, dtype=BF)
+    assert overlay._a16_format(b) == "nvfp4" and overlay._a16_ok(b, x)
+    b.experts.w2_weight_scale = torch.zeros(E, H * I // 128, dtype=torch.uint8)   # int4-sized scales: no
+    assert not overlay._a16_ok(b, x)
+    assert overlay._a16_format(_block()) == "int4"
