@@ -77,6 +77,20 @@ def router_bufs(device, rows: int = 64, experts: int = 1024):
 _W8_SHARED = {}
 
 
+def tensor_cache(cache: dict, tensors, build):
+    """``build()`` once per set of live tensors: the entry is found again while every tensor of the set is alive (the
+    same objects, not just the same addresses) and is dropped when the first of them is freed, so a cache of
+    converted weights does not outlive the weights it was made from."""
+    key = tuple((t.data_ptr(), tuple(t.shape), t.dtype) for t in tensors)
+    hit = cache.get(key)
+    if hit is not None and all(r() is t for r, t in zip(hit[0], tensors)):
+        return hit[1]
+    val = build()
+    cache[key] = (tuple(weakref.ref(t) for t in tensors), val)
+    weakref.finalize(tensors[0], cache.pop, key, None)
+    return val
+
+
 def shared_w8_as_bf16(sq1, ss1, sq2, ss2, H: int, op: str = "a16_moe_decode"):
     """The shared expert given as the reference passes it to its MoE op (qwenfast.py:1092-1113, 1196-1200): INT8
     gate_up sq1 [2Is, H] and down sq2 [H, Is] with bf16 group scales ss1 / ss2 (``w8_quant`` format, group 128 or
@@ -84,7 +98,7 @@ def shared_w8_as_bf16(sq1, ss1, sq2, ss2, H: int, op: str = "a16_moe_decode"):
     (``w8g_unpack``) and repacked. Done once per weight tensor: the result is cached for as long as ``sq1`` lives, so
     only the first call allocates (make it before any graph capture). The weights are then rounded to bf16 (relative
     2^-9 per weight) where the reference's w8g arithmetic applies the scale to fp32 group sums -- within the layer's
-    tolerance (tested against that arithmetic)."""
+    tolerance (tested against that arithmetic). The converted copy is dropped when ``sq1`` is freed."""
     for name, q, sc in (("shq1 / shs1", sq1, ss1), ("shq2 / shs2", sq2, ss2)):
         _req(q is not None and sc is not None and q.dtype == torch.int8 and q.dim() == 2 and q.is_contiguous()
              and sc.dtype == BF16 and sc.dim() == 2 and sc.is_contiguous() and sc.size(0) == q.size(0)
@@ -93,17 +107,15 @@ def shared_w8_as_bf16(sq1, ss1, sq2, ss2, H: int, op: str = "a16_moe_decode"):
     Is = sq2.size(1)
     _req(tuple(sq1.shape) == (2 * Is, H) and tuple(sq2.shape) == (H, Is),
          f"{op}: INT8 shared-expert weights must be gate_up [2Is, H] and down [H, Is]")
-    key = (sq1.data_ptr(), ss1.data_ptr(), sq2.data_ptr(), ss2.data_ptr(), H, Is)
-    hit = _W8_SHARED.get(key)
-    if hit is not None and all(r() is t for r, t in zip(hit[0], (sq1, ss1, sq2, ss2))):
-        return hit[1], hit[2]
-    w1 = torch.empty(2 * Is, H, dtype=BF16, device=sq1.device)
-    w2 = torch.empty(H, Is, dtype=BF16, device=sq1.device)
-    w8g_unpack(sq1, ss1, w1)
-    w8g_unpack(sq2, ss2, w2)
-    wk1, wk2 = repack_bf16(w1, gated=True), repack_bf16(w2, gated=False)
-    _W8_SHARED[key] = (tuple(weakref.ref(t) for t in (sq1, ss1, sq2, ss2)), wk1, wk2)
-    return wk1, wk2
+
+    def build():
+        w1 = torch.empty(2 * Is, H, dtype=BF16, device=sq1.device)
+        w2 = torch.empty(H, Is, dtype=BF16, device=sq1.device)
+        w8g_unpack(sq1, ss1, w1)
+        w8g_unpack(sq2, ss2, w2)
+        return repack_bf16(w1, gated=True), repack_bf16(w2, gated=False)
+
+    return tensor_cache(_W8_SHARED, (sq1, ss1, sq2, ss2), build)
 
 
 def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:

@@ -312,7 +312,7 @@ def test_int8_shared_expert_as_the_reference_passes_it(cfg1, cuda):
         outs.append(out)
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1]) and ops.moe_error_word(bufs["ctrl"]) == 0
-    key_hits = [v for k, v in ops._W8_SHARED.items() if k[0] == dq[0].data_ptr()]
+    key_hits = [v for k, v in ops._W8_SHARED.items() if k[0][0] == dq[0].data_ptr()]
     assert len(key_hits) == 1                              # converted once
     shared = w8_ref.shared_expert_w8g(x.cpu(), sq1, ss1, sq2, ss2)
     ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], shared=shared,

@@ -152,3 +152,27 @@ def test_a16_ok_accepts_nvfp4_experts():
     b.experts.w2_weight_scale = torch.zeros(E, H * I // 128, dtype=torch.uint8)   # int4-sized scales: no
     assert not overlay._a16_ok(b, x)
     assert overlay._a16_format(_block()) == "int4"
+
+
+def test_tensor_cache_follows_the_tensors_lifetime():
+    """The cache of converted weights (ops.tensor_cache): built once per live set of tensors, rebuilt for other
+    tensors, dropped when the tensors are freed."""
+    import gc
+    from qwenfast_b200 import ops
+    cache, calls = {}, []
+
+    def build():
+        calls.append(1)
+        return len(calls)
+
+    a, b = torch.zeros(4), torch.ones(4)
+    assert ops.tensor_cache(cache, (a, b), build) == 1
+    assert ops.tensor_cache(cache, (a, b), build) == 1 and len(calls) == 1
+    c = torch.zeros(4)
+    assert ops.tensor_cache(cache, (c, b), build) == 2 and len(cache) == 2
+    del a
+    gc.collect()
+    assert len(cache) == 1
+    del c
+    gc.collect()
+    assert cache == {}
