@@ -144,9 +144,11 @@ int launch_router(const void* x, const void* w, int rows, int H, int E, int topk
 
 }  // namespace
 
-extern "C" int qf_router_topk(const void* x, const void* w, int rows, int hidden, int experts, int topk,
-                              int renormalize, float* topk_weights, int32_t* topk_ids, void* logits, float* scratch,
-                              int64_t scratch_numel, int32_t* counter, int pdl, qf_stream_t stream) {
+namespace {
+// Argument checks of both router entry points, made before anything is enqueued on the stream.
+int router_args(const void* x, const void* w, int rows, int hidden, int experts, int topk, const float* topk_weights,
+                const int32_t* topk_ids, const void* logits, const float* scratch, int64_t scratch_numel,
+                const int32_t* counter) {
     QF_REQUIRE(x && w && topk_weights && topk_ids && logits && scratch && counter,
                "router_topk: null pointer argument");
     QF_REQUIRE(rows >= 1 && rows <= QF_MAX_TOKENS, "router_topk: rows must be in [1, %d], got %d", QF_MAX_TOKENS,
@@ -160,6 +162,16 @@ extern "C" int qf_router_topk(const void* x, const void* w, int rows, int hidden
     QF_REQUIRE(scratch_numel >= (int64_t)rows * experts, "router_topk: scratch needs %lld floats, got %lld",
                (long long)rows * experts, (long long)scratch_numel);
     QF_REQUIRE(qf::aligned(x, 16) && qf::aligned(w, 16), "router_topk: x and w must be 16-byte aligned");
+    return QF_OK;
+}
+}  // namespace
+
+extern "C" int qf_router_topk(const void* x, const void* w, int rows, int hidden, int experts, int topk,
+                              int renormalize, float* topk_weights, int32_t* topk_ids, void* logits, float* scratch,
+                              int64_t scratch_numel, int32_t* counter, int pdl, qf_stream_t stream) {
+    const int rc = router_args(x, w, rows, hidden, experts, topk, topk_weights, topk_ids, logits, scratch,
+                               scratch_numel, counter);
+    if (rc != QF_OK) return rc;
     const int bpw = (hidden / 32 + RW - 1) / RW;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (bpw <= 1) return launch_router<1>(x, w, rows, hidden, experts, topk, renormalize, topk_weights, topk_ids,
@@ -183,11 +195,14 @@ extern "C" int qf_router_topk(const void* x, const void* w, int rows, int hidden
 // outputs. Limit: rows * experts <= 64 * 1024 (256 KB of fp32, plus one counter word); every GPU that loads the
 // library keeps this array until the process exits.
 //
-// Set-up: the first call on a device (with that device current) resolves the array's device address with
-// cudaGetSymbolAddress and caches it; make that first call before any stream capture. Each call then clears the
-// counter with cudaMemsetAsync on the caller's stream and launches the same kernel as qf_router_topk.
-// All calls on a device share the array and it keeps the last call's contents, so calls that can overlap on the
-// GPU (different streams, or no ordering between them) race with each other; order them on one stream.
+// Set-up: the first call in a CUDA context (the device's primary context, as the runtime uses it, or another context
+// the host made current) resolves the array's device address in that context with cudaGetSymbolAddress and caches it
+// under the context's unique id; make that first call before any stream capture. A later call in a different context
+// (after cudaDeviceReset, or on another context of the same device) resolves the address again. Each call checks its
+// arguments, then clears the counter with cudaMemsetAsync on the caller's stream and launches the same kernel as
+// qf_router_topk; a call that fails its checks enqueues nothing.
+// All calls in a context share the array and it keeps the last call's contents, so calls that can overlap on the GPU
+// (different streams, or no ordering between them) race with each other; order them on one stream.
 namespace {
 constexpr int NOALLOC_SCRATCH_FLOATS = QF_MAX_TOKENS * QF_MAX_EXPERTS;
 // [0, NOALLOC_SCRATCH_FLOATS): logits scratch; the next word: ticket counter
@@ -195,11 +210,47 @@ static __device__ __align__(256) uint32_t g_router_noalloc[NOALLOC_SCRATCH_FLOAT
 
 struct NoAllocSlot {
     bool ready;
+    unsigned long long ctx_id;   // unique id of the context the address belongs to
     float* scratch;
     int32_t* counter;
 };
 std::mutex g_noalloc_mu;
 NoAllocSlot g_noalloc_slot[64];
+
+// Unique id of the calling thread's current CUDA context (driver cuCtxGetCurrent + cuCtxGetId, reached through the
+// runtime's driver entry-point query, so the library still links against the runtime only). Ids are never reused,
+// unlike context handles.
+int current_context_id(unsigned long long* id) {
+    using GetCurrent = int (*)(void**);
+    using GetId = int (*)(void*, unsigned long long*);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    if (get_current == nullptr || get_id == nullptr) {
+        void* f0 = nullptr;
+        void* f1 = nullptr;
+        cudaDriverEntryPointQueryResult q0, q1;
+        cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f0, cudaEnableDefault, &q0);
+        if (e == cudaSuccess) e = cudaGetDriverEntryPoint("cuCtxGetId", &f1, cudaEnableDefault, &q1);
+        if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: cudaGetDriverEntryPoint");
+        QF_REQUIRE(q0 == cudaDriverEntryPointSuccess && q1 == cudaDriverEntryPointSuccess && f0 && f1,
+                   "router_topk_noalloc: the driver does not provide cuCtxGetCurrent / cuCtxGetId");
+        get_current = reinterpret_cast<GetCurrent>(f0);
+        get_id = reinterpret_cast<GetId>(f1);
+    }
+    void* ctx = nullptr;
+    QF_REQUIRE(get_current(&ctx) == 0, "router_topk_noalloc: cuCtxGetCurrent failed");
+    if (ctx == nullptr) {
+        // no context is current on this thread yet: the runtime's primary context of the current device becomes
+        // current (a context the host made current itself is never replaced)
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaSetDevice(dev);
+        if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: initialising the primary context");
+        QF_REQUIRE(get_current(&ctx) == 0 && ctx != nullptr, "router_topk_noalloc: no current CUDA context");
+    }
+    QF_REQUIRE(get_id(ctx, id) == 0, "router_topk_noalloc: cuCtxGetId failed");
+    return QF_OK;
+}
 }  // namespace
 
 extern "C" int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, int experts, int topk,
@@ -212,19 +263,26 @@ extern "C" int qf_router_topk_noalloc(const void* x, const void* w, int rows, in
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: cudaGetDevice");
     QF_REQUIRE(dev >= 0 && dev < 64, "router_topk_noalloc: device ordinal %d out of range", dev);
+    unsigned long long ctx_id = 0;
+    int rc = current_context_id(&ctx_id);
+    if (rc != QF_OK) return rc;
     NoAllocSlot slot;
     {
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
-        if (!g_noalloc_slot[dev].ready) {
+        if (!g_noalloc_slot[dev].ready || g_noalloc_slot[dev].ctx_id != ctx_id) {
             void* base = nullptr;
             e = cudaGetSymbolAddress(&base, g_router_noalloc);
             if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: cudaGetSymbolAddress");
             g_noalloc_slot[dev].scratch = static_cast<float*>(base);
             g_noalloc_slot[dev].counter = reinterpret_cast<int32_t*>(static_cast<uint32_t*>(base) + NOALLOC_SCRATCH_FLOATS);
+            g_noalloc_slot[dev].ctx_id = ctx_id;
             g_noalloc_slot[dev].ready = true;
         }
         slot = g_noalloc_slot[dev];
     }
+    rc = router_args(x, w, rows, hidden, experts, topk, topk_weights, topk_ids, logits, slot.scratch,
+                     NOALLOC_SCRATCH_FLOATS, slot.counter);
+    if (rc != QF_OK) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     e = cudaMemsetAsync(slot.counter, 0, sizeof(int32_t), st);
     if (e != cudaSuccess) return qf::cuda_status(e, "router_topk_noalloc: clearing the counter");
