@@ -37,10 +37,17 @@ enum {
 #define QF_MAX_EXPERTS 1024
 
 /* MoE control block: int32[QF_MOE_CTRL_WORDS], zeroed once by the caller, re-armed by the kernel itself.
- * Word QF_MOE_CTRL_ERR is sticky: non-zero after a launch means a bounded wait ran out or a routed expert id was
- * out of range (QF_MOE_ERR_* bits); the caller clears it. */
+ * Word QF_MOE_CTRL_ERR is sticky: non-zero after a launch means a bounded wait ran out or a routed expert id was out
+ * of range (QF_MOE_ERR_* bits). After a TIMEOUT or PIPELINE error the caller must zero the control block (except
+ * the mirror words below) AND the pbuf workspace again before the next launch: pbuf holds counters that an
+ * interrupted launch leaves behind. BAD_EXPERT leaves the workspace consistent.
+ * Words QF_MOE_CTRL_MIRROR, +1: optional 64-bit device-visible address (low word first) of a uint32 in mapped pinned
+ * host memory; when it is non-zero, every launch that ends with a non-zero (sticky, so accumulated) error word stores
+ * the word there, so a host can poll for kernel errors without synchronising. The kernel's re-arm keeps these two
+ * words. */
 #define QF_MOE_CTRL_WORDS 2048
 #define QF_MOE_CTRL_ERR 3
+#define QF_MOE_CTRL_MIRROR 2046
 /* Size of the optional MoE timeline buffer (int64 entries). */
 #define QF_MOE_DBG_NUMEL (32 * 512)
 #define QF_MOE_ERR_TIMEOUT 0x1
@@ -68,8 +75,10 @@ int qf_router_topk(const void* x, const void* w, int rows, int hidden, int exper
  * inference engine's plugin enqueue, whose device memory is fixed at start-up, or a launcher running during CUDA-graph
  * capture cannot hand over scratch tensors: this variant keeps the fp32 logit scratch and the ticket counter in a
  * static device array of the library (rows * experts <= 64 * 1024, i.e. 256 KB per GPU, held until exit) and calls no
- * allocator. The first call on a device (device current) resolves that array's address -- make it before any stream
- * capture. Each call clears the counter on `stream`; calls that may overlap on the GPU share the array and race. */
+ * allocator. The first call in a CUDA context (the device's primary context, or one the host made current) resolves
+ * that array's address in that context -- make it before any stream capture; a later call in another context (after
+ * cudaDeviceReset, say) resolves it again. Each call checks its arguments before enqueueing anything, then clears the
+ * counter on `stream`; calls that may overlap on the GPU share the array and race. */
 int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, int experts, int topk, int renormalize,
                            float* topk_weights, int32_t* topk_ids, void* logits, int pdl, qf_stream_t stream);
 

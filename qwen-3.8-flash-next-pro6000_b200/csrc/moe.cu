@@ -94,7 +94,7 @@ enum : int {
     C_SPLIT = 80,   // [64] split-K arrivals per (shared tile, token group)
     C_DONE = 160,   // [QF_MAX_EXPERTS] finished gate_up items per unique expert
 };
-static_assert(C_DONE + QF_MAX_EXPERTS <= QF_MOE_CTRL_WORDS, "ctrl layout");
+static_assert(C_DONE + QF_MAX_EXPERTS <= QF_MOE_CTRL_MIRROR, "ctrl layout");
 
 enum : int { K_STOP = 0, K_GL, K_S1, K_G1, K_S1F, K_S2, K_G2, K_CB };
 
@@ -1275,8 +1275,16 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     __syncthreads();
     if (misc[MISC_FLAG]) {
         __threadfence();
-        for (int i = tid; i < QF_MOE_CTRL_WORDS; i += MOE_THREADS)
+        for (int i = tid; i < QF_MOE_CTRL_MIRROR; i += MOE_THREADS)
             if (i != C_ERR) ctrl[i] = 0u;
+        if (tid == 0) {   // the sticky error word, copied to the caller's host-mapped mirror word (if any)
+            const uint32_t err = qf::ld_volatile(ctrl + C_ERR);
+            const uint64_t mirror = (uint64_t)ctrl[QF_MOE_CTRL_MIRROR] | ((uint64_t)ctrl[QF_MOE_CTRL_MIRROR + 1] << 32);
+            if (err != 0u && mirror != 0ull) {
+                *reinterpret_cast<volatile uint32_t*>(mirror) = err;
+                __threadfence_system();
+            }
+        }
     }
 }
 

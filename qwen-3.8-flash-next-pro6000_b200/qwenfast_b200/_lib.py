@@ -14,6 +14,7 @@ QF_MAX_TOPK = 16
 QF_MAX_EXPERTS = 1024
 QF_MOE_CTRL_WORDS = 2048
 QF_MOE_CTRL_ERR = 3
+QF_MOE_CTRL_MIRROR = 2046
 QF_MOE_ERR_TIMEOUT = 0x1
 QF_MOE_ERR_BAD_EXPERT = 0x2
 QF_MOE_ERR_PIPELINE = 0x4

@@ -118,13 +118,21 @@ def shared_w8_as_bf16(sq1, ss1, sq2, ss2, H: int, op: str = "a16_moe_decode"):
     return tensor_cache(_W8_SHARED, (sq1, ss1, sq2, ss2), build)
 
 
+# control block -> (its pinned host mirror of the sticky error word, the pbuf it is used with): see moe_workspace
+_MOE_MIRRORS = {}
+
+
 def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
-    """Caller-owned scratch for ``a16_moe_decode`` (the reference's ``_a16_bufs``, qwenfast.py:1044-1059)."""
+    """Caller-owned scratch for ``a16_moe_decode`` (the reference's ``_a16_bufs``, qwenfast.py:1044-1059).
+
+    The control block gets a host mirror of its sticky error word (``err_host``, pinned host memory whose address
+    sits in ctrl words QF_MOE_CTRL_MIRROR..+1): every launch that ends with an error copies the word there, and the
+    ops read it before their next launch on this workspace without synchronising (``check_moe_error``)."""
     lib = _lib.load()
     v = [ctypes.c_int64() for _ in range(6)]
     _lib.check(lib.qf_a16_moe_workspace(M, H, I, topk, Is, *[ctypes.byref(a) for a in v]), "moe_workspace")
     hb, yb, gl, ctrl, pb, sh = (a.value for a in v)
-    return dict(
+    bufs = dict(
         hbuf=torch.empty(hb // 2, dtype=BF16, device=device),
         ybuf=torch.empty(yb // 2, dtype=BF16, device=device),
         gl=torch.empty(gl, dtype=torch.float32, device=device),
@@ -132,7 +140,43 @@ def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
         pbuf=torch.zeros(max(pb, 1), dtype=torch.float32, device=device),   # holds counters: zeroed once
         shbuf=torch.empty(max(sh // 2, 1), dtype=BF16, device=device),
         none=torch.empty(0, dtype=BF16, device=device),
+        err_host=torch.zeros(1, dtype=torch.int32, pin_memory=True),
     )
+    attach_error_mirror(bufs["ctrl"], bufs["err_host"], bufs["pbuf"])
+    return bufs
+
+
+def attach_error_mirror(ctrl: torch.Tensor, err_host: torch.Tensor, pbuf: torch.Tensor):
+    """Point the control block's mirror words at ``err_host`` (pinned int32 [1]; under unified addressing its host
+    address is also its device address) and remember the pair, so that the ops check it before each launch."""
+    _req(err_host.dtype == torch.int32 and err_host.is_pinned() and err_host.numel() >= 1,
+         "attach_error_mirror: err_host must be a pinned int32 host tensor")
+    _req(ctrl.dtype == torch.int32 and ctrl.numel() >= _lib.QF_MOE_CTRL_WORDS and ctrl.is_contiguous(),
+         "attach_error_mirror: ctrl must be a contiguous int32 control block")
+    ctrl.view(torch.int64)[_lib.QF_MOE_CTRL_MIRROR // 2] = err_host.data_ptr()
+    key = ctrl.data_ptr()
+    _MOE_MIRRORS[key] = (weakref.ref(ctrl), err_host, pbuf)
+    weakref.finalize(ctrl, _MOE_MIRRORS.pop, key, None)
+
+
+def check_moe_error(ctrl: torch.Tensor):
+    """Raise RuntimeError when an earlier launch on this control block reported an error through its host mirror (a
+    plain read of pinned host memory: no synchronisation). Before raising, the workspace is made usable again on the
+    current stream: the control block (except its mirror words) and pbuf are zeroed, as a hard error requires."""
+    ent = _MOE_MIRRORS.get(ctrl.data_ptr())
+    if ent is None or ent[0]() is not ctrl:
+        return
+    err = int(ent[1][0])
+    if err == 0:
+        return
+    ctrl[: _lib.QF_MOE_CTRL_MIRROR].zero_()
+    ent[2].zero_()
+    ent[1].zero_()
+    names = [n for b, n in ((_lib.QF_MOE_ERR_TIMEOUT, "a bounded wait ran out"),
+                            (_lib.QF_MOE_ERR_BAD_EXPERT, "a routed expert id was out of range"),
+                            (_lib.QF_MOE_ERR_PIPELINE, "a pipeline wait ran out")) if err & b]
+    raise RuntimeError(f"a16_moe_decode: an earlier launch on this workspace reported error {err:#x} "
+                       f"({'; '.join(names)}); its outputs were undefined, the workspace has been reset")
 
 
 def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, shared, hbuf, ybuf, gl, ctrl, out,
@@ -165,6 +209,7 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
     w13 / w2 the e2m1 codes (int32, int4 kernel layout), s13 / s2 the E4M3 group-16 scales (uint8 [E, N*K/16]),
     gs13 / gs2 the per-expert multipliers 1 / g (C ABI ``qf_a16_moe_decode_nvfp4``; routing given, not fused)."""
     op = "a16_moe_decode" if router_w is None else "moe_layer_decode"
+    check_moe_error(ctrl)
     if x_stage is None:
         _cuda(x, "x", op)
         dev = x.device
@@ -282,6 +327,17 @@ def moe_combine(ybuf: torch.Tensor, x: torch.Tensor, w_gate: Optional[torch.Tens
 def moe_error_word(ctrl: torch.Tensor) -> int:
     """The sticky error word of a MoE control block (reads the device; synchronises)."""
     return int(ctrl[_lib.QF_MOE_CTRL_ERR].item())
+
+
+def clear_moe_error(ctrl: torch.Tensor, pbuf: Optional[torch.Tensor] = None):
+    """Zero the sticky error word (and, after a hard error, pbuf) and the host mirror of this control block."""
+    ctrl[_lib.QF_MOE_CTRL_ERR] = 0
+    if pbuf is not None:
+        pbuf.zero_()
+    ent = _MOE_MIRRORS.get(ctrl.data_ptr())
+    if ent is not None and ent[0]() is ctrl:
+        torch.cuda.synchronize(ctrl.device)
+        ent[1].zero_()
 
 
 @dataclass

@@ -11,6 +11,8 @@ import os
 import pytest
 import torch
 
+from qwenfast_b200._lib import QF_MOE_CTRL_MIRROR
+
 from conftest import GOLDEN
 from oracle import moe_ref
 from qwenfast_b200 import formats, ops, synthetic
@@ -73,7 +75,7 @@ def test_config0_against_golden(cuda):
     out = run_moe(x.to(cuda), gold["ids"].to(cuda), gold["weights"].to(cuda), lw, bufs)
     torch.cuda.synchronize()
     assert_close_to_oracle(out, gold["out_rounded"], gold["out_truth"])
-    assert int(bufs["ctrl"].abs().sum().item()) == 0
+    assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
 
 
 def test_config0_layer_step(cuda):
@@ -105,7 +107,7 @@ def test_config1_full_layer(cfg1, cuda):
     tru = moe_ref.moe_truth(xs, i_c, w_c, C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
                             shared_w=(C["sh_gu"], C["sh_d"]))
     assert_close_to_oracle(out, ref, tru)
-    assert int(bufs["ctrl"].abs().sum().item()) == 0
+    assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
 
 
 def test_config1_precomputed_shared(cfg1, cuda):
@@ -149,7 +151,7 @@ def test_batch_invariance_and_back_to_back(cfg1, cuda):
     oracle = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"],
                                  w_gate=C["w_gate"], shared_w=(C["sh_gu"], C["sh_d"]))
     assert_close_to_oracle(single, oracle)
-    assert int(bufs["ctrl"].abs().sum().item()) == 0
+    assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
 
 
 def gate_up_split(M, I, topk):
@@ -186,7 +188,7 @@ def test_odd_shared_shape_and_workspace_reuse(cuda, M):
     assert torch.equal(again, out)
     if gate_up_split(M, cfg.I, cfg.topk) == gate_up_split(1, cfg.I, cfg.topk):
         assert torch.equal(single, out)
-    assert int(bufs["ctrl"].abs().sum().item()) == 0
+    assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
 
 
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 16, 32, 64])
@@ -249,10 +251,16 @@ def test_duplicate_and_out_of_range_ids(cuda):
     out2 = run_moe(x, bad.to(cuda), w.to(cuda), lw, bufs)
     torch.cuda.synchronize()
     assert ops.moe_error_word(bufs["ctrl"]) & 0x2
+    assert int(bufs["err_host"][0]) & 0x2          # the host mirror saw it without another synchronisation
     assert torch.isfinite(out2.float()).all()
     ok_rows = [0, 2, 3]
     assert torch.equal(out2[ok_rows].cpu(), out[ok_rows].cpu())
-    bufs["ctrl"].zero_()
+    # the next call on this workspace raises (and resets the workspace) instead of launching
+    with pytest.raises(RuntimeError, match="out of range"):
+        run_moe(x, ids.to(cuda), w.to(cuda), lw, bufs)
+    out3 = run_moe(x, ids.to(cuda), w.to(cuda), lw, bufs)
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) == 0 and torch.equal(out3.cpu(), out.cpu())
 
 
 def test_repack_kernels_match_host_layout(cuda):
@@ -344,8 +352,10 @@ def test_bounded_wait_runs_out_and_is_reported(cfg1, cuda):
     elapsed = time.time() - t0
     assert ops.moe_error_word(bufs["ctrl"]) & _lib.QF_MOE_ERR_TIMEOUT
     assert 0.2 < elapsed < 30, elapsed
-    bufs["ctrl"].zero_()
-    bufs["pbuf"].zero_()
+    assert int(bufs["err_host"][0]) & _lib.QF_MOE_ERR_TIMEOUT
+    # the op reports the earlier launch's error before its next launch and resets the control block and pbuf
+    with pytest.raises(RuntimeError, match="bounded wait ran out"):
+        run_moe(x, ids, w, lw, bufs)
     out = run_moe(x, ids, w, lw, bufs)
     torch.cuda.synchronize()
     assert ops.moe_error_word(bufs["ctrl"]) == 0
