@@ -182,14 +182,27 @@ int qf_bf16_repack(const void* w, void* wk, int N, int K, int gated, qf_stream_t
 int qf_bf16_unpack(const void* wk, void* w, int N, int K, int gated, qf_stream_t stream);
 
 /* ------------------------------------------------------------------------------------------------------------
- * W8A16 group-scaled INT8 GEMM: y[M, N] = x[M, K] @ (q * s)^T, fp32 accumulation, bf16 out.
+ * W8A16 group-scaled INT8 GEMM: y[M, N] = x[M, K] @ (q * s)^T, fp32 accumulation, bf16 out (tcgen05 tensor cores).
  * Replaces `w8g_gemm` (serve/qwenfast/qf_w8g.cu:303-336, binding serve/qwenfast/qf_bind.cpp:42,133);
- *   x bf16 [M, K] row stride ldx (ldx % 8 == 0, 16-byte aligned); q int8 [N, K]; s bf16 [N, K/group];
- *   y bf16 [M, N] row stride ldy. M 1..QF_MAX_TOKENS, K % 128 == 0, group 128 (or 64).
- *   rpw: accepted for signature parity (row-per-warp hint of the reference); the bits 0x100 / 0x200 are ignored.
+ *   x bf16 [M, K] row stride ldx (ldx % 8 == 0, 16-byte aligned); q int8 [N, K] canonical row-major (16-byte
+ *   aligned); s bf16 [N, K/group]; y bf16 [M, N] row stride ldy. M 1..QF_MAX_TOKENS, N % 128 == 0, K % 64 == 0,
+ *   group 128 or 64. Every product is exact (int8 weights and tokens scaled by a power of two as fp16) and the sums
+ *   are fp32; the result does not depend on timing.
+ *   fix: caller-owned float buffer of qf_w8g_fixup_elems(N) elements, zero-filled before its first use; every call
+ *   leaves its counters zero again (after a non-zero qf_w8g_take_status, zero it again). Calls that may run
+ *   concurrently need their own. The launch is cooperative (every CTA resident), with programmatic dependent launch
+ *   when pdl != 0.
+ *   rpw: accepted for signature parity. The reference's rows-per-warp value and its 0x100 / 0x200 bits choose between
+ *   its SM120 CUDA-core and mma.sync kernels; this build has one tcgen05 kernel and ignores them.
  * ------------------------------------------------------------------------------------------------------------ */
 int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const void* s, void* y, int64_t ldy, int M, int N,
-                int K, int group, int rpw, int pdl, qf_stream_t stream);
+                int K, int group, int rpw, float* fix, int64_t fix_elems, int pdl, qf_stream_t stream);
+/* Elements (float) of the W8A16 fixup buffer for an N-row weight on the current device. */
+int qf_w8g_fixup_elems(int N, int64_t* elems);
+/* Sticky device status of the W8A16 kernel since the last call (synchronises the device, then clears it): 0 = every
+ * bounded wait completed; bit 0 = a weight-ring wait ran out, bit 1 = a unit (operand / accumulator) wait, bit 2 =
+ * the final tensor-core wait, bit 3 = the wait for the other runs of a split tile (the outputs are then undefined). */
+int qf_w8g_take_status(uint32_t* status);
 /* w bf16 [rows, K] = bf16(q * s). Replaces `w8g_unpack` (serve/qwenfast/qf_w8g.cu:338-351). */
 int qf_w8g_unpack(const int8_t* q, const void* s, void* w, int64_t rows, int K, int group, qf_stream_t stream);
 

@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "qwenfast_b200.h"
 
@@ -306,6 +307,16 @@ __device__ __forceinline__ void biased_w4(uint32_t q, uint32_t* p) {
         const uint32_t s = q >> (4 * i);
         asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(p[i]) : "r"(s), "r"(MASK), "r"(MAGIC));
     }
+}
+// Instruction descriptor kind::f16 with fp16 A and B (K-major), fp32 D, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// bf16 pair -> fp16 pair of the values times `mul` (a power of two); exact when the products are fp16 values.
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2_scaled(uint32_t v, float mul) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(__uint_as_float(v & 0xFFFF0000u) * mul), "f"(__uint_as_float(v << 16) * mul));
+    return r;
 }
 // int4 word -> four bf16x2 of the signed codes code - 8 (lop3 to 128 + code, then one bf16x2 subtract; exact).
 __device__ __forceinline__ void signed_w4(uint32_t q, uint32_t* p) {

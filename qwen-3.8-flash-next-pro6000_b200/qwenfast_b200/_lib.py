@@ -43,7 +43,9 @@ SIGNATURES = {
     "qf_w4_unpack": [_p, _p, _p, _p, _i, _i, _i, _i, _p],
     "qf_bf16_repack": [_p, _p, _i, _i, _i, _p],
     "qf_bf16_unpack": [_p, _p, _i, _i, _i, _p],
-    "qf_w8g_gemm": [_p, _l, _p, _p, _p, _l, _i, _i, _i, _i, _i, _i, _p],
+    "qf_w8g_gemm": [_p, _l, _p, _p, _p, _l, _i, _i, _i, _i, _i, _p, _l, _i, _p],
+    "qf_w8g_fixup_elems": [_i, _p],
+    "qf_w8g_take_status": [_p],
     "qf_w8g_unpack": [_p, _p, _p, _l, _i, _i, _p],
     "qf_w8a8_gemm": [_p, _l, _p, _p, _p, _l, _i, _i, _i, _p, _p, _p, _p, _i, _p],
     "qf_w8_repack": [_p, _p, _i, _i, _p],

@@ -399,8 +399,31 @@ def moe_layer_step(x: torch.Tensor, lw: MoELayerWeights, topk: int, bufs: dict, 
 
 
 # ------------------------------------------------------------------------------------------------- INT8
-def w8g_gemm(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, rpw: int = 0, pdl: bool = False) -> torch.Tensor:
-    """y = x @ (q * s)^T (W8A16, group-scaled int8). Mirrors ``w8g_gemm`` (serve/qwenfast/qf_w8g.cu:303-336)."""
+_W8G_FIXUP = {}
+
+
+def w8g_fixup(N: int, device, stream=None) -> torch.Tensor:
+    """The W8A16 GEMM's fixup buffer (split-tile partial sums and zero-kept counters) for an N-row weight, one per
+    (device, stream, N); the first call allocates (make it before any CUDA-graph capture)."""
+    dev = torch.device(device)
+    st = (stream or torch.cuda.current_stream(dev)).cuda_stream
+    key = (dev.index, st, N)
+    buf = _W8G_FIXUP.get(key)
+    if buf is None:
+        n = ctypes.c_int64(0)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().qf_w8g_fixup_elems(N, ctypes.byref(n)), "w8g_fixup_elems")
+        buf = _W8G_FIXUP[key] = torch.zeros(n.value, dtype=torch.float32, device=dev)
+    return buf
+
+
+def w8g_gemm(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, rpw: int = 0, pdl: bool = False,
+             fixup: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ (q * s)^T (W8A16, group-scaled int8) on the tensor cores. Mirrors ``w8g_gemm``
+    (serve/qwenfast/qf_w8g.cu:303-336): x bf16 [M, K] (unit column stride, row stride % 8 == 0), q int8 [N, K] as
+    stored (canonical), s bf16 [N, K/group], group 128 or 64; returns y bf16 [M, N]. ``rpw`` is accepted for signature
+    parity (it selects among the reference's SM120 kernels). ``fixup``: the split-tile buffer (``w8g_fixup``; the
+    current stream's by default)."""
     op = "w8g_gemm"
     _cuda(x, "x", op)
     _req(q.is_cuda and s.is_cuda and x.dtype == BF16, f"{op}: x bf16, q, s on CUDA")
@@ -412,11 +435,25 @@ def w8g_gemm(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, rpw: int = 0, pd
     M, K = x.shape
     N = q.shape[0]
     group = K // s.shape[1]
+    if fixup is None:
+        fixup = w8g_fixup(N, x.device)
     y = torch.empty(M, N, dtype=BF16, device=x.device)
     with torch.cuda.device(x.device):
         _lib.check(_lib.load().qf_w8g_gemm(x.data_ptr(), x.stride(0), q.data_ptr(), s.data_ptr(), y.data_ptr(), N, M,
-                                           N, K, group, int(rpw), int(bool(pdl)), _stream(x.device)), op)
+                                           N, K, group, int(rpw), fixup.data_ptr(), fixup.numel(), int(bool(pdl)),
+                                           _stream(x.device)), op)
     return y
+
+
+def w8g_take_status() -> int:
+    """Sticky wait-timeout bits of the W8A16 kernel since the last call (0 = clean); clears them. After a non-zero
+    status the fixup buffers may hold partial counts, so the cached ones are zeroed again."""
+    v = ctypes.c_uint32(0)
+    _lib.check(_lib.load().qf_w8g_take_status(ctypes.byref(v)), "w8g_take_status")
+    if v.value:
+        for buf in _W8G_FIXUP.values():
+            buf.zero_()
+    return v.value
 
 
 def w8g_unpack(q: torch.Tensor, s: torch.Tensor, w: torch.Tensor):

@@ -4,7 +4,7 @@ scratch caches, and the calls themselves. Same function names, argument meaning 
 reference; the shape gates follow this build's limits and weight formats instead of the reference's fixed model
 (H = 2560, M <= 8, NVFP4 / Marlin experts):
 
-* ``w8_quant`` / ``_w8_rpw`` / ``w8_linear`` -- the INT8 (W8A16, group-scaled) dense projections
+* ``w8_quant`` / ``w8_linear`` -- the INT8 (W8A16, group-scaled) dense projections
   (qwenfast.py:301-315, 331-334, 337-360). A call the kernel does not take (bias, more than 64 rows, unsupported
   K or layout, torch.compile tracing) declines to the reference's own fallback: the weight rows are unpacked on the
   device into bf16 (``w8g_unpack``) and multiplied with ``torch.nn.functional.linear``.
@@ -50,15 +50,10 @@ def w8_quant(w: torch.Tensor, rows_per_chunk: int = 8192) -> dict:
     return dict(kind="w8", q=q, s=sc, shape=(N, K), G=G)
 
 
-def _w8_rpw(M: int, K: int) -> int:
-    """Rows-per-warp hint of the reference's w8g kernel (qwenfast.py:331-334). The sm_100a kernel takes and ignores
-    it (its tiling is fixed); kept so that callers pass the same arguments."""
-    return 4 if M > 4 and K == 2560 else 2
-
-
 def w8_route(entry, x: torch.Tensor, bias=None) -> Optional[str]:
     """None when ``w8_linear`` runs the kernel for this call, else the first failing condition (the decline path's
-    reason): the gate of qwenfast.py:346-349 with this build's limits (M <= 64 rows, K % 64 == 0, G 128 or 64)."""
+    reason): the gate of qwenfast.py:346-349 with this build's limits (M <= 64 rows, output rows a multiple of 128,
+    K % 64 == 0, G 128 or 64)."""
     p, r0, r1 = entry
     N, K = p["shape"]
     x2 = x.reshape(-1, K)
@@ -66,6 +61,7 @@ def w8_route(entry, x: torch.Tensor, bias=None) -> Optional[str]:
     checks = (
         ("bias", bias is None),
         ("rows", 1 <= M <= _lib.QF_MAX_TOKENS),
+        ("shape", (r1 - r0) % 128 == 0),
         ("group", p["G"] in (64, 128) and K % 64 == 0 and K % p["G"] == 0),
         ("dtype", x2.dtype == BF16),
         ("layout", x2.stride(1) == 1 and x2.stride(0) % 8 == 0 and x2.data_ptr() % 16 == 0),
@@ -104,7 +100,7 @@ def w8_linear(entry, x: torch.Tensor, bias: Optional[torch.Tensor] = None) -> to
         return x.new_empty((*shp[:-1], n_out))
     if w8_route(entry, x, bias) is None:
         q, s = (p["q"], p["s"]) if (r0 == 0 and r1 == N) else (p["q"][r0:r1], p["s"][r0:r1])
-        y = ops.w8g_gemm(x2, q, s, _w8_rpw(x2.shape[0], K))
+        y = ops.w8g_gemm(x2, q, s, 0)
         return y.view(*shp[:-1], n_out)
     w = _w8_unpack_rows(p, r0, r1)
     return torch.nn.functional.linear(x2, w, bias).view(*shp[:-1], n_out)

@@ -23,11 +23,6 @@ def test_w8_quant_matches_reference_function():
         assert torch.equal(p["q"], r["q"]) and torch.equal(p["s"], r["s"]), tag
 
 
-def test_w8_rpw_hint():
-    assert [overlay._w8_rpw(M, 2560) for M in (1, 4, 5, 8)] == [2, 2, 4, 4]
-    assert overlay._w8_rpw(8, 6144) == 2 and overlay._w8_rpw(8, 640) == 2
-
-
 def _w8_entry(N=256, K=256):
     w = (torch.randn(N, K, generator=torch.Generator().manual_seed(0)) * 0.02).to(BF)
     return (overlay.w8_quant(w), 0, N)
@@ -44,6 +39,7 @@ def test_w8_route_gate_reasons():
     e64 = (overlay.w8_quant(torch.randn(128, 192).to(BF)), 0, 128)
     assert e64[0]["G"] == 64 and overlay.w8_route(e64, torch.randn(3, 192).to(BF)) == "device"
     assert overlay.w8_route(e, x) == "device"                                 # CPU tensors never reach the kernel
+    assert overlay.w8_route((e[0], 0, 200), x) == "shape"                     # output rows not a multiple of 128
 
 
 def test_w8_linear_empty_rows():
