@@ -43,10 +43,13 @@ def parse():
     ap.add_argument("--steps", type=int, default=480)
     ap.add_argument("--warmup", type=int, default=48)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--M", type=int, default=10)
+    ap.add_argument("--M", type=int, default=0, help="tokens per layer-step (default: the config's: 10, or 64 for config 4)")
+    ap.add_argument("--config", type=int, default=0,
+                    help="1 or 4 (default: config 1 on one GPU, config 4 -- expert parallel, M=64, seed 7 -- on more)")
     ap.add_argument("--layers", type=int, default=16)
     ap.add_argument("--zipf", type=float, default=0.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config4", action="store_true", help="skip the one-GPU config-4 record of the N=1 line")
     ap.add_argument("--sweep", default="")
     ap.add_argument("--sweep-configs", default="2,3",
                     help="which sweep records to take (comma list of 2, 3, nvfp4)")
@@ -174,17 +177,20 @@ def time_cpu(cfg, M, steps, warmup, budget_s):
 
 
 def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
     from qwenfast_b200 import synthetic
-    cfg = synthetic.CONFIGS[1]
-    us, n, cores = time_cpu(cfg, args.M, args.steps, 4, budget_s=150.0)
+    cfg_id = args.config or (4 if world > 1 else 1)
+    cfg = synthetic.CONFIGS[cfg_id]
+    M = args.M or cfg.M
+    us, n, cores = time_cpu(cfg, M, args.steps, 4, budget_s=150.0)
     line = {"impl": "reference", "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
             "warmup": 4, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16/int4 (fp32 accumulate)", "data": "synthetic",
-            "config": {"workload": f"config1 MoE layer-step M={args.M} (CPU oracle port of the reference torch path)",
-                       "H": cfg.H, "E": cfg.E, "I": cfg.I, "topk": cfg.topk, "Is": cfg.Is, "M": args.M},
+            "config": {"workload": f"config{cfg_id} MoE layer-step M={M} (CPU oracle port of the reference torch path)",
+                       "config_id": cfg_id, "H": cfg.H, "E": cfg.E, "I": cfg.I, "topk": cfg.topk, "Is": cfg.Is,
+                       "M": M},
             "cpu_baseline": {"value": us, "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": f"{n} layer-steps (router + routed experts + shared) on the host"},
             "e2e": {"value": us, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -192,13 +198,13 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------------------------------------ GPU arm
-def build_layers(cfg, nl, dev, zipf=0.0):
+def build_layers(cfg, nl, dev, zipf=0.0, seed_base=1000):
     import torch
     from qwenfast_b200 import synthetic
     from qwenfast_b200.ops import MoELayerWeights
     layers = []
     for l in range(nl):
-        L = synthetic.make_moe_layer(cfg, device=dev, seed=1000 + l, zipf_s=zipf)
+        L = synthetic.make_moe_layer(cfg, device=dev, seed=seed_base + l, zipf_s=zipf)
         layers.append(MoELayerWeights.from_canonical(L["router"], L["w13"], L["s13"], L["w2"], L["s2"], L["w_gate"],
                                                      L["sh_gu"], L["sh_d"]))
         del L
@@ -206,34 +212,32 @@ def build_layers(cfg, nl, dev, zipf=0.0):
     return layers
 
 
-def run_ours(args):
+def workload_seeds(cfg_id):
+    """(weight seed base, token seed base) of a bench workload: config 1 layers 1000 + l, config 4 (seed 7) 7000 + l
+    and tokens 7100 + l -- one synthetic layer per slot of the cycled graph."""
+    return (1000, 1000) if cfg_id == 1 else (7000, 7100)
+
+
+def measure(cfg, cfg_id, M, NL, dev, args, rank, world, epar, zipf=0.0, timed_clocks=False, host_e2e=True):
+    """One workload: NL synthetic layers cycled in CUDA graphs so that every step streams its experts from HBM.
+    Times exactly args.steps layer-steps (reps of the NL-layer graph plus one graph of the remainder) after at least
+    args.warmup untimed ones, then the kernel-only graphs (MoE launch, separate router op, collective) and the end-to-end
+    loop through the public op with host buffers. Every rank runs the same sequence (the graphs hold collectives under
+    expert parallelism). Returns a dict of measurements (rank-max device times)."""
     import torch
     import torch.distributed as dist
-    from qwenfast_b200 import build as qbuild
     from qwenfast_b200 import ep, ops, synthetic
 
-    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    qbuild.build()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
-    cfg = synthetic.CONFIGS[1]
-    M, NL = args.M, args.layers
-    # N > 1: expert parallelism -- the same layers on every rank (same seeds), each rank holding E/N experts of
-    # each, the tokens replicated, one all-reduce of the slot buffer per layer-step (strong scaling of one step)
-    epar = world > 1
-    layers = build_layers(cfg, NL, dev, args.zipf)
+    wseed, tseed = workload_seeds(cfg_id)
+    layers = build_layers(cfg, NL, dev, zipf, wseed)
     shards = [ep.shard_weights(lw, rank, world) for lw in layers] if epar else layers
     lo, hi = ep.shard_range(cfg.E, rank, world)
     bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, cfg.Is, dev)
     rb = ops.router_bufs(dev)
     # independent N(0, 1) tokens per layer (chaining outputs into the next layer would correlate the tokens and
     # shrink the number of distinct experts below the configuration's)
-    xs = [synthetic.make_tokens(cfg, M=M, device=dev, seed=1000 + l) for l in range(NL)]
+    xs = [synthetic.make_tokens(cfg, M=M, device=dev, seed=tseed + l) for l in range(NL)]
     outs = [torch.empty_like(xs[0]) for _ in range(NL)]
-    x0 = xs[0]
 
     def layer_step(x, l, out, pdl=True):
         if epar:
@@ -243,26 +247,30 @@ def run_ours(args):
             _, tw, ids, _ = ops.moe_layer_step(x, layers[l], cfg.topk, bufs, rb, out, pdl=pdl)
         return tw, ids
 
-    def step(l, pdl=True):
-        return layer_step(xs[l], l, outs[l], pdl)
-
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
         for _ in range(2):
             for l in range(NL):
-                step(l)
+                layer_step(xs[l], l, outs[l])
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
     err = ops.moe_error_word(bufs["ctrl"])
     if err:
         raise RuntimeError(f"MoE kernel reported error word {err:#x}")
 
+    steps = max(1, args.steps)
+    rem = steps % NL
     g_full = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_full):
-        tws = [step(l) for l in range(NL)]
+        tws = [layer_step(xs[l], l, outs[l]) for l in range(NL)]
+    g_rem = None
+    if rem:
+        g_rem = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_rem):
+            for l in range(rem):
+                layer_step(xs[l], l, outs[l])
     ids_list = [t[1] for t in tws]
-    tw_list = [t[0] for t in tws]
     # kernel-only graph of the layer-step launches (router inside, no collective or combine): the per-launch time of
     # the roofline's kernel
     r_tw = torch.empty(M, cfg.topk, dtype=torch.float32, device=dev)
@@ -289,57 +297,62 @@ def run_ours(args):
         for l in range(NL):
             ops.router_topk(xs[l], layers[l].router, cfg.topk, True, rb[0], rb[1])
 
-    def timed(graph, reps):
+    def rank_max(v):
+        if world > 1:
+            t = torch.tensor([v], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+        return v
+
+    def timed(fn):
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         ev0.record()
-        for _ in range(reps):
-            graph.replay()
+        fn()
         ev1.record()
         torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return rank_max(ev0.elapsed_time(ev1))
 
-    warm_reps = max(1, math.ceil(max(args.warmup, 3) / NL))
-    reps = max(1, math.ceil(args.steps / NL))
+    reps, warm_reps = steps // NL, max(1, math.ceil(max(args.warmup, 3) / NL))
+
+    def run_steps():
+        for _ in range(reps):
+            g_full.replay()
+        if g_rem is not None:
+            g_rem.replay()
+
     for _ in range(warm_reps):
         g_full.replay()
     torch.cuda.synchronize()
-    # soak ~1 s under the same load first, so clocks settle and the sampler sees the timed regime; every rank
-    # replays the same number of times (the graph holds collectives under expert parallelism)
-    t0 = time.perf_counter()
-    g_full.replay()
-    torch.cuda.synchronize()
-    dt = torch.tensor([time.perf_counter() - t0], device=dev)
-    if world > 1:
-        dist.all_reduce(dt, op=dist.ReduceOp.MAX)
-    n_soak = max(1, min(2000, math.ceil(1.0 / max(float(dt.item()), 1e-6))))
-    with ClockSampler(local) as clk:
-        for i in range(n_soak):
-            g_full.replay()
-            if i % 8 == 7:
-                torch.cuda.synchronize()
+    clk = None
+    if timed_clocks:
+        # soak ~1 s under the same load first, so clocks settle and the sampler sees the timed regime; every rank
+        # replays the same number of times
+        t0 = time.perf_counter()
+        g_full.replay()
         torch.cuda.synchronize()
-        ms_full = timed(g_full, reps)
-    steps = reps * NL
+        n_soak = max(1, min(2000, math.ceil(1.0 / max(rank_max(time.perf_counter() - t0), 1e-6))))
+        with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as sampler:
+            for i in range(n_soak):
+                g_full.replay()
+                if i % 8 == 7:
+                    torch.cuda.synchronize()
+            torch.cuda.synchronize()
+            ms_full = timed(run_steps)
+        clk = sampler.summary()
+    else:
+        ms_full = timed(run_steps)
     us_step = ms_full * 1e3 / steps
-    for _ in range(warm_reps):
-        g_moe.replay()
-    us_moe = timed(g_moe, reps) * 1e3 / steps
-    for _ in range(warm_reps):
-        g_router.replay()
-    us_router = timed(g_router, reps) * 1e3 / steps
-    us_coll = None
-    if g_coll is not None:
+    res = dict(us_step=us_step, steps=steps, warmup_run=warm_reps * NL + (NL if timed_clocks else 0), clocks=clk)
+    for name, g in (("us_moe", g_moe), ("us_router", g_router), ("us_coll", g_coll)):
+        if g is None:
+            res[name] = None
+            continue
         for _ in range(warm_reps):
-            g_coll.replay()
-        us_coll = timed(g_coll, reps) * 1e3 / steps
+            g.replay()
+        res[name] = timed(lambda: [g.replay() for _ in range(max(1, reps))]) * 1e3 / (NL * max(1, reps))
     torch.cuda.synchronize()
     err = ops.moe_error_word(bufs["ctrl"])
     if err:
@@ -355,95 +368,126 @@ def run_ours(args):
     moe_b = [u * per_e + shared_b + act_b for u in U]
     loc_b = [u * per_e + (shared_b if rank == 0 else 0) + act_b for u in U_loc]
     router_b = cfg.E * cfg.H * 2 + M * cfg.H * 2
-    step_b = statistics.mean(moe_b) + router_b
+    res.update(U=U, moe_b=moe_b, step_b=statistics.mean(moe_b) + router_b,
+               launch_b=statistics.mean(loc_b) + router_b)
+
+    if host_e2e:
+        # end to end through the public ops: pinned host x in, result out, every step. One GPU: the fused layer-step
+        # reads x from pinned host memory itself (staged to device memory inside the launch) and writes out to pinned
+        # host memory; expert parallelism: copy-engine transfers around the step.
+        xh = xs[0].cpu().pin_memory()
+        oh = torch.empty_like(xh).pin_memory()
+        xd = torch.empty_like(xs[0])
+        od = torch.empty_like(xs[0])
+
+        def e2e_step(l):
+            if epar:
+                xd.copy_(xh, non_blocking=True)
+                layer_step(xd, l, od)
+                oh.copy_(od, non_blocking=True)
+            else:
+                ops.moe_layer_step(xh, layers[l], cfg.topk, bufs, rb, oh, x_stage=xd)
+
+        for l in range(NL):
+            e2e_step(l)
+        torch.cuda.synchronize()
+        n_e2e = min(steps, 4 * NL)
+        res["e2e_us"] = timed(lambda: [e2e_step(i % NL) for i in range(n_e2e)]) * 1e3 / n_e2e
+        res["e2e_steps"] = n_e2e
+    del g_full, g_rem, g_moe, g_router, g_coll
+    return res
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from qwenfast_b200 import build as qbuild
+    from qwenfast_b200 import synthetic
+
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    qbuild.build()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    # config 1 (M = 10) is the one-GPU headline; the expert-parallel runs measure config 4 (M = 64 replicated, seed 7,
+    # E / N contiguous experts per rank), whose one-GPU baseline the N = 1 line carries as "config4"
+    cfg_id = args.config or (4 if world > 1 else 1)
+    cfg = synthetic.CONFIGS[cfg_id]
+    M, NL = args.M or cfg.M, args.layers
+    epar = world > 1
+    r = measure(cfg, cfg_id, M, NL, dev, args, rank, world, epar, zipf=args.zipf, timed_clocks=True)
     peak, peak_kind = load_peaks()
-    # the layer-step launch streams its experts, the shared expert (rank 0), the activations and the router weights
-    launch_b = statistics.mean(loc_b) + router_b
-    achieved = launch_b / (us_moe * 1e-6) / 1e9
+    achieved = r["launch_b"] / (r["us_moe"] * 1e-6) / 1e9
     rank_frac = None
     if epar:
-        # per-rank HBM fraction of the local MoE kernel (each rank's own kernel time, not the max)
+        # per-rank HBM fraction of the local MoE kernel
         mine = torch.tensor([achieved / peak], device=dev)
         allf = [torch.zeros_like(mine) for _ in range(world)]
         dist.all_gather(allf, mine)
         rank_frac = [round(float(t.item()), 4) for t in allf]
-
-    # end to end through the public ops: pinned host x in, result out, every step. One GPU: the fused layer-step
-    # reads x from pinned host memory itself (staged to device memory inside the launch) and writes out to pinned
-    # host memory; expert parallelism: copy-engine transfers around the step.
-    xh = x0.cpu().pin_memory()
-    oh = torch.empty_like(xh).pin_memory()
-    xd = torch.empty_like(x0)
-    od = torch.empty_like(x0)
-
-    def e2e_step(l):
-        if epar:
-            xd.copy_(xh, non_blocking=True)
-            layer_step(xd, l, od)
-            oh.copy_(od, non_blocking=True)
-        else:
-            ops.moe_layer_step(xh, layers[l], cfg.topk, bufs, rb, oh, x_stage=xd)
-
-    for l in range(NL):
-        e2e_step(l)
-    torch.cuda.synchronize()
-    n_e2e = min(args.steps, 4 * NL)
-    if world > 1:
-        dist.barrier()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for i in range(n_e2e):
-        e2e_step(i % NL)
-    ev1.record()
-    torch.cuda.synchronize()
-    e2e_ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    us_e2e = e2e_ms * 1e3 / n_e2e
+    c4 = None
+    if world == 1 and cfg_id == 1 and not args.no_config4:
+        cfg4 = synthetic.CONFIGS[4]
+        torch.cuda.empty_cache()
+        r4 = measure(cfg4, 4, cfg4.M, NL, dev, args, rank, world, False, host_e2e=False)
+        c4 = {"workload": "config4 layer-step on one GPU (M=64 replicated tokens, seed 7, all 512 experts): the "
+                          "single-GPU baseline of the expert-parallel scaling runs",
+              "us_per_layer_step": r4["us_step"], "us_moe_kernel": r4["us_moe"],
+              "unique_experts_mean": statistics.mean(r4["U"]),
+              "hbm_frac_moe_kernel": r4["launch_b"] / (r4["us_moe"] * 1e-6) / 1e9 / peak}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         us_cpu, n_cpu, cores = time_cpu(cfg, M, steps=40, warmup=4, budget_s=20.0)
         cpu = {"value": us_cpu, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{n_cpu} config-1 layer-steps (M={M}) of the CPU oracle, torch fp32 on {cores} threads"}
+               "sample": f"{n_cpu} config-{cfg_id} layer-steps (M={M}) of the CPU oracle, torch fp32 on {cores} threads"}
 
     if rank == 0:
+        traffic = load_traffic("moe_persistent_kernel")
+        if cfg_id == 1:
+            wl = (f"config1 decode MoE layer-step (router top-10 + 512-expert W4A16 + bf16 shared expert + combine), "
+                  f"M={M}")
+        else:
+            wl = (f"config4 decode MoE layer-step (M={M} tokens replicated, seed 7), expert-parallel over {world} GPUs "
+                  f"({cfg.E // world} contiguous experts each, NCCL all-reduce of the slot buffer, then the combine)"
+                  if epar else f"config4 decode MoE layer-step (M={M} tokens, seed 7) on one GPU")
         line = {
-            "metric": METRIC, "value": us_step, "unit": UNIT, "n_gpus": world, "steps": steps, "warmup": warm_reps * NL,
-            "ms_per_step": us_step / 1e3, "higher_is_better": False, "scaling": "strong" if epar else "weak",
+            "metric": METRIC, "value": r["us_step"], "unit": UNIT, "n_gpus": world, "steps": r["steps"],
+            "warmup": args.warmup, "warmup_run": r["warmup_run"],
+            "ms_per_step": r["us_step"] / 1e3, "higher_is_better": False, "scaling": "strong" if epar else "weak",
             "vs_baseline": None,
             "dtype": "bf16 activations, int4 experts, fp32 accumulate", "data": "synthetic",
-            "config": {"workload": f"config1 decode MoE layer-step (router top-10 + 512-expert W4A16 + bf16 shared "
-                                   f"expert + combine), M={M}" + (f", expert-parallel over {world} GPUs "
-                                                                  f"({cfg.E // world} experts each, NCCL all-reduce "
-                                                                  f"of the slot buffer)" if epar else ""),
+            "config": {"workload": wl, "config_id": cfg_id,
                        "H": cfg.H, "E": cfg.E, "I": cfg.I, "topk": cfg.topk, "Is": cfg.Is, "M": M,
                        "layers_cycled": NL, "zipf_s": args.zipf,
-                       "l2": f"weights cycled over {NL} layers (~{statistics.mean(moe_b) * NL / 1e9:.1f} GB touched "
-                             f"per cycle) > 126 MB L2; no flush",
+                       "l2": f"weights cycled over {NL} layers (~{statistics.mean(r['moe_b']) * NL / 1e9:.1f} GB "
+                             f"touched per cycle) > 126 MB L2; no flush",
                        "parallelism": f"ep{world}" if epar else "single GPU", "graph": "CUDA graph + PDL"},
-            "hbm_gbs_step": step_b / (us_step * 1e-6) / 1e9,
-            "unique_experts_mean": statistics.mean(U),
-            "us_moe_kernel": us_moe, "us_router_kernel": us_router,
-            "us_collective": us_coll, "rank_hbm_frac": rank_frac,
+            "hbm_gbs_step": r["step_b"] / (r["us_step"] * 1e-6) / 1e9,
+            "unique_experts_mean": statistics.mean(r["U"]),
+            "us_moe_kernel": r["us_moe"], "us_router_kernel": r["us_router"],
+            "us_collective": r["us_coll"], "rank_hbm_frac": rank_frac,
+            "nccl_ranks": dist.get_world_size() if epar else None,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "kernel": "moe_persistent_kernel (layer-step launch, router inside)",
-                         "bytes_per_launch": launch_b,
-                         "traffic": load_traffic("moe_persistent_kernel")},
-            "e2e": {"value": us_e2e, "unit": UNIT, "h2d_bytes_per_step": M * cfg.H * 2,
-                    "d2h_bytes_per_step": M * cfg.H * 2, "steps": n_e2e},
+                         "bytes_per_launch": r["launch_b"],
+                         "traffic": traffic, "traffic_source": "profiles/traffic.json: ncu dram bytes of one launch "
+                                                               "of this config, scaled by its distinct experts"},
+            "e2e": {"value": r["e2e_us"], "unit": UNIT, "h2d_bytes_per_step": M * cfg.H * 2,
+                    "d2h_bytes_per_step": M * cfg.H * 2, "steps": r["e2e_steps"]},
             # ours per step: the fused layer-step launch (+ the combine under expert parallelism; the all-reduce is
             # NCCL's)
-            "gpu_launches": (2 if epar else 1) * steps,
-            "clocks": clk.summary(),
+            "gpu_launches": (2 if epar else 1) * r["steps"],
+            "clocks": r["clocks"],
         }
+        if c4:
+            line["config4"] = c4
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
-        del g_full, g_moe, g_router, g_coll
         dist.destroy_process_group()
 
 

@@ -150,8 +150,10 @@ int qf_a16_moe_decode_nvfp4(const void* x, const int32_t* topk_ids, const float*
  * 16-byte aligned); outputs topk_w fp32 [M, topk], topk_ids int32 [M, topk], logits bf16 [M, E]. The logits are
  * fp32 dot products in this kernel's own order, rounded to bf16 (within one bf16 ulp of qf_router_topk's); ids and
  * weights follow from them exactly as in qf_router_topk. Other arguments as qf_a16_moe_decode; ctrl also holds the
- * barrier's counter (re-armed by the kernel). All CTAs of the launch must become resident (one per SM): the barrier's
- * wait is bounded (~1 s), after which the sticky error word is set and the items stop.
+ * barrier's counter (re-armed by the kernel). All CTAs of the launch (one per SM) must be resident at once for the grid
+ * barriers: the launch is cooperative, so the runtime co-schedules the grid or refuses it -- this entry then returns
+ * QF_ERR_UNSUPPORTED and the caller takes the two-launch path (qf_router_topk, then qf_a16_moe_decode). The
+ * barrier's wait is still bounded (~1 s), after which the sticky error word is set and the items stop.
  * x_stage: NULL (x is device memory), or a device buffer bf16 [M, H], 16-byte aligned: then x is pinned host memory
  *   (page-locked, mapped into the device's address space, as cudaHostAlloc gives under unified addressing) that the
  *   kernel itself copies into x_stage (each CTA a slice, then a second grid barrier) instead of a copy-engine transfer;

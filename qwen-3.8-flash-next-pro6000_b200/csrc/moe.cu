@@ -1514,8 +1514,11 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
         if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute (carveout)");
         if (dev < 64) carveout_set[fmt][dev] = true;
     }
-    // Grid: one CTA per SM (three pipelines each; the CTA allocates all 512 tensor-memory columns). Residency is not
-    // required for correctness: an item only waits for items claimed before it, by pipelines that are already running.
+    // Grid: one CTA per SM (three pipelines each; the CTA allocates all 512 tensor-memory columns). The item queue
+    // needs no co-residency (an item only waits for items claimed before it, by pipelines that are already running),
+    // but the fused router's grid barriers (its logits; x copied from host memory) need every CTA resident at once:
+    // that launch is cooperative, so the runtime either co-schedules the whole grid or refuses it (then this entry
+    // returns QF_ERR_UNSUPPORTED and the caller takes the two-launch path: router_topk, then a16_moe_decode).
 
     Params p;
     p.x = static_cast<const __nv_bfloat16*>(x);
@@ -1558,6 +1561,17 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
     if (fr && fr->x_stage) {   // x is pinned host memory (read by the kernel through its mapping); x_stage its copy
         p.xsrc = p.x;
         p.x = static_cast<const __nv_bfloat16*>(fr->x_stage);
+    }
+    if (fr != nullptr) {
+        ce = qf::launch_coop(kern, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,
+                             reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);
+        if (ce == cudaErrorCooperativeLaunchTooLarge) {
+            (void)cudaGetLastError();
+            qf::set_error("moe_layer_decode: the %d CTAs of the fused layer-step cannot all be resident (grid barriers); "
+                          "use router_topk + a16_moe_decode", sms * CTAS_PER_SM);
+            return QF_ERR_UNSUPPORTED;
+        }
+        return qf::cuda_status(ce, "moe_layer_decode: launch");
     }
     ce = qf::launch_ex(kern, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,
                        reinterpret_cast<cudaStream_t>(stream), pdl != 0, p);

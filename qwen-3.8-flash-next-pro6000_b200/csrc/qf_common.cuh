@@ -53,6 +53,24 @@ cudaError_t launch_ex(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStrea
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
+// The same as a cooperative launch: every CTA of the grid is resident at once (the runtime refuses a grid that cannot
+// be, with cudaErrorCooperativeLaunchTooLarge), as grid-wide barriers require. Composes with PDL (measured on B200).
+template <typename Kern, typename... Args>
+cudaError_t launch_coop(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 
 // ---------------------------------------------------------------------------------------------- device side
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }

@@ -9,6 +9,7 @@ LIB_NAME = "libqwenfast_b200.so"
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 
 QF_OK = 0
+QF_ERR_UNSUPPORTED = -3
 QF_MAX_TOKENS = 64
 QF_MAX_TOPK = 16
 QF_MAX_EXPERTS = 1024
@@ -79,8 +80,15 @@ def exported_symbols():
     return ["qf_last_error"] + list(SIGNATURES)
 
 
+class Unsupported(RuntimeError):
+    """A valid request this build declines (QF_ERR_UNSUPPORTED), e.g. a fused layer-step whose grid cannot be
+    co-resident; callers that have another path take it."""
+
+
 def check(status: int, what: str = ""):
-    """Raise RuntimeError (the reference's TORCH_CHECK failure type) for a non-zero status."""
+    """Raise RuntimeError (the reference's TORCH_CHECK failure type) for a non-zero status (``Unsupported`` for
+    QF_ERR_UNSUPPORTED)."""
     if status != QF_OK:
         msg = load().qf_last_error().decode(errors="replace")
-        raise RuntimeError(f"{what}: {msg}" if what and not msg.startswith(what) else msg)
+        text = f"{what}: {msg}" if what and not msg.startswith(what) else msg
+        raise Unsupported(text) if status == QF_ERR_UNSUPPORTED else RuntimeError(text)

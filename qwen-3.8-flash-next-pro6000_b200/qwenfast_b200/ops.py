@@ -376,25 +376,37 @@ def moe_layer_step(x: torch.Tensor, lw: MoELayerWeights, topk: int, bufs: dict, 
                    x_stage: Optional[torch.Tensor] = None):
     """One decode MoE layer-step: the reference's ``dual`` fast path (qwenfast.py:1177-1201: router_topk, then
     a16_moe_decode with the shared expert computed in-kernel). ``fused`` (default) runs the router inside the MoE
-    launch (``qf_moe_layer_decode``); ``fused=False`` launches ``router_topk`` (scratch ``rbufs``) and then
-    ``a16_moe_decode``. Host I/O (fused only): ``x`` and ``out`` pinned host tensors and ``x_stage`` a CUDA
-    bf16 [M, H] buffer -- the kernel reads x from host memory and writes out there, no copy-engine transfers.
-    Returns (out, topk_w, topk_ids, logits)."""
+    launch (``qf_moe_layer_decode``, a cooperative launch); if that grid cannot be co-resident on this device the
+    launch is declined and the step takes the two launches of ``fused=False``: ``router_topk`` (scratch ``rbufs``),
+    then ``a16_moe_decode``. Host I/O: ``x`` and ``out`` pinned host tensors and ``x_stage`` a CUDA bf16 [M, H]
+    buffer -- the fused kernel reads x from host memory and writes out there (the two-launch path copies through
+    ``x_stage`` and a device buffer instead). Returns (out, topk_w, topk_ids, logits)."""
     M = x.shape[0]
     dev = x.device if x_stage is None else x_stage.device
-    if not fused:
-        tw, ids, logits = router_topk(x, lw.router, topk, renormalize, rbufs[0], rbufs[1], pdl)
-        a16_moe_decode(x, ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
-                       bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"], lw.sh_w13, None,
-                       lw.sh_w2, None, bufs["shbuf"], pdl=pdl)
-        return out, tw, ids, logits
-    tw = torch.empty(M, topk, dtype=torch.float32, device=dev)
-    ids = torch.empty(M, topk, dtype=torch.int32, device=dev)
-    logits = torch.empty(M, lw.E, dtype=BF16, device=dev)
-    a16_moe_decode(x, ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"], bufs["ybuf"],
-                   bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"], lw.sh_w13, None, lw.sh_w2, None,
-                   bufs["shbuf"], pdl=pdl, router_w=lw.router, renormalize=renormalize, logits=logits,
-                   x_stage=x_stage)
+    if fused:
+        tw = torch.empty(M, topk, dtype=torch.float32, device=dev)
+        ids = torch.empty(M, topk, dtype=torch.int32, device=dev)
+        logits = torch.empty(M, lw.E, dtype=BF16, device=dev)
+        try:
+            a16_moe_decode(x, ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
+                           bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, 4, None, bufs["pbuf"], lw.sh_w13, None,
+                           lw.sh_w2, None, bufs["shbuf"], pdl=pdl, router_w=lw.router, renormalize=renormalize,
+                           logits=logits, x_stage=x_stage)
+            return out, tw, ids, logits
+        except _lib.Unsupported:
+            pass   # the fused grid cannot be co-resident here: the reference's two launches instead
+    xd = x
+    if not x.is_cuda:
+        _req(x_stage is not None, "moe_layer_step: a host x needs x_stage")
+        x_stage.copy_(x, non_blocking=True)
+        xd = x_stage
+    od = out if out.is_cuda else torch.empty(M, x.shape[1], dtype=BF16, device=dev)
+    tw, ids, logits = router_topk(xd, lw.router, topk, renormalize, rbufs[0], rbufs[1], pdl)
+    a16_moe_decode(xd, ids, tw, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
+                   bufs["ybuf"], bufs["gl"], bufs["ctrl"], od, 4, None, bufs["pbuf"], lw.sh_w13, None, lw.sh_w2,
+                   None, bufs["shbuf"], pdl=pdl)
+    if od is not out:
+        out.copy_(od, non_blocking=True)
     return out, tw, ids, logits
 
 

@@ -14,7 +14,8 @@
 2. ``config0.pt`` -- the toy configuration's oracle outputs (router + MoE) with input checksums, used by the GPU
    parity tests without recomputing the oracle.
 
-Usage: python tests/golden/make_golden.py [--reference /root/reference]
+Usage: python tests/golden/make_golden.py --reference <checkout of the reference repository>
+(or set QWENFAST_REFERENCE to that directory)
 """
 import argparse
 import ast
@@ -57,8 +58,11 @@ def checksum(*ts):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("QWENFAST_REFERENCE"),
+                    help="root of the reference repository (required; or QWENFAST_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or QWENFAST_REFERENCE) must name the reference repository")
     ref = args.reference
     qf_src = extract(os.path.join(ref, "serve/overlays/sglang/srt/qwenfast.py"), ["w8_quant"])
     t_src = extract(os.path.join(ref, "serve/qwenfast/test_a16moe.py"), ["w8q", "route", "shared_ref", "truth"])

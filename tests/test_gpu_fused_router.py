@@ -146,3 +146,40 @@ def test_fused_host_io_matches_device_io(cuda):
         assert torch.equal(ids_h, ids_d) and torch.equal(tw_h, tw_d) and torch.equal(lg_h, lg_d)
         assert torch.equal(oh, out_d.cpu())
     assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
+
+
+def test_declined_fused_launch_takes_the_two_launch_path(cuda, monkeypatch):
+    """When the fused layer-step's cooperative grid cannot be co-resident, qf_moe_layer_decode returns
+    QF_ERR_UNSUPPORTED (nothing enqueued) and moe_layer_step runs router_topk + a16_moe_decode instead -- for device
+    buffers and for pinned host x / out. The refusal is simulated at the library boundary (a full B200 always
+    co-schedules the grid)."""
+    from qwenfast_b200 import _lib
+    cfg = synthetic.CONFIGS[1]
+    L, lw = layer(cfg, cuda)
+    x = synthetic.make_tokens(cfg, device=cuda, seed=41)
+    bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, cfg.Is, cuda)
+    rb = ops.router_bufs(cuda)
+    ref = torch.empty_like(x)
+    _, tw_r, ids_r, lg_r = ops.moe_layer_step(x, lw, cfg.topk, bufs, rb, ref, fused=False)
+    torch.cuda.synchronize()
+    lib = _lib.load()
+
+    class Refusing:   # the library with a fused entry that declines, everything else forwarded
+        def __getattr__(self, name):
+            return getattr(lib, name)
+
+        @staticmethod
+        def qf_moe_layer_decode(*args):
+            return _lib.QF_ERR_UNSUPPORTED
+
+    monkeypatch.setattr(_lib, "load", lambda *a, **k: Refusing())
+    out = torch.empty_like(x)
+    _, tw, ids, lg = ops.moe_layer_step(x, lw, cfg.topk, bufs, rb, out)
+    xs = torch.empty_like(x)
+    xh = x.cpu().pin_memory()
+    oh = torch.empty(cfg.M, cfg.H, dtype=BF).pin_memory()
+    ops.moe_layer_step(xh, lw, cfg.topk, bufs, rb, oh, x_stage=xs)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref) and torch.equal(ids, ids_r) and torch.equal(tw, tw_r) and torch.equal(lg, lg_r)
+    assert torch.equal(oh, ref.cpu())
+    assert ops.moe_error_word(bufs["ctrl"]) == 0

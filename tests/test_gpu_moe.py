@@ -22,9 +22,13 @@ pytestmark = pytest.mark.gpu
 BF = torch.bfloat16
 
 
-def assert_close_to_oracle(out, ref_rounded, ref_truth=None):
+def assert_close_to_oracle(out, ref_rounded, ref_truth=None, label=""):
     """max-abs 2e-2, widened elementwise by two bf16 ulps of the reference value (one output rounding step already
-    exceeds 2e-2 once |out| >= 4), and relative L2 1e-2."""
+    exceeds 2e-2 once |out| >= 4), and relative L2 1e-2 against the rounded oracle. Against the all-fp32 truth:
+    relative L2 1e-2 and max-abs <= max(2e-2, floor + one bf16 step of max|truth|), where floor = max|rounded oracle -
+    truth| is what the reference's own rounding points already give (0.035 at config 1, up to 0.22 on the Zipf sweep
+    where outputs reach |20|): no bf16-output kernel with those rounding points can meet a flat 2e-2 there. The
+    measured max-abs against the truth is printed."""
     out = out.float().cpu()
     ref = ref_rounded.float()
     d = out - ref
@@ -32,8 +36,15 @@ def assert_close_to_oracle(out, ref_rounded, ref_truth=None):
     tol = 2e-2 + 2.0 ** -6 * ref.abs()
     assert bool((d.abs() <= tol).all()) and rel <= 1e-2, (d.abs().max().item(), rel)
     if ref_truth is not None:
-        rel_t = ((out - ref_truth).norm() / ref_truth.norm()).item()
+        tru = ref_truth.float()
+        rel_t = ((out - tru).norm() / tru.norm()).item()
+        max_t = (out - tru).abs().max().item()
+        floor = (ref - tru).abs().max().item()
+        bound = max(2e-2, floor + 2.0 ** -7 * tru.abs().max().item())
+        print(f"[parity {label}] max|out-truth| {max_t:.4f} (reference rounding floor {floor:.4f}, bound {bound:.4f}), "
+              f"rel-L2 {rel_t:.2e}, max|truth| {tru.abs().max().item():.2f}")
         assert rel_t <= 1e-2, rel_t
+        assert max_t <= bound, (max_t, floor, bound)
 
 
 def canon_cpu(L):
@@ -74,7 +85,7 @@ def test_config0_against_golden(cuda):
     bufs = ops.moe_workspace(cfg.M, cfg.H, cfg.I, cfg.topk, 0, cuda)
     out = run_moe(x.to(cuda), gold["ids"].to(cuda), gold["weights"].to(cuda), lw, bufs)
     torch.cuda.synchronize()
-    assert_close_to_oracle(out, gold["out_rounded"], gold["out_truth"])
+    assert_close_to_oracle(out, gold["out_rounded"], gold["out_truth"], "config0 golden")
     assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
 
 
@@ -106,7 +117,7 @@ def test_config1_full_layer(cfg1, cuda):
                               shared_w=(C["sh_gu"], C["sh_d"]))
     tru = moe_ref.moe_truth(xs, i_c, w_c, C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
                             shared_w=(C["sh_gu"], C["sh_d"]))
-    assert_close_to_oracle(out, ref, tru)
+    assert_close_to_oracle(out, ref, tru, "config1 M=10")
     assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
 
 
@@ -205,7 +216,9 @@ def test_token_sweep_with_zipf_routing(cfg1, cuda, M):
     assert ops.moe_error_word(bufs["ctrl"]) == 0
     ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
                               shared_w=(C["sh_gu"], C["sh_d"]))
-    assert_close_to_oracle(out, ref)
+    tru = moe_ref.moe_truth(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
+                            shared_w=(C["sh_gu"], C["sh_d"]))
+    assert_close_to_oracle(out, ref, tru, f"config2 zipf M={M}")
     if M == 64:
         counts = torch.bincount(ids.cpu().flatten().long(), minlength=cfg.E)
         assert counts.max().item() > 16, "the skewed router should give some expert several token groups"
@@ -228,7 +241,7 @@ def test_global_scales_and_odd_shapes(cuda):
         ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), L["w13"], L["s13"], L["w2"], L["s2"], gs13=gs13,
                                   gs2=gs2)
         tru = moe_ref.moe_truth(x.cpu(), ids.cpu(), w.cpu(), L["w13"], L["s13"], L["w2"], L["s2"], gs13=gs13, gs2=gs2)
-        assert_close_to_oracle(out, ref, tru)
+        assert_close_to_oracle(out, ref, tru, "odd shapes")
 
 
 def test_duplicate_and_out_of_range_ids(cuda):
