@@ -1,7 +1,9 @@
-"""Build the native library (CUDA kernels + C ABI) in-tree with nvcc for sm_100a.
+"""Build the native libraries in-tree: the CUDA kernels + C ABI with nvcc for sm_100a (``libqwenfast_b200.so``), and
+the torch operator registration over that C ABI with g++ against torch's headers (``libqwenfast_b200_torch.so``:
+``torch.ops.qwenfast_b200.*``).
 
 ``python -m qwenfast_b200.build`` (with the package directory on ``sys.path``) or ``build()`` from Python. The
-library lands next to this file as ``libqwenfast_b200.so``; it is rebuilt only when a source or header changed.
+libraries land next to this file; each is rebuilt only when a source or header it depends on changed.
 """
 import os
 import subprocess
@@ -10,10 +12,12 @@ from concurrent.futures import ThreadPoolExecutor
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 SRC_DIR = os.path.join(os.path.dirname(PKG_DIR), "csrc")
+TORCH_SRC_DIR = os.path.join(os.path.dirname(PKG_DIR), "csrc_torch")
 REPO_ROOT = os.path.dirname(os.path.dirname(PKG_DIR))
 INCLUDE_DIR = os.path.join(REPO_ROOT, "include")
 BUILD_DIR = os.path.join(REPO_ROOT, "_build")
 LIB_PATH = os.path.join(PKG_DIR, "libqwenfast_b200.so")
+TORCH_LIB_PATH = os.path.join(PKG_DIR, "libqwenfast_b200_torch.so")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
@@ -68,7 +72,33 @@ def build(force: bool = False, verbose: bool = False, extra_flags=None) -> str:
         list(ex.map(run, jobs))
     if force or jobs or _stale(LIB_PATH, objs):
         run([_nvcc()] + ARCH_FLAGS + ["-shared", "-Xcompiler", "-fPIC", "-o", LIB_PATH] + objs + ["-lcudart"])
+    build_torch_ops(force=force, verbose=verbose)
     return LIB_PATH
+
+
+def build_torch_ops(force: bool = False, verbose: bool = False) -> str:
+    """g++ the TORCH_LIBRARY registration (``csrc_torch/torch_ops.cpp``) against torch's headers into
+    ``libqwenfast_b200_torch.so``, linked to ``libqwenfast_b200.so`` (found next to it through $ORIGIN) and torch."""
+    import torch
+    from torch.utils import cpp_extension as ce
+    srcs = sorted(os.path.join(TORCH_SRC_DIR, f) for f in os.listdir(TORCH_SRC_DIR) if f.endswith(".cpp"))
+    deps = srcs + [os.path.join(INCLUDE_DIR, f) for f in os.listdir(INCLUDE_DIR) if f.endswith(".h")] + [LIB_PATH]
+    if not force and not _stale(TORCH_LIB_PATH, deps):
+        return TORCH_LIB_PATH
+    home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    tlib = ce.library_paths()[0]
+    cmd = (["g++", "-O2", "-std=c++17", "-fPIC", "-shared",
+            f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}"]
+           + [f"-I{p}" for p in ce.include_paths()] + [f"-I{os.path.join(home, 'include')}", f"-I{INCLUDE_DIR}"]
+           + srcs + ["-o", TORCH_LIB_PATH, f"-L{PKG_DIR}", "-lqwenfast_b200", "-Wl,-rpath,$ORIGIN",
+                     f"-L{tlib}", f"-Wl,-rpath,{tlib}", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-lc10", "-lc10_cuda",
+                     f"-L{os.path.join(home, 'lib64')}", "-lcudart"])
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("g++ failed:\n" + " ".join(cmd) + "\n" + r.stdout + r.stderr)
+    return TORCH_LIB_PATH
 
 
 if __name__ == "__main__":

@@ -140,6 +140,7 @@ def moe_workspace(M: int, H: int, I: int, topk: int, Is: int, device) -> dict:
         pbuf=torch.zeros(max(pb, 1), dtype=torch.float32, device=device),   # holds counters: zeroed once
         shbuf=torch.empty(max(sh // 2, 1), dtype=BF16, device=device),
         none=torch.empty(0, dtype=BF16, device=device),
+        none_i64=torch.empty(0, dtype=torch.int64, device=device),   # an absent timeline buffer (operators' dbg)
         err_host=torch.zeros(1, dtype=torch.int32, pin_memory=True),
     )
     attach_error_mirror(bufs["ctrl"], bufs["err_host"], bufs["pbuf"])

@@ -5,9 +5,9 @@ reference; the shape gates follow this build's limits and weight formats instead
 (H = 2560, M <= 8, NVFP4 / Marlin experts):
 
 * ``w8_quant`` / ``w8_linear`` -- the INT8 (W8A16, group-scaled) dense projections
-  (qwenfast.py:301-315, 331-334, 337-360). A call the kernel does not take (bias, more than 64 rows, unsupported
-  K or layout, torch.compile tracing) declines to the reference's own fallback: the weight rows are unpacked on the
-  device into bf16 (``w8g_unpack``) and multiplied with ``torch.nn.functional.linear``.
+  (qwenfast.py:301-315, 337-360). A call the kernel does not take (bias, more than 64 rows, unsupported
+  K, N or layout) declines to the reference's own fallback: the weight rows are unpacked on the device into bf16
+  (``w8g_unpack``) and multiplied with ``torch.nn.functional.linear``.
 * ``w8a8_linear`` -- the per-token W8A8 projection (no reference code); more than 16 rows run as 16-row calls of
   the same kernel (per-token quantisation makes rows independent, so the result is the same bits).
 * ``why_not`` / ``_a16_ok`` / ``_a16_shared`` / ``dual`` -- the decode MoE block (qwenfast.py:1076-1201): the
@@ -17,7 +17,9 @@ reference; the shape gates follow this build's limits and weight formats instead
   distribution recorder) is the caller's, as it is not part of this library.
 
 Blocks and layers are read by attribute, so SGLang's module objects (``Qwen2MoeSparseMoeBlock``, ``FusedMoE``,
-``LinearBase``) and any object with the same attribute names work. Nothing here imports sglang.
+``LinearBase``) and any object with the same attribute names work. Nothing here imports sglang. The kernels are
+called through the registered operators ``torch.ops.qwenfast_b200.*`` (``torch_ops``), so the fast paths also run
+inside ``torch.compile``d forwards; the host mirror of the MoE error word is checked on eager calls only.
 """
 import os
 from collections import namedtuple
@@ -25,7 +27,7 @@ from typing import Optional
 
 import torch
 
-from . import _lib, formats, ops
+from . import _lib, formats, ops, torch_ops
 
 BF16 = torch.bfloat16
 TopKOutput = namedtuple("TopKOutput", ["topk_weights", "topk_ids", "router_logits"])   # SGLang StandardTopKOutput
@@ -65,7 +67,6 @@ def w8_route(entry, x: torch.Tensor, bias=None) -> Optional[str]:
         ("group", p["G"] in (64, 128) and K % 64 == 0 and K % p["G"] == 0),
         ("dtype", x2.dtype == BF16),
         ("layout", x2.stride(1) == 1 and x2.stride(0) % 8 == 0 and x2.data_ptr() % 16 == 0),
-        ("compile", not torch.compiler.is_compiling()),
         ("device", x2.is_cuda),
     )
     return next((name for name, good in checks if not good), None)
@@ -84,7 +85,7 @@ def _w8_unpack_rows(p: dict, r0: int, r1: int) -> torch.Tensor:
     if buf is None or buf.numel() < need:
         buf = _pk_scratch[dev] = torch.empty(need, dtype=BF16, device=dev)
     w = buf[:need].view(r1 - r0, K)
-    ops.w8g_unpack(p["q"][r0:r1], p["s"][r0:r1], w)
+    torch_ops.load().w8g_unpack(p["q"][r0:r1], p["s"][r0:r1], w)
     return w
 
 
@@ -100,7 +101,7 @@ def w8_linear(entry, x: torch.Tensor, bias: Optional[torch.Tensor] = None) -> to
         return x.new_empty((*shp[:-1], n_out))
     if w8_route(entry, x, bias) is None:
         q, s = (p["q"], p["s"]) if (r0 == 0 and r1 == N) else (p["q"][r0:r1], p["s"][r0:r1])
-        y = ops.w8g_gemm(x2, q, s, 0)
+        y = torch_ops.load().w8g_gemm(x2, q, s, 0)
         return y.view(*shp[:-1], n_out)
     w = _w8_unpack_rows(p, r0, r1)
     return torch.nn.functional.linear(x2, w, bias).view(*shp[:-1], n_out)
@@ -124,7 +125,7 @@ def w8a8_linear(p: dict, x: torch.Tensor, bias: Optional[torch.Tensor] = None) -
         x2 = x2.contiguous()
     y = torch.empty(M, N, dtype=BF16, device=x2.device)
     for m0 in range(0, M, 16):
-        y[m0:m0 + 16] = ops.w8a8_gemm(x2[m0:m0 + 16], p["qk"], p["sw"])
+        y[m0:m0 + 16] = torch_ops.load().w8a8_gemm(x2[m0:m0 + 16], p["qk"], p["sw"])
     if bias is not None:
         y = (y.float() + bias.float()).to(BF16)
     return y.view(*shp[:-1], N)
@@ -258,7 +259,6 @@ def why_not(block, x: torch.Tensor, lora_active: bool = False) -> Optional[str]:
         ("waterfill", not getattr(topk, "enable_waterfill", False) and getattr(topk, "waterfill_balancer", None) is None),
         ("simulate", os.environ.get("SGLANG_SIMULATE_UNIFORM_EXPERTS", "") in ("", "0", "false")
          and os.environ.get("SGLANG_SIMULATE_ROUND_ROBIN_EXPERTS", "") in ("", "0", "false")),
-        ("compile", not torch.compiler.is_compiling()),
         ("device", x.is_cuda and gw.device == x.device),
     )
     return next((name for name, good in checks if not good), None)
@@ -282,6 +282,9 @@ def dual(block, hidden_states: torch.Tensor, orig=None, lora_active: bool = Fals
     cfg = block.topk.topk_config
     x = hidden_states
     M, H = x.shape
+    qops = torch_ops.load()
+    none = torch.empty(0, dtype=BF16, device=x.device)
+    opt = lambda t: none if t is None else t   # noqa: E731 -- empty tensors mean "absent" to the operators
     if _a16_ok(block, x):
         w13, s13, g13, w2, s2, g2 = _a16_weights(block)
         sh = _a16_shared(block)
@@ -290,31 +293,30 @@ def dual(block, hidden_states: torch.Tensor, orig=None, lora_active: bool = Fals
             shared = (shared_output if shared_output is not None
                       else block._forward_shared_experts(x.clone(), apply_gate=False))   # the kernel gates it
             shared = shared.contiguous()
-        E = block.gate.weight.shape[0]
         I = w2.shape[1] * 8 // H
         b = _a16_bufs(x.device, H, I, cfg.top_k, sh[2] if sh is not None else 0)
+        if not torch.compiler.is_compiling():
+            ops.check_moe_error(b["ctrl"])
         out = torch.empty_like(x)
+        wg = block.shared_expert_gate.weight.view(-1)
         if _a16_format(block) == "nvfp4":   # the reference's order: the router op, then the MoE op
             scratch, counter = _router_bufs(x.device)
-            tw, ids, logits = ops.router_topk(x, block.gate.weight, cfg.top_k, bool(cfg.renormalize), scratch,
-                                              counter, True)
-            ops.a16_moe_decode(x, ids, tw, w13, s13, g13, w2, s2, g2, block.shared_expert_gate.weight.view(-1),
-                               shared, b["hbuf"], b["ybuf"], b["gl"], b["ctrl"], out, 4, None, b["pbuf"],
-                               sh[0] if sh is not None else None, None, sh[1] if sh is not None else None, None,
-                               b["shbuf"], fmt="nvfp4")
+            tw, ids, logits = qops.router_topk(x, block.gate.weight, cfg.top_k, bool(cfg.renormalize), scratch,
+                                               counter, True)
+            qops.a16_moe_decode_nvfp4(x, ids, tw, w13, s13, opt(g13), w2, s2, opt(g2), wg, opt(shared), b["hbuf"],
+                                      b["ybuf"], b["gl"], b["ctrl"], out, 4, b["none_i64"], b["pbuf"],
+                                      sh[0] if sh is not None else none, none, sh[1] if sh is not None else none,
+                                      none, b["shbuf"])
             block._qf_topk = TopKOutput(tw, ids, logits)
             return out, None
-        tw = torch.empty(M, cfg.top_k, dtype=torch.float32, device=x.device)
-        ids = torch.empty(M, cfg.top_k, dtype=torch.int32, device=x.device)
-        logits = torch.empty(M, E, dtype=BF16, device=x.device)
-        ops.a16_moe_decode(x, ids, tw, w13, s13, g13, w2, s2, g2, block.shared_expert_gate.weight.view(-1), shared,
-                           b["hbuf"], b["ybuf"], b["gl"], b["ctrl"], out, 4, None, b["pbuf"],
-                           sh[0] if sh is not None else None, None, sh[1] if sh is not None else None, None,
-                           b["shbuf"], router_w=block.gate.weight, renormalize=bool(cfg.renormalize), logits=logits)
+        tw, ids, logits = qops.moe_layer_decode(x, block.gate.weight, bool(cfg.renormalize), w13, s13, opt(g13), w2,
+                                                s2, opt(g2), wg, opt(shared), sh[0] if sh is not None else none,
+                                                sh[1] if sh is not None else none, cfg.top_k, b["hbuf"], b["ybuf"],
+                                                b["gl"], b["ctrl"], b["pbuf"], b["shbuf"], out)
         block._qf_topk = TopKOutput(tw, ids, logits)
         return out, None
     scratch, counter = _router_bufs(x.device)
-    tw, ids, logits = ops.router_topk(x, block.gate.weight, cfg.top_k, bool(cfg.renormalize), scratch, counter, True)
+    tw, ids, logits = qops.router_topk(x, block.gate.weight, cfg.top_k, bool(cfg.renormalize), scratch, counter, True)
     if shared_output is None:
         shared_output = block._forward_shared_experts(x.clone(), apply_gate=True)
     block._qf_topk = TopKOutput(tw, ids, logits)
