@@ -10,12 +10,9 @@
 // tensor cores in fp32 and then scaled once (exact products, no per-weight scale multiply).
 //
 // B200 structure
-//   * One CTA per SM (148 on B200) running NVP = 3 independent pipelines. A pipeline is 6 warps: 4 consumer warps
-//     (one warpgroup, each thread owns one weight row of a 128-row tile), a producer warp (lane 0) and an MMA warp
-//     (lane 0 issues). One more warp (lane 0) is the signal agent of all three. The pipelines share the routing plan
-//     and the tensor-memory allocation (a 160-column slice each); everything else (ring, barriers, job slots) is
-//     per pipeline. Three pipelines per SM hide the latency of each stage's hand-offs (mbarrier, TMEM store / load,
-//     tcgen05.commit), which one pipeline alone cannot: a stage is a chain of such waits around the dequantisation.
+//   * One CTA per SM (148 on B200) running NVP = 3 independent pipelines. A pipeline is 5 warps: 4 consumer warps
+//     and a producer warp (lane 0). One more warp (lane 0) is the signal agent of all three. The pipelines share
+//     the routing plan; everything else (ring, barriers, job slots) is per pipeline.
 //   * Work items, claimed in order from a global queue by each pipeline's producer:
 //       GL  shared-expert gate logits          S1  shared gate_up tile, one of 4 k-splits, one 16-token group
 //       G1  expert u gate_up tile + group      S1F shared gate_up split-K sum + SwiGLU
@@ -23,27 +20,32 @@
 //       CB  top-k combine of one 128-column tile for 8 tokens (+ gated shared term)
 //     An item only depends on items claimed before it, by pipelines that are already running, so the queue cannot
 //     deadlock for any grid size.
-//   * The producer streams each item's weights through an NST-stage shared-memory ring with 1-D bulk copies (TMA
-//     engine, mbarrier completion): per stage 8 KB of weights (128 rows x 128 k int4, or x 32 k bf16) and, for int4,
-//     the stage's 128 row scales. Every cross-CTA dependency (gate_up -> down, split-K -> finalize -> shared down,
-//     all producers of a column tile -> combine) is acquired by the producer (bounded wait) before it marks the
-//     stage full, so consumers never spin on other CTAs. Item bases are computed once per item.
-//   * The consumers copy the matching k-slice of the item's token rows (x for gate_up, h for down; at most 16 rows
-//     of 256 B) themselves, one 16-byte cp.async per chunk straight into the B operand, one stage ahead.
-//   * Contraction on the 5th-generation tensor cores (tcgen05), double-buffered. int4 stages (128 rows x 128 k, one
-//     scale group): every consumer thread turns its row's 16 int4 words into bf16x2 of the signed codes (code - 8:
-//     one lop3 and one bf16x2 subtract each, exact) and stores them to TMEM (tcgen05.st) as the A operand, while
-//     the token rows land in the canonical K-major shared-memory B layout (N = 16). The MMA warp issues
-//     tcgen05.mma kind::f16 per k16 step (A in TMEM, B in SMEM, fp32 D in TMEM), then tcgen05.commit. While the
-//     tensor cores run stage s, the consumers dequantise stage s+1, then read back (tcgen05.ld) and scale stage s,
-//     adding the stages up in registers in k order (all 16 tokens of the thread's row).
-//     bf16 stages (shared expert, 32 k): the ring stage itself is the A operand (SMEM descriptor).
-//     gate_up tiles interleave gate row j (even lane) and up row j (odd lane): SwiGLU is one shuffle.
+//   * The producer streams each item's weights through an NST-stage shared-memory ring with the TMA engine
+//     (mbarrier completion): per stage 8 KB of weights (128 rows x 128 k int4, or x 32 k bf16; 1-D bulk copy), for
+//     int4 the stage's 128 row scales, and the matching k-slice of the item's token rows (x for gate_up, h for down):
+//     one tensor copy of up to 16 consecutive rows for the shared expert, 1-D copies of one or two gathered rows, or
+//     4-row gather copies (tile::gather4) of more, for a routed expert. Every cross-CTA dependency (gate_up -> down,
+//     split-K -> finalize -> shared down, all producers of a column tile -> combine) is acquired by the producer
+//     (bounded wait) before it copies the dependent rows and marks the stage full, so consumers never spin on other
+//     CTAs, and a stage arrives whole: the four consumer warps of a pipeline run unsynchronised through an item.
+//   * Contraction: a decode item has few tokens (about one per routed expert at 10 tokens x top-10 of 512 experts),
+//     so each stage is a matrix-vector product that streams 8 KB of weights for a handful of columns. The weights
+//     are stored in the tensor cores' register-fragment order (m16n8k16): consumer warp w owns the two 16-row tiles
+//     2w, 2w + 1 of every 128-row stage, and one 16-byte shared-memory load gives a lane the int4 codes of four
+//     k16 steps of one tile. Each 32-bit word turns into the four bf16x2 A registers of one step with a shift, a
+//     lop3 and a bf16x2 subtract per register (code - 8, exact), and feeds mma.sync m16n8k16 (bf16, fp32
+//     accumulate) once per 8 tokens. No shared-memory or tensor-memory round trip sits between the copy engine and
+//     the tensor cores. (tcgen05 with N = 16 token columns spends one tensor-memory store, one 128-row MMA chain and
+//     one tensor-memory load per stage whatever the token count; at decode sizes that chain, not HBM, set the rate.)
+//     bf16 stages (shared expert, 32 k) are already in fragment order and feed the mma directly.
+//     gate_up tiles put gate row j in fragment row g and up row j in fragment row g + 8: one thread holds both.
 //   * Consumers signal completed items through a per-pipeline record ring; the agent turns each record into one
 //     gpu-scope release (fence + atomic add) on the control block. Consumer warps never execute a gpu-scope fence.
 //   * The routing plan (unique experts, per-expert token lists, group offsets) is rebuilt identically by every CTA
 //     from topk_ids with shared-memory atomics (token bit masks), so no CTA waits for a plan.
-//   * Every wait is bounded; a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains.
+//   * Every wait is bounded; a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains. The consumer
+//     warps of a pipeline agree on each item's outcome through a reducing named barrier (barrier.red.and) before its
+//     epilogue, so a wait that runs out in one warp ends the item in all four and no barrier is left waiting.
 #include "qf_common.cuh"
 #include "topk.cuh"
 
@@ -54,23 +56,30 @@ using qf::bf16_hi;
 using qf::bf16_lo;
 using qf::bf16r;
 
-constexpr int NCW = 4;                        // consumer warps of a pipeline (128 threads = 128 weight rows)
+constexpr int NCW = 4;                        // consumer warps of a pipeline (two 16-row tiles of 128 each)
 constexpr int NVP = 3;                        // pipelines per CTA
-constexpr int VP_WARPS = NCW + 2;             // consumers, producer, MMA warp
-constexpr int VP_PRODUCER = NCW, VP_MMA = NCW + 1;
+constexpr int VP_WARPS = NCW + 1;             // consumers, producer
+constexpr int VP_PRODUCER = NCW;
 constexpr int AGENT_WARP = NVP * VP_WARPS;
 constexpr int MOE_THREADS = (NVP * VP_WARPS + 1) * 32;
-constexpr int NBUF = 2;                       // A / B / D buffers of the pipelined stages (per pipeline)
 constexpr int CONS_THREADS = NCW * 32;
 constexpr int CTAS_PER_SM = 1;
-constexpr int TG = 16;                        // tokens per token group (two n8 tiles)
-constexpr int NST = 7;                        // ring stages per pipeline
+constexpr int TG = 16;                        // tokens per token group (two n8 tiles of the mma)
+constexpr int NST = 5;                        // ring stages per pipeline
 constexpr int NEPI = 8;                       // completion-record ring
 constexpr int W4_KC = 128;                    // int4 k per stage (one scale group)
 constexpr int BF_KC = 32;                     // bf16 k per stage
 constexpr int STAGE_W = 8192;                 // weight bytes of a stage (128 rows x 128 k int4 or x 32 k bf16)
 constexpr int STAGE_S = 256;                  // scale bytes of an int4 stage (one per row)
-constexpr int STAGE_BYTES = STAGE_W + STAGE_S;
+constexpr int STAGE_TOK = STAGE_W + STAGE_S;  // offset of the stage's token block
+// token block of a pipelined stage: [token (16)][k]. int4 stages (128 k = 256 B per row): rows copied one by one
+// sit at a 272-byte stride (the 8 lanes of each 16-byte shared-memory load phase hit distinct banks), rows of a
+// 4-row gather copy back to back (256 B); bf16 stages (32 k): 64 B per row, back to back (conflict-free as it is).
+constexpr int BROW_W4 = 272;
+constexpr int BROW_G4 = 256;
+constexpr int BROW_BF = 64;
+constexpr int GATHER_MIN = 3;                 // tokens from which a routed item's rows come by 4-row gathers
+constexpr int STAGE_BYTES = STAGE_TOK + TG * BROW_W4;
 constexpr int NSPLIT = 4;                     // split-K of the shared expert's gate_up
 constexpr int G1_SPLIT = 2;                   // k halves of a routed gate_up item (finished by the later half) when
                                               // all halves fit in one wave of pipelines (small M)
@@ -103,9 +112,6 @@ struct StageDesc {
 };
 struct EpiRec {     // one completion record: add `add` to ctrl[idx] (idx < 0: nothing; kind STOP ends the agent)
     int idx, add;
-};
-struct MmaJob {     // what the MMA warp issues for one pipelined stage
-    int16_t kind, ring;
 };
 
 struct Params {
@@ -141,20 +147,23 @@ struct Params {
     int wofs;   // expert id of the first expert in w13 / s13 / w2 / s2 / gs13 / gs2 (mode 1: elo)
     const uint8_t* f13;   // NVFP4 experts (FMT 1): E4M3 group-16 scales in the layout of formats.nvfp4_scale_map
     const uint8_t* f2;
+    // token-row sources of the stages' token blocks (tensor maps, encoded per launch)
+    CUtensorMap xt;   // x [M, H] bf16, box 32 k x tok_box rows: the shared expert's gate_up tokens
+    CUtensorMap xg;   // x [M, H] bf16, box 128 k x 1 row: a routed expert's gate_up tokens (4-row gathers)
+    CUtensorMap hg;   // hbuf [M * topk, I] bf16, box 128 k x 1 row: a routed expert's down tokens (by slot)
+    CUtensorMap ht;   // shared-expert h [M, Is] bf16, box 32 k x tok_box rows: its down tokens
+    int tok_box;      // rows of the xt / ht boxes: min(TG, M)
 };
 
 // shared memory map (dynamic): NVP pipeline blocks, then the routing plan
-constexpr int BST_BYTES = TG * (W4_KC / 8) * 16;                      // B operand [k chunk][16 tokens][16 B]
 constexpr int VO_RING = 0;
-constexpr int VO_BST = VO_RING + NST * STAGE_BYTES;
-constexpr int VO_BAR = VO_BST + NBUF * BST_BYTES;                     // full, empty, efull, eempty, ab-ready, mma-done
-constexpr int VO_DESC = VO_BAR + (2 * NST + 2 * NEPI + 2 * NBUF) * 8;
+constexpr int VO_BAR = VO_RING + NST * STAGE_BYTES;                   // full, empty, efull, eempty
+constexpr int VO_DESC = VO_BAR + (2 * NST + 2 * NEPI) * 8;
 constexpr int VO_EPI = VO_DESC + NST * (int)sizeof(StageDesc);
-constexpr int VO_JOB = VO_EPI + NEPI * (int)sizeof(EpiRec);
-constexpr int VO_FLAG = VO_JOB + NBUF * (int)sizeof(MmaJob);         // int: this group finishes the item
+constexpr int VO_FLAG = VO_EPI + NEPI * (int)sizeof(EpiRec);         // int: this group finishes the item
 constexpr int VP_BYTES = (VO_FLAG + 4 + 127) & ~127;
 constexpr int OFF_PLAN = NVP * VP_BYTES;
-static_assert(VO_BST % 128 == 0 && VO_BAR % 8 == 0 && VP_BYTES % 128 == 0, "shared memory alignment");
+static_assert(STAGE_BYTES % 128 == 0 && VO_BAR % 8 == 0 && VP_BYTES % 128 == 0, "shared memory alignment");
 constexpr int PLAN_ULIST = 0;                                         // int16 [QF_MAX_EXPERTS]
 constexpr int PLAN_GPRE = PLAN_ULIST + QF_MAX_EXPERTS * 2;            // int16 [QF_MAX_EXPERTS + 1]
 constexpr int PLAN_TOFF = PLAN_GPRE + (QF_MAX_EXPERTS + 8) * 2;
@@ -183,15 +192,7 @@ constexpr int RPC_MAX = 8;                                          // router ro
 static_assert(RROWS_BYTES >= 4096 * 2 * 7, "x tile of the fused router");
 
 enum : int { DBG_CONSUMERS = 30, DBG_STOP = 31, DBG_ENTRY = 0xFFF };   // timeline events (dbg)
-enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_TMEM = 6, MISC_DUPS = 7 };
-
-// tensor memory map (columns of this CTA's allocation; fp32 / bf16x2 per 32-bit column, lane = tile row)
-constexpr uint32_t TM_COLS = 512;
-constexpr uint32_t TM_VP = 160;    // columns per pipeline
-constexpr uint32_t TM_A = 0;       // NBUF x 64 columns: A tiles of 128-k int4 stages (8 k16 steps x 8 columns)
-constexpr uint32_t TM_D = 128;     // NBUF x 16 columns: fp32 partial of each stage
-static_assert(TM_D + NBUF * 16 <= TM_VP && TM_A + NBUF * 64 <= TM_D && NVP * TM_VP <= TM_COLS, "tensor memory map");
-constexpr uint32_t IDESC = qf::idesc_bf16(128, TG);
+enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_DUPS = 7 };
 
 // Errors that stop the pipeline (waits that ran out). An out-of-range expert id is reported but not fatal: the
 // slot is skipped and the rest of the layer is computed.
@@ -294,39 +295,92 @@ __device__ __forceinline__ const __nv_bfloat16* token_row(const Params& p, const
     return p.hsh + (size_t)(TG * d.tg + n) * p.Is;   // K_S2
 }
 
-// Dequantise this thread's row of an int4 stage (w: its first 16-byte load; quads are 128 lanes apart) into
-// TMEM columns ta .. ta + 63 (signed codes, natural k order: word w, k = 8w .. +8, becomes columns 4w .. 4w + 3).
-__device__ __forceinline__ void stage_w4_to_tmem(const uint8_t* w, uint32_t ta) {
+// ------------------------------------------------------------------------------- register-path stage contraction
+// A lane (g = lane / 4, t4 = lane % 4) of consumer warp w holds the m16n8k16 fragments of m16 tiles 2w + m (m = 0, 1)
+// and n8 token tiles n (n = 0, 1): accumulator d[2 m + n][i] is row 16 (2w + m) + g + 8 (i / 2) of the stage, token
+// 8 n + 2 t4 + (i % 2). Inside each 64-k half of a stage the weights' k order is permuted so that the lane's four
+// k16 steps use one 32-byte run of each token row: step s of half h takes k = 64 h + 16 t4 + 4 s + (0 .. 3) in mma
+// columns (2 t4, 2 t4 + 1, 2 t4 + 8, 2 t4 + 9). The layouts are built by the repack kernels below.
+
+// NVFP4 pair j of a word (nibbles j and j + 4, e2m1 codes) -> bf16x2 of code * scale (exact): sign to bit 15,
+// exponent and mantissa to bits 6..8 (a bf16 of 2^-126 times the code), times 2^126, times the row's scale.
+__device__ __forceinline__ uint32_t nvfp4_pair(uint32_t q, int j, uint32_t scale) {
+    const uint32_t a = (6 - 4 * j) >= 0 ? (q << (6 - 4 * j)) : (q >> (4 * j - 6));
+    const uint32_t b = q << (12 - 4 * j);
+    const uint32_t bits = (a & 0x01C001C0u) | (b & 0x80008000u);
+    uint32_t v, r;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(v) : "r"(bits), "r"(0x7E807E80u));   // 2^126
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(scale));
+    return r;
+}
+
+// One int4 / NVFP4 stage (128 rows x 128 k) of warp rw's two m16 tiles: d = fresh fp32 partials of the stage.
+// sb: the ring stage (weights in fragment order: [tile (8)][half (2)][lane (32)][4 words]); bb: the token block,
+// row stride brow. TWO: the item has more than 8 tokens (second n8 tile). NVFP4 (FMT 1): fsc = the lane's eight
+// E4M3 scales of the stage, byte (m * 2 + h) * 2 + (row g : 0, row g + 8 : 1) (each covers the lane's 16 k).
+template <int FMT, bool TWO>
+__device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, int brow, int rw, int lane, uint2 fsc,
+                                         float (&d)[4][4]) {
+    const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-    for (int hq = 0; hq < 4; ++hq) {
-        const uint4 q = *reinterpret_cast<const uint4*>(w + hq * 128 * 16);
-        uint32_t v[8];
-        qf::signed_w4(q.x, v + 0);
-        qf::signed_w4(q.y, v + 4);
-        qf::tmem_st8(ta + 16 * hq, v);
-        qf::signed_w4(q.z, v + 0);
-        qf::signed_w4(q.w, v + 4);
-        qf::tmem_st8(ta + 16 * hq + 8, v);
+    for (int j = 0; j < 4; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t* tb = bb + g * brow + h * 128 + t4 * 32;
+        const uint4 x0a = *reinterpret_cast<const uint4*>(tb), x0b = *reinterpret_cast<const uint4*>(tb + 16);
+        uint4 x1a = make_uint4(0u, 0u, 0u, 0u), x1b = x1a;
+        if constexpr (TWO) {
+            x1a = *reinterpret_cast<const uint4*>(tb + 8 * brow);
+            x1b = *reinterpret_cast<const uint4*>(tb + 8 * brow + 16);
+        }
+        const uint32_t xw0[8] = {x0a.x, x0a.y, x0a.z, x0a.w, x0b.x, x0b.y, x0b.z, x0b.w};
+        const uint32_t xw1[8] = {x1a.x, x1a.y, x1a.z, x1a.w, x1b.x, x1b.y, x1b.z, x1b.w};
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+            const uint4 a = *reinterpret_cast<const uint4*>(sb + (((2 * rw + m) * 2 + h) * 32 + lane) * 16);
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+            uint32_t sA = 0u, sB = 0u;
+            if constexpr (FMT == 1) {
+                const uint32_t ws = (m == 0 ? fsc.x : fsc.y) >> (16 * h);
+                sA = qf::e4m3_scale_bf16x2(ws & 0xFFu);
+                sB = qf::e4m3_scale_bf16x2((ws >> 8) & 0xFFu);
+            }
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                // A registers of step s: (row g, k+0|1) (row g+8, k+0|1) (row g, k+2|3) (row g+8, k+2|3) = the
+                // word's nibble pairs (0,4) (1,5) (2,6) (3,7)
+                uint32_t v[4];
+                if constexpr (FMT == 0) {
+                    qf::signed_w4(aw[s], v);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[j] = nvfp4_pair(aw[s], j, (j & 1) ? sB : sA);
+                }
+                qf::mma_bf16(d[2 * m], v[0], v[1], v[2], v[3], xw0[2 * s], xw0[2 * s + 1]);
+                if constexpr (TWO) qf::mma_bf16(d[2 * m + 1], v[0], v[1], v[2], v[3], xw1[2 * s], xw1[2 * s + 1]);
+            }
+        }
     }
 }
 
-// NVFP4: this thread's row of a stage (e2m1 codes in the int4 word layout) -> TMEM columns ta .. ta + 63 as bf16
-// code * group scale (exact); sc = the row's eight E4M3 scales of the stage (group g = byte g: word j of quad q
-// covers k 32q + 8j .. +8, group 2q + j / 2).
-__device__ __forceinline__ void stage_nvfp4_to_tmem(const uint8_t* w, uint32_t ta, uint2 sc) {
+// One bf16 stage (128 rows x 32 k, [tile (8)][step (2)][lane (32)][8 elements] = the A registers of each k16 step)
+// of warp rw's two m16 tiles; token block row stride BROW_BF, the lane's 8 k = 8 t4 .. 8 t4 + 7 of each token.
+template <bool TWO>
+__device__ __forceinline__ void stage_bf16(const uint8_t* sb, const uint8_t* bb, int rw, int lane, float (&d)[4][4]) {
+    const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-    for (int hq = 0; hq < 4; ++hq) {
-        const uint4 q = *reinterpret_cast<const uint4*>(w + hq * 128 * 16);
-        const uint32_t sw = (hq < 2 ? sc.x : sc.y) >> (16 * (hq & 1));
-        const uint32_t s0 = qf::e4m3_scale_bf16x2(sw & 0xFFu), s1 = qf::e4m3_scale_bf16x2((sw >> 8) & 0xFFu);
-        uint32_t v[8];
-        qf::nvfp4_w4(q.x, s0, v + 0);
-        qf::nvfp4_w4(q.y, s0, v + 4);
-        qf::tmem_st8(ta + 16 * hq, v);
-        qf::nvfp4_w4(q.z, s1, v + 0);
-        qf::nvfp4_w4(q.w, s1, v + 4);
-        qf::tmem_st8(ta + 16 * hq + 8, v);
-    }
+    for (int j = 0; j < 4; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.f;
+    const uint4 x0 = *reinterpret_cast<const uint4*>(bb + g * BROW_BF + t4 * 16);
+    const uint4 x1 = TWO ? *reinterpret_cast<const uint4*>(bb + (8 + g) * BROW_BF + t4 * 16) : make_uint4(0u, 0u, 0u, 0u);
+    const uint32_t xw0[4] = {x0.x, x0.y, x0.z, x0.w}, xw1[4] = {x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+            const uint4 a = *reinterpret_cast<const uint4*>(sb + (((2 * rw + m) * 2 + s) * 32 + lane) * 16);
+            qf::mma_bf16(d[2 * m], a.x, a.y, a.z, a.w, xw0[2 * s], xw0[2 * s + 1]);
+            if constexpr (TWO) qf::mma_bf16(d[2 * m + 1], a.x, a.y, a.z, a.w, xw1[2 * s], xw1[2 * s + 1]);
+        }
 }
 
 // Shared-expert gate logit of one token, x[t] . w_gate in fp32: lane-strided fma chain over 16-byte chunks, then an
@@ -530,16 +584,12 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     const int vw = warp - vp * VP_WARPS;   // role within the pipeline: 0..3 consumers, VP_PRODUCER, VP_MMA
     uint8_t* vb = smem + vp * VP_BYTES;
     uint8_t* ring = vb + VO_RING;
-    uint8_t* bst = vb + VO_BST;
     uint64_t* full = reinterpret_cast<uint64_t*>(vb + VO_BAR);
     uint64_t* empty = full + NST;
     uint64_t* efull = empty + NST;
     uint64_t* eempty = efull + NEPI;
-    uint64_t* abr = eempty + NEPI;      // [NBUF] A/B of a pipelined stage written (the consumer warps arrive)
-    uint64_t* mmab = abr + NBUF;        // [NBUF] the stage's mmas completed (tcgen05.commit)
     StageDesc* desc = reinterpret_cast<StageDesc*>(vb + VO_DESC);
     EpiRec* epi = reinterpret_cast<EpiRec*>(vb + VO_EPI);
-    MmaJob* jobs = reinterpret_cast<MmaJob*>(vb + VO_JOB);
 
     if (tid == 0) {
         for (int v = 0; v < NVP; ++v) {
@@ -552,17 +602,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 qf::mbar_init(f + 2 * NST + i, NCW);          // efull
                 qf::mbar_init(f + 2 * NST + NEPI + i, 1);     // eempty
             }
-            for (int i = 0; i < NBUF; ++i) {
-                qf::mbar_init(f + 2 * NST + 2 * NEPI + i, NCW);        // abr
-                qf::mbar_init(f + 2 * NST + 2 * NEPI + NBUF + i, 1);   // mmab
-            }
         }
         qf::mbar_fence_init();
         misc[MISC_DBGN] = 0;
-    }
-    if (warp == 0) {   // tensor memory: one warp allocates the SM's 512 columns; pipeline v uses [160 v, 160 v + 160)
-        qf::tmem_alloc(reinterpret_cast<uint32_t*>(misc + MISC_TMEM), TM_COLS);
-        qf::tmem_relinquish();
     }
     // fused router: this CTA's router rows (load-time constants) are requested before the wait on the previous
     // kernel; CTA c owns rows [c rpc, c rpc + rpc)
@@ -702,8 +744,6 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         __syncthreads();
     }
     qf::pdl_launch_dependents();
-    const uint32_t tmem_all = (uint32_t)misc[MISC_TMEM];
-    const uint32_t tmem = tmem_all + TM_VP * (uint32_t)vp;   // this pipeline's slice
 
     const Layout& L = *reinterpret_cast<const Layout*>(plan + PLAN_LAYOUT);
 
@@ -758,6 +798,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
         if (lane == 0) {
             // ========================================================== producer (one thread)
             const uint64_t pol = qf::policy_evict_first();
+            // the copy engine reads x (possibly staged by this launch's own threads) and, later, rows other CTAs wrote:
+            // order this thread's view of them (acquired at the barriers and counters) before its copies
+            qf::fence_proxy_async();
             int st = 0;
             uint32_t ph = 0;
             int next = first_item;
@@ -868,6 +911,42 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 } else {
                     d.kc = 0;
                 }
+                // the k-slice of the item's token rows rides in every stage (token block at STAGE_TOK): the shared
+                // expert's consecutive rows as one tensor copy (rows beyond M read zeros), a routed expert's rows one
+                // by one (row stride BROW_W4) or, from GATHER_MIN rows, in 4-row gathers (stride BROW_G4; a partial
+                // last group repeats its last row). Rows beyond the item's tokens hold stale data: the mma columns
+                // they feed are never read.
+                const bool w4k = kind == K_G1 || kind == K_G2;
+                const bool g4 = w4k && ntok >= GATHER_MIN;
+                if (bytes != 0) {
+                    if (kind == K_S1 || kind == K_S2) bytes += (uint32_t)(p.tok_box * BF_KC * 2);
+                    else bytes += (uint32_t)((g4 ? (ntok + 3) / 4 * 4 : ntok) * W4_KC * 2);
+                }
+                auto copy_tokens = [&](uint8_t* sb, int kidx) {
+                    uint8_t* tb = sb + STAGE_TOK;
+                    if (kind == K_S1) {
+                        qf::tma_tile_2d(tb, &p.xt, split * (p.H / NSPLIT) + kidx * BF_KC, TG * tg, full + st);
+                    } else if (kind == K_S2) {
+                        qf::tma_tile_2d(tb, &p.ht, kidx * BF_KC, TG * tg, full + st);
+                    } else if (!g4) {
+                        for (int n = 0; n < ntok; ++n)
+                            qf::bulk_g2s(tb + n * BROW_W4, token_row(p, d, toff, tlist, n) + (size_t)kidx * W4_KC,
+                                         W4_KC * 2, full + st);
+                    } else {
+                        const void* map = kind == K_G1 ? static_cast<const void*>(&p.xg) : static_cast<const void*>(&p.hg);
+                        const int x0 = (kind == K_G1 ? split * (p.H / G1_SPLIT) : 0) + kidx * W4_KC;
+                        const int16_t* tl = tlist + toff[u] + TG * tg;
+                        for (int n0 = 0; n0 < ntok; n0 += 4) {
+                            int r[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const int sl = tl[min(n0 + j, ntok - 1)];
+                                r[j] = kind == K_G1 ? sl / p.topk : sl;
+                            }
+                            qf::tma_gather4(tb + n0 * BROW_G4, map, x0, r[0], r[1], r[2], r[3], full + st);
+                        }
+                    }
+                };
                 for (int kidx = 0; kidx < nk; ++kidx) {
                     if (!qf::mbar_wait(empty + st, ph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
                     uint8_t* sb = ring + st * STAGE_BYTES;
@@ -875,16 +954,21 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     if (bytes == 0) {
                         qf::mbar_arrive(full + st);
                     } else if (kidx == 0 && dep_idx >= 0) {
-                        // weights first; the stage is marked full (arrive) only after the item's inputs are acquired
+                        // weights first; the token rows (the item's inputs, written by other CTAs) are copied, and the
+                        // stage is marked full (arrive), only after the inputs are acquired; the proxy fence orders
+                        // the copy engine's reads after that acquire
                         qf::mbar_expect_tx(full + st, bytes);
                         qf::bulk_g2s_hint(sb, wsrc, STAGE_W, full + st, pol);
                         if (ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, ssrc, STAGE_S, full + st, pol);
                         wait_counter(ctrl, dep_idx, dep_target);
+                        qf::fence_proxy_async();
+                        copy_tokens(sb, kidx);
                         qf::mbar_arrive(full + st);
                     } else {
                         qf::mbar_arrive_expect_tx(full + st, bytes);
                         qf::bulk_g2s_hint(sb, wsrc, STAGE_W, full + st, pol);
                         if (ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, ssrc, STAGE_S, full + st, pol);
+                        copy_tokens(sb, kidx);
                     }
                     wsrc += STAGE_W;
                     if (ssrc != nullptr) ssrc += W4_KC;
@@ -894,56 +978,16 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             }
         }
         __syncwarp();
-    } else if (vw == VP_MMA) {
-        // ============================================================== MMA issuer (one lane issues)
-        // stage s uses buffer s % NBUF, its (s / NBUF)-th use. Descriptors advance by constants: one k16 step is
-        // 2 chunks of B (512 B, +32 in the 16-byte address field), 8 columns of an A tile in TMEM, or 2 chunks of a
-        // bf16 A stage (4096 B, +256).
-        const uint64_t bdesc0 = qf::smem_desc(bst, 256, 128);
-        const uint64_t adesc0 = qf::smem_desc(ring, 2048, 128);
-        for (uint32_t s = 0;; ++s) {
-            const int b = (int)(s & 1u);
-            if (!qf::mbar_wait(abr + b, (s >> 1) & 1u, PIPE_WAIT_NS)) {
-                set_err(ctrl, QF_MOE_ERR_PIPELINE);
-                break;
-            }
-            const MmaJob job = jobs[b];
-            if (job.kind == K_STOP) break;
-            if (lane == 0) {
-                qf::tc_fence_after();
-                const uint64_t bd = bdesc0 + (uint64_t)(b * (BST_BYTES >> 4));
-                const uint32_t dcol = tmem + TM_D + 16 * b;
-                if (job.kind == K_G1 || job.kind == K_G2) {
-                    const uint32_t ta = tmem + TM_A + 64 * b;
-#pragma unroll
-                    for (int j = 0; j < W4_KC / 16; ++j) qf::mma_ts(dcol, ta + 8 * j, bd + 32 * j, IDESC, j != 0);
-                } else {
-                    const uint64_t ad = adesc0 + (uint64_t)(job.ring * (STAGE_BYTES >> 4));
-#pragma unroll
-                    for (int j = 0; j < BF_KC / 16; ++j) qf::mma_ss(dcol, ad + 256 * j, bd + 32 * j, IDESC, j != 0);
-                }
-                qf::mma_commit(mmab + b);
-            }
-            __syncwarp();
-        }
     } else {
-        // ============================================================== consumers (one warpgroup per pipeline)
-        // A warp reaches only the TMEM lanes of its hardware quarter (warp index % 4): pipeline 1's consumer warps
-        // (6..9) own quarters 2, 3, 0, 1. Rows follow the quarter; ctid is just a unique index within the group.
+        // ============================================================== consumers (4 warps per pipeline)
+        // Warp rw owns the m16 tiles 2 rw, 2 rw + 1 of every 128-row stage; acc[2 m + n][i] = row 16 (2 rw + m) + g +
+        // 8 (i / 2) of the item's tile, token 8 n + 2 t4 + (i % 2) (see stage_w4).
         const int rw = vw;                    // 0..3: consumer warp within the pipeline
-        const int q4 = warp & 3;              // TMEM lane quarter
         const int ctid = rw * 32 + lane;      // 0..127
-        const int row = 32 * q4 + lane;       // tile row (= TMEM lane) owned by this thread
-        const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
-        const int woff = row * 16;
-        const int soff = STAGE_W + row * 2;
-        const uint32_t ta0 = tmem + lane_base + TM_A;
-        const uint32_t td0 = tmem + lane_base + TM_D;
+        const int g = lane >> 2, t4 = lane & 3;
         int st = 0, es = 0;
         uint32_t ph = 0, eph = 0;
-        uint32_t mcount = 0;    // pipelined stages so far (identical in the pipeline's consumer threads)
-        uint32_t mph = 0;       // bit b: phase of mmab[b] at its next wait
-        float acc[16];          // this thread's row, tokens 0..15
+        float acc[4][4];
         // optional timeline: (globaltimer << 12) | tag in the CTA's first 31 entries, tag = event | pipeline << 5;
         // events: 1..7 an item of that kind starts (its first stage is in the ring), 16 + kind its stages are done,
         // DBG_CONSUMERS the pipeline's consumers start (routing plan built), DBG_STOP they stop
@@ -966,96 +1010,39 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             if (lane == 0) qf::mbar_arrive(efull + es);
             if (++es == NEPI) { es = 0; eph ^= 1u; }
         };
-        // wait for the mmas of the stage in buffer bq; free its ring slot (bf16 stages: the A operand lives there)
-        // and add its partial, times sc, for all 16 token columns (columns beyond the item's tokens hold zeros: their
-        // B rows were zero-filled)
-        auto retire = [&](int bq, int ring_slot, float sc) {
-            if (!qf::mbar_wait(mmab + bq, (mph >> bq) & 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
-            mph ^= 1u << bq;
-            qf::tc_fence_after();
-            if (ring_slot >= 0) {
-                __syncwarp();
-                if (lane == 0) qf::mbar_arrive(empty + ring_slot);
-            }
-            uint32_t v[16];
-            qf::tmem_ld16(td0 + 16 * bq, v);
-            qf::tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = fmaf(__uint_as_float(v[i]), sc, acc[i]);
-            qf::tc_fence_before();
-        };
-        // this thread's token chunks of an item's stages: int4 stages have 16 tokens x 16 chunks (two per thread:
-        // tokens t/16 and 8 + t/16, chunk t % 16), bf16 stages 16 x 4 (threads 0..63: token t/4, chunk t % 4);
-        // sources advance by one stage's k per stage, a token beyond the item reads zeros (zero-fill copy)
-        struct XChunks {
-            const char* src0;
-            const char* src1;
-            uint32_t n0, n1;
-            int step0, step1, dst;
-            bool act, two;
-        };
-        auto xchunks = [&](const StageDesc& dd) {
-            XChunks c;
-            const bool w4d = dd.kind == K_G1 || dd.kind == K_G2;
-            const int lg = w4d ? 4 : 2;
-            const int xn = ctid >> lg, xc = ctid & ((1 << lg) - 1);
-            c.act = xn < TG;
-            c.two = w4d;
-            c.dst = (xc * TG + xn) * 16;
-            const __nv_bfloat16* r0 = token_row(p, dd, toff, tlist, xn);
-            const __nv_bfloat16* r1 = w4d ? token_row(p, dd, toff, tlist, xn + 8) : nullptr;
-            c.src0 = r0 != nullptr ? reinterpret_cast<const char*>(r0 + 8 * xc) : reinterpret_cast<const char*>(p.x);
-            c.src1 = r1 != nullptr ? reinterpret_cast<const char*>(r1 + 8 * xc) : reinterpret_cast<const char*>(p.x);
-            c.n0 = r0 != nullptr ? 16u : 0u;
-            c.n1 = r1 != nullptr ? 16u : 0u;
-            c.step0 = r0 != nullptr ? dd.kc * 2 : 0;
-            c.step1 = r1 != nullptr ? dd.kc * 2 : 0;
-            return c;
-        };
-        auto xissue = [&](const XChunks& c, int b) {
-            if (c.act) qf::cp_async16(bst + b * BST_BYTES + c.dst, c.src0, c.n0);
-            if (c.two) qf::cp_async16(bst + b * BST_BYTES + c.dst + 8 * 16, c.src1, c.n1);
-        };
-        bool pre = false;   // this thread already copied the current item's first token chunks
-        // stop the MMA warp (its next stage is mcount; nothing of this pipeline is in flight)
-        auto stop_mma = [&]() {
-            qf::cp_async_wait_all();
-            const int bq = (int)(mcount & 1u);
-            if (ctid == 0) jobs[bq].kind = (int16_t)K_STOP;
+        // the ring slot of a consumed stage goes back to the producer (each warp arrives once it read its part)
+        auto release = [&](int slot) {
             __syncwarp();
-            if (lane == 0) qf::mbar_arrive(abr + bq);
+            if (lane == 0) qf::mbar_arrive(empty + slot);
         };
+        auto pipelined = [](int kind) { return kind == K_G1 || kind == K_G2 || kind == K_S1 || kind == K_S2; };
         for (;;) {
-            if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
+            // the item's first stage: every consumer thread of the pipeline takes the same decision (a wait that
+            // ran out in one thread ends the pipeline in all of them)
+            const bool got = qf::mbar_wait(full + st, ph, PIPE_WAIT_NS);
+            if (!qf::named_bar_and(1 + vp, CONS_THREADS, got)) {
                 set_err(ctrl, QF_MOE_ERR_PIPELINE);
-                stop_mma();
                 signal(-2, 0);
                 break;
             }
             const StageDesc d = desc[st];
             if (d.kind == K_STOP) {
                 stamp(DBG_STOP);
-                stop_mma();
                 signal(-2, 0);
                 break;
             }
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+            for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
             stamp(d.kind);
             const bool w4 = d.kind == K_G1 || d.kind == K_G2;
-            if (w4 || d.kind == K_S1 || d.kind == K_S2) {
+            if (pipelined(d.kind)) {
                 // ---------------------------------------------------------------- pipelined item: nk stages
+                // each warp runs through the stages on its own (a stage arrives whole: weights, scales, token rows)
                 const int nk = d.nk;
-                XChunks xc = xchunks(d);
-                int bcur = (int)(mcount & 1u);
-                if (!pre) xissue(xc, bcur);
-                pre = false;
-                // the previous pipelined stage of this item (its mmas may still run): buffer, ring slot, scale
-                bool pend = false;
-                int pb = 0, pr = -1;
-                float psc = 0.f;
-                bool failed = false;
-                // NVFP4: this row's E4M3 scales of the item's stages (1 KB per stage), one stage loaded ahead
+                const bool two = d.ntok > 8;
+                const int brow = d.ntok >= GATHER_MIN ? BROW_G4 : BROW_W4;   // the producer's choice for int4 stages
+                bool ok = true;
+                // NVFP4: this lane's E4M3 scales of the item's stages (1 KB per stage), one stage loaded ahead
                 const uint8_t* fsrc = nullptr;
                 uint2 scl = make_uint2(0u, 0u);
                 if constexpr (FMT == 1) {
@@ -1063,82 +1050,71 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                         const bool down = d.kind == K_G2;
                         const int K = down ? p.I : p.H, N = down ? p.H : 2 * p.I;
                         fsrc = (down ? p.f2 : p.f13) + (size_t)(ulist[d.u] - p.wofs) * ((size_t)N * K / 16) +
-                               (size_t)d.tile * (8 * (size_t)K) + (size_t)d.split * d.nk * 1024 + row * 8;
+                               (size_t)d.tile * (8 * (size_t)K) + (size_t)d.split * d.nk * 1024 + ctid * 8;
                         scl = __ldg(reinterpret_cast<const uint2*>(fsrc));
                     }
                 }
                 for (int kidx = 0;;) {
-                    // buffer bcur was last read by the mmas of stage mcount - 2, already retired
                     const uint8_t* sb = ring + st * STAGE_BYTES;
-                    float sc = 1.f;
+                    const uint8_t* bb = sb + STAGE_TOK;
+                    float dd[4][4];
                     if (w4) {
                         if constexpr (FMT == 0) {
-                            stage_w4_to_tmem(sb + woff, ta0 + 64 * bcur);
-                            sc = bf16_bits(*reinterpret_cast<const uint16_t*>(sb + soff));
-                        } else {
-                            stage_nvfp4_to_tmem(sb + woff, ta0 + 64 * bcur, scl);
-                            if (kidx + 1 < nk) scl = __ldg(reinterpret_cast<const uint2*>(fsrc + (size_t)(kidx + 1) * 1024));
-                        }
-                    }
-                    qf::cp_async_wait_all();
-                    qf::fence_proxy_async_smem();   // the tensor cores read bst through the async proxy
-                    if (w4) qf::tmem_wait_st();
-                    qf::tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (w4) qf::mbar_arrive(empty + st);   // the stage now lives in TMEM (bf16: read by the mmas)
-                        if (ctid == 0) {
-                            MmaJob j;
-                            j.kind = (int16_t)d.kind;
-                            j.ring = (int16_t)st;
-                            jobs[bcur] = j;
-                        }
-                        qf::mbar_arrive(abr + bcur);
-                    }
-                    if (pend) retire(pb, pr, psc);
-                    pend = true; pb = bcur; pr = w4 ? -1 : st; psc = sc;
-                    ++mcount;
-                    bcur ^= 1;
-                    if (++st == NST) { st = 0; ph ^= 1u; }
-                    if (++kidx == nk) {
-                        // buffer bcur is free (its stage was just retired) and is the next item's first buffer: if
-                        // that item's first stage is already in the ring, copy its first token chunks now, so that
-                        // the copy's L2 round trip overlaps this item's last retire and epilogue
-                        if (qf::mbar_test_wait(full + st, ph)) {
-                            const StageDesc dn = desc[st];
-                            if (dn.kind == K_G1 || dn.kind == K_G2 || dn.kind == K_S1 || dn.kind == K_S2) {
-                                xissue(xchunks(dn), bcur);
-                                pre = true;
+                            // the group-128 scales of rows (g, g + 8) of tiles 2 rw, 2 rw + 1
+                            const uint2 sc = *reinterpret_cast<const uint2*>(sb + STAGE_W + (rw * 8 + g) * 8);
+                            if (two) stage_w4<0, true>(sb, bb, brow, rw, lane, sc, dd);
+                            else stage_w4<0, false>(sb, bb, brow, rw, lane, sc, dd);
+                            release(st);
+                            const float sr[4] = {bf16_lo(sc.x), bf16_hi(sc.x), bf16_lo(sc.y), bf16_hi(sc.y)};
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float s0 = sr[2 * (j >> 1)], s1 = sr[2 * (j >> 1) + 1];
+                                acc[j][0] = fmaf(dd[j][0], s0, acc[j][0]);
+                                acc[j][1] = fmaf(dd[j][1], s0, acc[j][1]);
+                                acc[j][2] = fmaf(dd[j][2], s1, acc[j][2]);
+                                acc[j][3] = fmaf(dd[j][3], s1, acc[j][3]);
                             }
+                        } else {
+                            if (two) stage_w4<1, true>(sb, bb, brow, rw, lane, scl, dd);
+                            else stage_w4<1, false>(sb, bb, brow, rw, lane, scl, dd);
+                            release(st);
+                            if (kidx + 1 < nk) scl = __ldg(reinterpret_cast<const uint2*>(fsrc + (size_t)(kidx + 1) * 1024));
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) acc[j][i] += dd[j][i];
                         }
-                        break;
+                    } else {
+                        if (two) stage_bf16<true>(sb, bb, rw, lane, dd);
+                        else stage_bf16<false>(sb, bb, rw, lane, dd);
+                        release(st);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) acc[j][i] += dd[j][i];
                     }
-                    // buffer bcur is free again (its stage was just retired): copy the next stage's token chunks
-                    xc.src0 += xc.step0;
-                    xc.src1 += xc.step1;
-                    xissue(xc, bcur);
+                    if (++st == NST) { st = 0; ph ^= 1u; }
+                    if (++kidx == nk) break;
                     if (!qf::mbar_wait(full + st, ph, PIPE_WAIT_NS)) {
-                        set_err(ctrl, QF_MOE_ERR_PIPELINE);
-                        failed = true;
+                        ok = false;
                         break;
                     }
                 }
-                retire(pb, pr, psc);
-                stamp(16 + d.kind);
-                if (failed) {   // no mma of this pipeline is in flight any more: stop the MMA warp and the agent
-                    qf::cp_async_wait_all();
-                    stop_mma();
+                // the pipeline's consumer warps agree on the item's outcome before its epilogue
+                if (!qf::named_bar_and(1 + vp, CONS_THREADS, ok)) {
+                    set_err(ctrl, QF_MOE_ERR_PIPELINE);
                     signal(-2, 0);
                     break;
                 }
+                stamp(16 + d.kind);
             } else {
-                __syncwarp();
-                if (lane == 0) qf::mbar_arrive(empty + st);
+                release(st);
                 if (++st == NST) { st = 0; ph ^= 1u; }
             }
 
             // ------------------------------------------------------------ epilogues (item complete)
-            // acc[i] = row `row`, token i
+            // acc[2 m + n][i]: row 16 (2 rw + m) + g + 8 (i / 2) of the tile, token 8 n + 2 t4 + (i % 2); split
+            // partials are exchanged in this thread order (16 floats per thread, ctid-major)
             if (d.kind == K_GL) {
                 for (int tok = rw; tok < M; tok += NCW) {
                     const float a = gate_logit(p.x + (size_t)tok * p.H, p.wgate, p.H, lane);
@@ -1153,10 +1129,10 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     const int unit = (gpre[d.u] + d.tg) * L.R1 + d.tile;
                     uint32_t* cnt = reinterpret_cast<uint32_t*>(p.pbuf) + unit;
                     float* parts = p.pbuf + L.g1_part_off + (size_t)unit * G1_SPLIT * 2048;
-                    float* mine = parts + (size_t)d.split * 2048 + row * TG;
+                    float* mine = parts + (size_t)d.split * 2048 + ctid * 16;
 #pragma unroll
-                    for (int i = 0; i < 16; i += 4)
-                        __stcg(reinterpret_cast<float4*>(mine + i), make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
+                    for (int j = 0; j < 4; ++j)
+                        __stcg(reinterpret_cast<float4*>(mine + 4 * j), make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]));
                     __threadfence();
                     qf::named_bar(1 + vp, CONS_THREADS);
                     volatile int* gflag = reinterpret_cast<volatile int*>(vb + VO_FLAG);
@@ -1175,29 +1151,27 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
 #pragma unroll
                     for (int sp = 0; sp < G1_SPLIT; ++sp) {
                         if (sp == d.split || sp >= L.g1s) continue;
-                        const float* other = parts + (size_t)sp * 2048 + row * TG;
+                        const float* other = parts + (size_t)sp * 2048 + ctid * 16;
 #pragma unroll
-                        for (int i = 0; i < 16; i += 4) {
-                            const float4 q = __ldcg(reinterpret_cast<const float4*>(other + i));
-                            acc[i] += q.x; acc[i + 1] += q.y; acc[i + 2] += q.z; acc[i + 3] += q.w;
+                        for (int j = 0; j < 4; ++j) {
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(other + 4 * j));
+                            acc[j][0] += q.x; acc[j][1] += q.y; acc[j][2] += q.z; acc[j][3] += q.w;
                         }
                     }
                 }
                 if (d.kind == K_S1F) {
-                    const float* pb = p.pbuf + L.sh_off + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048 + row * TG;
+                    const float* pb = p.pbuf + L.sh_off + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT) * 2048 + ctid * 16;
 #pragma unroll
                     for (int sp = 0; sp < NSPLIT; ++sp) {   // fixed split order: the sum does not depend on timing
 #pragma unroll
-                        for (int i = 0; i < 16; i += 4) {
-                            const float4 q = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)sp * 2048 + i));
-                            acc[i] += q.x; acc[i + 1] += q.y; acc[i + 2] += q.z; acc[i + 3] += q.w;
+                        for (int j = 0; j < 4; ++j) {
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)sp * 2048 + 4 * j));
+                            acc[j][0] += q.x; acc[j][1] += q.y; acc[j][2] += q.z; acc[j][3] += q.w;
                         }
                     }
                 }
-                // rows interleave gate (even lane) and up (odd lane) of intermediate column j = row / 2; of the
-                // 16 tokens the even lane finishes 0..7, the odd lane 8..15
-                const bool odd = lane & 1;
-                const int col = 64 * d.tile + (row >> 1);
+                // fragment row g is gate row j = 64 tile + 8 (2 rw + m) + g, row g + 8 its up row: elements (0, 1)
+                // and (2, 3) of acc[2 m + n] are (gate, up) of tokens 8 n + 2 t4 and + 1
                 float gs = 1.f;
                 int tbase = 0;
                 if (d.kind == K_G1) {
@@ -1206,51 +1180,64 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     tbase = toff[d.u] + TG * d.tg;
                 }
 #pragma unroll
-                for (int ii = 0; ii < 8; ++ii) {
-                    // the even lane needs its partner's up of token ii, the odd lane its partner's gate of 8 + ii
-                    const float mine = odd ? acc[8 + ii] : acc[ii];
-                    const float theirs = __shfl_xor_sync(0xffffffffu, odd ? acc[ii] : acc[8 + ii], 1);
-                    const int n = odd ? 8 + ii : ii;
-                    const float g0 = odd ? theirs : mine, u0 = odd ? mine : theirs;
-                    if (n < d.ntok) {
-                        if (d.kind == K_G1) {
-                            const float gv = bf16r(bf16r(g0) * gs), uv = bf16r(bf16r(u0) * gs);
-                            p.hbuf[(size_t)tlist[tbase + n] * p.I + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
-                        } else {
-                            const float gv = bf16r(g0), uv = bf16r(u0);
-                            p.hsh[(size_t)(TG * d.tg + n) * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                for (int m = 0; m < 2; ++m) {
+                    const int col = 64 * d.tile + 8 * (2 * rw + m) + g;
+#pragma unroll
+                    for (int n = 0; n < 2; ++n)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int tok = 8 * n + 2 * t4 + h;
+                            if (tok >= d.ntok) continue;
+                            const float g0 = acc[2 * m + n][h], u0 = acc[2 * m + n][2 + h];
+                            if (d.kind == K_G1) {
+                                const float gv = bf16r(bf16r(g0) * gs), uv = bf16r(bf16r(u0) * gs);
+                                p.hbuf[(size_t)tlist[tbase + tok] * p.I + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                            } else {
+                                const float gv = bf16r(g0), uv = bf16r(u0);
+                                p.hsh[(size_t)(TG * d.tg + tok) * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
+                            }
                         }
-                    }
                 }
                 signal(d.kind == K_G1 ? C_DONE + d.u : C_SDONE + d.tg, 1);
             } else if (d.kind == K_S1) {
-                float* pb = p.pbuf + L.sh_off + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048 + row * TG;
+                float* pb = p.pbuf + L.sh_off + (size_t)((d.tile * L.ngs + d.tg) * NSPLIT + d.split) * 2048 + ctid * 16;
 #pragma unroll
-                for (int i = 0; i < 16; i += 4)
-                    __stcg(reinterpret_cast<float4*>(pb + i), make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]));
+                for (int j = 0; j < 4; ++j)
+                    __stcg(reinterpret_cast<float4*>(pb + 4 * j), make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]));
                 signal(C_SPLIT + d.tile * L.ngs + d.tg, 1);
             } else if (d.kind == K_G2) {
                 const int u = d.u, e = ulist[u];
                 const float g2 = p.gs2 ? bf16_bits(p.gs2[e - p.wofs]) : 1.f;
-                const int n0 = 128 * d.tile + row;
                 const int tbase = toff[u] + TG * d.tg;
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    if (i < d.ntok) {
-                        const float v = bf16r(acc[i]);
-                        // the token's first slot routed to e, then any later slot of the same token with e again
-                        for (int s = tlist[tbase + i]; s >= 0; s = dupn[s]) {
-                            const float w = bf16r(g2 * tws[s]);
-                            p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v * w);
+                for (int m = 0; m < 2; ++m)
+#pragma unroll
+                    for (int n = 0; n < 2; ++n)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int tok = 8 * n + 2 * t4 + (i & 1);
+                            if (tok >= d.ntok) continue;
+                            const int n0 = 128 * d.tile + 16 * (2 * rw + m) + g + 8 * (i >> 1);
+                            const float v = bf16r(acc[2 * m + n][i]);
+                            // the token's first slot routed to e, then any later slot of the same token with e again
+                            for (int s = tlist[tbase + tok]; s >= 0; s = dupn[s]) {
+                                const float w = bf16r(g2 * tws[s]);
+                                p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v * w);
+                            }
                         }
-                    }
-                }
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_S2) {
-                const int n0 = 128 * d.tile + row;
 #pragma unroll
-                for (int i = 0; i < 16; ++i)
-                    if (i < d.ntok) p.sbuf[(size_t)(TG * d.tg + i) * p.H + n0] = __float2bfloat16(acc[i]);
+                for (int m = 0; m < 2; ++m)
+#pragma unroll
+                    for (int n = 0; n < 2; ++n)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int tok = 8 * n + 2 * t4 + (i & 1);
+                            if (tok >= d.ntok) continue;
+                            const int n0 = 128 * d.tile + 16 * (2 * rw + m) + g + 8 * (i >> 1);
+                            p.sbuf[(size_t)(TG * d.tg + tok) * p.H + n0] = __float2bfloat16(acc[2 * m + n][i]);
+                        }
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_CB) {
                 // the producer acquired every producer of this tile (and the gate logits) before publishing it
@@ -1263,10 +1250,6 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
 
     // ------------------------------------------------------------------ exit: the last CTA re-arms ctrl
     __syncthreads();
-    if (warp == 0) {   // every mma this CTA issued has completed (each commit was waited for)
-        qf::tc_fence_after();
-        qf::tmem_dealloc(tmem_all, TM_COLS);
-    }
     if (tid == 0) {
         __threadfence();
         misc[MISC_FLAG] = atomicAdd(ctrl + C_EXIT, 1u) == gridDim.x - 1;
@@ -1289,46 +1272,55 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
 }
 
 // ------------------------------------------------------------------------------------------ weight repacking
-// Kernel layouts (one expert matrix [N, K]; see qwenfast_b200/formats.py for the same maps in torch):
-//   row order inside a 128-row tile r: plain -> 128r + lane; gate_up ("gated") -> even lane 2j = gate row 64r + j,
-//   odd lane 2j+1 = up row N/2 + 64r + j, so a SwiGLU pair sits in neighbouring lanes of one warp.
-//   int4 stage (128 k = one scale group, 8 KB): [half h (64 k)][quad q][lane (128)][4 words], word j of quad q
-//   holding k = 128st + 64h + 32q + 8j .. +8 with nibble i = k index [0,2,4,6,1,3,5,7][i]; scales [stage][lane].
-//   bf16 stage (32 k, 8 KB): [k chunk c (4)][lane (128)][8 elements] = the canonical K-major no-swizzle tile.
+// Kernel layouts (one expert matrix [N, K]; qwenfast_b200/formats.py computes the same maps with torch):
+//   128-row tiles; inside a tile, m16 tile m holds rows 16 m .. 16 m + 15 (plain), or for gate_up ("gated") gate rows
+//   64 r + 8 m + g at fragment rows g = 0..7 and the matching up rows N/2 + 64 r + 8 m + g at fragment rows 8 + g.
+//   int4 stage (128 k = one scale group, 8 KB): [m16 tile m (8)][64-k half h (2)][lane (32)][step s (4)] words; the
+//   word of lane (g, t4) holds rows A = 16 m + g and B = A + 8 at k = 128 st + 64 h + 16 t4 + 4 s + (0..3), nibbles
+//   0, 4, 2, 6 = A's k+0, k+1, k+2, k+3 and 1, 5, 3, 7 = B's (so pair j = nibbles (j, j + 4) is A register j of the
+//   mma step). Scales per stage: [consumer warp w (4)][g (8)][c (4)] bf16, row 16 (2 w + c / 2) + g + 8 (c % 2).
+//   bf16 stage (32 k, 8 KB): [m16 tile m (8)][step s (2)][lane (32)][8 elements], element 2 w + h of lane (g, t4) =
+//   row 16 m + g + 8 (w % 2), k = 32 st + 8 t4 + 4 s + 2 (w / 2) + h.
 __device__ __forceinline__ int kernel_row_to_src(int pos, int N, int gated) {
     if (!gated) return pos;
     const int r = pos >> 7, rho = pos & 127;
-    return (rho & 1) ? N / 2 + 64 * r + (rho >> 1) : 64 * r + (rho >> 1);
+    const int j = 64 * r + 8 * (rho >> 4) + (rho & 7);
+    return (rho & 8) ? N / 2 + j : j;
 }
 
-// word o of an expert's kernel-layout matrix -> (source row, source word along K)
-__device__ __forceinline__ void w4_word_src(long long o, int N, int K, int gated, int& row, int& kw) {
+// word o of an expert's int4 kernel-layout matrix -> its two source rows and the first of its four k
+__device__ __forceinline__ void w4_word_src(long long o, int N, int K, int gated, int& ra, int& rb, int& k0) {
     const long long per_tile = 128LL * K / 8;
     const int r = (int)(o / per_tile);
     const int ot = (int)(o - r * per_tile);
-    const int st = ot >> 11;
-    const int os = ot & 2047;
-    const int j = os & 3, rho = (os >> 2) & 127, hq = os >> 9;
-    kw = 16 * st + 8 * (hq >> 1) + 4 * (hq & 1) + j;
-    row = kernel_row_to_src(128 * r + rho, N, gated);
+    const int st = ot >> 11, os = ot & 2047;
+    const int s = os & 3, lane = (os >> 2) & 31, h = (os >> 7) & 1, m = os >> 8;
+    k0 = 128 * st + 64 * h + 16 * (lane & 3) + 4 * s;
+    ra = kernel_row_to_src(128 * r + 16 * m + (lane >> 2), N, gated);
+    rb = kernel_row_to_src(128 * r + 16 * m + (lane >> 2) + 8, N, gated);
 }
 
 __device__ __forceinline__ void w4_scale_src(long long o, int N, int K, int gated, int& row, int& grp) {
     const int r = (int)(o / K);
     const int ot = (int)(o - (long long)r * K);
     grp = ot >> 7;
-    row = kernel_row_to_src(128 * r + (ot & 127), N, gated);
+    const int e = ot & 127, w = e >> 5, g = (e >> 2) & 7, c = e & 3;
+    row = kernel_row_to_src(128 * r + 16 * (2 * w + (c >> 1)) + g + 8 * (c & 1), N, gated);
 }
 
-__device__ __forceinline__ uint32_t nib_perm(uint32_t v, bool forward) {
-    // forward: nibble i <- k index [0,2,4,6,1,3,5,7][i]; backward: inverse
-    const int fwd[8] = {0, 2, 4, 6, 1, 3, 5, 7};
+// four codes (k+0..k+3, low nibble first) of rows A and B -> the kernel word, and back
+__device__ __forceinline__ uint32_t w4_spread(uint32_t a, uint32_t b) {
+    const int pos[4] = {0, 4, 2, 6};   // nibble of k+j
     uint32_t o = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        if (forward) o |= ((v >> (4 * fwd[i])) & 0xFu) << (4 * i);
-        else o |= ((v >> (4 * i)) & 0xFu) << (4 * fwd[i]);
-    }
+    for (int j = 0; j < 4; ++j) o |= (((a >> (4 * j)) & 0xFu) << (4 * pos[j])) | (((b >> (4 * j)) & 0xFu) << (4 * pos[j] + 4));
+    return o;
+}
+__device__ __forceinline__ uint32_t w4_gather(uint32_t w, int rowb) {
+    const int pos[4] = {0, 4, 2, 6};
+    uint32_t o = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o |= ((w >> (4 * pos[j] + 4 * rowb)) & 0xFu) << (4 * j);
     return o;
 }
 
@@ -1339,11 +1331,19 @@ __global__ void w4_repack_kernel(const uint32_t* __restrict__ src, const uint16_
     const long long total = (long long)E * words;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
         const long long e = i / words, o = i - e * words;
-        int row, kw;
-        w4_word_src(o, N, K, gated, row, kw);
-        const long long si = e * words + (long long)row * (K / 8) + kw;
-        if (!unpack) dst[i] = nib_perm(src[si], true);
-        else dst[si] = nib_perm(src[i], false);
+        int ra, rb, k0;
+        w4_word_src(o, N, K, gated, ra, rb, k0);
+        // the canonical half-words (four codes each) of rows A and B at k0
+        const long long ha = (e * words + (long long)ra * (K / 8) + k0 / 8) * 2 + ((k0 >> 2) & 1);
+        const long long hb = (e * words + (long long)rb * (K / 8) + k0 / 8) * 2 + ((k0 >> 2) & 1);
+        if (!unpack) {
+            const uint16_t* h = reinterpret_cast<const uint16_t*>(src);
+            dst[i] = w4_spread(h[ha], h[hb]);
+        } else {
+            uint16_t* h = reinterpret_cast<uint16_t*>(dst);
+            h[ha] = (uint16_t)w4_gather(src[i], 0);
+            h[hb] = (uint16_t)w4_gather(src[i], 1);
+        }
         if (o < ents) {
             int srow, grp;
             w4_scale_src(o, N, K, gated, srow, grp);
@@ -1363,9 +1363,10 @@ __global__ void bf16_repack_kernel(const uint16_t* __restrict__ src, uint16_t* _
         const int r = (int)(o / per_tile);
         const int ot = (int)(o - r * per_tile);
         const int st = ot >> 12, os = ot & 4095;
-        const int c = os >> 10, rho = (os >> 3) & 127, el = os & 7;
-        const int k = 32 * st + 8 * c + el;
-        const int row = kernel_row_to_src(128 * r + rho, N, gated);
+        const int el = os & 7, lane = (os >> 3) & 31, s = (os >> 8) & 1, m = os >> 9;
+        const int w = el >> 1, h = el & 1;
+        const int k = 32 * st + 8 * (lane & 3) + 4 * s + 2 * (w >> 1) + h;
+        const int row = kernel_row_to_src(128 * r + 16 * m + (lane >> 2) + 8 * (w & 1), N, gated);
         const long long si = (long long)row * K + k;
         if (!unpack) dst[o] = src[si];
         else dst[si] = src[o];
@@ -1514,7 +1515,7 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
         if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cudaFuncSetAttribute (carveout)");
         if (dev < 64) carveout_set[fmt][dev] = true;
     }
-    // Grid: one CTA per SM (three pipelines each; the CTA allocates all 512 tensor-memory columns). The item queue
+    // Grid: one CTA per SM (three pipelines each; the shared memory of one CTA fills the SM). The item queue
     // needs no co-residency (an item only waits for items claimed before it, by pipelines that are already running),
     // but the fused router's grid barriers (its logits; x copied from host memory) need every CTA resident at once:
     // that launch is cooperative, so the runtime either co-schedules the whole grid or refuses it (then this entry
@@ -1561,6 +1562,28 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
     if (fr && fr->x_stage) {   // x is pinned host memory (read by the kernel through its mapping); x_stage its copy
         p.xsrc = p.x;
         p.x = static_cast<const __nv_bfloat16*>(fr->x_stage);
+    }
+    // tensor maps of the token-row sources (the copy engine's view of x, hbuf and the shared expert's h)
+    {
+        qf::EncodeTiled enc = nullptr;
+        ce = qf::encode_tiled_fn(&enc);
+        if (ce != cudaSuccess) return qf::cuda_status(ce, "a16_moe_decode: cuTensorMapEncodeTiled entry point");
+        auto encode2d = [&](CUtensorMap* m, const void* base, int rows, int cols, int box_cols, int box_rows) {
+            const cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+            const cuuint64_t gstride[1] = {(cuuint64_t)cols * 2};
+            const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+            const cuuint32_t estr[2] = {1, 1};
+            return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        };
+        p.tok_box = M < TG ? M : TG;
+        CUresult cr = encode2d(&p.xt, p.x, M, H, BF_KC, p.tok_box);
+        if (cr == CUDA_SUCCESS) cr = encode2d(&p.xg, p.x, M, H, W4_KC, 1);
+        if (cr == CUDA_SUCCESS) cr = encode2d(&p.hg, p.hbuf, M * topk, I, W4_KC, 1);
+        if (cr == CUDA_SUCCESS && has_shw) cr = encode2d(&p.ht, p.hsh, M, Is, BF_KC, p.tok_box);
+        else if (!has_shw) p.ht = p.xt;   // no shared-expert down items read it
+        QF_REQUIRE(cr == CUDA_SUCCESS, "a16_moe_decode: cuTensorMapEncodeTiled failed (%d)", (int)cr);
     }
     if (fr != nullptr) {
         ce = qf::launch_coop(kern, dim3(sms * CTAS_PER_SM), dim3(MOE_THREADS), MOE_SMEM,

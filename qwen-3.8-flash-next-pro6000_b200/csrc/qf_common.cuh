@@ -2,6 +2,7 @@
 // wrappers, bounded waits, and the C-ABI error plumbing.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -27,6 +28,11 @@ cudaError_t launch_w8a8_tc(const int8_t* xq, const float* sx, const int8_t* q, c
 cudaError_t w8a8_tc_take_status(unsigned* out);
 // canonical [N, K] int8 <-> the W8A8 kernel layout (unpack = 1 for the inverse)
 cudaError_t launch_w8_repack(const int8_t* src, int8_t* dst, int N, int K, int unpack, cudaStream_t st);
+// cuTensorMapEncodeTiled through the runtime's driver entry point (resolved once per process)
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+cudaError_t encode_tiled_fn(EncodeTiled* fn);
 
 #define QF_REQUIRE(cond, ...)                                  \
     do {                                                       \
@@ -196,6 +202,24 @@ __device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32
         "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// ---- tensor copies (TMA engine, tiled): global -> shared through a tensor map (a __grid_constant__ parameter)
+// 2-D box at (x, y) (x in elements, x * element size a multiple of 16 bytes); rows outside the tensor read zeros.
+__device__ __forceinline__ void tma_tile_2d(void* dst, const void* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+// Four rows y0..y3 (any order) of a map whose box is one row high, columns from x: the rows land back to back.
+__device__ __forceinline__ void tma_gather4(void* dst, const void* map, int x, int y0, int y1, int y2, int y3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_u32(bar))
+        : "memory");
+}
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -207,6 +231,19 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 // ---- named barrier over a subset of warps (non-.aligned form: callers may arrive from divergent code)
 __device__ __forceinline__ void named_bar(int id, int threads) {
     asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+// Named barrier that also ANDs a predicate over its threads: every thread gets the same result.
+__device__ __forceinline__ bool named_bar_and(int id, int threads, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
 }
 // Arrive on a named barrier without waiting for it (the producer side of a one-way hand-off).
 __device__ __forceinline__ void named_bar_arrive(int id, int threads) {

@@ -33,8 +33,6 @@
 //     writes y. No run waits for another, so the grid need not be co-resident.
 //   * Every wait is bounded; a wait that runs out sets a bit of the sticky status word (qf_w8g_take_status) and
 //     the CTA drains (the affected outputs are undefined).
-#include <cuda.h>
-
 #include "qf_common.cuh"
 
 namespace {
@@ -381,24 +379,6 @@ __global__ void __launch_bounds__(G_THREADS, Cfg<NT>::MINB)
 
 __device__ unsigned g_w8g_err;
 
-using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-cudaError_t encode_tiled_fn(EncodeTiled* fn) {
-    static EncodeTiled cached = nullptr;
-    if (cached == nullptr) {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
-        if (e != cudaSuccess) return e;
-        if (q != cudaDriverEntryPointSuccess || f == nullptr) return cudaErrorNotSupported;
-        cached = reinterpret_cast<EncodeTiled>(f);
-    }
-    *fn = cached;
-    return cudaSuccess;
-}
-
 template <int NT>
 cudaError_t launch_w8g_tc(const CUtensorMap& map, const void* x, int ldx, const void* s, void* y, int ldy,
                           float* fixp, uint32_t* fixc, int M, int N, int K, int G, int t0, long long units, int sms,
@@ -441,6 +421,20 @@ cudaError_t launch_w8g_tc(const CUtensorMap& map, const void* x, int ldx, const 
 
 }  // namespace
 
+cudaError_t qf::encode_tiled_fn(EncodeTiled* fn) {
+    static EncodeTiled cached = nullptr;
+    if (cached == nullptr) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return e;
+        if (q != cudaDriverEntryPointSuccess || f == nullptr) return cudaErrorNotSupported;
+        cached = reinterpret_cast<EncodeTiled>(f);
+    }
+    *fn = cached;
+    return cudaSuccess;
+}
+
 extern "C" int qf_w8g_fixup_elems(int N, int64_t* elems) {
     QF_REQUIRE(elems && N >= 128 && N % 128 == 0, "w8g_fixup_elems: N must be a multiple of 128, got %d", N);
     int dev = 0;
@@ -475,8 +469,8 @@ extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const vo
     if (rc != QF_OK) return rc;
     QF_REQUIRE(fix_elems >= need, "w8g_gemm: the fixup buffer needs %lld floats, got %lld", (long long)need,
                (long long)fix_elems);
-    EncodeTiled enc = nullptr;
-    cudaError_t e = encode_tiled_fn(&enc);
+    qf::EncodeTiled enc = nullptr;
+    cudaError_t e = qf::encode_tiled_fn(&enc);
     if (e != cudaSuccess) return qf::cuda_status(e, "w8g_gemm: cuTensorMapEncodeTiled entry point");
     // the canonical weight as a 2-D tensor (K bytes per row); one box = one unit (64 k x 128 rows), 64-byte swizzle
     CUtensorMap map;

@@ -24,7 +24,7 @@ from . import formats
 from .ops import MoELayerWeights
 
 FORMAT = "qwenfast_b200.moe_layer"
-VERSION = 1
+VERSION = 2   # 2: int4 / bf16 / NVFP4 stages in mma fragment order
 _TENSORS = ("router", "w13", "s13", "w2", "s2", "w_gate", "sh_w13", "sh_w2")
 
 

@@ -6,14 +6,18 @@ Canonical (what a checkpoint loader holds, and the synthetic configurations' def
     dequantised weight ``(code - 8) * scale``.
 
 Kernel layout (one expert matrix [N, K]; ``gated`` for gate_up, where N = 2I rows are gate then up)
-    128-row tiles; inside tile r, lane (row slot) p holds row 128r + p (plain) or, for gate_up, gate row 64r + p/2
-    (even p) and up row N/2 + 64r + p/2 (odd p), so a SwiGLU pair sits in neighbouring lanes of one warp.
-    int4: each tile is a run of stages of 128 k (one scale group, 8 KB); a stage is [64-k half h][quad q][lane p]
-    [4 words], word j of quad q holding k = 128s + 64h + 32q + 8j .. +8 with nibble i = k index
-    [0,2,4,6,1,3,5,7][i], so one lop3 per bf16x2 pair yields natural k order and a warp's 16-byte loads are
-    contiguous. Scales: per stage [lane p] (128 bf16).
-bf16 (the shared expert): stages of 32 k laid out [k chunk c of 4][lane p][8 elements] -- the canonical K-major,
-    no-swizzle tensor-core tile (8-row core matrices of 16-byte rows), used directly as the MMA's A operand.
+    128-row tiles of eight m16 tiles (the tensor cores' m16n8k16 register fragments). Plain: m16 tile m of tile r
+    holds rows 128r + 16m .. +15. gate_up: its fragment rows g = 0..7 are gate rows 64r + 8m + g and rows 8 + g the
+    matching up rows N/2 + 64r + 8m + g, so one lane's fragment holds a whole SwiGLU pair.
+    int4: each tile is a run of stages of 128 k (one scale group, 8 KB); a stage is [m16 tile m][64-k half h]
+    [lane (32)][step s (4)] words. The word of lane (g, t4) holds rows A = 16m + g and B = A + 8 at the four k
+    128st + 64h + 16t4 + 4s + (0..3): nibbles 0, 4, 2, 6 are A's codes, 1, 5, 3, 7 B's, so nibble pair (j, j + 4)
+    is the mma's A register j after one lop3, and the lane's k run matches one 32-byte run of each token row.
+    Scales per stage: [consumer warp w (4)][g (8)][c (4)] bf16 = row 16(2w + c/2) + g + 8(c % 2).
+bf16 (the shared expert): stages of 32 k laid out [m16 tile m][step s (2)][lane][8 elements]: element 2w + h of lane
+    (g, t4) is row 16m + g + 8(w % 2) at k = 32st + 8t4 + 4s + 2(w // 2) + h -- the A registers of each k16 step.
+NVFP4: the e2m1 codes in the int4 layout; the E4M3 scales (one per 16 k) per stage [w][lane][8 bytes], byte
+    (mm * 2 + h) * 2 + ro = row 16(2w + mm) + g + 8 ro, group 8st + 4h + t4 (the lane's 16 k of that half).
 
 W8A8 weights (int8 [N, K]): contiguous 16 KB tiles [N/128][K/128][128 rows][128 B], each row's 16-byte k chunk c
     stored at position c ^ (row % 8) -- the K-major 128-byte-swizzle operand layout of the tensor cores.
@@ -27,7 +31,8 @@ import torch
 
 from . import _lib
 
-NIBBLE_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
+# kernel-word nibble i holds row B (i odd) or A (i even) at k offset KPOS[i] of the word's four k
+KPOS = (0, 0, 2, 2, 1, 1, 3, 3)
 
 
 # ------------------------------------------------------------------------------------------ canonical helpers
@@ -46,18 +51,6 @@ def unpack_int4(words: torch.Tensor) -> torch.Tensor:
     return q.reshape(*words.shape[:-1], words.shape[-1] * 8)
 
 
-def _nibble_perm(words: torch.Tensor, forward: bool) -> torch.Tensor:
-    v = words.to(torch.int64) & 0xFFFFFFFF
-    out = torch.zeros_like(v)
-    for i, src in enumerate(NIBBLE_ORDER):
-        if forward:
-            out |= ((v >> (4 * src)) & 0xF) << (4 * i)
-        else:
-            out |= ((v >> (4 * i)) & 0xF) << (4 * src)
-    out = torch.where(out >= 2 ** 31, out - 2 ** 32, out)
-    return out.to(torch.int32)
-
-
 # ----------------------------------------------------------------------------------------------- index maps
 def kernel_row_source(N: int, gated: bool, device=None) -> torch.Tensor:
     """Kernel row position -> source row."""
@@ -65,41 +58,49 @@ def kernel_row_source(N: int, gated: bool, device=None) -> torch.Tensor:
     if not gated:
         return p
     r, rho = p // 128, p % 128
-    return torch.where(rho % 2 == 0, 64 * r + rho // 2, N // 2 + 64 * r + rho // 2)
+    j = 64 * r + 8 * (rho // 16) + rho % 8
+    return torch.where((rho & 8) == 0, j, N // 2 + j)
 
 
-def w4_word_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
-    """Kernel-layout word o -> canonical word index row * (K/8) + kw, for one [N, K] matrix."""
+def w4_code_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
+    """Kernel-layout code (word o, nibble i), flattened o * 8 + i -> canonical code index row * K + k."""
     o = torch.arange(N * K // 8, device=device, dtype=torch.int64)
     per_tile = 128 * K // 8
     r, ot = o // per_tile, o % per_tile
     st, os_ = ot // 2048, ot % 2048
-    j, rho, hq = os_ & 3, (os_ >> 2) & 127, os_ >> 9
-    kw = 16 * st + 8 * (hq >> 1) + 4 * (hq & 1) + j
-    row = kernel_row_source(N, gated, device)[128 * r + rho]
-    return row * (K // 8) + kw
+    s, lane, h, m = os_ & 3, (os_ >> 2) & 31, (os_ >> 7) & 1, os_ >> 8
+    k0 = 128 * st + 64 * h + 16 * (lane & 3) + 4 * s
+    src = kernel_row_source(N, gated, device)
+    ra = src[128 * r + 16 * m + (lane >> 2)]
+    rb = src[128 * r + 16 * m + (lane >> 2) + 8]
+    i = torch.arange(8, device=device, dtype=torch.int64)
+    kpos = torch.tensor(KPOS, device=device, dtype=torch.int64)
+    row = torch.where((i & 1) == 0, ra[:, None], rb[:, None])
+    return (row * K + k0[:, None] + kpos[None, :]).reshape(-1)
 
 
 def w4_scale_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     """Kernel-layout scale entry o -> canonical index row * (K/128) + group."""
     o = torch.arange(N * K // 128, device=device, dtype=torch.int64)
     r, ot = o // K, o % K
-    st, rho = ot // 128, ot % 128
-    row = kernel_row_source(N, gated, device)[128 * r + rho]
+    st, e = ot // 128, ot % 128
+    w, g, c = e >> 5, (e >> 2) & 7, e & 3
+    row = kernel_row_source(N, gated, device)[128 * r + 16 * (2 * w + (c >> 1)) + g + 8 * (c & 1)]
     return row * (K // 128) + st
 
 
 def nvfp4_scale_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     """NVFP4 kernel-layout scale byte o -> canonical index row * (K/16) + group, for one [N, K] matrix: per 128-row
-    tile r and 128-k stage st, [lane p (128)][group g (8)] -- each kernel row's eight E4M3 scales of the stage
-    together, so one 8-byte load gives a thread its row's scales."""
+    tile r and 128-k stage st, [consumer warp w (4)][lane (32)][8 bytes], byte (mm * 2 + h) * 2 + ro = row
+    16(2w + mm) + g + 8 ro at 16-k group 8st + 4h + t4 -- one 8-byte load gives a lane every scale of its stage."""
     o = torch.arange(N * K // 16, device=device, dtype=torch.int64)
     per_tile = 128 * K // 16
     r, ot = o // per_tile, o % per_tile
     st, os_ = ot // 1024, ot % 1024
-    rho, g = os_ // 8, os_ % 8
-    row = kernel_row_source(N, gated, device)[128 * r + rho]
-    return row * (K // 16) + 8 * st + g
+    w, lane, b = os_ >> 8, (os_ >> 3) & 31, os_ & 7
+    mm, h, ro = b >> 2, (b >> 1) & 1, b & 1
+    row = kernel_row_source(N, gated, device)[128 * r + 16 * (2 * w + mm) + (lane >> 2) + 8 * ro]
+    return row * (K // 16) + 8 * st + 4 * h + (lane & 3)
 
 
 def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
@@ -108,9 +109,10 @@ def bf16_elem_map(N: int, K: int, gated: bool, device=None) -> torch.Tensor:
     per_tile = 128 * K
     r, ot = o // per_tile, o % per_tile
     st, os_ = ot >> 12, ot & 4095
-    c, rho, el = os_ >> 10, (os_ >> 3) & 127, os_ & 7
-    k = 32 * st + 8 * c + el
-    row = kernel_row_source(N, gated, device)[128 * r + rho]
+    el, lane, s, m = os_ & 7, (os_ >> 3) & 31, (os_ >> 8) & 1, os_ >> 9
+    w, h = el >> 1, el & 1
+    k = 32 * st + 8 * (lane & 3) + 4 * s + 2 * (w >> 1) + h
+    row = kernel_row_source(N, gated, device)[128 * r + 16 * m + (lane >> 2) + 8 * (w & 1)]
     return row * K + k
 
 
@@ -138,30 +140,52 @@ def _check_w4(qweight, scales):
 
 
 # ------------------------------------------------------------------------------------------ torch versions
+_CHUNK = 16   # experts per gather step of the torch repacks (bounds the temporary code tensors)
+
+
+def _codes_to_kernel(words: torch.Tensor, N: int, K: int, gated: bool) -> torch.Tensor:
+    """Canonical code words int32 [E, N*K/8] -> kernel-layout words int32 [E, N*K/8] (codes gathered)."""
+    E = words.shape[0]
+    cmap = w4_code_map(N, K, gated, words.device)
+    out = torch.empty(E, N * K // 8, dtype=torch.int32, device=words.device)
+    for e0 in range(0, E, _CHUNK):
+        codes = unpack_int4(words[e0:e0 + _CHUNK]).to(torch.uint8)
+        out[e0:e0 + _CHUNK] = pack_int4(codes[:, cmap].view(codes.shape[0], -1))
+    return out
+
+
+def _codes_to_canonical(wk: torch.Tensor, N: int, K: int, gated: bool) -> torch.Tensor:
+    """Inverse of ``_codes_to_kernel``."""
+    E = wk.shape[0]
+    cmap = w4_code_map(N, K, gated, wk.device)
+    out = torch.empty(E, N * K // 8, dtype=torch.int32, device=wk.device)
+    for e0 in range(0, E, _CHUNK):
+        codes = unpack_int4(wk[e0:e0 + _CHUNK]).to(torch.uint8)
+        canon = torch.empty_like(codes)
+        canon[:, cmap] = codes
+        out[e0:e0 + _CHUNK] = pack_int4(canon)
+    return out
+
+
 def repack_w4_torch(qweight: torch.Tensor, scales: torch.Tensor, gated: bool):
     E, N, K = _check_w4(qweight, scales)
-    wm = w4_word_map(N, K, gated, qweight.device)
-    sm = w4_scale_map(N, K, gated, qweight.device)
-    wk = _nibble_perm(qweight.reshape(E, -1)[:, wm], True)
-    sk = scales.reshape(E, -1)[:, sm]
+    wk = _codes_to_kernel(qweight.reshape(E, -1), N, K, gated)
+    sk = scales.reshape(E, -1)[:, w4_scale_map(N, K, gated, qweight.device)]
     return wk.contiguous(), sk.contiguous()
 
 
 def unpack_w4_torch(wk: torch.Tensor, sk: torch.Tensor, N: int, K: int, gated: bool):
     E = wk.shape[0]
-    wm = w4_word_map(N, K, gated, wk.device)
-    sm = w4_scale_map(N, K, gated, wk.device)
-    q = torch.empty(E, N * K // 8, dtype=torch.int32, device=wk.device)
-    q[:, wm] = _nibble_perm(wk, False)
+    q = _codes_to_canonical(wk, N, K, gated)
     s = torch.empty(E, N * K // 128, dtype=sk.dtype, device=sk.device)
-    s[:, sm] = sk
+    s[:, w4_scale_map(N, K, gated, sk.device)] = sk
     return q.view(E, N, K // 8), s.view(E, N, K // 128)
 
 
 def repack_nvfp4(wp: torch.Tensor, sf: torch.Tensor, gated: bool):
     """Canonical NVFP4 experts (the reference's checkpoint format: codes uint8 [E, N, K/2], even k in the low
     nibble; E4M3 scales [E, N, K/16]) -> the kernel layout on the tensors' device: the codes in the int4 layout
-    (int32 [E, N*K/8], read as eight codes per word with the lowest k in the low nibble), the scales uint8
+    (int32 [E, N*K/8]), the scales uint8
     [E, N*K/16] per ``nvfp4_scale_map``. Returns (wk, sk)."""
     if wp.dtype != torch.uint8 or wp.dim() != 3 or sf.dtype != torch.float8_e4m3fn:
         raise RuntimeError("NVFP4 experts need codes uint8 [E, N, K/2] and float8_e4m3fn scales [E, N, K/16]")
@@ -169,9 +193,8 @@ def repack_nvfp4(wp: torch.Tensor, sf: torch.Tensor, gated: bool):
     K = 2 * K2
     if tuple(sf.shape) != (E, N, K // 16) or N % 128 or K % 128:
         raise RuntimeError(f"NVFP4 scales must be [E, N, K/16] = {(E, N, K // 16)} with N, K multiples of 128")
-    words = wp.contiguous().view(torch.int32).view(E, N, K // 8)
-    wm = w4_word_map(N, K, gated, wp.device)
-    wk = _nibble_perm(words.reshape(E, -1)[:, wm], True)
+    words = wp.contiguous().view(torch.int32).view(E, N * K // 8)
+    wk = _codes_to_kernel(words, N, K, gated)
     sk = sf.contiguous().view(torch.uint8).reshape(E, -1)[:, nvfp4_scale_map(N, K, gated, wp.device)]
     return wk.contiguous(), sk.contiguous()
 
@@ -179,8 +202,7 @@ def repack_nvfp4(wp: torch.Tensor, sf: torch.Tensor, gated: bool):
 def unpack_nvfp4(wk: torch.Tensor, sk: torch.Tensor, N: int, K: int, gated: bool):
     """Inverse of ``repack_nvfp4`` (exact): (codes uint8 [E, N, K/2], scales float8_e4m3fn [E, N, K/16])."""
     E = wk.shape[0]
-    words = torch.empty(E, N * K // 8, dtype=torch.int32, device=wk.device)
-    words[:, w4_word_map(N, K, gated, wk.device)] = _nibble_perm(wk, False)
+    words = _codes_to_canonical(wk, N, K, gated)
     sf = torch.empty(E, N * K // 16, dtype=torch.uint8, device=sk.device)
     sf[:, nvfp4_scale_map(N, K, gated, sk.device)] = sk
     return words.view(torch.uint8).view(E, N, K // 2), sf.view(torch.float8_e4m3fn).view(E, N, K // 16)

@@ -14,7 +14,7 @@ def test_w4_round_trip(N, K, gated):
     wk, sk = formats.repack_w4_torch(q, s, gated)
     q2, s2 = formats.unpack_w4_torch(wk, sk, N, K, gated)
     assert torch.equal(q, q2) and torch.equal(s, s2)
-    assert torch.equal(formats.w4_word_map(N, K, gated).sort().values, torch.arange(N * K // 8))
+    assert torch.equal(formats.w4_code_map(N, K, gated).sort().values, torch.arange(N * K))
     assert torch.equal(formats.w4_scale_map(N, K, gated).sort().values, torch.arange(N * K // 128))
 
 
@@ -26,37 +26,54 @@ def test_bf16_round_trip(N, K, gated):
     assert torch.equal(formats.bf16_elem_map(N, K, gated).sort().values, torch.arange(N * K))
 
 
-def test_gate_up_rows_interleave_in_lanes():
+def test_gate_up_rows_pair_in_fragments():
     src = formats.kernel_row_source(256, True)
-    # tile 0: even lane 2j is gate row j, odd lane 2j+1 the matching up row 128 + j; tile 1 continues at gate row 64
-    assert src[:6].tolist() == [0, 128, 1, 129, 2, 130]
-    assert src[128:132].tolist() == [64, 192, 65, 193]
+    # tile 0, m16 tile 0: fragment rows 0..7 are gate rows 0..7, rows 8..15 the matching up rows 128..135; m16 tile 1
+    # continues at gate row 8; tile 1 starts at gate row 64
+    assert src[:16].tolist() == list(range(8)) + list(range(128, 136))
+    assert src[16:18].tolist() == [8, 9] and src[24:26].tolist() == [136, 137]
+    assert src[128:130].tolist() == [64, 65] and src[136] == 192
 
 
-def test_pack_unpack_int4_and_nibble_order():
+def test_pack_unpack_int4():
     codes = torch.randint(0, 16, (3, 5, 64))
     words = formats.pack_int4(codes)
     assert torch.equal(formats.unpack_int4(words).long(), codes)
-    # kernel nibble order: nibble i of a kernel word holds k = [0,2,4,6,1,3,5,7][i] of its eight
-    w = formats.pack_int4(torch.arange(8).view(1, 8))
-    p = formats._nibble_perm(w, True)
-    assert [(int(p) >> (4 * i)) & 0xF for i in range(8)] == [0, 2, 4, 6, 1, 3, 5, 7]
-    assert torch.equal(formats._nibble_perm(p, False), w)
 
 
-def test_stage_layout_positions():
-    # int4: a stage is 128 k x 128 rows = 2048 words [half h][quad q][lane p][word j], k = 128s + 64h + 32q + 8j
-    N, K = 128, 256
-    wm = formats.w4_word_map(N, K, False)
-    s, h, q, p, j = 1, 1, 1, 5, 2
-    o = 2048 * s + 512 * (2 * h + q) + 4 * p + j
-    assert int(wm[o]) == p * (K // 8) + (16 * s + 8 * h + 4 * q + j)
-    # scales: [stage][lane]
-    sm = formats.w4_scale_map(N, K, False)
-    assert int(sm[128 * 1 + 5]) == 5 * (K // 128) + 1
-    # bf16: a stage is 32 k x 128 rows [chunk c][lane p][8 elements], k = 32s + 8c + el
-    bm = formats.bf16_elem_map(N, 64, False)
-    assert int(bm[4096 * 1 + 1024 * 2 + 8 * 3 + 4]) == 3 * 64 + (32 + 16 + 4)
+def _w4_positions(N, K, gated, r, st, m, h, lane, s):
+    """(kernel word index, rows A / B, first k) of tile r, stage st, m16 tile m, half h, lane, step s."""
+    src = formats.kernel_row_source(N, gated)
+    o = r * (128 * K // 8) + st * 2048 + ((m * 2 + h) * 32 + lane) * 4 + s
+    g, t4 = lane >> 2, lane & 3
+    return o, int(src[128 * r + 16 * m + g]), int(src[128 * r + 16 * m + g + 8]), 128 * st + 64 * h + 16 * t4 + 4 * s
+
+
+@pytest.mark.parametrize("gated", [False, True])
+def test_stage_layout_positions(gated):
+    # int4: word [tile][stage][m16 tile m][half h][lane][step s] holds rows A (nibbles 0, 4, 2, 6 = k+0..k+3) and
+    # B = A + 8 (nibbles 1, 5, 3, 7) of its lane's fragment
+    N, K = 256, 384
+    codes = torch.randint(0, 16, (1, N, K), generator=torch.Generator().manual_seed(3))
+    q = formats.pack_int4(codes)
+    s_ = torch.rand(1, N, K // 128).to(torch.bfloat16)
+    wk, sk = formats.repack_w4_torch(q, s_, gated)
+    for (r, st, m, h, lane, s) in ((0, 0, 0, 0, 0, 0), (1, 2, 7, 1, 31, 3), (0, 1, 3, 0, 13, 2), (1, 0, 5, 1, 6, 1)):
+        o, ra, rb, k0 = _w4_positions(N, K, gated, r, st, m, h, lane, s)
+        word = int(wk[0, o]) & 0xFFFFFFFF
+        got = [(word >> (4 * i)) & 15 for i in range(8)]
+        want = [int(codes[0, ra if i % 2 == 0 else rb, k0 + formats.KPOS[i]]) for i in range(8)]
+        assert got == want
+    # scales: stage st, [warp w][g][c] = row 16 (2w + c/2) + g + 8 (c % 2)
+    src = formats.kernel_row_source(N, gated)
+    w, g, c, st = 2, 5, 3, 1
+    row = int(src[128 + 16 * (2 * w + 1) + g + 8])
+    assert sk[0, 1 * K + 128 * st + w * 32 + g * 4 + c] == s_[0, row, st]
+    # bf16: a stage is 32 k x 128 rows [m16 tile m][step s][lane][8], element 2w + h = row 16m + g + 8(w%2),
+    # k = 32 st + 8 t4 + 4 s + 2 (w // 2) + h
+    bm = formats.bf16_elem_map(128, 64, False)
+    m, s, lane, el = 3, 1, 9, 5   # g = 2, t4 = 1, w = 2, h = 1
+    assert int(bm[4096 * 1 + ((m * 2 + s) * 32 + lane) * 8 + el]) == (16 * m + 2) * 64 + (32 + 8 + 4 + 2 + 1)
 
 
 @pytest.mark.parametrize("N,K", [(128, 128), (256, 2048), (384, 640)])
@@ -71,8 +88,9 @@ def test_w8_layout_round_trip_and_swizzle(N, K):
 
 def test_nvfp4_kernel_layout():
     """NVFP4 experts (the reference's format) in the kernel layout: exact round trip, and each position holds what
-    the kernel reads there -- a thread of lane p in tile r reads stage st's word (quad q, word j) at
-    [st][q][p][j] (nibble i = k 32q + 8j + [0,2,4,6,1,3,5,7][i]) and its eight group scales at [st][p][0..8)."""
+    the kernel reads there -- the codes in the int4 fragment layout, and lane (g, t4) of consumer warp w finds the
+    E4M3 scale of row 16 (2w + mm) + g + 8 ro, 16-k group 8 st + 4 h + t4 at byte (mm * 2 + h) * 2 + ro of its
+    8 bytes [st][w][lane]."""
     from oracle import nvfp4_ref
     g = torch.Generator().manual_seed(5)
     E, N, K = 2, 256, 384
@@ -83,12 +101,14 @@ def test_nvfp4_kernel_layout():
         assert torch.equal(wp2, wp) and torch.equal(sf2.view(torch.uint8), sf.view(torch.uint8))
         codes = nvfp4_ref.unpack_e2m1(wp)                      # [E, N, K]
         src = formats.kernel_row_source(N, gated)
-        perm = formats.NIBBLE_ORDER
-        for e, r, st, q, p, j in ((0, 0, 0, 0, 0, 0), (1, 1, 2, 3, 127, 3), (0, 1, 1, 2, 77, 1), (1, 0, 2, 1, 6, 2)):
-            word = int(wk[e, r * (128 * K // 8) + st * 2048 + q * 512 + p * 4 + j]) & 0xFFFFFFFF
-            row = int(src[128 * r + p])
+        for e, r, st, m, h, lane, s in ((0, 0, 0, 0, 0, 0, 0), (1, 1, 2, 7, 1, 31, 3), (0, 1, 1, 2, 0, 17, 1)):
+            o, ra, rb, k0 = _w4_positions(N, K, gated, r, st, m, h, lane, s)
+            word = int(wk[e, o]) & 0xFFFFFFFF
             for i in range(8):
-                assert (word >> (4 * i)) & 15 == int(codes[e, row, 128 * st + 32 * q + 8 * j + perm[i]])
-            for gi in range(8):
-                got = int(sk[e, r * (128 * K // 16) + st * 1024 + p * 8 + gi])
-                assert got == int(sf.view(torch.uint8)[e, row, 8 * st + gi])
+                assert (word >> (4 * i)) & 15 == int(codes[e, ra if i % 2 == 0 else rb, k0 + formats.KPOS[i]])
+        sfu = sf.view(torch.uint8)
+        for e, r, st, w, lane, b in ((0, 0, 0, 0, 0, 0), (1, 1, 2, 3, 31, 7), (0, 1, 1, 2, 9, 5)):
+            mm, h, ro = b >> 2, (b >> 1) & 1, b & 1
+            row = int(src[128 * r + 16 * (2 * w + mm) + (lane >> 2) + 8 * ro])
+            got = int(sk[e, r * (128 * K // 16) + st * 1024 + (w * 32 + lane) * 8 + b])
+            assert got == int(sfu[e, row, 8 * st + 4 * h + (lane & 3)])
