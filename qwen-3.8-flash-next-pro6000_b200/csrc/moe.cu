@@ -32,9 +32,9 @@
 //     so each stage is a matrix-vector product that streams 8 KB of weights for a handful of columns. The weights
 //     are stored in the tensor cores' register-fragment order (m16n8k16): consumer warp w owns the two 16-row tiles
 //     2w, 2w + 1 of every 128-row stage, and one 16-byte shared-memory load gives a lane the int4 codes of four
-//     k16 steps of one tile. Each 32-bit word turns into the four bf16x2 A registers of one step with a shift, a
-//     lop3 and a bf16x2 subtract per register (code - 8, exact), and feeds mma.sync m16n8k16 (bf16, fp32
-//     accumulate) once per 8 tokens. No shared-memory or tensor-memory round trip sits between the copy engine and
+//     k16 steps of one tile. Each 32-bit word turns into the four bf16x2 A registers of one step with a shift and
+//     a lop3 per register (the biased code 128 + code, exact), and feeds mma.sync m16n8k16 (bf16, fp32 accumulate)
+//     once per 8 tokens; the bias is taken off once per stage by an mma of a constant fragment against the tokens. No shared-memory or tensor-memory round trip sits between the copy engine and
 //     the tensor cores. (tcgen05 with N = 16 token columns spends one tensor-memory store, one 128-row MMA chain and
 //     one tensor-memory load per stage whatever the token count; at decode sizes that chain, not HBM, set the rate.)
 //     bf16 stages (shared expert, 32 k) are already in fragment order and feed the mma directly.
@@ -318,10 +318,16 @@ __device__ __forceinline__ uint32_t nvfp4_pair(uint32_t q, int j, uint32_t scale
 // sb: the ring stage (weights in fragment order: [tile (8)][half (2)][lane (32)][4 words]); bb: the token block,
 // row stride brow. TWO: the item has more than 8 tokens (second n8 tile). NVFP4 (FMT 1): fsc = the lane's eight
 // E4M3 scales of the stage, byte (m * 2 + h) * 2 + (row g : 0, row g + 8 : 1) (each covers the lane's 16 k).
+// int4 (FMT 0): the A registers hold the biased codes 128 + code (one lop3 each, exact), and the bias is removed
+// once per stage and token: an mma of the constant -136 (= -(128 + the zero point 8)) against the same token
+// fragments gives -136 * (sum of the token's 128 k), the same for every row, added to both tiles' partials.
+// Every product is exact; the partials are fp32.
 template <int FMT, bool TWO>
 __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, int brow, int rw, int lane, uint2 fsc,
                                          float (&d)[4][4]) {
     const int g = lane >> 2, t4 = lane & 3;
+    constexpr uint32_t NEG136 = 0xC308C308u;   // bf16 -136 in both halves
+    float corr[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int j = 0; j < 4; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.f;
 #pragma unroll
@@ -340,6 +346,15 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
             const uint4 a = *reinterpret_cast<const uint4*>(sb + (((2 * rw + m) * 2 + h) * 32 + lane) * 16);
             const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
             uint32_t sA = 0u, sB = 0u;
+            if constexpr (FMT == 0) {
+                if (m == 0) {   // the bias term of this half's four k16 steps (once per token tile)
+#pragma unroll
+                    for (int s = 0; s < 4; ++s) {
+                        qf::mma_bf16(corr[0], NEG136, NEG136, NEG136, NEG136, xw0[2 * s], xw0[2 * s + 1]);
+                        if constexpr (TWO) qf::mma_bf16(corr[1], NEG136, NEG136, NEG136, NEG136, xw1[2 * s], xw1[2 * s + 1]);
+                    }
+                }
+            }
             if constexpr (FMT == 1) {
                 const uint32_t ws = (m == 0 ? fsc.x : fsc.y) >> (16 * h);
                 sA = qf::e4m3_scale_bf16x2(ws & 0xFFu);
@@ -351,7 +366,7 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
                 // word's nibble pairs (0,4) (1,5) (2,6) (3,7)
                 uint32_t v[4];
                 if constexpr (FMT == 0) {
-                    qf::signed_w4(aw[s], v);
+                    qf::biased_w4(aw[s], v);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 4; ++j) v[j] = nvfp4_pair(aw[s], j, (j & 1) ? sB : sA);
@@ -360,6 +375,15 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
                 if constexpr (TWO) qf::mma_bf16(d[2 * m + 1], v[0], v[1], v[2], v[3], xw1[2 * s], xw1[2 * s + 1]);
             }
         }
+    }
+    if constexpr (FMT == 0) {
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                d[2 * m][i] += corr[0][i];
+                if constexpr (TWO) d[2 * m + 1][i] += corr[1][i];
+            }
     }
 }
 
