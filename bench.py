@@ -690,8 +690,9 @@ def decode_timeline(dbg, sms):
         elif 17 <= code <= 23 and open_items.get((c, vp), (0,))[0] == code - 16:
             dur.setdefault(code - 16, []).append((t - open_items.pop((c, vp))[1], t))
     med = lambda v: sorted(v)[len(v) // 2]
+    stops = [t for t, _, _, code in ev if code == 31]   # absent when a CTA's stamp slots ran out first
     out = dict(consumers_start_us=round(med([t for t, _, _, code in ev if code == 30]), 2),
-               last_stop_us=round(max(t for t, _, _, code in ev if code == 31), 2), kinds={})
+               last_stop_us=round(max(stops), 2) if stops else None, kinds={})
     for k, st in sorted(starts.items()):
         dd = dur.get(k, [])
         out["kinds"][KIND_NAMES[k]] = dict(

@@ -46,6 +46,8 @@
 //   * Every wait is bounded; a wait that runs out sets QF_MOE_ERR_* in ctrl and the kernel drains. The consumer
 //     warps of a pipeline agree on each item's outcome through a reducing named barrier (barrier.red.and) before its
 //     epilogue, so a wait that runs out in one warp ends the item in all four and no barrier is left waiting.
+#include <type_traits>
+
 #include "qf_common.cuh"
 #include "topk.cuh"
 
@@ -188,8 +190,10 @@ static_assert(SCR_RTW + MAXSLOTS * 4 <= NST * STAGE_BYTES, "plan scratch (pipeli
 // fused router: this CTA's router rows live in pipeline 1's ring (idle until the plan is done)
 constexpr int RROWS_BYTES = NST * STAGE_BYTES;
 constexpr int RPC_MAX = 8;                                          // router rows per CTA
-// fused router: token tiles of x in pipeline 2's ring (idle until the plan is done); H <= 4096 gives >= 7 tokens
-static_assert(RROWS_BYTES >= 4096 * 2 * 7, "x tile of the fused router");
+// fused router: token tiles of x in the blocks of pipelines 2 .. NVP - 1 (idle until the plan is done); H <= 4096
+// gives >= 7 tokens per tile
+constexpr int XTILE_BYTES = (NVP - 2) * VP_BYTES;
+static_assert(NVP >= 3 && XTILE_BYTES >= 4096 * 2 * 7, "x tile of the fused router");
 
 enum : int { DBG_CONSUMERS = 30, DBG_STOP = 31, DBG_ENTRY = 0xFFF };   // timeline events (dbg)
 enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_DUPS = 7 };
@@ -327,9 +331,8 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
                                          float (&d)[4][4]) {
     const int g = lane >> 2, t4 = lane & 3;
     constexpr uint32_t NEG136 = 0xC308C308u;   // bf16 -136 in both halves
-    float corr[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.f;
+    float corr[2][4];
+    // every accumulator chain starts with a zero-input mma (h = 0, s = 0): no register clearing per stage
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
         const uint8_t* tb = bb + g * brow + h * 128 + t4 * 32;
@@ -350,8 +353,13 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
                 if (m == 0) {   // the bias term of this half's four k16 steps (once per token tile)
 #pragma unroll
                     for (int s = 0; s < 4; ++s) {
-                        qf::mma_bf16(corr[0], NEG136, NEG136, NEG136, NEG136, xw0[2 * s], xw0[2 * s + 1]);
-                        if constexpr (TWO) qf::mma_bf16(corr[1], NEG136, NEG136, NEG136, NEG136, xw1[2 * s], xw1[2 * s + 1]);
+                        if (h == 0 && s == 0) {
+                            qf::mma_bf16_z(corr[0], NEG136, NEG136, NEG136, NEG136, xw0[0], xw0[1]);
+                            if constexpr (TWO) qf::mma_bf16_z(corr[1], NEG136, NEG136, NEG136, NEG136, xw1[0], xw1[1]);
+                        } else {
+                            qf::mma_bf16(corr[0], NEG136, NEG136, NEG136, NEG136, xw0[2 * s], xw0[2 * s + 1]);
+                            if constexpr (TWO) qf::mma_bf16(corr[1], NEG136, NEG136, NEG136, NEG136, xw1[2 * s], xw1[2 * s + 1]);
+                        }
                     }
                 }
             }
@@ -371,10 +379,19 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
 #pragma unroll
                     for (int j = 0; j < 4; ++j) v[j] = nvfp4_pair(aw[s], j, (j & 1) ? sB : sA);
                 }
-                qf::mma_bf16(d[2 * m], v[0], v[1], v[2], v[3], xw0[2 * s], xw0[2 * s + 1]);
-                if constexpr (TWO) qf::mma_bf16(d[2 * m + 1], v[0], v[1], v[2], v[3], xw1[2 * s], xw1[2 * s + 1]);
+                if (h == 0 && s == 0) {
+                    qf::mma_bf16_z(d[2 * m], v[0], v[1], v[2], v[3], xw0[0], xw0[1]);
+                    if constexpr (TWO) qf::mma_bf16_z(d[2 * m + 1], v[0], v[1], v[2], v[3], xw1[0], xw1[1]);
+                } else {
+                    qf::mma_bf16(d[2 * m], v[0], v[1], v[2], v[3], xw0[2 * s], xw0[2 * s + 1]);
+                    if constexpr (TWO) qf::mma_bf16(d[2 * m + 1], v[0], v[1], v[2], v[3], xw1[2 * s], xw1[2 * s + 1]);
+                }
             }
         }
+    }
+    if constexpr (!TWO && FMT != 0) {   // the unused token tile's accumulators (added up by the caller): zero
+#pragma unroll
+        for (int m = 0; m < 2; ++m) d[2 * m + 1][0] = d[2 * m + 1][1] = d[2 * m + 1][2] = d[2 * m + 1][3] = 0.f;
     }
     if constexpr (FMT == 0) {
 #pragma unroll
@@ -392,8 +409,10 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
 template <bool TWO>
 __device__ __forceinline__ void stage_bf16(const uint8_t* sb, const uint8_t* bb, int rw, int lane, float (&d)[4][4]) {
     const int g = lane >> 2, t4 = lane & 3;
+    if constexpr (!TWO) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0.f;
+        for (int m = 0; m < 2; ++m) d[2 * m + 1][0] = d[2 * m + 1][1] = d[2 * m + 1][2] = d[2 * m + 1][3] = 0.f;
+    }
     const uint4 x0 = *reinterpret_cast<const uint4*>(bb + g * BROW_BF + t4 * 16);
     const uint4 x1 = TWO ? *reinterpret_cast<const uint4*>(bb + (8 + g) * BROW_BF + t4 * 16) : make_uint4(0u, 0u, 0u, 0u);
     const uint32_t xw0[4] = {x0.x, x0.y, x0.z, x0.w}, xw1[4] = {x1.x, x1.y, x1.z, x1.w};
@@ -402,8 +421,13 @@ __device__ __forceinline__ void stage_bf16(const uint8_t* sb, const uint8_t* bb,
 #pragma unroll
         for (int s = 0; s < 2; ++s) {
             const uint4 a = *reinterpret_cast<const uint4*>(sb + (((2 * rw + m) * 2 + s) * 32 + lane) * 16);
-            qf::mma_bf16(d[2 * m], a.x, a.y, a.z, a.w, xw0[2 * s], xw0[2 * s + 1]);
-            if constexpr (TWO) qf::mma_bf16(d[2 * m + 1], a.x, a.y, a.z, a.w, xw1[2 * s], xw1[2 * s + 1]);
+            if (s == 0) {
+                qf::mma_bf16_z(d[2 * m], a.x, a.y, a.z, a.w, xw0[0], xw0[1]);
+                if constexpr (TWO) qf::mma_bf16_z(d[2 * m + 1], a.x, a.y, a.z, a.w, xw1[0], xw1[1]);
+            } else {
+                qf::mma_bf16(d[2 * m], a.x, a.y, a.z, a.w, xw0[2 * s], xw0[2 * s + 1]);
+                if constexpr (TWO) qf::mma_bf16(d[2 * m + 1], a.x, a.y, a.z, a.w, xw1[2 * s], xw1[2 * s + 1]);
+            }
         }
 }
 
@@ -546,7 +570,7 @@ __device__ __noinline__ void fused_router(const Params& p, uint8_t* smem, const 
     // launch, with its instructions fetched cold) and few registers
     const int nc = p.H / 8;
     uint8_t* xs = smem + 2 * VP_BYTES;
-    const int tile_tok = min(M, RROWS_BYTES / (p.H * 2));
+    const int tile_tok = min(M, XTILE_BYTES / (p.H * 2));
     for (int t0 = 0; t0 < M; t0 += tile_tok) {
         const int nt = min(tile_tok, M - t0);
         const char* xsrc = reinterpret_cast<const char*>(p.x + (size_t)t0 * p.H);
@@ -778,8 +802,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             // Consumer warps arrive on efull[slot] of their pipeline after their item's global stores; this thread
             // makes those stores visible at gpu scope (fence) and publishes the item's counter increment. It polls
             // the pipelines' rings without blocking (a suspended wait on one ring would hold up the others).
-            int es0 = 0, es1 = 0, es2 = 0;
-            uint32_t eph0 = 0, eph1 = 0, eph2 = 0;
+            // per pipeline v, bits 4v .. 4v + 2: the next record slot, bit 4v + 3: its phase
+            static_assert(NEPI == 8 && NVP <= 8, "agent ring state packing");
+            uint32_t estate = 0u;
             uint32_t alive = (1u << NVP) - 1u;
             long long idle_since = clock64();
             const long long idle_limit = (long long)(2 * PIPE_WAIT_NS);
@@ -788,8 +813,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
 #pragma unroll
                 for (int v = 0; v < NVP; ++v) {
                     if (!(alive & (1u << v))) continue;
-                    int& es = v == 0 ? es0 : (v == 1 ? es1 : es2);
-                    uint32_t& eph = v == 0 ? eph0 : (v == 1 ? eph1 : eph2);
+                    const int es = (int)((estate >> (4 * v)) & 7u);
+                    const uint32_t eph = (estate >> (4 * v + 3)) & 1u;
                     uint8_t* vbv = smem + v * VP_BYTES;
                     uint64_t* ef = reinterpret_cast<uint64_t*>(vbv + VO_BAR) + 2 * NST;
                     if (!qf::mbar_test_wait(ef + es, eph)) continue;
@@ -802,7 +827,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                             atomicAdd(ctrl + r.idx, (uint32_t)r.add);
                         }
                         qf::mbar_arrive(ef + NEPI + es);
-                        if (++es == NEPI) { es = 0; eph ^= 1u; }
+                        // slot + 1; from slot 7 the carry flips the phase bit (and stays inside the 4-bit field)
+                        const uint32_t f = (((estate >> (4 * v)) & 0xFu) + 1u) & 0xFu;
+                        estate = (estate & ~(0xFu << (4 * v))) | (f << (4 * v));
                     }
                     any = true;
                 }
@@ -1086,18 +1113,24 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                         if constexpr (FMT == 0) {
                             // the group-128 scales of rows (g, g + 8) of tiles 2 rw, 2 rw + 1
                             const uint2 sc = *reinterpret_cast<const uint2*>(sb + STAGE_W + (rw * 8 + g) * 8);
-                            if (two) stage_w4<0, true>(sb, bb, brow, rw, lane, sc, dd);
-                            else stage_w4<0, false>(sb, bb, brow, rw, lane, sc, dd);
-                            release(st);
-                            const float sr[4] = {bf16_lo(sc.x), bf16_hi(sc.x), bf16_lo(sc.y), bf16_hi(sc.y)};
+                            // one code path per token-tile count (the second tile's work only when it exists)
+                            auto run = [&](auto two_c) {
+                                constexpr bool T2 = decltype(two_c)::value;
+                                stage_w4<0, T2>(sb, bb, brow, rw, lane, sc, dd);
+                                release(st);
+                                const float sr[4] = {bf16_lo(sc.x), bf16_hi(sc.x), bf16_lo(sc.y), bf16_hi(sc.y)};
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const float s0 = sr[2 * (j >> 1)], s1 = sr[2 * (j >> 1) + 1];
-                                acc[j][0] = fmaf(dd[j][0], s0, acc[j][0]);
-                                acc[j][1] = fmaf(dd[j][1], s0, acc[j][1]);
-                                acc[j][2] = fmaf(dd[j][2], s1, acc[j][2]);
-                                acc[j][3] = fmaf(dd[j][3], s1, acc[j][3]);
-                            }
+                                for (int j = 0; j < 4; ++j) {
+                                    if (!T2 && (j & 1)) continue;
+                                    const float s0 = sr[2 * (j >> 1)], s1 = sr[2 * (j >> 1) + 1];
+                                    acc[j][0] = fmaf(dd[j][0], s0, acc[j][0]);
+                                    acc[j][1] = fmaf(dd[j][1], s0, acc[j][1]);
+                                    acc[j][2] = fmaf(dd[j][2], s1, acc[j][2]);
+                                    acc[j][3] = fmaf(dd[j][3], s1, acc[j][3]);
+                                }
+                            };
+                            if (two) run(std::true_type{});
+                            else run(std::false_type{});
                         } else {
                             if (two) stage_w4<1, true>(sb, bb, brow, rw, lane, scl, dd);
                             else stage_w4<1, false>(sb, bb, brow, rw, lane, scl, dd);

@@ -259,6 +259,15 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// The same with a zero accumulator input: D = A(16x16 bf16) * B(16x8 bf16) (starts an accumulation chain).
+__device__ __forceinline__ void mma_bf16_z(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                           uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // int4 word -> four bf16x2 of (code - 8). The word's nibbles hold k = [0, 2, 4, 6, 1, 3, 5, 7] of eight
 // consecutive k (kernel layout), so the pairs come out in natural order: (k0,k1) (k2,k3) (k4,k5) (k6,k7).
 // (0x4300 | n) is the bf16 value 128 + n; subtracting 136 leaves n - 8, exactly.

@@ -47,18 +47,46 @@ __device__ void topk_row(const T* __restrict__ row, int E, int topk, int renorm,
     float v[PL];
     uint32_t rk[PL];
     float mx = -INFINITY;
+    // element i of this lane: expert i * 32 + lane, or, for rows of exactly 32 * PL experts (16-byte aligned, PL a
+    // multiple of 8), expert lane * PL + i, loaded as 16-byte words. Both element types take the same mapping under
+    // the same condition, so the router kernel (fp32 rows) and the fused router (bf16 rows) sum the softmax in the
+    // same order; the ranking carries the id, so the selection does not depend on which lane holds which expert.
+    constexpr int PER16 = 16 / (int)sizeof(T);
+    constexpr bool VEC = PL % 8 == 0;
+    const bool vec = VEC && E == 32 * PL && (reinterpret_cast<uintptr_t>(row) & 15u) == 0u;
+    if (vec) {
 #pragma unroll
-    for (int i = 0; i < PL; ++i) {
-        const int e = i * 32 + lane;
-        v[i] = e < E ? load_logit(row + e) : -INFINITY;
-        mx = fmaxf(mx, v[i]);
+        for (int c = 0; c < (VEC ? PL / PER16 : 1); ++c) {
+            const uint4 w = __ldcg(reinterpret_cast<const uint4*>(row + lane * PL) + c);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if constexpr (sizeof(T) == 2) {
+                    if (PER16 * c + 2 * j + 1 < PL) {
+                        v[PER16 * c + 2 * j] = __uint_as_float(ww[j] << 16);
+                        v[PER16 * c + 2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+                    }
+                } else {
+                    if (PER16 * c + j < PL) v[PER16 * c + j] = __uint_as_float(ww[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < PL; ++i) mx = fmaxf(mx, v[i]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < PL; ++i) {
+            const int e = i * 32 + lane;
+            v[i] = e < E ? load_logit(row + e) : -INFINITY;
+            mx = fmaxf(mx, v[i]);
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
-        const int e = i * 32 + lane;
+        const int e = vec ? lane * PL + i : i * 32 + lane;
         rk[i] = e < E ? rank_of(v[i], e) : 0u;
         sum += __expf(v[i] - mx);
     }
