@@ -51,8 +51,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config4", action="store_true", help="skip the one-GPU config-4 record of the N=1 line")
     ap.add_argument("--sweep", default="")
-    ap.add_argument("--sweep-configs", default="2,3",
-                    help="which sweep records to take (comma list of 2, 3, nvfp4)")
+    ap.add_argument("--sweep-configs", default="2,3,w8g",
+                    help="which sweep records to take (comma list of 2, 3, nvfp4, w8g)")
     ap.add_argument("--sweep-n", default="2048,4096,8192,12288", help="config-3 weight row counts N to sweep")
     ap.add_argument("--timeline", default="", help="write the per-CTA item timeline of config-1 layer-steps here")
     ap.add_argument("--timeline-m", default="1,10", help="token counts of the timeline")
@@ -159,10 +159,28 @@ def cpu_step(cfg, L, x):
                                shared_w=(L["sh_gu"], L["sh_d"]))
 
 
+def host_threads() -> int:
+    """CPU threads this process may really use: the affinity set, capped by the cgroup CPU quota (a container may
+    see every core of its host but be allowed a few of them; more threads than that only thrash)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        n = os.cpu_count() or 1
+    try:
+        with open("/sys/fs/cgroup/cpu.max") as f:
+            quota, period = f.read().split()[:2]
+        if quota != "max":
+            n = min(n, max(1, int(int(quota) / int(period))))
+    except (OSError, ValueError):
+        pass
+    return max(1, n)
+
+
 def time_cpu(cfg, M, steps, warmup, budget_s):
-    """Times the CPU oracle layer-step with every host thread. Returns (us per step, steps timed, threads)."""
+    """Times the CPU oracle layer-step with every host thread it may use. Returns (us per step, steps timed,
+    threads)."""
     import torch
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(host_threads())
     from qwenfast_b200 import synthetic
     L = cpu_layer(cfg)
     xs = [synthetic.make_tokens(cfg, M=M, seed=s) for s in range(4)]
@@ -493,7 +511,8 @@ def run_ours(args):
 
 def run_sweep(args):
     """Extra records (one GPU): config 2 -- the layer-step over M in {1..64} with Zipf-skewed routing across stacked
-    layers -- and config 3 -- the W8A8 GEMM (K=2048) over N and M. Every record carries its algorithmic bytes and the
+    layers --, config 3 -- the W8A8 GEMM (K=2048) over N and M --, "nvfp4" -- config-1 shapes on NVFP4 experts --
+    and "w8g" -- the W8A16 group-128 GEMM over K in {2048, 2560, 6144}, N and M <= 16. Every record carries its algorithmic bytes and the
     fraction of the measured HBM bandwidth. Written to ``args.sweep`` as a JSON list; one summary line per record."""
     import torch
     from qwenfast_b200 import build as qbuild
@@ -660,6 +679,36 @@ def run_sweep(args):
             print(json.dumps(rec), flush=True)
         del ws
         torch.cuda.empty_cache()
+    # ---------------------------------------------------------------- W8A16 group-128 GEMM (the dense projections)
+    # the op the reference calls for every int8 dense projection (serve/overlays/sglang/srt/qwenfast.py:351-353):
+    # canonical int8 weights + bf16 group-128 scales, M <= 16 rows
+    for K in (2048, 2560, 6144) if "w8g" in which else ():
+        for N in [int(n) for n in args.sweep_n.split(",") if n.strip()]:
+            copies = max(2, math.ceil(400e6 / (N * K)))   # > 3x the 126 MB L2 per cycle
+            g = torch.Generator(device=dev).manual_seed(N + K)
+            ws = [(torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int32).to(torch.int8),
+                   (torch.rand(N, K // 128, generator=g, device=dev) * 1e-3 + 1e-4).to(torch.bfloat16))
+                  for _ in range(copies)]
+            for M in (1, 4, 8, 16):
+                x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+
+                def gemms():
+                    for q, s8 in ws:
+                        ops.w8g_gemm(x, q, s8, 0, pdl=True)
+
+                ms = graph_time(gemms, reps=8)
+                if ops.w8g_take_status():
+                    raise RuntimeError(f"W8A16 kernel reported a wait timeout at N={N} K={K} M={M}")
+                us = ms * 1e3 / copies
+                b = N * K + 2 * N * K // 128 + 2 * M * K + 2 * M * N
+                rec = {"config": "w8g", "N": N, "K": K, "M": M, "us_per_gemm": us, "bytes": b,
+                       "achieved_gbs": b / (us * 1e-6) / 1e9, "peak_gbs": peak, "peak_kind": peak_kind,
+                       "l2": f"{copies} weight copies cycled (> L2)"}
+                rec["frac"] = rec["achieved_gbs"] / peak
+                records.append(rec)
+                print(json.dumps(rec), flush=True)
+            del ws
+            torch.cuda.empty_cache()
     with open(args.sweep, "w") as f:
         json.dump(records, f, indent=1)
 
