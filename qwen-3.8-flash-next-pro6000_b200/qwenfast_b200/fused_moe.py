@@ -5,7 +5,7 @@ It fills the slot that ``CompressedTensorsW4A4Nvfp4MoE`` fills for the reference
 ``create_weights``, :173-190 ``process_weights_after_loading``, :388-410 ``apply_weights``), for experts in this
 build's format: int4 codes with zero point 8, eight per int32 along K (lowest k in the low nibble), one bf16 scale per
 128 k. Where the reference hands the routed experts to a Marlin MoE runner, ``apply_weights`` calls
-``torch.ops.qwenfast_b200.a16_moe_decode``: the persistent tcgen05 kernel, routed experts only (the block adds the
+``torch.ops.qwenfast_b200.a16_moe_decode``: the persistent decode MoE kernel, routed experts only (the block adds the
 shared expert itself), out = bf16(sum over the top-k positions of bf16(bf16(expert_out) * bf16(topk_w))).
 
 Token counts up to 64 are one launch; larger batches (prefill) run as 64-token launches of the same kernel (each
