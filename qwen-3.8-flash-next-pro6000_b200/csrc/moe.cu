@@ -173,7 +173,9 @@ constexpr int PLAN_TLIST = PLAN_TOFF + (QF_MAX_EXPERTS + 8) * 2;      // int16 [
 constexpr int PLAN_SIDS = PLAN_TLIST + MAXSLOTS * 2;                  // int16 [MAXSLOTS] copy of topk_ids
 constexpr int PLAN_DUPN = PLAN_SIDS + MAXSLOTS * 2;                   // int16 [MAXSLOTS] next slot, same token+expert
 constexpr int PLAN_TW = PLAN_DUPN + MAXSLOTS * 2;                     // fp32 [MAXSLOTS] bf16-rounded topk_weights
-constexpr int PLAN_MISC = PLAN_TW + MAXSLOTS * 4;                     // int32 [64]
+constexpr int PLAN_QGU = PLAN_TW + MAXSLOTS * 4;                      // int16 [MAXSLOTS] token group -> its u
+constexpr int PLAN_TTOK = PLAN_QGU + MAXSLOTS * 2;                    // int16 [MAXSLOTS] token of each tlist entry
+constexpr int PLAN_MISC = PLAN_TTOK + MAXSLOTS * 2;                   // int32 [64]
 constexpr int PLAN_LAYOUT = PLAN_MISC + 64 * 4;                       // Layout (per-launch sizes, one copy per CTA)
 constexpr int PLAN_LAYOUT_BYTES = 256;
 constexpr int PLAN_BYTES = PLAN_LAYOUT + PLAN_LAYOUT_BYTES;
@@ -277,26 +279,6 @@ __device__ void make_layout(Layout& L, const Params& p, int M, int U, int Gt, in
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
     L.sh_off = ((size_t)QF_MAX_TOKENS * p.topk * L.R1 + 3) & ~(size_t)3;
     L.g1_part_off = L.sh_off + (L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0);
-}
-
-__device__ __forceinline__ int find_u(const int16_t* gpre, int U, int key) {   // largest u with gpre[u] <= key
-    int lo = 0, hi = U - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (gpre[mid] <= key) lo = mid; else hi = mid - 1;
-    }
-    return lo;
-}
-
-// ---------------------------------------------------------------------------------------------- consumer math
-// Row of token n of a stage's item (its k-slice base for stage 0), or nullptr for n beyond the item's tokens.
-__device__ __forceinline__ const __nv_bfloat16* token_row(const Params& p, const StageDesc& d, const int16_t* toff,
-                                                          const int16_t* tlist, int n) {
-    if (n >= d.ntok) return nullptr;
-    if (d.kind == K_G1) return p.x + (size_t)(tlist[toff[d.u] + TG * d.tg + n] / p.topk) * p.H + d.split * (p.H / G1_SPLIT);
-    if (d.kind == K_G2) return p.hbuf + (size_t)tlist[toff[d.u] + TG * d.tg + n] * p.I;
-    if (d.kind == K_S1) return p.x + (size_t)(TG * d.tg + n) * p.H + d.split * (p.H / NSPLIT);
-    return p.hsh + (size_t)(TG * d.tg + n) * p.Is;   // K_S2
 }
 
 // ------------------------------------------------------------------------------- register-path stage contraction
@@ -621,6 +603,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
     int16_t* sids = reinterpret_cast<int16_t*>(plan + PLAN_SIDS);
     int16_t* dupn = reinterpret_cast<int16_t*>(plan + PLAN_DUPN);
     float* tws = reinterpret_cast<float*>(plan + PLAN_TW);
+    int16_t* qgu = reinterpret_cast<int16_t*>(plan + PLAN_QGU);
+    int16_t* ttok = reinterpret_cast<int16_t*>(plan + PLAN_TTOK);
     int* misc = reinterpret_cast<int*>(plan + PLAN_MISC);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -763,6 +747,8 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 toff[u] = (int16_t)(chunk[32 + c] + exc[e]);
                 gpre[u] = (int16_t)(chunk[64 + c] + exg[e]);
                 toffe[e] = toff[u];
+                const int ng = (__popcll(mask[e]) + TG - 1) / TG;
+                for (int q = 0; q < ng; ++q) qgu[gpre[u] + q] = (int16_t)u;
             }
         }
         if (tid == 0) {
@@ -787,6 +773,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             if (first) {
                 const int j = __popcll(mask[e] & ((1ull << t) - 1ull));
                 tlist[toffe[e] + j] = (int16_t)s;
+                ttok[toffe[e] + j] = (int16_t)t;
             }
         }
         __syncthreads();
@@ -854,18 +841,25 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             qf::fence_proxy_async();
             int st = 0;
             uint32_t ph = 0;
-            int next = first_item;
             // diagnostic mode 2: CTA 0's first producer waits, before its first item, for a dependency that never
             // arrives; the bounded wait runs out, records QF_MOE_ERR_TIMEOUT and the launch drains
             bool never = p.mode == 2 && blockIdx.x == 0 && vp == 0;
-            for (;;) {
-                if (never) {
-                    never = false;
-                    wait_counter(ctrl, C_NEVER, 1u);
-                }
-                int item = next;
-                if (hard_error(ctrl)) item = L.total;
-                if (item < L.total) next = (int)atomicAdd(ctrl + C_QUEUE, 1u);   // claim ahead; in-order per CTA
+            // An item decoded from its queue index: the stage descriptor (written with the item's first stage; the
+            // consumers read it once), the weight / scale sources (advanced by a constant per stage), bytes per
+            // stage, and the counter that must be acquired before the first stage is marked full (its inputs).
+            struct Work {
+                StageDesc d;
+                const uint8_t* wsrc;
+                const uint16_t* ssrc;
+                uint32_t bytes, dep_target;
+                int dep_idx;               // -1: no input to acquire, or acquired while the item was decoded
+                uint32_t rows[TG / 2];     // routed item: its token rows (x row / hbuf slot), two per word; entries
+                                           // from ntok on repeat the last row (the tail of a 4-row gather)
+            };
+            // Decoding is plan arithmetic only (no waits): it runs one item ahead, while the current item's later
+            // stages wait for ring slots, so that an item boundary costs the ring no more than a stage does.
+            auto decode = [&](int item) {
+                Work w;
                 int kind = K_STOP, u = 0, tile = 0, tg = 0, split = 0, nk = 1, ntok = 0, e = 0;
                 if (item >= L.total) {
                     kind = K_STOP;
@@ -883,19 +877,27 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     const bool down = item >= L.b_g2;
                     const int j = item - (down ? L.b_g2 : L.b_g1);
                     // gate_up: (tile, k half) pairs, the two halves of a tile next to each other in the queue
+                    // token group q (all groups of all routed experts, expert-major), then its R tiles
                     const int R = down ? L.R2 : L.R1 * L.g1s;
-                    u = find_u(gpre, L.U, j / R);
-                    const int ngu = gpre[u + 1] - gpre[u];
-                    const int jj = j - R * gpre[u];
-                    const int th = jj / ngu;
-                    tg = jj - th * ngu;
-                    tile = down ? th : th / L.g1s;
-                    split = down ? 0 : th % L.g1s;
+                    const int q = j / R;
+                    const int th = j - q * R;
+                    u = qgu[q];
+                    tg = q - gpre[u];
+                    tile = down ? th : th >> (L.g1s - 1);
+                    split = down ? 0 : th & (L.g1s - 1);
                     kind = down ? K_G2 : K_G1;
                     e = ulist[u];
-                    const int K = down ? p.I : p.H;
-                    nk = (K + W4_KC - 1) / W4_KC / (down ? 1 : L.g1s);
-                    ntok = min(TG, (toff[u + 1] - toff[u]) - TG * tg);
+                    nk = ((down ? p.I : p.H) + W4_KC - 1) / W4_KC >> (down ? 0 : L.g1s - 1);
+                    const int tb = toff[u] + TG * tg;
+                    ntok = min(TG, toff[u + 1] - tb);
+                    const int16_t* tl = (down ? tlist : ttok) + tb;
+                    const int npad = ntok >= GATHER_MIN ? (ntok + 3) & ~3 : ntok;
+#pragma unroll
+                    for (int n = 0; n < TG; n += 2) {
+                        if (n >= npad) break;
+                        const uint32_t r0 = (uint16_t)tl[min(n, ntok - 1)], r1 = (uint16_t)tl[min(n + 1, ntok - 1)];
+                        w.rows[n / 2] = r0 | (r1 << 16);
+                    }
                 } else if (item < L.b_s2) {
                     const int j = item - L.b_s1f;
                     kind = K_S1F;
@@ -915,117 +917,146 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     tile = j / L.ngc;
                     tg = j - tile * L.ngc;
                 }
-                // dependencies of items without copies are resolved before their (empty) stage is published
-                if (kind == K_S1F) wait_counter(ctrl, C_SPLIT + tile * L.ngs + tg, (uint32_t)NSPLIT);
-                if (kind == K_CB) {
-                    wait_counter(ctrl, C_CNT + tile, L.tile_target);
-                    if (L.has_gate) wait_counter(ctrl, C_GLF, 1u);
-                }
-                // per item: the stage descriptor (written with the item's first stage; the consumers read it once),
-                // the weight / scale sources (advanced by a constant per stage), bytes per stage, and the counter
-                // that must be acquired before the first stage is marked full (the item's inputs), if any
-                StageDesc d;
+                StageDesc& d = w.d;
                 d.kind = (int16_t)kind; d.u = (int16_t)u; d.tile = (int16_t)tile; d.tg = (int16_t)tg;
                 d.split = (int16_t)split; d.kidx = 0; d.nk = (int16_t)nk; d.ntok = (int16_t)ntok;
-                const uint8_t* wsrc = nullptr;
-                const uint16_t* ssrc = nullptr;
-                uint32_t bytes = 0;
-                int dep_idx = -1;
-                uint32_t dep_target = 0;
+                w.wsrc = nullptr;
+                w.ssrc = nullptr;
+                w.bytes = 0;
+                w.dep_idx = -1;
+                w.dep_target = 0;
                 if (kind == K_G1 || kind == K_G2) {
                     const bool down = kind == K_G2;
                     const int K = down ? p.I : p.H;
                     const int N = down ? p.H : 2 * p.I;
                     d.kc = (int16_t)W4_KC;
-                    wsrc = (down ? p.w2 : p.w13) + (size_t)(e - p.wofs) * ((size_t)N * K / 2) + (size_t)tile * (128 * (size_t)K / 2) +
-                           (size_t)split * nk * STAGE_W;
+                    w.wsrc = (down ? p.w2 : p.w13) + (size_t)(e - p.wofs) * ((size_t)N * K / 2) +
+                             (size_t)tile * (128 * (size_t)K / 2) + (size_t)split * nk * STAGE_W;
                     if constexpr (FMT == 0) {
-                        bytes = STAGE_W + STAGE_S;
-                        ssrc = (down ? p.s2 : p.s13) + (size_t)(e - p.wofs) * ((size_t)N * K / 128) + (size_t)tile * K +
-                               (size_t)split * nk * W4_KC;
+                        w.bytes = STAGE_W + STAGE_S;
+                        w.ssrc = (down ? p.s2 : p.s13) + (size_t)(e - p.wofs) * ((size_t)N * K / 128) + (size_t)tile * K +
+                                 (size_t)split * nk * W4_KC;
                     } else {
                         // the item's E4M3 scales (1 KB per stage, contiguous) into L2; the consumers load them
-                        bytes = STAGE_W;
+                        w.bytes = STAGE_W;
                         qf::prefetch_l2((down ? p.f2 : p.f13) + (size_t)(e - p.wofs) * ((size_t)N * K / 16) +
                                             (size_t)tile * (8 * (size_t)K) + (size_t)split * nk * 1024,
                                         (uint32_t)nk * 1024u);
                     }
-                    if (down) { dep_idx = C_DONE + u; dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])); }
+                    if (down) { w.dep_idx = C_DONE + u; w.dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])); }
                 } else if (kind == K_S1 || kind == K_S2) {
                     const bool down = kind == K_S2;
                     const int K = down ? p.Is : p.H;
                     const int k0 = down ? 0 : split * (p.H / NSPLIT);
                     d.kc = (int16_t)BF_KC;
-                    bytes = STAGE_W;
-                    wsrc = (down ? p.shw2 : p.shw13) + (size_t)tile * (128 * (size_t)K * 2) + (size_t)(k0 / BF_KC) * STAGE_W;
-                    if (down) { dep_idx = C_SDONE + tg; dep_target = (uint32_t)L.Rs1; }
+                    w.bytes = STAGE_W;
+                    w.wsrc = (down ? p.shw2 : p.shw13) + (size_t)tile * (128 * (size_t)K * 2) + (size_t)(k0 / BF_KC) * STAGE_W;
+                    if (down) { w.dep_idx = C_SDONE + tg; w.dep_target = (uint32_t)L.Rs1; }
                 } else {
                     d.kc = 0;
+                }
+                if (w.bytes != 0) {
+                    if (kind == K_S1 || kind == K_S2) w.bytes += (uint32_t)(p.tok_box * BF_KC * 2);
+                    else w.bytes += (uint32_t)((ntok >= GATHER_MIN ? (ntok + 3) / 4 * 4 : ntok) * W4_KC * 2);
+                }
+                return w;
+            };
+            // the first item was claimed before the plan; the second is claimed now (claims run two items ahead)
+            int next = first_item < L.total ? (int)atomicAdd(ctrl + C_QUEUE, 1u) : L.total;
+            uint32_t herr = 0u;
+            Work cur = decode(first_item);
+            for (;;) {
+                if (never) {
+                    never = false;
+                    wait_counter(ctrl, C_NEVER, 1u);
+                }
+                const StageDesc& d = cur.d;
+                const int kind = d.kind;
+                // dependencies of items without copies are resolved before their (empty) stage is published
+                if (kind == K_S1F) wait_counter(ctrl, C_SPLIT + d.tile * L.ngs + d.tg, (uint32_t)NSPLIT);
+                if (kind == K_CB) {
+                    wait_counter(ctrl, C_CNT + d.tile, L.tile_target);
+                    if (L.has_gate) wait_counter(ctrl, C_GLF, 1u);
                 }
                 // the k-slice of the item's token rows rides in every stage (token block at STAGE_TOK): the shared
                 // expert's consecutive rows as one tensor copy (rows beyond M read zeros), a routed expert's rows one
                 // by one (row stride BROW_W4) or, from GATHER_MIN rows, in 4-row gathers (stride BROW_G4; a partial
                 // last group repeats its last row). Rows beyond the item's tokens hold stale data: the mma columns
                 // they feed are never read.
-                const bool w4k = kind == K_G1 || kind == K_G2;
-                const bool g4 = w4k && ntok >= GATHER_MIN;
-                if (bytes != 0) {
-                    if (kind == K_S1 || kind == K_S2) bytes += (uint32_t)(p.tok_box * BF_KC * 2);
-                    else bytes += (uint32_t)((g4 ? (ntok + 3) / 4 * 4 : ntok) * W4_KC * 2);
-                }
+                const int ntok = d.ntok;
+                const bool g4 = (kind == K_G1 || kind == K_G2) && ntok >= GATHER_MIN;
                 auto copy_tokens = [&](uint8_t* sb, int kidx) {
                     uint8_t* tb = sb + STAGE_TOK;
                     if (kind == K_S1) {
-                        qf::tma_tile_2d(tb, &p.xt, split * (p.H / NSPLIT) + kidx * BF_KC, TG * tg, full + st);
+                        qf::tma_tile_2d(tb, &p.xt, d.split * (p.H / NSPLIT) + kidx * BF_KC, TG * d.tg, full + st);
                     } else if (kind == K_S2) {
-                        qf::tma_tile_2d(tb, &p.ht, kidx * BF_KC, TG * tg, full + st);
-                    } else if (!g4) {
-                        for (int n = 0; n < ntok; ++n)
-                            qf::bulk_g2s(tb + n * BROW_W4, token_row(p, d, toff, tlist, n) + (size_t)kidx * W4_KC,
-                                         W4_KC * 2, full + st);
+                        qf::tma_tile_2d(tb, &p.ht, kidx * BF_KC, TG * d.tg, full + st);
                     } else {
-                        const void* map = kind == K_G1 ? static_cast<const void*>(&p.xg) : static_cast<const void*>(&p.hg);
-                        const int x0 = (kind == K_G1 ? split * (p.H / G1_SPLIT) : 0) + kidx * W4_KC;
-                        const int16_t* tl = tlist + toff[u] + TG * tg;
-                        for (int n0 = 0; n0 < ntok; n0 += 4) {
-                            int r[4];
+                        const int x0 = (kind == K_G1 ? d.split * (p.H / G1_SPLIT) : 0) + kidx * W4_KC;
+                        if (!g4) {   // one or two rows
+                            const __nv_bfloat16* base = kind == K_G1 ? p.x : p.hbuf;
+                            const size_t ld = kind == K_G1 ? (size_t)p.H : (size_t)p.I;
+                            qf::bulk_g2s(tb, base + (size_t)(cur.rows[0] & 0xFFFFu) * ld + x0, W4_KC * 2, full + st);
+                            if (ntok > 1)
+                                qf::bulk_g2s(tb + BROW_W4, base + (size_t)(cur.rows[0] >> 16) * ld + x0, W4_KC * 2,
+                                             full + st);
+                        } else {
+                            const void* map = kind == K_G1 ? static_cast<const void*>(&p.xg) : static_cast<const void*>(&p.hg);
 #pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const int sl = tl[min(n0 + j, ntok - 1)];
-                                r[j] = kind == K_G1 ? sl / p.topk : sl;
+                            for (int n0 = 0; n0 < TG; n0 += 4) {
+                                if (n0 >= ntok) break;
+                                const uint32_t a = cur.rows[n0 / 2], b = cur.rows[n0 / 2 + 1];
+                                qf::tma_gather4(tb + n0 * BROW_G4, map, x0, (int)(a & 0xFFFFu), (int)(a >> 16),
+                                                (int)(b & 0xFFFFu), (int)(b >> 16), full + st);
                             }
-                            qf::tma_gather4(tb + n0 * BROW_G4, map, x0, r[0], r[1], r[2], r[3], full + st);
                         }
                     }
                 };
+                Work nxt;
+                const int nk = d.nk;
                 for (int kidx = 0; kidx < nk; ++kidx) {
                     if (!qf::mbar_wait(empty + st, ph ^ 1u, PIPE_WAIT_NS)) set_err(ctrl, QF_MOE_ERR_PIPELINE);
                     uint8_t* sb = ring + st * STAGE_BYTES;
                     if (kidx == 0) desc[st] = d;
-                    if (bytes == 0) {
+                    if (cur.bytes == 0) {
                         qf::mbar_arrive(full + st);
-                    } else if (kidx == 0 && dep_idx >= 0) {
+                    } else if (kidx == 0 && cur.dep_idx >= 0) {
                         // weights first; the token rows (the item's inputs, written by other CTAs) are copied, and the
                         // stage is marked full (arrive), only after the inputs are acquired; the proxy fence orders
-                        // the copy engine's reads after that acquire
-                        qf::mbar_expect_tx(full + st, bytes);
-                        qf::bulk_g2s_hint(sb, wsrc, STAGE_W, full + st, pol);
-                        if (ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, ssrc, STAGE_S, full + st, pol);
-                        wait_counter(ctrl, dep_idx, dep_target);
-                        qf::fence_proxy_async();
+                        // the copy engine's reads of global memory after that acquire
+                        qf::mbar_expect_tx(full + st, cur.bytes);
+                        qf::bulk_g2s_hint(sb, cur.wsrc, STAGE_W, full + st, pol);
+                        if (cur.ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, cur.ssrc, STAGE_S, full + st, pol);
+                        wait_counter(ctrl, cur.dep_idx, cur.dep_target);
+                        qf::fence_proxy_async_global();
                         copy_tokens(sb, kidx);
                         qf::mbar_arrive(full + st);
                     } else {
-                        qf::mbar_arrive_expect_tx(full + st, bytes);
-                        qf::bulk_g2s_hint(sb, wsrc, STAGE_W, full + st, pol);
-                        if (ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, ssrc, STAGE_S, full + st, pol);
+                        qf::mbar_arrive_expect_tx(full + st, cur.bytes);
+                        qf::bulk_g2s_hint(sb, cur.wsrc, STAGE_W, full + st, pol);
+                        if (cur.ssrc != nullptr) qf::bulk_g2s_hint(sb + STAGE_W, cur.ssrc, STAGE_S, full + st, pol);
                         copy_tokens(sb, kidx);
                     }
-                    wsrc += STAGE_W;
-                    if (ssrc != nullptr) ssrc += W4_KC;
+                    cur.wsrc += STAGE_W;
+                    if (cur.ssrc != nullptr) cur.ssrc += W4_KC;
                     if (++st == NST) { st = 0; ph ^= 1u; }
+                    if (kidx == 0 && kind != K_STOP) {
+                        // look ahead: claim the item after the next one and decode the next one; if its input is
+                        // complete already, acquire it now (then the proxy fence orders every later copy of this
+                        // thread after it). After a hard error anywhere (read one item ahead) the next item is the
+                        // stop.
+                        const int item = (herr & HARD_ERR) ? L.total : next;
+                        herr = qf::ld_volatile(ctrl + C_ERR);
+                        if (item < L.total) next = (int)atomicAdd(ctrl + C_QUEUE, 1u);
+                        nxt = decode(item);
+                        if (nxt.dep_idx >= 0 && qf::ld_acquire(ctrl + nxt.dep_idx) >= nxt.dep_target) {
+                            nxt.dep_idx = -1;
+                            qf::fence_proxy_async_global();
+                        }
+                    }
                 }
                 if (kind == K_STOP) break;
+                cur = nxt;
             }
         }
         __syncwarp();
@@ -1229,13 +1260,26 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 }
                 // fragment row g is gate row j = 64 tile + 8 (2 rw + m) + g, row g + 8 its up row: elements (0, 1)
                 // and (2, 3) of acc[2 m + n] are (gate, up) of tokens 8 n + 2 t4 and + 1
+                // the destination rows of the lane's four tokens (j = 2 n + h: token 8 n + 2 t4 + h; -1: none), loaded
+                // before the math (independent shared-memory loads): hbuf by slot for a routed expert, the shared
+                // expert's h by token. The shared expert has no global multiplier (gs = 1: bf16r(bf16r(g) * 1) is
+                // bf16r(g)).
+                const bool routed = d.kind == K_G1;
                 float gs = 1.f;
                 int tbase = 0;
-                if (d.kind == K_G1) {
+                if (routed) {
                     const int e = ulist[d.u];
                     gs = p.gs13 ? bf16_bits(p.gs13[e - p.wofs]) : 1.f;
                     tbase = toff[d.u] + TG * d.tg;
                 }
+                int row[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int tok = 8 * (j >> 1) + 2 * t4 + (j & 1);
+                    row[j] = tok >= d.ntok ? -1 : (routed ? tlist[tbase + tok] : TG * d.tg + tok);
+                }
+                __nv_bfloat16* const dst = routed ? p.hbuf : p.hsh;
+                const int ldd = routed ? p.I : p.Is;
 #pragma unroll
                 for (int m = 0; m < 2; ++m) {
                     const int col = 64 * d.tile + 8 * (2 * rw + m) + g;
@@ -1243,16 +1287,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                     for (int n = 0; n < 2; ++n)
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
-                            const int tok = 8 * n + 2 * t4 + h;
-                            if (tok >= d.ntok) continue;
+                            const int r = row[2 * n + h];
+                            if (r < 0) continue;
                             const float g0 = acc[2 * m + n][h], u0 = acc[2 * m + n][2 + h];
-                            if (d.kind == K_G1) {
-                                const float gv = bf16r(bf16r(g0) * gs), uv = bf16r(bf16r(u0) * gs);
-                                p.hbuf[(size_t)tlist[tbase + tok] * p.I + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
-                            } else {
-                                const float gv = bf16r(g0), uv = bf16r(u0);
-                                p.hsh[(size_t)(TG * d.tg + tok) * p.Is + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
-                            }
+                            const float gv = bf16r(bf16r(g0) * gs), uv = bf16r(bf16r(u0) * gs);
+                            dst[(size_t)r * ldd + col] = __float2bfloat16(gv / (1.f + __expf(-gv)) * uv);
                         }
                 }
                 signal(d.kind == K_G1 ? C_DONE + d.u : C_SDONE + d.tg, 1);
@@ -1266,22 +1305,46 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 const int u = d.u, e = ulist[u];
                 const float g2 = p.gs2 ? bf16_bits(p.gs2[e - p.wofs]) : 1.f;
                 const int tbase = toff[u] + TG * d.tg;
+                // the first slot of each of the lane's four tokens routed to e (j = 2 n + h: token 8 n + 2 t4 + h;
+                // -1: none) and its weight, loaded before any store (independent shared-memory loads)
+                int sl[4];
+                float wt[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int tok = 8 * (j >> 1) + 2 * t4 + (j & 1);
+                    sl[j] = tok < d.ntok ? tlist[tbase + tok] : -1;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) wt[j] = sl[j] >= 0 ? bf16r(g2 * tws[sl[j]]) : 0.f;
 #pragma unroll
                 for (int m = 0; m < 2; ++m)
 #pragma unroll
                     for (int n = 0; n < 2; ++n)
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
-                            const int tok = 8 * n + 2 * t4 + (i & 1);
-                            if (tok >= d.ntok) continue;
+                            const int j = 2 * n + (i & 1);
+                            if (sl[j] < 0) continue;
                             const int n0 = 128 * d.tile + 16 * (2 * rw + m) + g + 8 * (i >> 1);
-                            const float v = bf16r(acc[2 * m + n][i]);
-                            // the token's first slot routed to e, then any later slot of the same token with e again
-                            for (int s = tlist[tbase + tok]; s >= 0; s = dupn[s]) {
-                                const float w = bf16r(g2 * tws[s]);
-                                p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(v * w);
-                            }
+                            p.ybuf[(size_t)sl[j] * p.H + n0] = __float2bfloat16(bf16r(acc[2 * m + n][i]) * wt[j]);
                         }
+                if (misc[MISC_DUPS] != 0) {
+                    // a token that names e in more than one slot (possible only through the op's API): the same
+                    // row, weighted by each later slot's weight, into that slot
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        if (sl[j] < 0) continue;
+                        for (int s = dupn[sl[j]]; s >= 0; s = dupn[s]) {
+                            const float w = bf16r(g2 * tws[s]);
+#pragma unroll
+                            for (int m = 0; m < 2; ++m)
+#pragma unroll
+                                for (int i = (j & 1); i < 4; i += 2) {
+                                    const int n0 = 128 * d.tile + 16 * (2 * rw + m) + g + 8 * (i >> 1);
+                                    p.ybuf[(size_t)s * p.H + n0] = __float2bfloat16(bf16r(acc[2 * m + (j >> 1)][i]) * w);
+                                }
+                        }
+                    }
+                }
                 signal(C_CNT + d.tile, 1);
             } else if (d.kind == K_S2) {
 #pragma unroll

@@ -227,6 +227,9 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
 }
 // Order this thread's earlier generic-proxy accesses (and those it acquired) before its later async-proxy ones.
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async;" ::: "memory"); }
+// The same, for global memory only: orders this thread's generic-proxy view of global memory (e.g. rows acquired from
+// other CTAs) before its later async-proxy (bulk / tensor copy) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // ---- named barrier over a subset of warps (non-.aligned form: callers may arrive from divergent code)
 __device__ __forceinline__ void named_bar(int id, int threads) {
