@@ -100,6 +100,7 @@ enum : int {
     C_RBAR = 4,     // fused router: CTAs whose logits are stored (grid barrier)
     C_XBAR = 5,     // fused router with host input: CTAs whose slice of x is in device memory (grid barrier)
     C_NEVER = 6,    // diagnostic mode 2: a word nothing increments (a dependency that never arrives)
+    C_TBAR = 7,     // fused router above TOPK_ALL_MAX tokens: CTAs whose share of the top-k is stored (grid barrier)
     C_CNT = 8,      // [64] column-tile arrivals
     C_SDONE = 72,   // [4] finished shared gate_up tiles per token group
     C_SPLIT = 80,   // [64] split-K arrivals per (shared tile, token group)
@@ -192,10 +193,6 @@ static_assert(SCR_RTW + MAXSLOTS * 4 <= NST * STAGE_BYTES, "plan scratch (pipeli
 // fused router: this CTA's router rows live in pipeline 1's ring (idle until the plan is done)
 constexpr int RROWS_BYTES = NST * STAGE_BYTES;
 constexpr int RPC_MAX = 8;                                          // router rows per CTA
-// fused router: token tiles of x in the blocks of pipelines 2 .. NVP - 1 (idle until the plan is done); H <= 4096
-// gives >= 7 tokens per tile
-constexpr int XTILE_BYTES = (NVP - 2) * VP_BYTES;
-static_assert(NVP >= 3 && XTILE_BYTES >= 4096 * 2 * 7, "x tile of the fused router");
 
 enum : int { DBG_CONSUMERS = 30, DBG_STOP = 31, DBG_ENTRY = 0xFFF };   // timeline events (dbg)
 enum : int { MISC_U = 0, MISC_NTOK = 1, MISC_GT = 2, MISC_FLAG = 3, MISC_DBGN = 5, MISC_DUPS = 7 };
@@ -535,55 +532,91 @@ __device__ void shard_tile(const Params& p, const Layout& L, const int16_t* sids
 
 // ------------------------------------------------------------------------------------------------ fused router
 // logits[t, e] = bf16(x[t] . w[e]) for this CTA's router rows (already requested into rrows), a grid barrier, then
-// this CTA's own top-k of every token into rids / rtw (serve/qwenfast/qf_router.cu). Not inlined: it runs once per
-// launch, and as a separate function its registers do not compete with the pipelines' loops.
+// the top-k of every token into rids / rtw (serve/qwenfast/qf_router.cu). Up to TOPK_ALL_MAX tokens every CTA
+// selects every token itself (at most one token per warp), so the plan needs no ids from memory; above that, CTA c
+// selects token c (and c + grid ...) into the caller's ids / weights outputs, a second grid barrier follows, and every
+// CTA reads them back. Not inlined: it runs once per launch, and as a separate function its registers do not compete
+// with the pipelines' loops.
+// This CTA's router rows [r0, r0 + nrows) times every token, with the standalone router's arithmetic (router.cu):
+// the 16 warps split the hidden dimension into 32-k blocks (BPW consecutive blocks per warp, BPW the power of two the
+// standalone router picks for H); per token tile of 8 a warp runs two m16n8k16 mmas per block (this CTA's rows as the
+// A operand: rows g < nrows, the others zero; the tokens' x from L2 as B); the per-warp fp32 partials are summed in
+// warp order through red (shared memory). The x of TB token tiles is requested before the first of their mmas.
+template <int BPW>
+__device__ __forceinline__ void router_logits(const Params& p, float* red, const uint8_t* rrows, int r0, int nrows) {
+    constexpr int TB = 16 / BPW < 8 ? 16 / BPW : 8;
+    static_assert(MOE_THREADS / 32 == 16 && 16 * RPC_MAX * QF_MAX_TOKENS * 4 <= VP_BYTES, "router partials");
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 2, t4 = lane & 3;
+    const int M = p.M, nblk = p.H / 32, b0 = warp * BPW;
+    const int ntile = (M + 7) >> 3, rp = ntile * 8;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    const uint4* wrow = reinterpret_cast<const uint4*>(rrows) + (size_t)g * (p.H / 8) + t4;
+    for (int nt0 = 0; nt0 < ntile; nt0 += TB) {
+        uint4 xv[TB][BPW];
+#pragma unroll
+        for (int tb = 0; tb < TB; ++tb) {
+            const int tok = (nt0 + tb) * 8 + g;
+            const uint4* xr = reinterpret_cast<const uint4*>(p.x + (size_t)(tok < M ? tok : 0) * p.H) + t4;
+#pragma unroll
+            for (int i = 0; i < BPW; ++i) xv[tb][i] = (tok < M && b0 + i < nblk) ? __ldcg(xr + 4 * (b0 + i)) : zero;
+        }
+#pragma unroll
+        for (int tb = 0; tb < TB; ++tb) {
+            const int nt = nt0 + tb;
+            if (nt >= ntile) break;
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int i = 0; i < BPW; ++i) {
+                if (b0 + i < nblk) {
+                    const uint4 wa = g < nrows ? wrow[4 * (b0 + i)] : zero;
+                    qf::mma_bf16(d, wa.x, 0u, wa.y, 0u, xv[tb][i].x, xv[tb][i].y);
+                    qf::mma_bf16(d, wa.z, 0u, wa.w, 0u, xv[tb][i].z, xv[tb][i].w);
+                }
+            }
+            if (g < nrows) {
+                red[(warp * RPC_MAX + g) * rp + nt * 8 + 2 * t4] = d[0];
+                red[(warp * RPC_MAX + g) * rp + nt * 8 + 2 * t4 + 1] = d[1];
+            }
+        }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nrows * M; idx += MOE_THREADS) {
+        const int r = idx % nrows, t = idx / nrows;
+        float sum = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < 16; ++ww) sum += red[(ww * RPC_MAX + r) * rp + t];
+        p.logits[(size_t)t * p.E + r0 + r] = __float2bfloat16(sum);
+    }
+}
+
+constexpr int TOPK_ALL_MAX = 16;
 __device__ __noinline__ void fused_router(const Params& p, uint8_t* smem, const uint8_t* rrows, int r0, int nrows,
                                           int* rids, float* rtw) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int M = p.M, E = p.E, topk = p.topk;
     uint32_t* ctrl = p.ctrl;
-    // logits: one warp per (token, row) pair, lanes over 16-byte k chunks (fp32 fma in chunk order, then a butterfly
-    // sum); then a grid barrier, and every CTA selects the top-k of every token itself (the same routine as the
-    // router kernel), so the plan needs no ids from memory
     qf::cp_async_wait_all();
     __syncthreads();
-    // x is staged in shared memory by token tiles (pipeline 2's ring, idle until the plan is done), then one warp
-    // per (token, row) pair reads both operands from shared memory; a small loop body (this code runs once per
-    // launch, with its instructions fetched cold) and few registers
-    const int nc = p.H / 8;
-    uint8_t* xs = smem + 2 * VP_BYTES;
-    const int tile_tok = min(M, XTILE_BYTES / (p.H * 2));
-    for (int t0 = 0; t0 < M; t0 += tile_tok) {
-        const int nt = min(tile_tok, M - t0);
-        const char* xsrc = reinterpret_cast<const char*>(p.x + (size_t)t0 * p.H);
-        for (int c = tid; c < nt * nc; c += MOE_THREADS) qf::cp_async16(xs + 16 * c, xsrc + 16 * c, 16u);
-        qf::cp_async_wait_all();
-        __syncthreads();
-#pragma unroll 1
-        for (int pr = warp; pr < nt * nrows; pr += MOE_THREADS / 32) {
-            const int tt = pr / nrows, r = pr - tt * nrows;
-            const uint4* xr = reinterpret_cast<const uint4*>(xs) + (size_t)tt * nc;
-            const uint4* wr = reinterpret_cast<const uint4*>(rrows) + (size_t)r * nc;
-            float a = 0.f;
-#pragma unroll 2
-            for (int c = lane; c < nc; c += 32) {
-                const uint4 xv = xr[c], wv = wr[c];
-                const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xw[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    a = fmaf(__uint_as_float(ww[i] << 16), __uint_as_float(xw[i] << 16), a);
-                    a = fmaf(__uint_as_float(ww[i] & 0xffff0000u), __uint_as_float(xw[i] & 0xffff0000u), a);
-                }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-            if (lane == 0) p.logits[(size_t)(t0 + tt) * E + r0 + r] = __float2bfloat16(a);
-        }
-        __syncthreads();   // the tile's x is consumed before the next tile overwrites it
-    }
+    // logits with the standalone router's arithmetic (router.cu), so that both routers give the same bits
+    const int bpw = (p.H / 32 + 15) / 16;
+    float* red = reinterpret_cast<float*>(smem + 2 * VP_BYTES);   // pipeline 2's ring, idle until the plan is done
+    if (bpw <= 1) router_logits<1>(p, red, rrows, r0, nrows);
+    else if (bpw <= 2) router_logits<2>(p, red, rrows, r0, nrows);
+    else if (bpw <= 4) router_logits<4>(p, red, rrows, r0, nrows);
+    else router_logits<8>(p, red, rrows, r0, nrows);
     grid_barrier(ctrl, C_RBAR);
-    for (int t = warp; t < M; t += MOE_THREADS / 32)
-        qf::topk_row_any(p.logits + (size_t)t * E, E, topk, p.renorm, rtw + t * topk, rids + t * topk);
+    if (M <= TOPK_ALL_MAX) {
+        for (int t = warp; t < M; t += MOE_THREADS / 32)
+            qf::topk_row_any(p.logits + (size_t)t * E, E, topk, p.renorm, rtw + t * topk, rids + t * topk);
+    } else {
+        for (int t = (int)blockIdx.x + (int)gridDim.x * warp; t < M; t += (int)gridDim.x * (MOE_THREADS / 32))
+            qf::topk_row_any(p.logits + (size_t)t * E, E, topk, p.renorm, p.tw_out + t * topk, p.ids_out + t * topk);
+        grid_barrier(ctrl, C_TBAR);
+        for (int s = tid; s < M * topk; s += MOE_THREADS) {
+            rids[s] = __ldcg(p.ids_out + s);
+            rtw[s] = __ldcg(p.tw_out + s);
+        }
+    }
     __syncthreads();
 }
 
@@ -690,7 +723,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             const int e = fused ? rids[s] : p.ids[s];
             const float twv = fused ? rtw[s] : p.tw[s];
             tws[s] = bf16r(twv);   // the down epilogues read the slot weights from here, not from L2
-            if (fused && blockIdx.x == 0) {   // the fused router's outputs for the caller
+            if (fused && blockIdx.x == 0 && M <= TOPK_ALL_MAX) {   // the fused router's outputs for the caller
                 p.ids_out[s] = e;
                 p.tw_out[s] = twv;
             }
