@@ -86,8 +86,8 @@ constexpr int NSPLIT = 4;                     // split-K of the shared expert's 
 constexpr int G1_SPLIT = 2;                   // k halves of a routed gate_up item (finished by the later half) when
                                               // all halves fit in one wave of pipelines (small M)
 constexpr int MAXSLOTS = QF_MAX_TOKENS * QF_MAX_TOPK;
-constexpr int CB_TOK = 8;                     // tokens of a combine item (x 16 column chunks = one per thread)
-constexpr int CB_BATCH = 4;                   // slot loads a combine thread keeps in flight (registers)
+constexpr int CB_TOK = 4;                     // tokens of a combine item (x 32 four-column chunks = one per thread)
+constexpr int CB_BATCH = 8;                   // slot loads a combine thread keeps in flight (registers)
 constexpr uint64_t DEP_WAIT_NS = 1000000000ull;    // cross-CTA dependency waits
 constexpr uint64_t PIPE_WAIT_NS = 4000000000ull;   // ring waits (longer: they cover the dependency waits)
 
@@ -476,38 +476,58 @@ __device__ __forceinline__ uint4 finish8(const float (&a)[8], bool has_gate, flo
     return o;
 }
 
+__device__ __forceinline__ void add4(float (&a)[4], uint2 v) {
+    a[0] += bf16_lo(v.x);
+    a[1] += bf16_hi(v.x);
+    a[2] += bf16_lo(v.y);
+    a[3] += bf16_hi(v.y);
+}
+// finish8 for 4 columns (the same arithmetic per column)
+__device__ __forceinline__ uint2 finish4(const float (&a)[4], bool has_gate, float gl, uint2 sv) {
+    float r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = bf16r(a[j]);
+    if (has_gate) {
+        const float gate = 1.f / (1.f + __expf(-gl));
+        r[0] = fmaf(gate, bf16_lo(sv.x), r[0]);
+        r[1] = fmaf(gate, bf16_hi(sv.x), r[1]);
+        r[2] = fmaf(gate, bf16_lo(sv.y), r[2]);
+        r[3] = fmaf(gate, bf16_hi(sv.y), r[3]);
+    }
+    const __nv_bfloat162 b0 = __floats2bfloat162_rn(r[0], r[1]), b1 = __floats2bfloat162_rn(r[2], r[3]);
+    return make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
+}
+
 // Combine of one 128-column tile for tokens CB_TOK g .. CB_TOK g + CB_TOK - 1: out = bf16(gate * shared +
-// bf16(sum_kpos y)); a thread owns one (token, 8 columns). The shared row, the gate logit and CB_BATCH slots are
-// requested before the first add (one L2 round trip per CB_BATCH slots); the sum runs in top-k order.
+// bf16(sum_kpos y)); a thread owns one (token, 4 columns). The shared row, the gate logit and CB_BATCH routed slots
+// are requested before the first add (one L2 round trip per CB_BATCH slots); the sum runs in top-k order.
 __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int g, int ctid) {
     const int H = p.H, topk = p.topk;
-    const int t = CB_TOK * g + (ctid >> 4), n = 128 * c + 8 * (ctid & 15);
+    const int t = CB_TOK * g + (ctid >> 5), n = 128 * c + 4 * (ctid & 31);
     if (t >= p.M) return;
-    uint4 sv = make_uint4(0u, 0u, 0u, 0u);
+    uint2 sv = make_uint2(0u, 0u);
     float gl = 0.f;
     if (L.has_gate) {
         gl = __ldcg(p.gl + t);
-        if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
-        else sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
+        if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint2*>(p.sbuf + (size_t)t * H + n));
+        else sv = __ldcg(reinterpret_cast<const uint2*>(p.shared + (size_t)t * H + n));
     }
-    float a[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a[j] = 0.f;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k0 = 0; k0 < topk; k0 += CB_BATCH) {
-        uint4 v[CB_BATCH];
+        uint2 v[CB_BATCH];
         bool live[CB_BATCH];
 #pragma unroll
         for (int b = 0; b < CB_BATCH; ++b) {
             const int kp = k0 + b, s = t * topk + kp;
             const int e = kp < topk ? sids[s] : -1;
             live[b] = e >= 0 && e >= p.elo && e < p.ehi;
-            if (live[b]) v[b] = __ldcg(reinterpret_cast<const uint4*>(p.ybuf + (size_t)s * H + n));
+            if (live[b]) v[b] = __ldcg(reinterpret_cast<const uint2*>(p.ybuf + (size_t)s * H + n));
         }
 #pragma unroll
         for (int b = 0; b < CB_BATCH; ++b)
-            if (live[b]) add8(a, v[b]);
+            if (live[b]) add4(a, v[b]);
     }
-    *reinterpret_cast<uint4*>(p.out + (size_t)t * H + n) = finish8(a, L.has_gate != 0, gl, sv);
+    *reinterpret_cast<uint2*>(p.out + (size_t)t * H + n) = finish4(a, L.has_gate != 0, gl, sv);
 }
 
 // Expert-parallel shard (mode 1), one 128-column tile, tokens CB_TOK g ..: make ybuf the shard's exact contribution
@@ -516,18 +536,18 @@ __device__ void combine_tile(const Params& p, const Layout& L, const int16_t* si
 // local experts were written by the down-projection epilogues.
 __device__ void shard_tile(const Params& p, const Layout& L, const int16_t* sids, int c, int g, int ctid) {
     const int H = p.H, topk = p.topk;
-    const int t = CB_TOK * g + (ctid >> 4), n = 128 * c + 8 * (ctid & 15);
+    const int t = CB_TOK * g + (ctid >> 5), n = 128 * c + 4 * (ctid & 31);
     if (t >= p.M) return;
-    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-    uint4 sv = zero;
-    if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint4*>(p.sbuf + (size_t)t * H + n));
-    else if (p.shared != nullptr) sv = __ldcg(reinterpret_cast<const uint4*>(p.shared + (size_t)t * H + n));
+    const uint2 zero = make_uint2(0u, 0u);
+    uint2 sv = zero;
+    if (L.has_shw) sv = __ldcg(reinterpret_cast<const uint2*>(p.sbuf + (size_t)t * H + n));
+    else if (p.shared != nullptr) sv = __ldcg(reinterpret_cast<const uint2*>(p.shared + (size_t)t * H + n));
     for (int kp = 0; kp < topk; ++kp) {
         const int s = t * topk + kp;
         const int e = sids[s];
-        if (e < 0 || e < p.elo || e >= p.ehi) *reinterpret_cast<uint4*>(p.ybuf + (size_t)s * H + n) = zero;
+        if (e < 0 || e < p.elo || e >= p.ehi) *reinterpret_cast<uint2*>(p.ybuf + (size_t)s * H + n) = zero;
     }
-    *reinterpret_cast<uint4*>(p.ybuf + (size_t)(p.M * topk + t) * H + n) = sv;
+    *reinterpret_cast<uint2*>(p.ybuf + (size_t)(p.M * topk + t) * H + n) = sv;
 }
 
 // ------------------------------------------------------------------------------------------------ fused router
