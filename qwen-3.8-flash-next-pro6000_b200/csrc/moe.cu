@@ -301,16 +301,12 @@ __device__ __forceinline__ uint32_t nvfp4_pair(uint32_t q, int j, uint32_t scale
 // sb: the ring stage (weights in fragment order: [tile (8)][half (2)][lane (32)][4 words]); bb: the token block,
 // row stride brow. TWO: the item has more than 8 tokens (second n8 tile). NVFP4 (FMT 1): fsc = the lane's eight
 // E4M3 scales of the stage, byte (m * 2 + h) * 2 + (row g : 0, row g + 8 : 1) (each covers the lane's 16 k).
-// int4 (FMT 0): the A registers hold the biased codes 128 + code (one lop3 each, exact), and the bias is removed
-// once per stage and token: an mma of the constant -136 (= -(128 + the zero point 8)) against the same token
-// fragments gives -136 * (sum of the token's 128 k), the same for every row, added to both tiles' partials.
-// Every product is exact; the partials are fp32.
+// int4 (FMT 0): the A registers hold the signed codes code - 8 (one lop3 to the biased code 128 + code and one
+// bf16x2 subtract of 136, both exact). Every product is exact; the partials are fp32.
 template <int FMT, bool TWO>
 __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, int brow, int rw, int lane, uint2 fsc,
                                          float (&d)[4][4]) {
     const int g = lane >> 2, t4 = lane & 3;
-    constexpr uint32_t NEG136 = 0xC308C308u;   // bf16 -136 in both halves
-    float corr[2][4];
     // every accumulator chain starts with a zero-input mma (h = 0, s = 0): no register clearing per stage
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -328,20 +324,6 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
             const uint4 a = *reinterpret_cast<const uint4*>(sb + (((2 * rw + m) * 2 + h) * 32 + lane) * 16);
             const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
             uint32_t sA = 0u, sB = 0u;
-            if constexpr (FMT == 0) {
-                if (m == 0) {   // the bias term of this half's four k16 steps (once per token tile)
-#pragma unroll
-                    for (int s = 0; s < 4; ++s) {
-                        if (h == 0 && s == 0) {
-                            qf::mma_bf16_z(corr[0], NEG136, NEG136, NEG136, NEG136, xw0[0], xw0[1]);
-                            if constexpr (TWO) qf::mma_bf16_z(corr[1], NEG136, NEG136, NEG136, NEG136, xw1[0], xw1[1]);
-                        } else {
-                            qf::mma_bf16(corr[0], NEG136, NEG136, NEG136, NEG136, xw0[2 * s], xw0[2 * s + 1]);
-                            if constexpr (TWO) qf::mma_bf16(corr[1], NEG136, NEG136, NEG136, NEG136, xw1[2 * s], xw1[2 * s + 1]);
-                        }
-                    }
-                }
-            }
             if constexpr (FMT == 1) {
                 const uint32_t ws = (m == 0 ? fsc.x : fsc.y) >> (16 * h);
                 sA = qf::e4m3_scale_bf16x2(ws & 0xFFu);
@@ -353,7 +335,7 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
                 // word's nibble pairs (0,4) (1,5) (2,6) (3,7)
                 uint32_t v[4];
                 if constexpr (FMT == 0) {
-                    qf::biased_w4(aw[s], v);
+                    qf::signed_w4(aw[s], v);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 4; ++j) v[j] = nvfp4_pair(aw[s], j, (j & 1) ? sB : sA);
@@ -371,15 +353,6 @@ __device__ __forceinline__ void stage_w4(const uint8_t* sb, const uint8_t* bb, i
     if constexpr (!TWO && FMT != 0) {   // the unused token tile's accumulators (added up by the caller): zero
 #pragma unroll
         for (int m = 0; m < 2; ++m) d[2 * m + 1][0] = d[2 * m + 1][1] = d[2 * m + 1][2] = d[2 * m + 1][3] = 0.f;
-    }
-    if constexpr (FMT == 0) {
-#pragma unroll
-        for (int m = 0; m < 2; ++m)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                d[2 * m][i] += corr[0][i];
-                if constexpr (TWO) d[2 * m + 1][i] += corr[1][i];
-            }
     }
 }
 
@@ -1337,7 +1310,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 for (int m = 0; m < 2; ++m) {
                     const int col = 64 * d.tile + 8 * (2 * rw + m) + g;
 #pragma unroll
-                    for (int n = 0; n < 2; ++n)
+                    for (int n = 0; n < (d.ntok > 8 ? 2 : 1); ++n)   // the second token tile only when it has tokens
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
                             const int r = row[2 * n + h];
@@ -1372,7 +1345,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
 #pragma unroll
                 for (int m = 0; m < 2; ++m)
 #pragma unroll
-                    for (int n = 0; n < 2; ++n)
+                    for (int n = 0; n < (d.ntok > 8 ? 2 : 1); ++n)   // the second token tile only when it has tokens
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const int j = 2 * n + (i & 1);
@@ -1403,7 +1376,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
 #pragma unroll
                 for (int m = 0; m < 2; ++m)
 #pragma unroll
-                    for (int n = 0; n < 2; ++n)
+                    for (int n = 0; n < (d.ntok > 8 ? 2 : 1); ++n)   // the second token tile only when it has tokens
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             const int tok = 8 * n + 2 * t4 + (i & 1);
