@@ -1,0 +1,286 @@
+// W8A16 group-scaled INT8 GEMM for decode token counts (M <= 16) on register fragments: mma.sync m16n8k16 with fp16
+// operands, fp32 accumulation. Included by w8g_tc.cu (it shares that file's status word and helpers); qf_w8g_gemm
+// routes M <= 16 with K % 128 == 0 here and everything else to the tensor-memory kernel.
+//
+//   y[t, n] = bf16( sum over 64-k halves h of  s[n, g(h)] * 2^e[t, h] * sum_{k in h} q[n, k] * x16[t, k] )
+//
+// where x16[t, k] = fp16(x[t, k] * 2^-e[t, h]) and e[t, h] = floor(log2 max|x[t, h]|) - 14 (clamped), so the slice's
+// largest value lands in [2^14, 2^15): the conversion is exact down to 2^-31 of that maximum, and the int8 weights are
+// exact in fp16 (i8x4_to_f16), so every product is exact and only the fp32 sums round -- the arithmetic of
+// serve/qwenfast/qf_w8g.cu:47-139 (fp32 group sums times the group scale) up to fp32 association.
+//
+// Structure (a weight stream, like the decode MoE kernel's register path):
+//   * One CTA per item = (128-row tile, split of the K stages): the tiles' K / 128 stages are cut into S splits of ks
+//     stages each, S chosen so that the grid covers the GPU about two CTAs deep (S <= S_MAX). 160 threads: warps 0-3 consume,
+//     warp 4 (one lane) is the producer.
+//   * Producer: an NST-stage ring of 16 KB weight stages (128 rows x 128 k, one TMA 2-D tile each, 128-byte swizzle:
+//     the four 16-byte chunks a lane reads are spread over all banks), requested before griddepcontrol.wait (the
+//     weights are load-time data).
+//   * Consumers, first: the item's token slices (fp16 with the per-(token, 64-k) exponent, 16-byte chunks swizzled by
+//     token) and group scales into shared memory; then per stage and 64-k half, warp w runs the m16 tiles 2w, 2w + 1:
+//     one 16-byte load per row and half gives the four k16 steps of that row (k = 64 h + 16 t4 + 4 s + 0..3 in the
+//     mma columns 2 t4, 2 t4 + 1, 2 t4 + 8, 2 t4 + 9, the same permutation for the tokens), a second n8 token tile
+//     only above 8 tokens. Each half's fp32 partial is scaled by s[row] * 2^e[token] into the accumulators.
+//   * Splits of one tile are added without waiting: each item stores its fp32 partial to its own slot of the fixup
+//     buffer and counts itself on the tile's counter; the item that counts last adds all slots in split order (the
+//     same sum whichever split comes last), writes y and re-arms the counter.
+//   * Every wait is bounded; a wait that runs out sets a bit of the status word (qf_w8g_take_status).
+#pragma once
+
+namespace w8rf {
+
+constexpr int THREADS = 160;
+constexpr int ROWS = 128;                 // weight rows per tile
+constexpr int SK = 128;                   // k per stage
+constexpr int STAGE = ROWS * SK;          // 16 KB of int8
+constexpr int NST = 3;                    // ring stages
+constexpr int KS_MAX = 12;                // stages per item
+constexpr int S_MAX = 8;                  // splits per tile
+constexpr int MT = 16;                    // staged token rows (M <= 16)
+constexpr int TOK_STAGE = 2 * MT * 128;   // fp16 token slices of one stage: [half][token][128 B]
+constexpr int PART = MT * ROWS;           // floats of one fixup slot
+constexpr uint64_t WAIT_NS = 2000000000ull;
+
+// shared memory (base aligned to 1024 for the swizzled TMA tiles): ring [NST][STAGE] | tokens [ks][TOK_STAGE] |
+// factors float [ks][2][MT] | scales float [ks][2][ROWS] | full[NST], empty[NST] | flag
+__host__ __device__ constexpr int off_tok() { return NST * STAGE; }
+__host__ __device__ constexpr int off_fac(int ks) { return off_tok() + ks * TOK_STAGE; }
+__host__ __device__ constexpr int off_sc(int ks) { return off_fac(ks) + ks * 2 * MT * 4; }
+__host__ __device__ constexpr int off_bar(int ks) { return off_sc(ks) + ks * 2 * ROWS * 4; }
+__host__ __device__ constexpr int smem_bytes(int ks) { return off_bar(ks) + 2 * NST * 8 + 16 + 1024; }
+
+struct Params {
+    CUtensorMap wmap;   // q [N, K] uint8; box 128 k x 128 rows, 128-byte swizzle
+    const __nv_bfloat16* x;
+    const __nv_bfloat16* s;
+    __nv_bfloat16* y;
+    float* fix;
+    uint32_t* cnt;
+    unsigned* err;
+    int ldx, ldy, M, N, K, group, ks, S, KT;
+};
+
+__device__ __forceinline__ float pow2f(int k) { return __uint_as_float((uint32_t)(127 + k) << 23); }
+
+template <bool TWO>
+__global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ks = p.ks;
+    uint8_t* ring = smem;
+    uint8_t* tok = smem + off_tok();
+    float* fac = reinterpret_cast<float*>(smem + off_fac(ks));
+    float* sc = reinterpret_cast<float*>(smem + off_sc(ks));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + off_bar(ks));
+    uint64_t* empty = full + NST;
+    int* flag = reinterpret_cast<int*>(empty + NST);
+    const int item = blockIdx.x, tile = item / p.S, split = item - tile * p.S;
+    const int j0 = split * ks, nks = min(ks, p.KT - j0);   // this item's stages: K stages j0 .. j0 + nks - 1
+    if (tid == 0) {
+        for (int i = 0; i < NST; ++i) {
+            qf::mbar_init(full + i, 1);
+            qf::mbar_init(empty + i, 4);
+        }
+        qf::mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == 4) {
+        // ------------------------------------------------------------------ producer (one lane)
+        if (lane == 0) {
+            const uint64_t pol = qf::policy_evict_first();
+            for (int j = 0; j < nks; ++j) {
+                const int st = j % NST;
+                if (j >= NST && !qf::mbar_wait(empty + st, ((j / NST) - 1) & 1, WAIT_NS)) atomicOr(p.err, 16u);
+                qf::mbar_arrive_expect_tx(full + st, STAGE);
+                tma_load_2d(ring + st * STAGE, &p.wmap, (j0 + j) * SK, tile * ROWS, full + st, pol);
+            }
+        }
+        qf::pdl_wait();
+        return;
+    }
+
+    // ---------------------------------------------------------------------- consumers (128 threads)
+    qf::pdl_wait();   // x comes from the previous kernel
+    const int M = p.M, kb = j0 * SK;
+    // token slices: 8 threads per (stage, half, token) slice of 64 k, thread c the 16-byte chunk c (k 8c .. 8c + 7)
+    {
+        const int c = tid & 7, nsl = nks * 2 * M;
+        for (int sl0 = 0; sl0 < nsl; sl0 += ROWS / 8 * 4) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {   // four slices in flight per thread
+                const int sl = sl0 + u * (ROWS / 8) + (tid >> 3);
+                v[u] = make_uint4(0u, 0u, 0u, 0u);
+                if (sl < nsl) {
+                    const int t = sl % M, jh = sl / M;   // jh = stage * 2 + half
+                    v[u] = __ldcg(reinterpret_cast<const uint4*>(p.x + (size_t)t * p.ldx + kb + jh * 64 + c * 8));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int sl = sl0 + u * (ROWS / 8) + (tid >> 3);   // uniform within each group of 8 lanes
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+                uint32_t mx = 0u;   // largest |x| as a bit pattern (monotone for non-negative floats)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) mx = max(mx, max((w[i] << 16) & 0x7FFF0000u, w[i] & 0x7FFF0000u));
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if (sl < nsl) {
+                    const int t = sl % M, jh = sl / M;
+                    const int ex = mx == 0u ? 0 : max(-110, min(110, (int)(mx >> 23) - 127 - 14));
+                    const float mul = pow2f(-ex);
+                    uint32_t o[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const __half2 h2 = __floats2half2_rn(qf::bf16_lo(w[i]) * mul, qf::bf16_hi(w[i]) * mul);
+                        o[i] = *reinterpret_cast<const uint32_t*>(&h2);
+                    }
+                    *reinterpret_cast<uint4*>(tok + jh * (MT * 128) + t * 128 + ((c ^ (t & 7)) * 16)) =
+                        make_uint4(o[0], o[1], o[2], o[3]);
+                    if (c == 0) fac[jh * MT + t] = pow2f(ex);
+                }
+            }
+        }
+        // group scales of row tid (one per half: a 128-group gives both halves the same scale), all requested at once
+        const __nv_bfloat16* srow = p.s + (size_t)(tile * ROWS + tid) * (p.K / p.group);
+        __nv_bfloat16 sv[2 * KS_MAX];
+#pragma unroll
+        for (int jh = 0; jh < 2 * KS_MAX; ++jh)
+            if (jh < 2 * nks) sv[jh] = srow[(kb + jh * 64) / p.group];
+#pragma unroll
+        for (int jh = 0; jh < 2 * KS_MAX; ++jh)
+            if (jh < 2 * nks) sc[jh * ROWS + tid] = __bfloat162float(sv[jh]);
+    }
+    qf::named_bar(1, ROWS);
+
+    const int rw = warp, g = lane >> 2, t4 = lane & 3;
+    float acc[4][4];   // acc[2 m + n][i]: row 16 (2 rw + m) + g + 8 (i / 2), token 8 n + 2 t4 + (i % 2)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nks; ++j) {
+        const int st = j % NST;
+        if (ok && !qf::mbar_wait(full + st, (j / NST) & 1, WAIT_NS)) {
+            atomicOr(p.err, 32u);
+            ok = false;
+        }
+        const uint8_t* wb = ring + st * STAGE;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint8_t* tb = tok + (j * 2 + h) * (MT * 128);
+            const uint4 x0a = *reinterpret_cast<const uint4*>(tb + g * 128 + (((2 * t4) ^ g) * 16));
+            const uint4 x0b = *reinterpret_cast<const uint4*>(tb + g * 128 + (((2 * t4 + 1) ^ g) * 16));
+            uint4 x1a = make_uint4(0u, 0u, 0u, 0u), x1b = x1a;
+            if constexpr (TWO) {
+                x1a = *reinterpret_cast<const uint4*>(tb + (8 + g) * 128 + (((2 * t4) ^ g) * 16));
+                x1b = *reinterpret_cast<const uint4*>(tb + (8 + g) * 128 + (((2 * t4 + 1) ^ g) * 16));
+            }
+            const uint32_t xw0[8] = {x0a.x, x0a.y, x0a.z, x0a.w, x0b.x, x0b.y, x0b.z, x0b.w};
+            const uint32_t xw1[8] = {x1a.x, x1a.y, x1a.z, x1a.w, x1b.x, x1b.y, x1b.z, x1b.w};
+            const float* fh = fac + (j * 2 + h) * MT;
+            const float f00 = fh[2 * t4], f01 = fh[2 * t4 + 1];
+            const float f10 = TWO ? fh[8 + 2 * t4] : 0.f, f11 = TWO ? fh[9 + 2 * t4] : 0.f;
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const int r0 = 16 * (2 * rw + m) + g;
+                const uint4 wa = *reinterpret_cast<const uint4*>(wb + r0 * SK + (((4 * h + t4) ^ g) * 16));
+                const uint4 wc = *reinterpret_cast<const uint4*>(wb + (r0 + 8) * SK + (((4 * h + t4) ^ g) * 16));
+                const uint32_t aw[4] = {wa.x, wa.y, wa.z, wa.w}, cw[4] = {wc.x, wc.y, wc.z, wc.w};
+                float d0[4], d1[4];
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    uint32_t a0, a2, a1, a3;
+                    i8x4_to_f16(aw[s], a0, a2);   // row r0: k + 0|1, k + 2|3
+                    i8x4_to_f16(cw[s], a1, a3);   // row r0 + 8
+                    if (s == 0) {
+                        qf::mma_f16_z(d0, a0, a1, a2, a3, xw0[0], xw0[1]);
+                        if constexpr (TWO) qf::mma_f16_z(d1, a0, a1, a2, a3, xw1[0], xw1[1]);
+                    } else {
+                        qf::mma_f16(d0, a0, a1, a2, a3, xw0[2 * s], xw0[2 * s + 1]);
+                        if constexpr (TWO) qf::mma_f16(d1, a0, a1, a2, a3, xw1[2 * s], xw1[2 * s + 1]);
+                    }
+                }
+                const float* sh = sc + (j * 2 + h) * ROWS;
+                const float s0 = sh[r0], s1 = sh[r0 + 8];
+                acc[2 * m][0] = fmaf(d0[0], s0 * f00, acc[2 * m][0]);
+                acc[2 * m][1] = fmaf(d0[1], s0 * f01, acc[2 * m][1]);
+                acc[2 * m][2] = fmaf(d0[2], s1 * f00, acc[2 * m][2]);
+                acc[2 * m][3] = fmaf(d0[3], s1 * f01, acc[2 * m][3]);
+                if constexpr (TWO) {
+                    acc[2 * m + 1][0] = fmaf(d1[0], s0 * f10, acc[2 * m + 1][0]);
+                    acc[2 * m + 1][1] = fmaf(d1[1], s0 * f11, acc[2 * m + 1][1]);
+                    acc[2 * m + 1][2] = fmaf(d1[2], s1 * f10, acc[2 * m + 1][2]);
+                    acc[2 * m + 1][3] = fmaf(d1[3], s1 * f11, acc[2 * m + 1][3]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) qf::mbar_arrive(empty + st);
+    }
+    qf::pdl_launch_dependents();
+
+    // ---------------------------------------------------------------------- epilogue
+    const int ctid = tid;
+    auto store_y = [&](const float (&a)[4][4]) {
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int n = 0; n < (TWO ? 2 : 1); ++n)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int t = 8 * n + 2 * t4 + (i & 1);
+                    if (t < M)
+                        p.y[(size_t)t * p.ldy + tile * ROWS + 16 * (2 * rw + m) + g + 8 * (i >> 1)] =
+                            __float2bfloat16(a[2 * m + n][i]);
+                }
+    };
+    if (p.S == 1) {
+        store_y(acc);
+        return;
+    }
+    float* mine = p.fix + (size_t)item * PART + ctid * 16;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) __stcg(reinterpret_cast<float4*>(mine + 4 * j), make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]));
+    __threadfence();
+    qf::named_bar(1, ROWS);
+    if (ctid == 0) {
+        const bool last = atomicAdd(p.cnt + tile, 1u) == (uint32_t)(p.S - 1);
+        if (last) {
+            __threadfence();
+            p.cnt[tile] = 0u;
+        }
+        *flag = last ? 1 : 0;
+    }
+    qf::named_bar(1, ROWS);
+    if (*flag == 0) return;
+    __threadfence();
+    // the S <= S_MAX slots in split order (the same sum whichever split came last), in two passes of 8 floats per
+    // thread with every slot's loads in flight
+    float tot[4][4];
+    const float* part = p.fix + (size_t)tile * p.S * PART + ctid * 16;
+#pragma unroll
+    for (int ps = 0; ps < 2; ++ps) {
+        float4 q[S_MAX][2];
+#pragma unroll
+        for (int sp = 0; sp < S_MAX; ++sp)
+            if (sp < p.S) {
+#pragma unroll
+                for (int j = 0; j < 2; ++j) q[sp][j] = __ldcg(reinterpret_cast<const float4*>(part + (size_t)sp * PART + 4 * (2 * ps + j)));
+            }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            float4 a = q[0][j];
+#pragma unroll
+            for (int sp = 1; sp < S_MAX; ++sp)
+                if (sp < p.S) {
+                    a.x += q[sp][j].x; a.y += q[sp][j].y; a.z += q[sp][j].z; a.w += q[sp][j].w;
+                }
+            tot[2 * ps + j][0] = a.x; tot[2 * ps + j][1] = a.y; tot[2 * ps + j][2] = a.z; tot[2 * ps + j][3] = a.w;
+        }
+    }
+    store_y(tot);
+}
+
+}  // namespace w8rf

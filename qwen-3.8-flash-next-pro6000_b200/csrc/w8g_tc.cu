@@ -33,6 +33,8 @@
 //     writes y. No run waits for another, so the grid need not be co-resident.
 //   * Every wait is bounded; a wait that runs out sets a bit of the sticky status word (qf_w8g_take_status) and
 //     the CTA drains (the affected outputs are undefined).
+#include <algorithm>
+
 #include "qf_common.cuh"
 
 namespace {
@@ -379,6 +381,59 @@ __global__ void __launch_bounds__(G_THREADS, Cfg<NT>::MINB)
 
 __device__ unsigned g_w8g_err;
 
+#include "w8g_rf.cuh"
+
+// The register-fragment kernel's launch (M <= 16, K % 128 == 0): ks stages per item chosen so that the grid covers
+// the SMs about two CTAs deep (at most KS_MAX: larger weights take several waves) with at most S_MAX splits per tile
+// (S = ceil(K / 128 / ks)), at most `cap` items (fixup slots). Returns cudaErrorNotSupported when K needs more than
+// KS_MAX * S_MAX stages or the items do not fit the fixup buffer (the caller then uses the tensor-memory kernel).
+cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, void* y, int ldy, float* fix,
+                          uint32_t* cnt, long long cap, int M, int N, int K, int group, int sms, bool pdl, unsigned* err,
+                          cudaStream_t st) {
+    using namespace w8rf;
+    const int tiles = N / ROWS, KT = K / SK;
+    // about two items per SM, at least ceil(KT / S_MAX) stages per item (the last split adds at most S_MAX slots)
+    const long long target = 2LL * sms;
+    int ks = (int)std::min<long long>(KS_MAX, ((long long)tiles * KT + target - 1) / target);
+    ks = std::max(std::max(1, ks), (KT + S_MAX - 1) / S_MAX);
+    if (ks > KS_MAX) return cudaErrorNotSupported;   // K above KS_MAX * S_MAX * 128
+    const int S = (KT + ks - 1) / ks;
+    // two token tiles over several waves: the tensor-memory kernel (one stream per SM) is faster there (measured)
+    if (M > 8 && (long long)tiles * S > target) return cudaErrorNotSupported;
+    if ((long long)tiles * S > cap) return cudaErrorNotSupported;
+    qf::EncodeTiled enc = nullptr;
+    cudaError_t e = qf::encode_tiled_fn(&enc);
+    if (e != cudaSuccess) return e;
+    Params p{};
+    const cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)N};
+    const cuuint64_t gstride[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)SK, (cuuint32_t)ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult cr = enc(&p.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), gdim, gstride, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    p.x = static_cast<const __nv_bfloat16*>(x);
+    p.s = static_cast<const __nv_bfloat16*>(s);
+    p.y = static_cast<__nv_bfloat16*>(y);
+    p.fix = fix;
+    p.cnt = cnt;
+    p.err = err;
+    p.ldx = ldx; p.ldy = ldy; p.M = M; p.N = N; p.K = K; p.group = group; p.ks = ks; p.S = S; p.KT = KT;
+    const int smem = smem_bytes(ks);
+    auto kern = M > 8 ? w8g_rf_kernel<true> : w8g_rf_kernel<false>;
+    e = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem_bytes(KS_MAX));
+    if (e != cudaSuccess) return e;
+    static bool carveout_set[2] = {false, false};
+    if (!carveout_set[M > 8]) {   // several CTAs per SM need the largest shared-memory carveout
+        e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+        carveout_set[M > 8] = true;
+    }
+    return qf::launch_ex(kern, dim3(tiles * S), dim3(THREADS), (size_t)smem, st, pdl, p);
+}
+
 template <int NT>
 cudaError_t launch_w8g_tc(const CUtensorMap& map, const void* x, int ldx, const void* s, void* y, int ldy,
                           float* fixp, uint32_t* fixc, int M, int N, int K, int G, int t0, long long units, int sms,
@@ -469,8 +524,23 @@ extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const vo
     if (rc != QF_OK) return rc;
     QF_REQUIRE(fix_elems >= need, "w8g_gemm: the fixup buffer needs %lld floats, got %lld", (long long)need,
                (long long)fix_elems);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return qf::cuda_status(e, "w8g_gemm: cudaGetDevice");
+    unsigned* err = nullptr;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_w8g_err);
+    if (e != cudaSuccess) return qf::cuda_status(e, "w8g_gemm: status word");
+    const int sms = qf::sm_count(dev);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    float* fixp = fix;
+    uint32_t* fixc = reinterpret_cast<uint32_t*>(fix + (need - N / G_UN));
+    if (M <= 16 && K % w8rf::SK == 0) {   // decode token counts: the register-fragment kernel
+        e = launch_w8g_rf(q, x, (int)ldx, s, y, (int)ldy, fixp, fixc, (need - N / G_UN) / w8rf::PART, M, N, K, group,
+                          sms, pdl != 0, err, st);
+        if (e != cudaErrorNotSupported) return qf::cuda_status(e, "w8g_gemm: launch");
+    }
     qf::EncodeTiled enc = nullptr;
-    cudaError_t e = qf::encode_tiled_fn(&enc);
+    e = qf::encode_tiled_fn(&enc);
     if (e != cudaSuccess) return qf::cuda_status(e, "w8g_gemm: cuTensorMapEncodeTiled entry point");
     // the canonical weight as a 2-D tensor (K bytes per row); one box = one unit (64 k x 128 rows), 64-byte swizzle
     CUtensorMap map;
@@ -482,17 +552,7 @@ extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const vo
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     QF_REQUIRE(cr == CUDA_SUCCESS, "w8g_gemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
-    int dev = 0;
-    e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return qf::cuda_status(e, "w8g_gemm: cudaGetDevice");
-    unsigned* err = nullptr;
-    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_w8g_err);
-    if (e != cudaSuccess) return qf::cuda_status(e, "w8g_gemm: status word");
-    const int sms = qf::sm_count(dev);
     const long long units = (long long)(N / G_UN) * (K / G_UK);
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    float* fixp = fix;
-    uint32_t* fixc = reinterpret_cast<uint32_t*>(fix + (need - N / G_UN));
     const int NT = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     if (NT == 16) e = launch_w8g_tc<16>(map, x, (int)ldx, s, y, (int)ldy, fixp, fixc, M, N, K, group, 0, units, sms, pdl != 0, err, st);
     else if (NT == 32) e = launch_w8g_tc<32>(map, x, (int)ldx, s, y, (int)ldy, fixp, fixc, M, N, K, group, 0, units, sms, pdl != 0, err, st);

@@ -39,6 +39,32 @@ def test_w8g_strided_rows_and_group64(cuda):
     assert ((y.float().cpu() - truth).norm() / truth.norm()).item() < 4e-3
 
 
+@pytest.mark.parametrize("M", [3, 12])
+def test_w8g_decode_group64_and_token_range(cuda, M):
+    """The decode kernel (M <= 16, K % 128 == 0) with 64-k groups (a scale per half stage), a row stride above K,
+    a zero token, a token scaled by 4096 and one whose first half is scaled by 2^-20 (the per-(token, 64-k) fp16
+    exponent): within the reference's rel-L2 bound, and elementwise within bf16 rounding of the exact-product sum
+    plus an fp32 summation allowance."""
+    g = torch.Generator(device="cpu").manual_seed(7 + M)
+    N, K = 1024, 2048
+    q = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8)
+    s = (torch.rand(N, K // 64, generator=g) * 1e-3 + 1e-4).to(torch.bfloat16)
+    xb = torch.randn(M, K + 64, generator=g)
+    xb[0] = 0.0
+    xb[1] *= 4096.0
+    xb[2, :K // 2] *= 2.0 ** -20
+    xb = xb.to(torch.bfloat16)
+    y = ops.w8g_gemm(xb.to(cuda)[:, :K], q.to(cuda), s.to(cuda), 0).float().cpu()
+    deq = q.double() * s.double().repeat_interleave(64, dim=1)
+    xd = xb[:, :K].double()
+    truth = xd @ deq.T
+    assert ((y - truth).norm() / truth.norm()).item() < 4e-3
+    assert bool((y[0] == 0).all())
+    allowance = 2.0 ** -8 * truth.abs() + 2.0 ** -16 * (xd.abs() @ deq.abs().T)
+    assert bool(((y - truth).abs() <= allowance).all())
+    assert ops.w8g_take_status() == 0
+
+
 def test_w8g_unpack_exact(cuda):
     g = torch.Generator(device="cpu").manual_seed(2)
     w = (torch.randn(300, 1024, generator=g) * 0.02).to(torch.bfloat16)
