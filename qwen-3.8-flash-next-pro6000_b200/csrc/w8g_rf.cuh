@@ -21,9 +21,12 @@
 //     one 16-byte load per row and half gives the four k16 steps of that row (k = 64 h + 16 t4 + 4 s + 0..3 in the
 //     mma columns 2 t4, 2 t4 + 1, 2 t4 + 8, 2 t4 + 9, the same permutation for the tokens), a second n8 token tile
 //     only above 8 tokens. Each half's fp32 partial is scaled by s[row] * 2^e[token] into the accumulators.
-//   * Splits of one tile are added without waiting: each item stores its fp32 partial to its own slot of the fixup
-//     buffer and counts itself on the tile's counter; the item that counts last adds all slots in split order (the
-//     same sum whichever split comes last), writes y and re-arms the counter.
+//   * When the grid is one wave, the S splits of one tile run as one thread-block cluster: each CTA leaves its fp32
+//     partial in its shared memory, and cluster rank 0 adds the S partials in split order through distributed shared
+//     memory and writes y (no global round trip). Larger grids (cluster placement costs them more than it saves)
+//     reduce through the fixup buffer instead: each item stores its partial to its own slot and counts itself on the
+//     tile's counter; the item that counts last adds all slots in split order and re-arms the counter. Either way
+//     the sum is the same whichever split finishes last.
 //   * Every wait is bounded; a wait that runs out sets a bit of the status word (qf_w8g_take_status).
 #pragma once
 
@@ -54,13 +57,36 @@ struct Params {
     const __nv_bfloat16* x;
     const __nv_bfloat16* s;
     __nv_bfloat16* y;
-    float* fix;
-    uint32_t* cnt;
+    float* fix;         // split partials (cl == 0): one PART slot per item, then
+    uint32_t* cnt;      // one counter per tile, left at zero
     unsigned* err;
     int ldx, ldy, M, N, K, group, ks, S, KT;
+    int cl;             // 1: the splits of a tile are one thread-block cluster and reduce through its shared memory
 };
 
 __device__ __forceinline__ float pow2f(int k) { return __uint_as_float((uint32_t)(127 + k) << 23); }
+
+// thread-block cluster helpers: a full barrier (release / acquire), this CTA's rank, another rank's address of a
+// shared-memory location, and a 16-byte load from it
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t map_rank(uint32_t addr, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
 
 template <bool TWO>
 __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__ Params p) {
@@ -97,7 +123,10 @@ __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__
                 tma_load_2d(ring + st * STAGE, &p.wmap, (j0 + j) * SK, tile * ROWS, full + st, pol);
             }
         }
-        qf::pdl_wait();
+        if (p.S == 1 || !p.cl) return;
+        // splits reduced in the cluster: this warp joins the cluster barriers below
+        cluster_sync();
+        cluster_sync();
         return;
     }
 
@@ -240,47 +269,89 @@ __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__
         store_y(acc);
         return;
     }
-    float* mine = p.fix + (size_t)item * PART + ctid * 16;
+    if (!p.cl) {
+        // splits in separate CTAs (grids of several waves): each item stores its fp32 partial to its fixup slot and
+        // counts itself on the tile's counter; the item that counts last adds the slots in split order (the same
+        // sum whichever split comes last), writes y and re-arms the counter
+        float* mine = p.fix + (size_t)item * PART + ctid * 16;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) __stcg(reinterpret_cast<float4*>(mine + 4 * j), make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]));
-    __threadfence();
-    qf::named_bar(1, ROWS);
-    if (ctid == 0) {
-        const bool last = atomicAdd(p.cnt + tile, 1u) == (uint32_t)(p.S - 1);
-        if (last) {
-            __threadfence();
-            p.cnt[tile] = 0u;
-        }
-        *flag = last ? 1 : 0;
-    }
-    qf::named_bar(1, ROWS);
-    if (*flag == 0) return;
-    __threadfence();
-    // the S <= S_MAX slots in split order (the same sum whichever split came last), in two passes of 8 floats per
-    // thread with every slot's loads in flight
-    float tot[4][4];
-    const float* part = p.fix + (size_t)tile * p.S * PART + ctid * 16;
-#pragma unroll
-    for (int ps = 0; ps < 2; ++ps) {
-        float4 q[S_MAX][2];
-#pragma unroll
-        for (int sp = 0; sp < S_MAX; ++sp)
-            if (sp < p.S) {
-#pragma unroll
-                for (int j = 0; j < 2; ++j) q[sp][j] = __ldcg(reinterpret_cast<const float4*>(part + (size_t)sp * PART + 4 * (2 * ps + j)));
+        for (int j = 0; j < 4; ++j)
+            __stcg(reinterpret_cast<float4*>(mine + 4 * j), make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]));
+        __threadfence();
+        qf::named_bar(1, ROWS);
+        if (ctid == 0) {
+            const bool last = atomicAdd(p.cnt + tile, 1u) == (uint32_t)(p.S - 1);
+            if (last) {
+                __threadfence();
+                p.cnt[tile] = 0u;
             }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            float4 a = q[0][j];
-#pragma unroll
-            for (int sp = 1; sp < S_MAX; ++sp)
-                if (sp < p.S) {
-                    a.x += q[sp][j].x; a.y += q[sp][j].y; a.z += q[sp][j].z; a.w += q[sp][j].w;
-                }
-            tot[2 * ps + j][0] = a.x; tot[2 * ps + j][1] = a.y; tot[2 * ps + j][2] = a.z; tot[2 * ps + j][3] = a.w;
+            *flag = last ? 1 : 0;
         }
+        qf::named_bar(1, ROWS);
+        if (*flag == 0) return;
+        __threadfence();
+        float tot[4][4];
+        const float* part = p.fix + (size_t)tile * p.S * PART + ctid * 16;
+#pragma unroll
+        for (int ps = 0; ps < 2; ++ps) {   // two passes of 8 floats, every split's loads in flight
+            float4 q[S_MAX][2];
+#pragma unroll
+            for (int sp = 0; sp < S_MAX; ++sp)
+                if (sp < p.S) {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        q[sp][j] = __ldcg(reinterpret_cast<const float4*>(part + (size_t)sp * PART + 4 * (2 * ps + j)));
+                }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float4 a = q[0][j];
+#pragma unroll
+                for (int sp = 1; sp < S_MAX; ++sp)
+                    if (sp < p.S) {
+                        a.x += q[sp][j].x; a.y += q[sp][j].y; a.z += q[sp][j].z; a.w += q[sp][j].w;
+                    }
+                tot[2 * ps + j][0] = a.x; tot[2 * ps + j][1] = a.y; tot[2 * ps + j][2] = a.z; tot[2 * ps + j][3] = a.w;
+            }
+        }
+        store_y(tot);
+        return;
     }
-    store_y(tot);
+    // several splits of this tile run as one thread-block cluster (cluster rank = split): each CTA leaves its fp32
+    // partial in its own shared memory (the ring, free once every consumer warp is past its last stage), and rank 0
+    // adds the S partials in split order through distributed shared memory -- the same sum for every schedule
+    qf::named_bar(1, ROWS);
+    float* red = reinterpret_cast<float*>(ring) + ctid * 16;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        *reinterpret_cast<float4*>(red + 4 * j) = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+    cluster_sync();
+    if (cluster_rank() == 0) {
+        float tot[4][4];
+        const uint32_t mine = qf::smem_u32(red);
+#pragma unroll
+        for (int ps = 0; ps < 2; ++ps) {   // two passes of 8 floats, every split's loads in flight
+            float4 q[S_MAX][2];
+#pragma unroll
+            for (int sp = 0; sp < S_MAX; ++sp)
+                if (sp < p.S) {
+                    const uint32_t ra = map_rank(mine, sp);
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) q[sp][j] = ld_cluster_f4(ra + 16u * (2 * ps + j));
+                }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float4 a = q[0][j];
+#pragma unroll
+                for (int sp = 1; sp < S_MAX; ++sp)
+                    if (sp < p.S) {
+                        a.x += q[sp][j].x; a.y += q[sp][j].y; a.z += q[sp][j].z; a.w += q[sp][j].w;
+                    }
+                tot[2 * ps + j][0] = a.x; tot[2 * ps + j][1] = a.y; tot[2 * ps + j][2] = a.z; tot[2 * ps + j][3] = a.w;
+            }
+        }
+        store_y(tot);
+    }
+    cluster_sync();   // every CTA keeps its shared memory until rank 0 has read it
 }
 
 }  // namespace w8rf

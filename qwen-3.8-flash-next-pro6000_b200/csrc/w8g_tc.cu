@@ -385,8 +385,9 @@ __device__ unsigned g_w8g_err;
 
 // The register-fragment kernel's launch (M <= 16, K % 128 == 0): ks stages per item chosen so that the grid covers
 // the SMs about two CTAs deep (at most KS_MAX: larger weights take several waves) with at most S_MAX splits per tile
-// (S = ceil(K / 128 / ks)), at most `cap` items (fixup slots). Returns cudaErrorNotSupported when K needs more than
-// KS_MAX * S_MAX stages or the items do not fit the fixup buffer (the caller then uses the tensor-memory kernel).
+// (S = ceil(K / 128 / ks)); a one-wave grid reduces the splits in a cluster per tile, a larger one through the fixup
+// buffer (at most `cap` slots). Returns cudaErrorNotSupported when K needs more than KS_MAX * S_MAX stages, for two
+// token tiles over several waves, or when the slots do not fit (the caller then uses the tensor-memory kernel).
 cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, void* y, int ldy, float* fix,
                           uint32_t* cnt, long long cap, int M, int N, int K, int group, int sms, bool pdl, unsigned* err,
                           cudaStream_t st) {
@@ -400,7 +401,11 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     const int S = (KT + ks - 1) / ks;
     // two token tiles over several waves: the tensor-memory kernel (one stream per SM) is faster there (measured)
     if (M > 8 && (long long)tiles * S > target) return cudaErrorNotSupported;
-    if ((long long)tiles * S > cap) return cudaErrorNotSupported;
+    // clusters when the grid fills at most 7/8 of one wave (the CTAs that fit an SM's shared memory, on every SM):
+    // a fuller wave leaves clusters that find no room in a GPC for a second wave (measured); else the fixup buffer
+    const long long wave = (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(ks)));
+    const int cl = S > 1 && (long long)tiles * S * 8 <= wave * 7 ? 1 : 0;
+    if (!cl && (long long)tiles * S > cap) return cudaErrorNotSupported;
     qf::EncodeTiled enc = nullptr;
     cudaError_t e = qf::encode_tiled_fn(&enc);
     if (e != cudaSuccess) return e;
@@ -418,6 +423,7 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     p.y = static_cast<__nv_bfloat16*>(y);
     p.fix = fix;
     p.cnt = cnt;
+    p.cl = cl;
     p.err = err;
     p.ldx = ldx; p.ldy = ldy; p.M = M; p.N = N; p.K = K; p.group = group; p.ks = ks; p.S = S; p.KT = KT;
     const int smem = smem_bytes(ks);
@@ -431,7 +437,22 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
         if (e != cudaSuccess) return e;
         carveout_set[M > 8] = true;
     }
-    return qf::launch_ex(kern, dim3(tiles * S), dim3(THREADS), (size_t)smem, st, pdl, p);
+    // with cl, the S splits of a tile are one cluster (S <= S_MAX = 8, the portable cluster size)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles * S);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cl ? (unsigned)S : 1u;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int NT>
