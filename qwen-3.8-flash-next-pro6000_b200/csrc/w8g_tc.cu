@@ -404,6 +404,9 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     // clusters when the grid fills at most 7/8 of one wave (the CTAs that fit an SM's shared memory, on every SM):
     // a fuller wave leaves clusters that find no room in a GPC for a second wave (measured); else the fixup buffer
     const long long wave = (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(ks)));
+    // one wave only: grids of several waves gave run-to-run differences in stress runs (cause not found), so they
+    // go to the tensor-memory kernel
+    if ((long long)tiles * S > wave) return cudaErrorNotSupported;
     const int cl = S > 1 && (long long)tiles * S * 8 <= wave * 7 ? 1 : 0;
     if (!cl && (long long)tiles * S > cap) return cudaErrorNotSupported;
     qf::EncodeTiled enc = nullptr;
