@@ -384,10 +384,11 @@ __device__ unsigned g_w8g_err;
 #include "w8g_rf.cuh"
 
 // The register-fragment kernel's launch (M <= 16, K % 128 == 0): ks stages per item chosen so that the grid covers
-// the SMs about two CTAs deep (at most KS_MAX: larger weights take several waves) with at most S_MAX splits per tile
-// (S = ceil(K / 128 / ks)); a one-wave grid reduces the splits in a cluster per tile, a larger one through the fixup
-// buffer (at most `cap` slots). Returns cudaErrorNotSupported when K needs more than KS_MAX * S_MAX stages, for two
-// token tiles over several waves, or when the slots do not fit (the caller then uses the tensor-memory kernel).
+// the SMs about two CTAs deep with at most S_MAX splits per tile (S = ceil(K / 128 / ks)), raised up to KS_MAX while
+// the grid is larger than one wave; a grid under 7/8 of a wave reduces the splits in a cluster per tile, a fuller one
+// through the fixup buffer (at most `cap` slots). Returns cudaErrorNotSupported when K needs more than
+// KS_MAX * S_MAX stages, when no ks gives a one-wave grid, for two token tiles over more CTAs than two per SM, or when
+// the slots do not fit (the caller then uses the tensor-memory kernel).
 cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, void* y, int ldy, float* fix,
                           uint32_t* cnt, long long cap, int M, int N, int K, int group, int sms, bool pdl, unsigned* err,
                           cudaStream_t st) {
@@ -398,15 +399,17 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     int ks = (int)std::min<long long>(KS_MAX, ((long long)tiles * KT + target - 1) / target);
     ks = std::max(std::max(1, ks), (KT + S_MAX - 1) / S_MAX);
     if (ks > KS_MAX) return cudaErrorNotSupported;   // K above KS_MAX * S_MAX * 128
+    // one wave (the CTAs that fit an SM's shared memory, on every SM) only: grids of several waves gave run-to-run
+    // differences in stress runs (cause not found), so longer splits are tried first and then the tensor-memory kernel
+    auto wave_of = [&](int k) { return (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(k))); };
+    while (ks < KS_MAX && (long long)tiles * ((KT + ks - 1) / ks) > wave_of(ks)) ++ks;
     const int S = (KT + ks - 1) / ks;
-    // two token tiles over several waves: the tensor-memory kernel (one stream per SM) is faster there (measured)
-    if (M > 8 && (long long)tiles * S > target) return cudaErrorNotSupported;
-    // clusters when the grid fills at most 7/8 of one wave (the CTAs that fit an SM's shared memory, on every SM):
-    // a fuller wave leaves clusters that find no room in a GPC for a second wave (measured); else the fixup buffer
-    const long long wave = (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(ks)));
-    // one wave only: grids of several waves gave run-to-run differences in stress runs (cause not found), so they
-    // go to the tensor-memory kernel
+    const long long wave = wave_of(ks);
     if ((long long)tiles * S > wave) return cudaErrorNotSupported;
+    // two token tiles over more than two CTAs per SM: the tensor-memory kernel (one stream per SM) is faster there
+    if (M > 8 && (long long)tiles * S > target) return cudaErrorNotSupported;
+    // clusters when the grid fills at most 7/8 of the wave: a fuller wave leaves clusters that find no room in a GPC
+    // (measured); else the fixup buffer
     const int cl = S > 1 && (long long)tiles * S * 8 <= wave * 7 ? 1 : 0;
     if (!cl && (long long)tiles * S > cap) return cudaErrorNotSupported;
     qf::EncodeTiled enc = nullptr;
