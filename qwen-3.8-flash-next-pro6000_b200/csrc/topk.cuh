@@ -40,54 +40,28 @@ __device__ __forceinline__ float logit_of(uint32_t rank) {
 // warp-wide largest rank (a lane-local max tree, then one redux) and clears it; lane k keeps round k's winner. The
 // probabilities are formed afterwards, all lanes at once: p_k = exp(logit_k - max) / sum, the same operands as a
 // softmax over the row, and the renormalising sum runs over p_0, p_1, ... in selection order.
-template <int PL, typename T>
-__device__ void topk_row(const T* __restrict__ row, int E, int topk, int renorm, float* __restrict__ wout,
-                         int* __restrict__ iout) {
+// Element i of a lane is expert lane * PL + i when FULL (a row of exactly 32 * PL experts, PL a multiple of 8), else
+// expert i * 32 + lane (elements past E hold -inf). The ranking carries the id, so the selection does not depend on
+// which lane holds which expert; FULL fixes the softmax summation order, shared by every caller that loads a full row.
+template <int PL, bool FULL>
+__device__ __forceinline__ void topk_select(const float (&v)[PL], int E, int topk, int renorm, float* __restrict__ wout,
+                                            int* __restrict__ iout) {
     const int lane = threadIdx.x & 31;
-    float v[PL];
     uint32_t rk[PL];
     float mx = -INFINITY;
-    // element i of this lane: expert i * 32 + lane, or, for rows of exactly 32 * PL experts (16-byte aligned, PL a
-    // multiple of 8), expert lane * PL + i, loaded as 16-byte words. Both element types take the same mapping under
-    // the same condition, so the router kernel (fp32 rows) and the fused router (bf16 rows) sum the softmax in the
-    // same order; the ranking carries the id, so the selection does not depend on which lane holds which expert.
-    constexpr int PER16 = 16 / (int)sizeof(T);
-    constexpr bool VEC = PL % 8 == 0;
-    const bool vec = VEC && E == 32 * PL && (reinterpret_cast<uintptr_t>(row) & 15u) == 0u;
-    if (vec) {
 #pragma unroll
-        for (int c = 0; c < (VEC ? PL / PER16 : 1); ++c) {
-            const uint4 w = __ldcg(reinterpret_cast<const uint4*>(row + lane * PL) + c);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if constexpr (sizeof(T) == 2) {
-                    if (PER16 * c + 2 * j + 1 < PL) {
-                        v[PER16 * c + 2 * j] = __uint_as_float(ww[j] << 16);
-                        v[PER16 * c + 2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
-                    }
-                } else {
-                    if (PER16 * c + j < PL) v[PER16 * c + j] = __uint_as_float(ww[j]);
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < PL; ++i) mx = fmaxf(mx, v[i]);
-    } else {
-#pragma unroll
-        for (int i = 0; i < PL; ++i) {
-            const int e = i * 32 + lane;
-            v[i] = e < E ? load_logit(row + e) : -INFINITY;
-            mx = fmaxf(mx, v[i]);
-        }
-    }
+    for (int i = 0; i < PL; ++i) mx = fmaxf(mx, v[i]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
-        const int e = vec ? lane * PL + i : i * 32 + lane;
-        rk[i] = e < E ? rank_of(v[i], e) : 0u;
+        if constexpr (FULL) {
+            rk[i] = rank_of(v[i], lane * PL + i);
+        } else {
+            const int e = i * 32 + lane;
+            rk[i] = e < E ? rank_of(v[i], e) : 0u;
+        }
         sum += __expf(v[i] - mx);
     }
 #pragma unroll
@@ -123,6 +97,41 @@ __device__ void topk_row(const T* __restrict__ row, int E, int topk, int renorm,
     }
 }
 
+// one warp: the top-k of one row in memory (fp32 or bf16 logits)
+template <int PL, typename T>
+__device__ void topk_row(const T* __restrict__ row, int E, int topk, int renorm, float* __restrict__ wout,
+                         int* __restrict__ iout) {
+    const int lane = threadIdx.x & 31;
+    float v[PL];
+    constexpr int PER16 = 16 / (int)sizeof(T);
+    if constexpr (PL % 8 == 0) {
+        if (E == 32 * PL && (reinterpret_cast<uintptr_t>(row) & 15u) == 0u) {
+            // a full row: 16-byte words, lane l holding experts l * PL .. l * PL + PL - 1
+#pragma unroll
+            for (int c = 0; c < PL / PER16; ++c) {
+                const uint4 w = __ldcg(reinterpret_cast<const uint4*>(row + lane * PL) + c);
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    if constexpr (sizeof(T) == 2) {
+                        v[PER16 * c + 2 * j] = __uint_as_float(ww[j] << 16);
+                        v[PER16 * c + 2 * j + 1] = __uint_as_float(ww[j] & 0xFFFF0000u);
+                    } else {
+                        v[PER16 * c + j] = __uint_as_float(ww[j]);
+                    }
+                }
+            }
+            topk_select<PL, true>(v, 32 * PL, topk, renorm, wout, iout);
+            return;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+        const int e = i * 32 + lane;
+        v[i] = e < E ? load_logit(row + e) : -INFINITY;
+    }
+    topk_select<PL, false>(v, E, topk, renorm, wout, iout);
+}
 
 // one warp: the row's top-k into wout[0..topk) / iout[0..topk) (lanes 0..topk-1 write); E <= 1024
 template <typename T>
