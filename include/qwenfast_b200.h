@@ -101,7 +101,11 @@ int qf_router_topk_noalloc(const void* x, const void* w, int rows, int hidden, i
  *   out bf16 [M, H].
  * out[t] = bf16(sigmoid(x[t].w_gate) * shared[t] + bf16(sum over top-k positions, in order, of
  *          bf16(bf16(expert_out) * bf16(gs2 * bf16(topk_w)))))  -- the reference's rounding points.
- * phase: 3 or 4 (the whole layer); the reference's split phases 1 and 2 are not provided.
+ * phase: 3 or 4: the whole layer in one launch. 1 and 2: the reference's split phases (qf_a16moe.cu:889, 915) as
+ *   two launches of the same kernel over one workspace -- 1 computes the gate logits into gl and every routed
+ *   slot's bf16(SwiGLU(gate_up)) into hbuf, 2 the down projections, the weighting and the combine (with `shared`)
+ *   into out from hbuf and gl; phase 1 then phase 2 give the same bits as phase 4. Not with sh_w13 / sh_w2 (as in
+ *   the reference, in-kernel shared-expert weights need the whole layer), mode 0 only.
  * mode 0: full layer. mode 1: expert-parallel shard -- only experts in [expert_lo, expert_hi) are computed; their
  *   weighted slot outputs go to ybuf [M, topk + 1, H] with every other slot zero, slot `topk` holding the shared
  *   expert output when this shard computes it; qf_moe_combine then finishes the layer (after the caller has summed

@@ -147,6 +147,7 @@ struct Params {
     int renorm;
     const __nv_bfloat16* xsrc;   // fused router: x in pinned (mapped) host memory, copied into x by the kernel, or nullptr
     int M, H, I, E, topk, Is, mode, elo, ehi;
+    int phase;  // 0: the whole layer; 1: gate logits + gate_up (hbuf, gl); 2: down + combine from hbuf and gl
     int wofs;   // expert id of the first expert in w13 / s13 / w2 / s2 / gs13 / gs2 (mode 1: elo)
     const uint8_t* f13;   // NVFP4 experts (FMT 1): E4M3 group-16 scales in the layout of formats.nvfp4_scale_map
     const uint8_t* f2;
@@ -240,6 +241,7 @@ __device__ void grid_barrier(uint32_t* ctrl, int idx) {
 struct Layout {   // per-launch derived sizes, identical in every thread
     int R1, R2, Rs1, ngs, ngc, U, Gt, has_gate, has_shw;
     int b_s1, b_g1, b_s1f, b_s2, b_g2, b_cb, total;
+    int base, nq;                     // this launch's items are base + the queue claims 0 .. nq - 1 (phases)
     uint32_t tile_target;
     int g1s;                          // gate_up k splits this launch: G1_SPLIT or 1
     // pbuf (floats): [0, sh_off) the zero-kept gate_up half counters (uint32), sized for QF_MAX_TOKENS so that their
@@ -273,6 +275,11 @@ __device__ void make_layout(Layout& L, const Params& p, int M, int U, int Gt, in
     L.b_g2 = L.b_s2 + (L.has_shw ? L.R2 * L.ngs : 0);
     L.b_cb = L.b_g2 + L.R2 * L.Gt;
     L.total = L.b_cb + L.R2 * L.ngc;
+    // phase 1 ends with the gate_up items (no shared-expert weights in the split phases: b_g2 == b_s1f); phase 2
+    // starts with the down items
+    if (p.phase == 1) L.total = L.b_g2;
+    L.base = p.phase == 2 ? L.b_g2 : 0;
+    L.nq = L.total - L.base;
     L.tile_target = (uint32_t)(L.Gt + (L.has_shw ? L.ngs : 0));
     L.sh_off = ((size_t)QF_MAX_TOKENS * p.topk * L.R1 + 3) & ~(size_t)3;
     L.g1_part_off = L.sh_off + (L.has_shw ? (size_t)L.Rs1 * L.ngs * NSPLIT * 2048 : 0);
@@ -585,7 +592,7 @@ __device__ __forceinline__ void router_logits(const Params& p, float* red, const
 constexpr int TOPK_ALL_MAX = 16;
 __device__ __noinline__ void fused_router(const Params& p, uint8_t* smem, const uint8_t* rrows, int r0, int nrows,
                                           int* rids, float* rtw) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5;
     const int M = p.M, E = p.E, topk = p.topk;
     uint32_t* ctrl = p.ctrl;
     qf::cp_async_wait_all();
@@ -884,10 +891,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
             };
             // Decoding is plan arithmetic only (no waits): it runs one item ahead, while the current item's later
             // stages wait for ring slots, so that an item boundary costs the ring no more than a stage does.
-            auto decode = [&](int item) {
+            auto decode = [&](int claim) {
                 Work w;
                 int kind = K_STOP, u = 0, tile = 0, tg = 0, split = 0, nk = 1, ntok = 0, e = 0;
-                if (item >= L.total) {
+                const int item = L.base + claim;
+                if (claim >= L.nq) {
                     kind = K_STOP;
                 } else if (item < L.b_s1) {
                     kind = K_GL;
@@ -969,7 +977,11 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                                             (size_t)tile * (8 * (size_t)K) + (size_t)split * nk * 1024,
                                         (uint32_t)nk * 1024u);
                     }
-                    if (down) { w.dep_idx = C_DONE + u; w.dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u])); }
+                    // (phase 2: the gate_up items completed in the previous launch)
+                    if (down && p.phase != 2) {
+                        w.dep_idx = C_DONE + u;
+                        w.dep_target = (uint32_t)(L.R1 * (gpre[u + 1] - gpre[u]));
+                    }
                 } else if (kind == K_S1 || kind == K_S2) {
                     const bool down = kind == K_S2;
                     const int K = down ? p.Is : p.H;
@@ -988,7 +1000,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 return w;
             };
             // the first item was claimed before the plan; the second is claimed now (claims run two items ahead)
-            int next = first_item < L.total ? (int)atomicAdd(ctrl + C_QUEUE, 1u) : L.total;
+            int next = first_item < L.nq ? (int)atomicAdd(ctrl + C_QUEUE, 1u) : L.nq;
             uint32_t herr = 0u;
             Work cur = decode(first_item);
             for (;;) {
@@ -1002,7 +1014,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                 if (kind == K_S1F) wait_counter(ctrl, C_SPLIT + d.tile * L.ngs + d.tg, (uint32_t)NSPLIT);
                 if (kind == K_CB) {
                     wait_counter(ctrl, C_CNT + d.tile, L.tile_target);
-                    if (L.has_gate) wait_counter(ctrl, C_GLF, 1u);
+                    if (L.has_gate && p.phase != 2) wait_counter(ctrl, C_GLF, 1u);   // phase 2: gl is given
                 }
                 // the k-slice of the item's token rows rides in every stage (token block at STAGE_TOK): the shared
                 // expert's consecutive rows as one tensor copy (rows beyond M read zeros), a routed expert's rows one
@@ -1071,9 +1083,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1) moe_persistent_kernel(const __
                         // complete already, acquire it now (then the proxy fence orders every later copy of this
                         // thread after it). After a hard error anywhere (read one item ahead) the next item is the
                         // stop.
-                        const int item = (herr & HARD_ERR) ? L.total : next;
+                        const int item = (herr & HARD_ERR) ? L.nq : next;
                         herr = qf::ld_volatile(ctrl + C_ERR);
-                        if (item < L.total) next = (int)atomicAdd(ctrl + C_QUEUE, 1u);
+                        if (item < L.nq) next = (int)atomicAdd(ctrl + C_QUEUE, 1u);
                         nxt = decode(item);
                         if (nxt.dep_idx >= 0 && qf::ld_acquire(ctrl + nxt.dep_idx) >= nxt.dep_target) {
                             nxt.dep_idx = -1;
@@ -1602,8 +1614,7 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
                const FusedRouter* fr, int fmt = 0) {
     QF_REQUIRE(x && topk_ids && topk_w && w13 && s13 && w2 && s2 && hbuf && ybuf && gl && ctrl && out,
                "a16_moe_decode: null pointer argument");
-    QF_REQUIRE(phase == 3 || phase == 4,
-               "a16_moe_decode: phase must be 3 or 4 (whole layer); split phases 1/2 are not provided, got %d", phase);
+    QF_REQUIRE(phase >= 1 && phase <= 4, "a16_moe_decode: phase must be 1, 2, 3 or 4, got %d", phase);
     QF_REQUIRE(mode == 0 || mode == 1 || mode == 2,
                "a16_moe_decode: mode must be 0 (full layer), 1 (expert-parallel shard) or 2 (diagnostic), got %d",
                mode);
@@ -1621,6 +1632,11 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
         QF_REQUIRE(Is >= 64 && Is % 64 == 0 && Is <= 1024, "a16_moe_decode: Is must be a multiple of 64 in [64, 1024], got %d", Is);
     }
     QF_REQUIRE(!(has_shw || shared) || w_gate, "a16_moe_decode: a shared term needs w_gate");
+    if (phase <= 2) {   // the reference's split phases: gate_up (1) and down + combine (2) as separate launches
+        QF_REQUIRE(!has_shw, "a16_moe_decode: shared-expert weights need the whole layer (phase 3 or 4), got phase %d",
+                   phase);
+        QF_REQUIRE(mode == 0 && fr == nullptr, "a16_moe_decode: phases 1 and 2 run the full layer without the router");
+    }
     int64_t need_h, need_y, need_gl, need_ctrl, need_p, need_sh;
     qf_a16_moe_workspace(M, H, I, topk, has_shw ? Is : 0, &need_h, &need_y, &need_gl, &need_ctrl, &need_p, &need_sh);
     QF_REQUIRE(hbuf_bytes >= need_h && ybuf_bytes >= need_y && gl_numel >= need_gl && ctrl_numel >= need_ctrl,
@@ -1692,6 +1708,7 @@ int moe_launch(const void* x, const int32_t* topk_ids, const float* topk_w, cons
     p.dbg = reinterpret_cast<long long*>(dbg);
     p.M = M; p.H = H; p.I = I; p.E = E; p.topk = topk; p.Is = has_shw ? Is : 0;
     p.mode = mode; p.elo = expert_lo; p.ehi = expert_hi;
+    p.phase = phase <= 2 ? phase : 0;
     p.wofs = mode == 1 ? expert_lo : 0;
     p.f13 = p.f2 = nullptr;
     if (fmt == 1) {   // s13 / s2 are the E4M3 group-16 scales

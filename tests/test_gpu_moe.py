@@ -375,3 +375,36 @@ def test_bounded_wait_runs_out_and_is_reported(cfg1, cuda):
     ref = moe_ref.moe_rounded(x.cpu(), ids.cpu(), w.cpu(), C["w13"], C["s13"], C["w2"], C["s2"], w_gate=C["w_gate"],
                               shared_w=(C["sh_gu"], C["sh_d"]))
     assert_close_to_oracle(out, ref)
+
+
+@pytest.mark.parametrize("M", [1, 10, 64])
+def test_split_phases_equal_whole_layer(cfg1, cuda, M):
+    """The reference's split phases (qf_a16moe.cu:889, 915): phase 1 (gate logits into gl, gate_up + SwiGLU into
+    hbuf) then phase 2 (down, weighting, combine with the precomputed shared term) over one workspace give the same
+    bits as the one-launch layer (phase 4), queued without a sync; phase 1 alone leaves the control block re-armed.
+    In-kernel shared-expert weights are refused in the split phases, as in the reference."""
+    cfg, L, lw, C = cfg1
+    x = synthetic.make_tokens(cfg, M=M, device=cuda, seed=70 + M)
+    g = torch.Generator(device="cpu").manual_seed(M)
+    shared = (torch.randn(M, cfg.H, generator=g) * 0.05).to(BF).to(cuda)
+    w, ids, _ = ops.router_topk(x, lw.router, cfg.topk, True, *ops.router_bufs(cuda))
+    whole_bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, 0, cuda)
+    whole = run_moe(x, ids, w, lw, whole_bufs, shared=shared, use_shw=False)
+    bufs = ops.moe_workspace(M, cfg.H, cfg.I, cfg.topk, 0, cuda)
+    outs = []
+    for rep in range(2):
+        out = torch.empty_like(x)
+        for phase in (1, 2):
+            ops.a16_moe_decode(x, ids, w, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, shared, bufs["hbuf"],
+                               bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, phase, None, bufs["pbuf"], None, None,
+                               None, None, bufs["shbuf"])
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) == 0
+    assert int(bufs["ctrl"][:QF_MOE_CTRL_MIRROR].abs().sum().item()) == 0
+    for out in outs:
+        assert torch.equal(out, whole)
+    with pytest.raises(RuntimeError, match="whole layer"):
+        ops.a16_moe_decode(x, ids, w, lw.w13, lw.s13, None, lw.w2, lw.s2, None, lw.w_gate, None, bufs["hbuf"],
+                           bufs["ybuf"], bufs["gl"], bufs["ctrl"], torch.empty_like(x), 1, None, bufs["pbuf"],
+                           lw.sh_w13, None, lw.sh_w2, None, bufs["shbuf"])
