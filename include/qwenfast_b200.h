@@ -198,8 +198,11 @@ int qf_bf16_unpack(const void* wk, void* w, int N, int K, int gated, qf_stream_t
  *   leaves its counters zero again (after a non-zero qf_w8g_take_status, zero it again). Calls that may run
  *   concurrently need their own. The launch is cooperative (every CTA resident), with programmatic dependent launch
  *   when pdl != 0.
- *   rpw: accepted for signature parity. The reference's rows-per-warp value and its 0x100 / 0x200 bits choose between
- *   its SM120 CUDA-core and mma.sync kernels; this build has one tcgen05 kernel and ignores them.
+ *   rpw: the reference's path bits (qf_w8g.cu:315-318). 0x100 forces the tensor-memory (tcgen05) kernel, 0x200
+ *   forbids it: the register-fragment kernel runs, or the call fails with QF_ERR_UNSUPPORTED when that kernel does
+ *   not take the shape (M <= 16, K % 128 == 0 and a one-wave split); both bits together are invalid. Without them
+ *   the register-fragment kernel takes the decode shapes it supports and the tensor-memory kernel the rest. The low
+ *   byte (the reference's rows per warp of its CUDA-core kernel) has no counterpart and is ignored.
  * ------------------------------------------------------------------------------------------------------------ */
 int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const void* s, void* y, int64_t ldy, int M, int N,
                 int K, int group, int rpw, float* fix, int64_t fix_elems, int pdl, qf_stream_t stream);

@@ -535,7 +535,11 @@ extern "C" int qf_w8g_fixup_elems(int N, int64_t* elems) {
 extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const void* s, void* y, int64_t ldy, int M,
                            int N, int K, int group, int rpw, float* fix, int64_t fix_elems, int pdl,
                            qf_stream_t stream) {
-    (void)rpw;   // the reference's rows-per-warp / path hint of its SM120 kernels; one tensor-core path here
+    // rpw: the reference's path bits (qf_w8g.cu:315-318) -- 0x100 forces its tensor-core kernel, 0x200 forbids it;
+    // here they force / forbid the tensor-memory kernel (the register-fragment kernel otherwise takes decode shapes).
+    // The low byte (the reference's rows per warp of its CUDA-core kernel) has no counterpart.
+    const bool force_tm = (rpw & 0x100) != 0, forbid_tm = (rpw & 0x200) != 0;
+    QF_REQUIRE(!(force_tm && forbid_tm), "w8g_gemm: rpw cannot both force (0x100) and forbid (0x200) the tensor-memory kernel");
     QF_REQUIRE(x && q && s && y && fix, "w8g_gemm: null pointer argument");
     QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS, "w8g_gemm: M must be in [1, %d], got %d", QF_MAX_TOKENS, M);
     QF_REQUIRE(N >= 128 && N % 128 == 0, "w8g_gemm: N must be a multiple of 128, got %d", N);
@@ -561,10 +565,15 @@ extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const vo
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     float* fixp = fix;
     uint32_t* fixc = reinterpret_cast<uint32_t*>(fix + (need - N / G_UN));
-    if (M <= 16 && K % w8rf::SK == 0) {   // decode token counts: the register-fragment kernel
+    if (!force_tm && M <= 16 && K % w8rf::SK == 0) {   // decode token counts: the register-fragment kernel
         e = launch_w8g_rf(q, x, (int)ldx, s, y, (int)ldy, fixp, fixc, (need - N / G_UN) / w8rf::PART, M, N, K, group,
                           sms, pdl != 0, err, st);
         if (e != cudaErrorNotSupported) return qf::cuda_status(e, "w8g_gemm: launch");
+    }
+    if (forbid_tm) {
+        qf::set_error("w8g_gemm: rpw 0x200 forbids the tensor-memory kernel, and the register-fragment kernel does not "
+                      "take M %d, N %d, K %d (it needs M <= 16, K %% 128 == 0 and a one-wave split)", M, N, K);
+        return QF_ERR_UNSUPPORTED;
     }
     qf::EncodeTiled enc = nullptr;
     e = qf::encode_tiled_fn(&enc);

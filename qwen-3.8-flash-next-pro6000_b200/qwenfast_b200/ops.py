@@ -434,8 +434,9 @@ def w8g_gemm(x: torch.Tensor, q: torch.Tensor, s: torch.Tensor, rpw: int = 0, pd
              fixup: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x @ (q * s)^T (W8A16, group-scaled int8) on the tensor cores. Mirrors ``w8g_gemm``
     (serve/qwenfast/qf_w8g.cu:303-336): x bf16 [M, K] (unit column stride, row stride % 8 == 0), q int8 [N, K] as
-    stored (canonical), s bf16 [N, K/group], group 128 or 64; returns y bf16 [M, N]. ``rpw`` is accepted for signature
-    parity (it selects among the reference's SM120 kernels). ``fixup``: the split-tile buffer (``w8g_fixup``; the
+    stored (canonical), s bf16 [N, K/group], group 128 or 64; returns y bf16 [M, N]. ``rpw``: the reference's path bits
+    (qf_w8g.cu:315-318): 0x100 forces the tensor-memory kernel, 0x200 forbids it (RuntimeError when the
+    register-fragment kernel does not take the shape); the low byte (rows per warp) is ignored. ``fixup``: the split-tile buffer (``w8g_fixup``; the
     current stream's by default)."""
     op = "w8g_gemm"
     _cuda(x, "x", op)

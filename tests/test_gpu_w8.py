@@ -138,3 +138,28 @@ def test_w8a8_shapes_split_k(cuda, N, K, M):
     assert torch.equal(acc.cpu().long(), accr)
     assert torch.equal(y.cpu(), yr)
     assert ops.w8a8_take_status() == 0
+
+
+def test_w8g_rpw_force_and_forbid_bits(cuda):
+    """rpw 0x100 forces the tensor-memory kernel and 0x200 forbids it (qf_w8g.cu:315-318): both paths within the
+    reference's bound of the fp32 truth and each deterministic; the default path at a decode shape is the forbidden
+    one's (the register-fragment kernel); forbidding where only the tensor-memory kernel fits, or both bits, fails."""
+    g = torch.Generator(device="cpu").manual_seed(11)
+    w = (torch.randn(2048, 2048, generator=g) * 0.02).to(torch.bfloat16)
+    q, s = w8_ref.w8_quant(w)
+    truth_of = lambda x: x.float() @ w8_ref.w8g_dequant(q, s).T
+    qd, sd = q.to(cuda), s.to(cuda)
+    x = torch.randn(4, 2048, generator=g).to(torch.bfloat16)
+    xd = x.to(cuda)
+    ys = {r: ops.w8g_gemm(xd, qd, sd, r) for r in (0, 0x100, 0x200, 0x104)}
+    for r, y in ys.items():
+        truth = truth_of(x)
+        assert ((y.float().cpu() - truth).norm() / truth.norm()).item() < 4e-3, r
+        assert torch.equal(y, ops.w8g_gemm(xd, qd, sd, r)), r
+    assert torch.equal(ys[0], ys[0x200]) and torch.equal(ys[0x100], ys[0x104])
+    x32 = torch.randn(32, 2048, generator=g).to(torch.bfloat16).to(cuda)
+    with pytest.raises(RuntimeError, match="forbids the tensor-memory kernel"):
+        ops.w8g_gemm(x32, qd, sd, 0x200)
+    with pytest.raises(RuntimeError, match="cannot both"):
+        ops.w8g_gemm(xd, qd, sd, 0x300)
+    assert ops.w8g_take_status() == 0
