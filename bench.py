@@ -314,6 +314,13 @@ def measure(cfg, cfg_id, M, NL, dev, args, rank, world, epar, zipf=0.0, timed_cl
     with torch.cuda.graph(g_router):
         for l in range(NL):
             ops.router_topk(xs[l], layers[l].router, cfg.topk, True, rb[0], rb[1])
+    # the same layer-steps without programmatic dependent launch: each launch starts only after the previous one has
+    # ended, so the difference to us_step is what the chain's overlap (the next launch's prologue -- router rows
+    # requested, plan scratch cleared -- under the previous launch's tail) buys
+    g_nopdl = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_nopdl):
+        for l in range(NL):
+            layer_step(xs[l], l, outs[l], pdl=False)
 
     def rank_max(v):
         if world > 1:
@@ -364,7 +371,7 @@ def measure(cfg, cfg_id, M, NL, dev, args, rank, world, epar, zipf=0.0, timed_cl
         ms_full = timed(run_steps)
     us_step = ms_full * 1e3 / steps
     res = dict(us_step=us_step, steps=steps, warmup_run=warm_reps * NL + (NL if timed_clocks else 0), clocks=clk)
-    for name, g in (("us_moe", g_moe), ("us_router", g_router), ("us_coll", g_coll)):
+    for name, g in (("us_moe", g_moe), ("us_router", g_router), ("us_coll", g_coll), ("us_step_no_pdl", g_nopdl)):
         if g is None:
             res[name] = None
             continue
@@ -412,7 +419,7 @@ def measure(cfg, cfg_id, M, NL, dev, args, rank, world, epar, zipf=0.0, timed_cl
         n_e2e = min(steps, 4 * NL)
         res["e2e_us"] = timed(lambda: [e2e_step(i % NL) for i in range(n_e2e)]) * 1e3 / n_e2e
         res["e2e_steps"] = n_e2e
-    del g_full, g_rem, g_moe, g_router, g_coll
+    del g_full, g_rem, g_moe, g_router, g_coll, g_nopdl
     return res
 
 
@@ -487,6 +494,8 @@ def run_ours(args):
             "unique_experts_mean": statistics.mean(r["U"]),
             "us_moe_kernel": r["us_moe"], "us_router_kernel": r["us_router"],
             "us_collective": r["us_coll"], "rank_hbm_frac": rank_frac,
+            "pdl_chain": {"us_per_layer_step_pdl": r["us_step"], "us_per_layer_step_no_pdl": r["us_step_no_pdl"],
+                          "note": "the same graph of layer-steps launched without programmatic dependent launch"},
             "nccl_ranks": dist.get_world_size() if epar else None,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "kernel": "moe_persistent_kernel (layer-step launch, router inside)",
