@@ -170,6 +170,18 @@ int qf_moe_layer_decode(const void* x, void* x_stage, const void* router_w, int 
                         void* shbuf, int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk, int Is,
                         int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream);
 
+/* qf_moe_layer_decode on NVFP4 experts: the router inside the launch, then the layer of qf_a16_moe_decode_nvfp4
+ * (f13 / f2 the E4M3 group-16 scales in the kernel layout, gs13 / gs2 the per-expert multipliers); every other
+ * argument as qf_moe_layer_decode. */
+int qf_moe_layer_decode_nvfp4(const void* x, void* x_stage, const void* router_w, int renormalize, float* topk_w,
+                              int32_t* topk_ids, void* logits, const int32_t* w13, const void* f13, const void* gs13,
+                              const int32_t* w2, const void* f2, const void* gs2, const void* w_gate,
+                              const void* shared, const void* sh_w13, const void* sh_w2, void* hbuf,
+                              int64_t hbuf_bytes, void* ybuf, int64_t ybuf_bytes, float* gl, int64_t gl_numel,
+                              int32_t* ctrl, int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel, void* shbuf,
+                              int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk, int Is, int mode,
+                              int expert_lo, int expert_hi, int64_t* dbg, int pdl, qf_stream_t stream);
+
 /* Expert-parallel finish: out = the mode-0 combine of a ybuf [M, topk + 1, H] summed over the shards.
  * gl fp32 [M] is recomputed from x and w_gate when w_gate is given (has_shared != 0). */
 int qf_moe_combine(const void* ybuf, const void* x, const void* w_gate, int has_shared, void* out, int M, int H,

@@ -1809,6 +1809,22 @@ extern "C" int qf_moe_layer_decode(const void* x, void* x_stage, const void* rou
                       shbuf_bytes, out, M, H, I, E, topk, Is, 4, mode, expert_lo, expert_hi, dbg, pdl, stream, &fr);
 }
 
+extern "C" int qf_moe_layer_decode_nvfp4(const void* x, void* x_stage, const void* router_w, int renormalize,
+                                         float* topk_w, int32_t* topk_ids, void* logits, const int32_t* w13,
+                                         const void* f13, const void* gs13, const int32_t* w2, const void* f2,
+                                         const void* gs2, const void* w_gate, const void* shared, const void* sh_w13,
+                                         const void* sh_w2, void* hbuf, int64_t hbuf_bytes, void* ybuf,
+                                         int64_t ybuf_bytes, float* gl, int64_t gl_numel, int32_t* ctrl,
+                                         int64_t ctrl_numel, float* pbuf, int64_t pbuf_numel, void* shbuf,
+                                         int64_t shbuf_bytes, void* out, int M, int H, int I, int E, int topk, int Is,
+                                         int mode, int expert_lo, int expert_hi, int64_t* dbg, int pdl,
+                                         qf_stream_t stream) {
+    const FusedRouter fr{router_w, renormalize, logits, x_stage};
+    return moe_launch(x, topk_ids, topk_w, w13, f13, gs13, w2, f2, gs2, w_gate, shared, sh_w13, sh_w2, hbuf,
+                      hbuf_bytes, ybuf, ybuf_bytes, gl, gl_numel, ctrl, ctrl_numel, pbuf, pbuf_numel, shbuf,
+                      shbuf_bytes, out, M, H, I, E, topk, Is, 4, mode, expert_lo, expert_hi, dbg, pdl, stream, &fr, 1);
+}
+
 extern "C" int qf_moe_combine(const void* ybuf, const void* x, const void* w_gate, int has_shared, void* out, int M,
                               int H, int topk, int pdl, qf_stream_t stream) {
     QF_REQUIRE(ybuf && x && out, "moe_combine: null pointer argument");

@@ -39,6 +39,9 @@ SIGNATURES = {
     "qf_moe_layer_decode": [_p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                             _p, _l, _p, _l, _p, _l, _p, _l, _p, _l, _p, _l,
                             _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p],
+    "qf_moe_layer_decode_nvfp4": [_p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                  _p, _l, _p, _l, _p, _l, _p, _l, _p, _l, _p, _l,
+                                  _p, _i, _i, _i, _i, _i, _i, _i, _i, _i, _p, _i, _p],
     "qf_moe_combine": [_p, _p, _p, _i, _p, _i, _i, _i, _i, _p],
     "qf_w4_repack": [_p, _p, _p, _p, _i, _i, _i, _i, _p],
     "qf_w4_unpack": [_p, _p, _p, _p, _i, _i, _i, _i, _p],

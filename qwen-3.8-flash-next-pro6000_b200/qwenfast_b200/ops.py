@@ -208,7 +208,8 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
 
     ``fmt="nvfp4"``: the experts are NVFP4 (the reference's own format) in the layout of ``formats.repack_nvfp4`` --
     w13 / w2 the e2m1 codes (int32, int4 kernel layout), s13 / s2 the E4M3 group-16 scales (uint8 [E, N*K/16]),
-    gs13 / gs2 the per-expert multipliers 1 / g (C ABI ``qf_a16_moe_decode_nvfp4``; routing given, not fused)."""
+    gs13 / gs2 the per-expert multipliers 1 / g (C ABI ``qf_a16_moe_decode_nvfp4``, with ``router_w``
+    ``qf_moe_layer_decode_nvfp4``)."""
     op = "a16_moe_decode" if router_w is None else "moe_layer_decode"
     check_moe_error(ctrl)
     if x_stage is None:
@@ -238,7 +239,6 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
          f"{op}: w13 / w2 shapes do not match H={H}")
     _req(fmt in ("int4", "nvfp4"), f"{op}: fmt must be 'int4' or 'nvfp4'")
     if fmt == "nvfp4":
-        _req(router_w is None and x_stage is None, f"{op}: NVFP4 experts take the routing as input (no fused router)")
         _req(s13.dtype == torch.uint8 and tuple(s13.shape) == (E, 2 * I * H // 16) and s13.is_contiguous(),
              f"{op}: NVFP4 s13 must be the E4M3 scales uint8 [E, 2I*H/16] (formats.repack_nvfp4)")
         _req(s2.dtype == torch.uint8 and tuple(s2.shape) == (E, H * I // 16) and s2.is_contiguous(),
@@ -279,7 +279,8 @@ def a16_moe_decode(x, topk_ids, topk_w, w13, s13, gs13, w2, s2, gs2, w_gate, sha
              f"{op}: logits must be a contiguous bf16 [M, E] tensor on x's device")
         _req(int(phase) in (3, 4), f"{op}: phase must be 3 or 4")
         with torch.cuda.device(dev):
-            _lib.check(_lib.load().qf_moe_layer_decode(
+            layer_entry = _lib.load().qf_moe_layer_decode_nvfp4 if fmt == "nvfp4" else _lib.load().qf_moe_layer_decode
+            _lib.check(layer_entry(
                 x.data_ptr(), _ptr(x_stage), router_w.data_ptr(), int(bool(renormalize)), topk_w.data_ptr(),
                 topk_ids.data_ptr(),
                 logits.data_ptr(), w13.data_ptr(), s13.data_ptr(), _ptr(gs13), w2.data_ptr(), s2.data_ptr(),

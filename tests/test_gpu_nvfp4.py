@@ -71,3 +71,38 @@ def test_nvfp4_layer(cuda, E, H, I, topk, M, Is):
     if not Is:
         truth = nvfp4_ref.truth(x, ids, w, C["w13"], C["s13"], C["g13"], C["w2"], C["s2"], C["g2"])
     _assert_close(outs[0], ref, truth)
+
+
+@pytest.mark.parametrize("M", [1, 10])
+def test_nvfp4_fused_router_layer_step(cuda, M):
+    """NVFP4 experts with the router inside the launch (qf_moe_layer_decode_nvfp4): the logits equal the standalone
+    router's bit for bit (the same arithmetic), so ids, weights and the layer output equal the two-launch path
+    (router_topk, then the NVFP4 MoE op); ids are the oracle's given the logits."""
+    E, H, I, topk = 64, 2048, 512, 10
+    C = _layer(E, H, I, seed=90 + M)
+    g = torch.Generator().manual_seed(91 + M)
+    x = torch.randn(M, H, generator=g).to(BF).to(cuda)
+    wk13, sk13 = formats.repack_nvfp4(C["w13"].to(cuda), C["s13"].to(cuda), gated=True)
+    wk2, sk2 = formats.repack_nvfp4(C["w2"].to(cuda), C["s2"].to(cuda), gated=False)
+    gs13 = (1.0 / C["g13"][:, 0]).to(BF).to(cuda)
+    gs2 = (1.0 / C["g2"]).to(BF).to(cuda)
+    router = C["router"].to(cuda)
+    bufs = ops.moe_workspace(M, H, I, topk, 0, cuda)
+    tw = torch.empty(M, topk, dtype=torch.float32, device=cuda)
+    ids = torch.empty(M, topk, dtype=torch.int32, device=cuda)
+    lg = torch.empty(M, E, dtype=BF, device=cuda)
+    out_f = torch.empty_like(x)
+    ops.a16_moe_decode(x, ids, tw, wk13, sk13, gs13, wk2, sk2, gs2, None, None, bufs["hbuf"], bufs["ybuf"],
+                       bufs["gl"], bufs["ctrl"], out_f, 4, None, bufs["pbuf"], None, None, None, None, bufs["shbuf"],
+                       fmt="nvfp4", router_w=router, logits=lg)
+    w2_, ids2, lg2 = ops.router_topk(x, router, topk, True, *ops.router_bufs(cuda))
+    out_u = torch.empty_like(x)
+    ops.a16_moe_decode(x, ids2, w2_, wk13, sk13, gs13, wk2, sk2, gs2, None, None, bufs["hbuf"], bufs["ybuf"],
+                       bufs["gl"], bufs["ctrl"], out_u, 4, None, bufs["pbuf"], None, None, None, None, bufs["shbuf"],
+                       fmt="nvfp4")
+    torch.cuda.synchronize()
+    assert ops.moe_error_word(bufs["ctrl"]) == 0
+    assert torch.equal(lg, lg2)
+    assert torch.equal(ids, ids2) and torch.equal(tw, w2_) and torch.equal(out_f, out_u)
+    ow, oids = router_ref.topk_from_logits(lg.cpu(), topk, True)
+    assert torch.equal(ids.cpu(), oids)
