@@ -37,20 +37,19 @@ constexpr int ROWS = 128;                 // weight rows per tile
 constexpr int SK = 128;                   // k per stage
 constexpr int STAGE = ROWS * SK;          // 16 KB of int8
 constexpr int NST = 3;                    // ring stages
-constexpr int KS_MAX = 12;                // stages per item
+constexpr int KS_MAX = 16;                // stages per item
 constexpr int S_MAX = 8;                  // splits per tile
-constexpr int MT = 16;                    // staged token rows (M <= 16)
-constexpr int TOK_STAGE = 2 * MT * 128;   // fp16 token slices of one stage: [half][token][128 B]
-constexpr int PART = MT * ROWS;           // floats of one fixup slot
+constexpr int PART = 16 * ROWS;           // floats of one fixup slot (16 per consumer thread)
 constexpr uint64_t WAIT_NS = 2000000000ull;
 
-// shared memory (base aligned to 1024 for the swizzled TMA tiles): ring [NST][STAGE] | tokens [ks][TOK_STAGE] |
-// factors float [ks][2][MT] | scales float [ks][2][ROWS] | full[NST], empty[NST] | flag
+// shared memory (base aligned to 1024 for the swizzled TMA tiles), mt = the staged token rows (8, or 16 with the
+// second n8 token tile): ring [NST][STAGE] | tokens [ks][2 halves][mt][128 B] (fp16) | factors float [ks][2][mt] |
+// scales float [ks][2][ROWS] | full[NST], empty[NST] | flag
 __host__ __device__ constexpr int off_tok() { return NST * STAGE; }
-__host__ __device__ constexpr int off_fac(int ks) { return off_tok() + ks * TOK_STAGE; }
-__host__ __device__ constexpr int off_sc(int ks) { return off_fac(ks) + ks * 2 * MT * 4; }
-__host__ __device__ constexpr int off_bar(int ks) { return off_sc(ks) + ks * 2 * ROWS * 4; }
-__host__ __device__ constexpr int smem_bytes(int ks) { return off_bar(ks) + 2 * NST * 8 + 16 + 1024; }
+__host__ __device__ constexpr int off_fac(int ks, int mt) { return off_tok() + ks * 2 * mt * 128; }
+__host__ __device__ constexpr int off_sc(int ks, int mt) { return off_fac(ks, mt) + ks * 2 * mt * 4; }
+__host__ __device__ constexpr int off_bar(int ks, int mt) { return off_sc(ks, mt) + ks * 2 * ROWS * 4; }
+__host__ __device__ constexpr int smem_bytes(int ks, int mt) { return off_bar(ks, mt) + 2 * NST * 8 + 16 + 1024; }
 
 struct Params {
     CUtensorMap wmap;   // q [N, K] uint8; box 128 k x 128 rows, 128-byte swizzle
@@ -95,10 +94,11 @@ __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ks = p.ks;
     uint8_t* ring = smem;
+    constexpr int MT = TWO ? 16 : 8;   // staged token rows
     uint8_t* tok = smem + off_tok();
-    float* fac = reinterpret_cast<float*>(smem + off_fac(ks));
-    float* sc = reinterpret_cast<float*>(smem + off_sc(ks));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + off_bar(ks));
+    float* fac = reinterpret_cast<float*>(smem + off_fac(ks, MT));
+    float* sc = reinterpret_cast<float*>(smem + off_sc(ks, MT));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + off_bar(ks, MT));
     uint64_t* empty = full + NST;
     int* flag = reinterpret_cast<int*>(empty + NST);
     const int item = blockIdx.x, tile = item / p.S, split = item - tile * p.S;

@@ -384,11 +384,13 @@ __device__ unsigned g_w8g_err;
 #include "w8g_rf.cuh"
 
 // The register-fragment kernel's launch (M <= 16, K % 128 == 0): ks stages per item chosen so that the grid covers
-// the SMs about two CTAs deep with at most S_MAX splits per tile (S = ceil(K / 128 / ks)), raised up to KS_MAX while
-// the grid is larger than one wave; a grid under 7/8 of a wave reduces the splits in a cluster per tile, a fuller one
-// through the fixup buffer (at most `cap` slots). Returns cudaErrorNotSupported when K needs more than
-// KS_MAX * S_MAX stages, when no ks gives a one-wave grid, for two token tiles over more CTAs than two per SM, or when
-// the slots do not fit (the caller then uses the tensor-memory kernel).
+// the SMs about two CTAs deep with at most S_MAX splits per tile (S = ceil(K / 128 / ks)), raised while the grid is
+// larger than one wave. The shared memory is sized first as for 16 staged token rows with at most 12 stages (the CTA
+// placement measured best wherever that fits one wave); for up to 8 tokens, a shape that does not fit that way is
+// sized by its 8 staged rows with up to KS_MAX stages (more CTAs per SM). A grid under 7/8 of a wave reduces the
+// splits in a cluster per tile, a fuller one through the fixup buffer (at most `cap` slots). Returns
+// cudaErrorNotSupported when no sizing gives a one-wave grid, for two token tiles over more CTAs than two per SM, or
+// when the slots do not fit (the caller then uses the tensor-memory kernel).
 cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, void* y, int ldy, float* fix,
                           uint32_t* cnt, long long cap, int M, int N, int K, int group, int sms, bool pdl, unsigned* err,
                           cudaStream_t st) {
@@ -396,16 +398,23 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     const int tiles = N / ROWS, KT = K / SK;
     // about two items per SM, at least ceil(KT / S_MAX) stages per item (the last split adds at most S_MAX slots)
     const long long target = 2LL * sms;
-    int ks = (int)std::min<long long>(KS_MAX, ((long long)tiles * KT + target - 1) / target);
-    ks = std::max(std::max(1, ks), (KT + S_MAX - 1) / S_MAX);
-    if (ks > KS_MAX) return cudaErrorNotSupported;   // K above KS_MAX * S_MAX * 128
     // one wave (the CTAs that fit an SM's shared memory, on every SM) only: grids of several waves gave run-to-run
     // differences in stress runs (cause not found), so longer splits are tried first and then the tensor-memory kernel
-    auto wave_of = [&](int k) { return (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(k))); };
-    while (ks < KS_MAX && (long long)tiles * ((KT + ks - 1) / ks) > wave_of(ks)) ++ks;
-    const int S = (KT + ks - 1) / ks;
-    const long long wave = wave_of(ks);
-    if ((long long)tiles * S > wave) return cudaErrorNotSupported;
+    int ks = 0, S = 0, smem = 0;
+    long long wave = 0;
+    auto pick = [&](int rows, int ks_max) {   // smem sized for `rows` staged token rows, at most ks_max stages
+        int k = (int)std::min<long long>(ks_max, ((long long)tiles * KT + target - 1) / target);
+        k = std::max(std::max(1, k), (KT + S_MAX - 1) / S_MAX);
+        if (k > ks_max) return false;   // K above ks_max * S_MAX * 128
+        auto wave_of = [&](int kk) { return (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(kk, rows))); };
+        while (k < ks_max && (long long)tiles * ((KT + k - 1) / k) > wave_of(k)) ++k;
+        ks = k;
+        S = (KT + k - 1) / k;
+        wave = wave_of(k);
+        smem = smem_bytes(k, rows);
+        return (long long)tiles * S <= wave;
+    };
+    if (!pick(16, 12) && !(M <= 8 && pick(8, KS_MAX))) return cudaErrorNotSupported;
     // two token tiles over more than two CTAs per SM: the tensor-memory kernel (one stream per SM) is faster there
     if (M > 8 && (long long)tiles * S > target) return cudaErrorNotSupported;
     // clusters when the grid fills at most 7/8 of the wave: a fuller wave leaves clusters that find no room in a GPC
@@ -432,9 +441,9 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     p.cl = cl;
     p.err = err;
     p.ldx = ldx; p.ldy = ldy; p.M = M; p.N = N; p.K = K; p.group = group; p.ks = ks; p.S = S; p.KT = KT;
-    const int smem = smem_bytes(ks);
+    // (smem: the sizing picked above, at least what the kernel's layout for M uses)
     auto kern = M > 8 ? w8g_rf_kernel<true> : w8g_rf_kernel<false>;
-    e = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem_bytes(KS_MAX));
+    e = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem_bytes(KS_MAX, 16));
     if (e != cudaSuccess) return e;
     static bool carveout_set[2] = {false, false};
     if (!carveout_set[M > 8]) {   // several CTAs per SM need the largest shared-memory carveout
