@@ -470,7 +470,9 @@ def run_ours(args):
                "sample": f"{n_cpu} config-{cfg_id} layer-steps (M={M}) of the CPU oracle, torch fp32 on {cores} threads"}
 
     if rank == 0:
-        traffic = load_traffic("moe_persistent_kernel")
+        # the committed capture is of the config-1 one-GPU launch (profiles/moe_persistent_kernel_config1_M10.md);
+        # other workloads have no capture of their own
+        traffic = load_traffic("moe_persistent_kernel") if cfg_id == 1 and world == 1 else None
         if cfg_id == 1:
             wl = (f"config1 decode MoE layer-step (router top-10 + 512-expert W4A16 + bf16 shared expert + combine), "
                   f"M={M}")
@@ -500,8 +502,10 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "kernel": "moe_persistent_kernel (layer-step launch, router inside)",
                          "bytes_per_launch": r["launch_b"],
-                         "traffic": traffic, "traffic_source": "profiles/traffic.json: ncu dram bytes of one launch "
-                                                               "of this config, scaled by its distinct experts"},
+                         "traffic": traffic,
+                         "traffic_source": ("profiles/traffic.json: ncu dram read + write bytes of one config-1 "
+                                            "launch (M=10, one GPU)") if traffic is not None else
+                                           "no ncu capture of this workload"},
             "e2e": {"value": r["e2e_us"], "unit": UNIT, "h2d_bytes_per_step": M * cfg.H * 2,
                     "d2h_bytes_per_step": M * cfg.H * 2, "steps": r["e2e_steps"]},
             # ours per step: the fused layer-step launch (+ the combine under expert parallelism; the all-reduce is
