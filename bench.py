@@ -202,9 +202,11 @@ def run_reference(args):
     cfg_id = args.config or (4 if world > 1 else 1)
     cfg = synthetic.CONFIGS[cfg_id]
     M = args.M or cfg.M
-    us, n, cores = time_cpu(cfg, M, args.steps, 4, budget_s=150.0)
+    warm = max(4, args.warmup)   # at least one pass over the four inputs (every routed expert materialised)
+    us, n, cores = time_cpu(cfg, M, args.steps, warm, budget_s=150.0)
     line = {"impl": "reference", "metric": METRIC, "value": us, "unit": UNIT, "n_gpus": args.gpus, "steps": n,
-            "warmup": 4, "ms_per_step": us / 1e3, "higher_is_better": False, "scaling": "weak",
+            "warmup": args.warmup, "warmup_run": warm, "ms_per_step": us / 1e3, "higher_is_better": False,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "bf16/int4 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": f"config{cfg_id} MoE layer-step M={M} (CPU oracle port of the reference torch path)",
                        "config_id": cfg_id, "H": cfg.H, "E": cfg.E, "I": cfg.I, "topk": cfg.topk, "Is": cfg.Is,
