@@ -13,9 +13,9 @@
 //   * One CTA per item = (128-row tile, split of the K stages): the tiles' K / 128 stages are cut into S splits of ks
 //     stages each, S chosen so that the grid covers the GPU about two CTAs deep (S <= S_MAX). 160 threads: warps 0-3 consume,
 //     warp 4 (one lane) is the producer.
-//   * Producer: an NST-stage ring of 16 KB weight stages (128 rows x 128 k, one TMA 2-D tile each, 128-byte swizzle:
-//     the four 16-byte chunks a lane reads are spread over all banks), requested before griddepcontrol.wait (the
-//     weights are load-time data).
+//   * Producer: a ring of 16 KB weight stages, 3 deep (4 for items of at most 5 stages), each 128 rows x 128 k, one
+//     TMA 2-D tile with 128-byte swizzle (the four 16-byte chunks a lane reads are spread over all banks), requested
+//     before griddepcontrol.wait (the weights are load-time data).
 //   * Consumers, first: the item's token slices (fp16 with the per-(token, 64-k) exponent, 16-byte chunks swizzled by
 //     token) and group scales into shared memory; then per stage and 64-k half, warp w runs the m16 tiles 2w, 2w + 1:
 //     one 16-byte load per row and half gives the four k16 steps of that row (k = 64 h + 16 t4 + 4 s + 0..3 in the
@@ -36,20 +36,23 @@ constexpr int THREADS = 160;
 constexpr int ROWS = 128;                 // weight rows per tile
 constexpr int SK = 128;                   // k per stage
 constexpr int STAGE = ROWS * SK;          // 16 KB of int8
-constexpr int NST = 3;                    // ring stages
+constexpr int NST_SHORT = 4;              // ring stages for items of at most KS_SHORT stages (else 3)
+constexpr int KS_SHORT = 5;
 constexpr int KS_MAX = 16;                // stages per item
 constexpr int S_MAX = 8;                  // splits per tile
 constexpr int PART = 16 * ROWS;           // floats of one fixup slot (16 per consumer thread)
 constexpr uint64_t WAIT_NS = 2000000000ull;
 
-// shared memory (base aligned to 1024 for the swizzled TMA tiles), mt = the staged token rows (8, or 16 with the
-// second n8 token tile): ring [NST][STAGE] | tokens [ks][2 halves][mt][128 B] (fp16) | factors float [ks][2][mt] |
-// scales float [ks][2][ROWS] | full[NST], empty[NST] | flag
-__host__ __device__ constexpr int off_tok() { return NST * STAGE; }
-__host__ __device__ constexpr int off_fac(int ks, int mt) { return off_tok() + ks * 2 * mt * 128; }
-__host__ __device__ constexpr int off_sc(int ks, int mt) { return off_fac(ks, mt) + ks * 2 * mt * 4; }
-__host__ __device__ constexpr int off_bar(int ks, int mt) { return off_sc(ks, mt) + ks * 2 * ROWS * 4; }
-__host__ __device__ constexpr int smem_bytes(int ks, int mt) { return off_bar(ks, mt) + 2 * NST * 8 + 16 + 1024; }
+// shared memory (base aligned to 1024 for the swizzled TMA tiles), nst = the ring stages, mt = the staged token
+// rows (8, or 16 with the second n8 token tile): ring [nst][STAGE] | tokens [ks][2 halves][mt][128 B] (fp16) |
+// factors float [ks][2][mt] | scales float [ks][2][ROWS] | full[nst], empty[nst] | flag
+__host__ __device__ constexpr int off_tok(int nst) { return nst * STAGE; }
+__host__ __device__ constexpr int off_fac(int ks, int mt, int nst) { return off_tok(nst) + ks * 2 * mt * 128; }
+__host__ __device__ constexpr int off_sc(int ks, int mt, int nst) { return off_fac(ks, mt, nst) + ks * 2 * mt * 4; }
+__host__ __device__ constexpr int off_bar(int ks, int mt, int nst) { return off_sc(ks, mt, nst) + ks * 2 * ROWS * 4; }
+__host__ __device__ constexpr int smem_bytes(int ks, int mt, int nst) {
+    return off_bar(ks, mt, nst) + 2 * nst * 8 + 16 + 1024;
+}
 
 struct Params {
     CUtensorMap wmap;   // q [N, K] uint8; box 128 k x 128 rows, 128-byte swizzle
@@ -87,7 +90,7 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
     return v;
 }
 
-template <bool TWO>
+template <bool TWO, int NST>
 __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -95,10 +98,10 @@ __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__
     const int ks = p.ks;
     uint8_t* ring = smem;
     constexpr int MT = TWO ? 16 : 8;   // staged token rows
-    uint8_t* tok = smem + off_tok();
-    float* fac = reinterpret_cast<float*>(smem + off_fac(ks, MT));
-    float* sc = reinterpret_cast<float*>(smem + off_sc(ks, MT));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + off_bar(ks, MT));
+    uint8_t* tok = smem + off_tok(NST);
+    float* fac = reinterpret_cast<float*>(smem + off_fac(ks, MT, NST));
+    float* sc = reinterpret_cast<float*>(smem + off_sc(ks, MT, NST));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + off_bar(ks, MT, NST));
     uint64_t* empty = full + NST;
     int* flag = reinterpret_cast<int*>(empty + NST);
     const int item = blockIdx.x, tile = item / p.S, split = item - tile * p.S;

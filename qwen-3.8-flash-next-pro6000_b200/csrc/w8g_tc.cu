@@ -400,21 +400,31 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     const long long target = 2LL * sms;
     // one wave (the CTAs that fit an SM's shared memory, on every SM) only: grids of several waves gave run-to-run
     // differences in stress runs (cause not found), so longer splits are tried first and then the tensor-memory kernel
-    int ks = 0, S = 0, smem = 0;
+    int ks = 0, S = 0, smem = 0, rows_used = 16, nst = 3;
     long long wave = 0;
+    auto wave_of = [&](int kk, int rows, int stages) {
+        return (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(kk, rows, stages)));
+    };
     auto pick = [&](int rows, int ks_max) {   // smem sized for `rows` staged token rows, at most ks_max stages
         int k = (int)std::min<long long>(ks_max, ((long long)tiles * KT + target - 1) / target);
         k = std::max(std::max(1, k), (KT + S_MAX - 1) / S_MAX);
         if (k > ks_max) return false;   // K above ks_max * S_MAX * 128
-        auto wave_of = [&](int kk) { return (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(kk, rows))); };
-        while (k < ks_max && (long long)tiles * ((KT + k - 1) / k) > wave_of(k)) ++k;
+        while (k < ks_max && (long long)tiles * ((KT + k - 1) / k) > wave_of(k, rows, 3)) ++k;
         ks = k;
         S = (KT + k - 1) / k;
-        wave = wave_of(k);
-        smem = smem_bytes(k, rows);
+        wave = wave_of(k, rows, 3);
+        smem = smem_bytes(k, rows, 3);
+        rows_used = rows;
         return (long long)tiles * S <= wave;
     };
     if (!pick(16, 12) && !(M <= 8 && pick(8, KS_MAX))) return cudaErrorNotSupported;
+    // a ring of four stages for short items, where the grid still fits one wave with it (measured: 7-16 % faster for
+    // items of at most KS_SHORT stages, 3-5 % slower for longer ones)
+    if (ks <= KS_SHORT && (long long)tiles * S <= wave_of(ks, rows_used, NST_SHORT)) {
+        nst = NST_SHORT;
+        wave = wave_of(ks, rows_used, NST_SHORT);
+        smem = smem_bytes(ks, rows_used, NST_SHORT);
+    }
     // two token tiles over more than two CTAs per SM: the tensor-memory kernel (one stream per SM) is faster there
     if (M > 8 && (long long)tiles * S > target) return cudaErrorNotSupported;
     // clusters when the grid fills at most 7/8 of the wave: a fuller wave leaves clusters that find no room in a GPC
@@ -442,15 +452,17 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     p.err = err;
     p.ldx = ldx; p.ldy = ldy; p.M = M; p.N = N; p.K = K; p.group = group; p.ks = ks; p.S = S; p.KT = KT;
     // (smem: the sizing picked above, at least what the kernel's layout for M uses)
-    auto kern = M > 8 ? w8g_rf_kernel<true> : w8g_rf_kernel<false>;
-    e = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem_bytes(KS_MAX, 16));
+    const bool four = nst == NST_SHORT;
+    auto kern = M > 8 ? (four ? w8g_rf_kernel<true, NST_SHORT> : w8g_rf_kernel<true, 3>)
+                      : (four ? w8g_rf_kernel<false, NST_SHORT> : w8g_rf_kernel<false, 3>);
+    e = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem_bytes(KS_MAX, 16, nst));
     if (e != cudaSuccess) return e;
-    static bool carveout_set[2] = {false, false};
-    if (!carveout_set[M > 8]) {   // several CTAs per SM need the largest shared-memory carveout
+    static bool carveout_set[2][2] = {{false, false}, {false, false}};
+    if (!carveout_set[M > 8][four]) {   // several CTAs per SM need the largest shared-memory carveout
         e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
-        carveout_set[M > 8] = true;
+        carveout_set[M > 8][four] = true;
     }
     // with cl, the S splits of a tile are one cluster (S <= S_MAX = 8, the portable cluster size)
     cudaLaunchConfig_t cfg = {};
