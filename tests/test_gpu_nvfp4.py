@@ -106,3 +106,32 @@ def test_nvfp4_fused_router_layer_step(cuda, M):
     assert torch.equal(ids, ids2) and torch.equal(tw, w2_) and torch.equal(out_f, out_u)
     ow, oids = router_ref.topk_from_logits(lg.cpu(), topk, True)
     assert torch.equal(ids.cpu(), oids)
+
+
+@pytest.mark.parametrize("M", [1, 10])
+def test_nvfp4_split_phases_equal_whole_layer(cuda, M):
+    """The reference's split phases on NVFP4 experts: phase 1 (gate logits, gate_up + SwiGLU) then phase 2 (down,
+    weighting, combine with a precomputed shared term) give the bits of the one-launch layer (phase 4)."""
+    E, H, I, topk = 64, 2048, 512, 10
+    C = _layer(E, H, I, seed=70 + M)
+    g = torch.Generator().manual_seed(71 + M)
+    x = torch.randn(M, H, generator=g).to(BF).to(cuda)
+    shared = (torch.randn(M, H, generator=g) * 0.05).to(BF).to(cuda)
+    w_gate = (torch.randn(H, generator=g) * 0.02).to(BF).to(cuda)
+    wk13, sk13 = formats.repack_nvfp4(C["w13"].to(cuda), C["s13"].to(cuda), gated=True)
+    wk2, sk2 = formats.repack_nvfp4(C["w2"].to(cuda), C["s2"].to(cuda), gated=False)
+    gs13 = (1.0 / C["g13"][:, 0]).to(BF).to(cuda)
+    gs2 = (1.0 / C["g2"]).to(BF).to(cuda)
+    w, ids, _ = ops.router_topk(x, C["router"].to(cuda), topk, True, *ops.router_bufs(cuda))
+    outs = {}
+    for phases in ((4,), (1, 2)):
+        bufs = ops.moe_workspace(M, H, I, topk, 0, cuda)
+        out = torch.empty_like(x)
+        for phase in phases:
+            ops.a16_moe_decode(x, ids, w, wk13, sk13, gs13, wk2, sk2, gs2, w_gate, shared, bufs["hbuf"],
+                               bufs["ybuf"], bufs["gl"], bufs["ctrl"], out, phase, None, bufs["pbuf"], None, None,
+                               None, None, bufs["shbuf"], fmt="nvfp4")
+        torch.cuda.synchronize()
+        assert ops.moe_error_word(bufs["ctrl"]) == 0
+        outs[phases] = out
+    assert torch.equal(outs[(4,)], outs[(1, 2)])
