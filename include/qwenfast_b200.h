@@ -203,8 +203,8 @@ int qf_bf16_unpack(const void* wk, void* w, int N, int K, int gated, qf_stream_t
  * W8A16 group-scaled INT8 GEMM: y[M, N] = x[M, K] @ (q * s)^T, fp32 accumulation, bf16 out (tcgen05 tensor cores).
  * Replaces `w8g_gemm` (serve/qwenfast/qf_w8g.cu:303-336, binding serve/qwenfast/qf_bind.cpp:42,133);
  *   x bf16 [M, K] row stride ldx (ldx % 8 == 0, 16-byte aligned); q int8 [N, K] canonical row-major (16-byte
- *   aligned); s bf16 [N, K/group]; y bf16 [M, N] row stride ldy. M 1..QF_MAX_TOKENS, N % 128 == 0, K % 64 == 0,
- *   group 128 or 64. Every product is exact (int8 weights and tokens scaled by a power of two as fp16) and the sums
+ *   aligned); s bf16 [N, K/group]; y bf16 [M, N] row stride ldy. M 1..QF_MAX_TOKENS, N >= 8 and N % 8 == 0 (a last
+ *   tile of 128 rows past N computes zeros there), K % 64 == 0, group 128 or 64. Every product is exact (int8 weights and tokens scaled by a power of two as fp16) and the sums
  *   are fp32; the result does not depend on timing.
  *   fix: caller-owned float buffer of qf_w8g_fixup_elems(N) elements, zero-filled before its first use; every call
  *   leaves its counters zero again (after a non-zero qf_w8g_take_status, zero it again). Calls that may run

@@ -176,11 +176,11 @@ __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__
             }
         }
         // group scales of row tid (one per half: a 128-group gives both halves the same scale), all requested at once
-        const __nv_bfloat16* srow = p.s + (size_t)(tile * ROWS + tid) * (p.K / p.group);
+        const __nv_bfloat16* srow = p.s + (size_t)min(tile * ROWS + tid, p.N - 1) * (p.K / p.group);   // rows past N: 0
         __nv_bfloat16 sv[2 * KS_MAX];
 #pragma unroll
         for (int jh = 0; jh < 2 * KS_MAX; ++jh)
-            if (jh < 2 * nks) sv[jh] = srow[(kb + jh * 64) / p.group];
+            if (jh < 2 * nks) sv[jh] = tile * ROWS + tid < p.N ? srow[(kb + jh * 64) / p.group] : __float2bfloat16(0.f);
 #pragma unroll
         for (int jh = 0; jh < 2 * KS_MAX; ++jh)
             if (jh < 2 * nks) sc[jh * ROWS + tid] = __bfloat162float(sv[jh]);
@@ -263,9 +263,8 @@ __global__ void __launch_bounds__(THREADS) w8g_rf_kernel(const __grid_constant__
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const int t = 8 * n + 2 * t4 + (i & 1);
-                    if (t < M)
-                        p.y[(size_t)t * p.ldy + tile * ROWS + 16 * (2 * rw + m) + g + 8 * (i >> 1)] =
-                            __float2bfloat16(a[2 * m + n][i]);
+                    const int yrow = tile * ROWS + 16 * (2 * rw + m) + g + 8 * (i >> 1);
+                    if (t < M && yrow < p.N) p.y[(size_t)t * p.ldy + yrow] = __float2bfloat16(a[2 * m + n][i]);
                 }
     };
     if (p.S == 1) {

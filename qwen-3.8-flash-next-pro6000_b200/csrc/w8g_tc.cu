@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(G_THREADS, Cfg<NT>::MINB)
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int KT = K / G_UK;
-    const long long units = (long long)(N / G_UN) * KT;
+    const long long units = (long long)((N + G_UN - 1) / G_UN) * KT;   // a last tile past N: rows of zeros
     const int runs = gridDim.x;
     const int u0 = run_start(units, blockIdx.x, runs), u1 = run_start(units, blockIdx.x + 1, runs);
     const int nu = u1 - u0;
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(G_THREADS, Cfg<NT>::MINB)
         // the scale of this thread's row for unit u
         auto row_scale = [&](int u) {
             const int n = (u / KT) * G_UN + row;
-            return qf::bf16_bits(__ldg(s + (size_t)n * GS + ((u % KT) * G_UK) / G));
+            return n < N ? qf::bf16_bits(__ldg(s + (size_t)n * GS + ((u % KT) * G_UK) / G)) : 0.f;
         };
         int i = 0;
         float sc_next = nu > 0 ? row_scale(u0) : 0.f;
@@ -335,7 +335,7 @@ __global__ void __launch_bounds__(G_THREADS, Cfg<NT>::MINB)
             if (end - su == KT) {   // the whole tile: no other run contributes
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
-                    if (t0 + t < M) y[(size_t)(t0 + t) * ldy + n] = __float2bfloat16(acc[t]);
+                    if (t0 + t < M && n < N) y[(size_t)(t0 + t) * ldy + n] = __float2bfloat16(acc[t]);
                 continue;
             }
             // a tile split over several runs: this run's part goes to its slot (run r owns slots 2r -- the tile of
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(G_THREADS, Cfg<NT>::MINB)
             }
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-                if (t0 + t < M) y[(size_t)(t0 + t) * ldy + n] = __float2bfloat16(acc[t]);
+                if (t0 + t < M && n < N) y[(size_t)(t0 + t) * ldy + n] = __float2bfloat16(acc[t]);
             if (tid == 0) fixc[tile] = 0u;   // re-armed for the next call
             qf::named_bar(1, 128);           // lastf is rewritten by the next segment
         }
@@ -395,7 +395,7 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
                           uint32_t* cnt, long long cap, int M, int N, int K, int group, int sms, bool pdl, unsigned* err,
                           cudaStream_t st) {
     using namespace w8rf;
-    const int tiles = N / ROWS, KT = K / SK;
+    const int tiles = (N + ROWS - 1) / ROWS, KT = K / SK;   // a last tile past N: rows of zeros
     // about two items per SM, at least ceil(KT / S_MAX) stages per item (the last split adds at most S_MAX slots)
     const long long target = 2LL * sms;
     // one wave (the CTAs that fit an SM's shared memory, on every SM) only: grids of several waves gave run-to-run
@@ -539,7 +539,7 @@ cudaError_t qf::encode_tiled_fn(EncodeTiled* fn) {
 }
 
 extern "C" int qf_w8g_fixup_elems(int N, int64_t* elems) {
-    QF_REQUIRE(elems && N >= 128 && N % 128 == 0, "w8g_fixup_elems: N must be a multiple of 128, got %d", N);
+    QF_REQUIRE(elems && N >= 8 && N % 8 == 0, "w8g_fixup_elems: N must be a multiple of 8, got %d", N);
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return qf::cuda_status(e, "w8g_fixup_elems: cudaGetDevice");
@@ -549,7 +549,7 @@ extern "C" int qf_w8g_fixup_elems(int N, int64_t* elems) {
     // slot for more), then one counter per 128-row tile
     *elems = (int64_t)sms * 2 * 4 * 16 * G_UN;
     if ((int64_t)sms * 2 * 2 * 64 * G_UN > *elems) *elems = (int64_t)sms * 2 * 2 * 64 * G_UN;
-    *elems += N / G_UN;
+    *elems += (N + G_UN - 1) / G_UN;
     return QF_OK;
 }
 
@@ -563,7 +563,7 @@ extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const vo
     QF_REQUIRE(!(force_tm && forbid_tm), "w8g_gemm: rpw cannot both force (0x100) and forbid (0x200) the tensor-memory kernel");
     QF_REQUIRE(x && q && s && y && fix, "w8g_gemm: null pointer argument");
     QF_REQUIRE(M >= 1 && M <= QF_MAX_TOKENS, "w8g_gemm: M must be in [1, %d], got %d", QF_MAX_TOKENS, M);
-    QF_REQUIRE(N >= 128 && N % 128 == 0, "w8g_gemm: N must be a multiple of 128, got %d", N);
+    QF_REQUIRE(N >= 8 && N % 8 == 0, "w8g_gemm: N must be a multiple of 8, got %d", N);
     QF_REQUIRE(K >= 64 && K % 64 == 0 && K <= (1 << 20), "w8g_gemm: K must be a multiple of 64, got %d", K);
     QF_REQUIRE(group == 128 || group == 64, "w8g_gemm: group must be 128 or 64, got %d", group);
     QF_REQUIRE(K % group == 0, "w8g_gemm: K must be a multiple of the group size");
@@ -585,9 +585,10 @@ extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const vo
     const int sms = qf::sm_count(dev);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     float* fixp = fix;
-    uint32_t* fixc = reinterpret_cast<uint32_t*>(fix + (need - N / G_UN));
+    const int ntiles = (N + G_UN - 1) / G_UN;
+    uint32_t* fixc = reinterpret_cast<uint32_t*>(fix + (need - ntiles));
     if (!force_tm && M <= 16 && K % w8rf::SK == 0) {   // decode token counts: the register-fragment kernel
-        e = launch_w8g_rf(q, x, (int)ldx, s, y, (int)ldy, fixp, fixc, (need - N / G_UN) / w8rf::PART, M, N, K, group,
+        e = launch_w8g_rf(q, x, (int)ldx, s, y, (int)ldy, fixp, fixc, (need - ntiles) / w8rf::PART, M, N, K, group,
                           sms, pdl != 0, err, st);
         if (e != cudaErrorNotSupported) return qf::cuda_status(e, "w8g_gemm: launch");
     }
@@ -609,7 +610,7 @@ extern "C" int qf_w8g_gemm(const void* x, int64_t ldx, const int8_t* q, const vo
                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     QF_REQUIRE(cr == CUDA_SUCCESS, "w8g_gemm: cuTensorMapEncodeTiled failed (%d)", (int)cr);
-    const long long units = (long long)(N / G_UN) * (K / G_UK);
+    const long long units = (long long)ntiles * (K / G_UK);
     const int NT = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     if (NT == 16) e = launch_w8g_tc<16>(map, x, (int)ldx, s, y, (int)ldy, fixp, fixc, M, N, K, group, 0, units, sms, pdl != 0, err, st);
     else if (NT == 32) e = launch_w8g_tc<32>(map, x, (int)ldx, s, y, (int)ldy, fixp, fixc, M, N, K, group, 0, units, sms, pdl != 0, err, st);

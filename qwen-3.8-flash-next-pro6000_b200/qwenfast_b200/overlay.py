@@ -54,7 +54,7 @@ def w8_quant(w: torch.Tensor, rows_per_chunk: int = 8192) -> dict:
 
 def w8_route(entry, x: torch.Tensor, bias=None) -> Optional[str]:
     """None when ``w8_linear`` runs the kernel for this call, else the first failing condition (the decline path's
-    reason): the gate of qwenfast.py:346-349 with this build's limits (M <= 64 rows, output rows a multiple of 128,
+    reason): the gate of qwenfast.py:346-349 with this build's limits (M <= 64 rows, output rows a multiple of 8,
     K % 64 == 0, G 128 or 64)."""
     p, r0, r1 = entry
     N, K = p["shape"]
@@ -63,7 +63,7 @@ def w8_route(entry, x: torch.Tensor, bias=None) -> Optional[str]:
     checks = (
         ("bias", bias is None),
         ("rows", 1 <= M <= _lib.QF_MAX_TOKENS),
-        ("shape", (r1 - r0) % 128 == 0),
+        ("shape", r1 - r0 >= 8 and (r1 - r0) % 8 == 0),
         ("group", p["G"] in (64, 128) and K % 64 == 0 and K % p["G"] == 0),
         ("dtype", x2.dtype == BF16),
         ("layout", x2.stride(1) == 1 and x2.stride(0) % 8 == 0 and x2.data_ptr() % 16 == 0),

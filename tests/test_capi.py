@@ -69,7 +69,7 @@ def test_gemms_reject_bad_arguments(lib):
     p = ctypes.c_void_p(256)
     assert lib.qf_w8g_gemm(p, 2048, p, p, p, 2048, 0, 2048, 2048, 128, 0, p, 1 << 30, 0, None) == -1
     assert lib.qf_w8g_gemm(p, 2048, p, p, p, 2048, 4, 2048, 2048, 96, 0, p, 1 << 30, 0, None) == -1
-    assert lib.qf_w8g_gemm(p, 2048, p, p, p, 2048, 4, 2000, 2048, 128, 0, p, 1 << 30, 0, None) == -1
+    assert lib.qf_w8g_gemm(p, 2048, p, p, p, 2048, 4, 2004, 2048, 128, 0, p, 1 << 30, 0, None) == -1   # N % 8
     assert lib.qf_w8a8_gemm(p, 2048, p, p, p, 2048, 4, 2048, 2000, p, p, None, None, 1, None) == -1
     assert lib.qf_w4_repack(p, p, p, p, 1, 100, 256, 1, None) == -1
 

@@ -14,7 +14,8 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("N,K", [(2048, 2048), (1280, 2560), (2560, 640), (2560, 6144), (4096, 2048), (12288, 2560),
-                                 (16384, 2048), (8192, 6144), (12288, 6144)])
+                                 (16384, 2048), (8192, 6144), (12288, 6144), (16480, 2560), (13312, 2560),
+                                 (200, 256)])
 @pytest.mark.parametrize("M", [1, 2, 4, 8, 16, 64])
 def test_w8g_gemm_vs_fp32_truth(cuda, N, K, M):
     g = torch.Generator(device="cpu").manual_seed(N + K + M)

@@ -39,7 +39,8 @@ def test_w8_route_gate_reasons():
     e64 = (overlay.w8_quant(torch.randn(128, 192).to(BF)), 0, 128)
     assert e64[0]["G"] == 64 and overlay.w8_route(e64, torch.randn(3, 192).to(BF)) == "device"
     assert overlay.w8_route(e, x) == "device"                                 # CPU tensors never reach the kernel
-    assert overlay.w8_route((e[0], 0, 200), x) == "shape"                     # output rows not a multiple of 128
+    assert overlay.w8_route((e[0], 0, 200), x) == "device"                    # 200 rows: a multiple of 8 qualifies
+    assert overlay.w8_route((e[0], 0, 204), x) == "shape"                     # output rows not a multiple of 8
 
 
 def test_w8_linear_empty_rows():
