@@ -34,6 +34,9 @@
 //   * Every wait is bounded; a wait that runs out sets a bit of the sticky status word (qf_w8g_take_status) and
 //     the CTA drains (the affected outputs are undefined).
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "qf_common.cuh"
 
@@ -391,6 +394,50 @@ __device__ unsigned g_w8g_err;
 // splits in a cluster per tile, a fuller one through the fixup buffer (at most `cap` slots). Returns
 // cudaErrorNotSupported when no sizing gives a one-wave grid, for two token tiles over more CTAs than two per SM, or
 // when the slots do not fit (the caller then uses the tensor-memory kernel).
+// A decode-kernel instantiation (two token tiles, four ring stages) with its attributes set: the dynamic shared
+// memory limit for its largest sizing and the largest carveout (several CTAs per SM need it).
+static void* rf_kernel(bool two, bool four, cudaError_t* e) {
+    using namespace w8rf;
+    void* kern = two ? (four ? (void*)w8g_rf_kernel<true, NST_SHORT> : (void*)w8g_rf_kernel<true, 3>)
+                     : (four ? (void*)w8g_rf_kernel<false, NST_SHORT> : (void*)w8g_rf_kernel<false, 3>);
+    *e = qf::ensure_smem_attr(kern, smem_bytes(KS_MAX, 16, four ? NST_SHORT : 3));
+    if (*e != cudaSuccess) return nullptr;
+    static bool carveout_set[2][2] = {{false, false}, {false, false}};
+    if (!carveout_set[two][four]) {
+        *e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                  (int)cudaSharedmemCarveoutMaxShared);
+        if (*e != cudaSuccess) return nullptr;
+        carveout_set[two][four] = true;
+    }
+    return kern;
+}
+
+// CTAs of that instantiation one SM holds at once with `smem` bytes of dynamic shared memory, as the runtime counts
+// them (registers, shared memory and its per-CTA reservation); cached per (device, instantiation, size). 0 on error.
+static int rf_ctas_per_sm(bool two, bool four, int smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, int>, int> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const auto key = std::make_tuple(dev, (int)two, (int)four, smem);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        const auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    cudaError_t e = cudaSuccess;
+    void* kern = rf_kernel(two, four, &e);
+    int n = 0;
+    if (kern == nullptr || cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, w8rf::THREADS, (size_t)smem) !=
+                               cudaSuccess) {
+        (void)cudaGetLastError();
+        return 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = n;
+    return n;
+}
+
 cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, void* y, int ldy, float* fix,
                           uint32_t* cnt, long long cap, int M, int N, int K, int group, int sms, bool pdl, unsigned* err,
                           cudaStream_t st) {
@@ -398,12 +445,12 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     const int tiles = (N + ROWS - 1) / ROWS, KT = K / SK;   // a last tile past N: rows of zeros
     // about two items per SM, at least ceil(KT / S_MAX) stages per item (the last split adds at most S_MAX slots)
     const long long target = 2LL * sms;
-    // one wave (the CTAs that fit an SM's shared memory, on every SM) only: grids of several waves gave run-to-run
+    // one wave (the CTAs resident at once on every SM, as the runtime counts them) only: grids of several waves gave run-to-run
     // differences in stress runs (cause not found), so longer splits are tried first and then the tensor-memory kernel
     int ks = 0, S = 0, smem = 0, rows_used = 16, nst = 3;
     long long wave = 0;
-    auto wave_of = [&](int kk, int rows, int stages) {
-        return (long long)sms * std::max(1, (int)(227 * 1024 / smem_bytes(kk, rows, stages)));
+    auto wave_of = [&](int kk, int rows, int stages) {   // the CTAs resident at once on the whole GPU
+        return (long long)sms * rf_ctas_per_sm(M > 8, stages == NST_SHORT, smem_bytes(kk, rows, stages));
     };
     auto pick = [&](int rows, int ks_max) {   // smem sized for `rows` staged token rows, at most ks_max stages
         int k = (int)std::min<long long>(ks_max, ((long long)tiles * KT + target - 1) / target);
@@ -452,18 +499,8 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     p.err = err;
     p.ldx = ldx; p.ldy = ldy; p.M = M; p.N = N; p.K = K; p.group = group; p.ks = ks; p.S = S; p.KT = KT;
     // (smem: the sizing picked above, at least what the kernel's layout for M uses)
-    const bool four = nst == NST_SHORT;
-    auto kern = M > 8 ? (four ? w8g_rf_kernel<true, NST_SHORT> : w8g_rf_kernel<true, 3>)
-                      : (four ? w8g_rf_kernel<false, NST_SHORT> : w8g_rf_kernel<false, 3>);
-    e = qf::ensure_smem_attr(reinterpret_cast<const void*>(kern), smem_bytes(KS_MAX, 16, nst));
-    if (e != cudaSuccess) return e;
-    static bool carveout_set[2][2] = {{false, false}, {false, false}};
-    if (!carveout_set[M > 8][four]) {   // several CTAs per SM need the largest shared-memory carveout
-        e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 (int)cudaSharedmemCarveoutMaxShared);
-        if (e != cudaSuccess) return e;
-        carveout_set[M > 8][four] = true;
-    }
+    void* kern = rf_kernel(M > 8, nst == NST_SHORT, &e);
+    if (kern == nullptr) return e;
     // with cl, the S splits of a tile are one cluster (S <= S_MAX = 8, the portable cluster size)
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(tiles * S);
@@ -479,7 +516,8 @@ cudaError_t launch_w8g_rf(const void* q, const void* x, int ldx, const void* s, 
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, p);
+    void* args[] = {&p};
+    return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
 template <int NT>
