@@ -412,6 +412,107 @@ def moe_layer_step(x: torch.Tensor, lw: MoELayerWeights, topk: int, bufs: dict, 
     return out, tw, ids, logits
 
 
+class LayerStep:
+    """``moe_layer_step`` (fused router, int4 experts) prepared for one layer's weights and one workspace.
+
+    Every check of the weights and the workspace (types, shapes, devices) runs once, here, and the C-ABI argument list
+    is built once; a call checks x and out only, reads the workspace's host error mirror and makes one
+    ``qf_moe_layer_decode`` call (the C ABI still checks sizes, alignment and M on every call). The routing outputs
+    (topk_w fp32 [M, topk], topk_ids int32 [M, topk], logits bf16 [M, E]) are views of buffers this object holds, so
+    they are valid until its next call. Where the fused grid cannot be co-resident (``_lib.Unsupported``), a call
+    takes ``moe_layer_step``'s two launches instead, with router scratch made on first use."""
+
+    def __init__(self, lw: MoELayerWeights, topk: int, bufs: dict, renormalize: bool = True, pdl: bool = True):
+        op = "LayerStep"
+        dev = lw.w13.device
+        _req(dev.type == "cuda", f"{op}: the weights must be CUDA tensors")
+        H, I, E, Is = lw.H, lw.I, lw.E, lw.Is
+        _req(1 <= topk <= _lib.QF_MAX_TOPK and topk <= E, f"{op}: topk must be in [1, min(E, {_lib.QF_MAX_TOPK})]")
+
+        def tensor(t, name, dtype, numel):
+            _req(t is not None and t.dtype == dtype and t.is_contiguous() and t.numel() == numel and t.device == dev,
+                 f"{op}: {name} must be a contiguous {dtype} tensor of {numel} elements on the weights' device")
+
+        tensor(lw.router, "router", BF16, E * H)
+        tensor(lw.w13, "w13", torch.int32, E * 2 * I * H // 8)
+        tensor(lw.s13, "s13", BF16, E * 2 * I * H // 128)
+        tensor(lw.w2, "w2", torch.int32, E * H * I // 8)
+        tensor(lw.s2, "s2", BF16, E * H * I // 128)
+        has_shw = lw.sh_w13 is not None
+        _req(has_shw == (lw.sh_w2 is not None) and has_shw == (Is > 0), f"{op}: give both shared-expert weights, or none")
+        if has_shw:
+            tensor(lw.sh_w13, "sh_w13", BF16, 2 * Is * H)
+            tensor(lw.sh_w2, "sh_w2", BF16, H * Is)
+        if lw.w_gate is not None:
+            tensor(lw.w_gate, "w_gate", BF16, H)
+        for name in ("hbuf", "ybuf", "gl", "ctrl", "pbuf", "shbuf"):
+            t = bufs.get(name)
+            _req(t is not None and t.device == dev and t.is_contiguous(), f"{op}: workspace {name} missing or misplaced")
+        self.lw, self.topk, self.bufs, self.renormalize, self.pdl, self.dev = lw, topk, bufs, renormalize, pdl, dev
+        cap = _lib.QF_MAX_TOKENS
+        self._tw = torch.empty(cap, topk, dtype=torch.float32, device=dev)
+        self._ids = torch.empty(cap, topk, dtype=torch.int32, device=dev)
+        self._logits = torch.empty(cap, E, dtype=BF16, device=dev)
+        self._err = bufs["err_host"].numpy() if "err_host" in bufs else None
+        self._rbufs = None
+        b = bufs
+        nbytes = lambda t: t.numel() * t.element_size()   # noqa: E731
+        # qf_moe_layer_decode's arguments: (x, x_stage) + head + (out, M) + tail + (stream,)
+        self._head = (lw.router.data_ptr(), int(bool(renormalize)), self._tw.data_ptr(), self._ids.data_ptr(),
+                      self._logits.data_ptr(), lw.w13.data_ptr(), lw.s13.data_ptr(), None, lw.w2.data_ptr(),
+                      lw.s2.data_ptr(), None, _ptr(lw.w_gate), None, _ptr(lw.sh_w13) if has_shw else None,
+                      _ptr(lw.sh_w2) if has_shw else None, b["hbuf"].data_ptr(), nbytes(b["hbuf"]),
+                      b["ybuf"].data_ptr(), nbytes(b["ybuf"]), b["gl"].data_ptr(), b["gl"].numel(),
+                      b["ctrl"].data_ptr(), b["ctrl"].numel(), b["pbuf"].data_ptr(), b["pbuf"].numel(),
+                      b["shbuf"].data_ptr(), nbytes(b["shbuf"]))
+        self._tail = (H, I, E, topk, Is, 0, 0, E, None, int(bool(pdl)))
+        self._fn = _lib.load().qf_moe_layer_decode
+        self._fused = True
+        self._views = {}   # M -> the routing outputs' views
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor, x_stage: Optional[torch.Tensor] = None):
+        """One layer-step on x (bf16 [M, H]: a CUDA tensor, or a pinned host tensor with ``x_stage`` a CUDA bf16
+        [M, H] buffer) into out (bf16 [M, H]: CUDA, or pinned host memory with ``x_stage``). Returns
+        (out, topk_w, topk_ids, logits)."""
+        op = "LayerStep"
+        if self._err is not None and self._err[0] != 0:
+            check_moe_error(self.bufs["ctrl"])          # raises, after resetting the workspace
+        M = x.shape[0]
+        _req(x.dtype == BF16 and x.dim() == 2 and x.shape[1] == self.lw.H and x.is_contiguous(),
+             f"{op}: x must be contiguous bf16 [M, H]")
+        _req(out.dtype == BF16 and out.shape == x.shape and out.is_contiguous(), f"{op}: out must be bf16 [M, H]")
+        if x_stage is None:
+            _req(x.device == self.dev and out.device == self.dev, f"{op}: x and out must be on the weights' device")
+            xs = None
+        else:
+            _req(not x.is_cuda and x.is_pinned(), f"{op}: with x_stage, x must be a pinned host tensor")
+            _req(x_stage.device == self.dev and x_stage.dtype == BF16 and x_stage.shape == x.shape
+                 and x_stage.is_contiguous(), f"{op}: x_stage must be contiguous bf16 [M, H] on the weights' device")
+            _req(out.device == self.dev or (not out.is_cuda and out.is_pinned()),
+                 f"{op}: out must be on the weights' device or in pinned host memory")
+            xs = x_stage.data_ptr()
+        if self._fused:
+            try:
+                if torch.cuda.current_device() == self.dev.index:
+                    st = self._fn(x.data_ptr(), xs, *self._head, out.data_ptr(), M, *self._tail,
+                                  torch.cuda.current_stream().cuda_stream)
+                else:
+                    with torch.cuda.device(self.dev):
+                        st = self._fn(x.data_ptr(), xs, *self._head, out.data_ptr(), M, *self._tail,
+                                      torch.cuda.current_stream().cuda_stream)
+                _lib.check(st, "moe_layer_decode")
+                v = self._views.get(M)
+                if v is None:
+                    v = self._views[M] = (self._tw[:M], self._ids[:M], self._logits[:M])
+                return (out,) + v
+            except _lib.Unsupported:
+                self._fused = False
+        if self._rbufs is None:
+            self._rbufs = router_bufs(self.dev, _lib.QF_MAX_TOKENS, self.lw.E)
+        return moe_layer_step(x, self.lw, self.topk, self.bufs, self._rbufs, out, self.renormalize, self.pdl,
+                              fused=False, x_stage=x_stage)
+
+
 # ------------------------------------------------------------------------------------------------- INT8
 _W8G_FIXUP = {}
 
