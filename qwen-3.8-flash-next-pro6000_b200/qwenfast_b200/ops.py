@@ -572,6 +572,50 @@ def w8g_take_status() -> int:
     return v.value
 
 
+class W8Linear:
+    """``w8g_gemm`` prepared for one weight (q int8 [N, K], s bf16 [N, K/group]): the weight's checks, its group size
+    and its C-ABI arguments are made once; a call checks x, allocates y (or writes ``out``) and makes one
+    ``qf_w8g_gemm`` call with the current stream's fixup buffer (``w8g_fixup``, looked up once per stream). Same
+    launch and bits as ``w8g_gemm(x, q, s, rpw, pdl)``; the C ABI still checks sizes and alignment on every call."""
+
+    def __init__(self, q: torch.Tensor, s: torch.Tensor, rpw: int = 0, pdl: bool = False):
+        op = "W8Linear"
+        _req(q.is_cuda and s.is_cuda and q.device == s.device, f"{op}: q and s must be CUDA tensors on one device")
+        _req(q.dtype == torch.int8 and s.dtype == BF16 and q.dim() == 2 and s.dim() == 2 and q.is_contiguous()
+             and s.is_contiguous(), f"{op}: q must be contiguous int8 [N, K] and s contiguous bf16 [N, K/group]")
+        _req(s.size(0) == q.size(0) and q.size(1) % s.size(1) == 0, f"{op}: scale shape")
+        self.q, self.s, self.dev = q, s, q.device
+        self.N, self.K = q.shape
+        self.group = self.K // s.shape[1]
+        self._args = (q.data_ptr(), s.data_ptr())
+        self._rpw, self._pdl = int(rpw), int(bool(pdl))
+        self._fix = {}   # stream handle -> (fixup pointer, elements, the buffer)
+        self._fn = _lib.load().qf_w8g_gemm
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        op = "W8Linear"
+        _req(x.dtype == BF16 and x.dim() == 2 and x.shape[1] == self.K and x.stride(1) == 1 and x.device == self.dev,
+             f"{op}: x must be bf16 [M, K] with unit column stride on the weight's device")
+        M, N = x.shape[0], self.N
+        if out is None:
+            out = torch.empty(M, N, dtype=BF16, device=self.dev)
+        else:
+            _req(out.dtype == BF16 and out.dim() == 2 and out.shape[0] == M and out.shape[1] == N
+                 and out.is_contiguous() and out.device == self.dev, f"{op}: out must be contiguous bf16 [M, N]")
+        if torch.cuda.current_device() != self.dev.index:
+            with torch.cuda.device(self.dev):
+                return self(x, out)
+        stream = torch.cuda.current_stream()
+        st = stream.cuda_stream
+        fx = self._fix.get(st)
+        if fx is None:
+            buf = w8g_fixup(N, self.dev, stream)
+            fx = self._fix[st] = (buf.data_ptr(), buf.numel(), buf)
+        _lib.check(self._fn(x.data_ptr(), x.stride(0), *self._args, out.data_ptr(), N, M, N, self.K, self.group,
+                            self._rpw, fx[0], fx[1], self._pdl, st), "w8g_gemm")
+        return out
+
+
 def w8g_unpack(q: torch.Tensor, s: torch.Tensor, w: torch.Tensor):
     """w bf16 [rows, K] <- bf16(q * s). Mirrors ``w8g_unpack`` (serve/qwenfast/qf_w8g.cu:338-351)."""
     op = "w8g_unpack"

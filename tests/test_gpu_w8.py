@@ -164,3 +164,29 @@ def test_w8g_rpw_force_and_forbid_bits(cuda):
     with pytest.raises(RuntimeError, match="cannot both"):
         ops.w8g_gemm(xd, qd, sd, 0x300)
     assert ops.w8g_take_status() == 0
+
+
+def test_w8linear_equals_w8g_gemm(cuda):
+    """ops.W8Linear (the weight's checks and C-ABI arguments made once) launches what w8g_gemm launches: the same bits
+    for several M, group 128 and 64, a caller-given out, a strided x, and a second stream (its own fixup buffer)."""
+    g = torch.Generator(device="cpu").manual_seed(12)
+    for N, K in ((2048, 2048), (12288, 2560), (264, 192), (200, 256)):   # (264, 192): group 64
+        q, s = w8_ref.w8_quant((torch.randn(N, K, generator=g) * 0.02).to(torch.bfloat16))
+        qd, sd = q.to(cuda), s.to(cuda)
+        lin = ops.W8Linear(qd, sd)
+        for M in (1, 4, 16, 64):
+            x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(cuda)
+            assert torch.equal(lin(x), ops.w8g_gemm(x, qd, sd))
+        out = torch.empty(4, N, dtype=torch.bfloat16, device=cuda)
+        xs = torch.randn(4, 2 * K, generator=g).to(torch.bfloat16).to(cuda)[:, :K]
+        assert lin(xs, out) is out and torch.equal(out, ops.w8g_gemm(xs, qd, sd))
+        side = torch.cuda.Stream(cuda)
+        with torch.cuda.stream(side):
+            y2 = lin(xs)
+        side.synchronize()
+        assert torch.equal(y2, out)
+    with pytest.raises(RuntimeError, match="x must be"):
+        lin(torch.randn(2, 128, device=cuda).to(torch.bfloat16))
+    with pytest.raises(RuntimeError, match="out must be"):
+        lin(torch.randn(2, 256, device=cuda).to(torch.bfloat16), torch.empty(3, 200, dtype=torch.bfloat16, device=cuda))
+    assert ops.w8g_take_status() == 0
