@@ -687,3 +687,48 @@ def w8a8_take_status() -> int:
         for buf in _W8A8_FIXUP.values():
             buf.zero_()
     return v.value
+
+
+class W8A8Linear:
+    """``w8a8_gemm`` prepared for one weight (q int8 [N, K] in the ``formats.repack_w8`` layout, sw fp32 [N]): the
+    weight's checks and C-ABI arguments are made once, and per stream the fixup buffer (``w8a8_fixup``) and the
+    quantised-activation scratch (xq int8 [16*K], sx fp32 [16]) are made on first use and reused, stream-ordered. A
+    call checks x, allocates y (or writes ``out``) and makes one ``qf_w8a8_gemm`` call: the same launch and bits as
+    ``w8a8_gemm(x, q, sw, pdl=pdl)``."""
+
+    def __init__(self, q: torch.Tensor, sw: torch.Tensor, pdl: bool = True):
+        op = "W8A8Linear"
+        _req(q.is_cuda and sw.device == q.device, f"{op}: q and sw must be CUDA tensors on one device")
+        _req(q.dtype == torch.int8 and q.dim() == 2 and q.is_contiguous(), f"{op}: q must be contiguous int8 [N, K]")
+        _req(sw.dtype == torch.float32 and sw.numel() == q.size(0) and sw.is_contiguous(), f"{op}: sw fp32 [N]")
+        self.q, self.sw, self.dev = q, sw, q.device
+        self.N, self.K = q.shape
+        self._args = (q.data_ptr(), sw.data_ptr())
+        self._pdl = int(bool(pdl))
+        self._per_stream = {}   # stream handle -> (xq, sx, fixup pointer or None, the tensors)
+        self._fn = _lib.load().qf_w8a8_gemm
+
+    def __call__(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        op = "W8A8Linear"
+        _req(x.dtype == BF16 and x.dim() == 2 and x.shape[1] == self.K and x.stride(1) == 1 and x.device == self.dev,
+             f"{op}: x must be bf16 [M, K] with unit column stride on the weight's device")
+        M, N = x.shape[0], self.N
+        if out is None:
+            out = torch.empty(M, N, dtype=BF16, device=self.dev)
+        else:
+            _req(out.dtype == BF16 and out.dim() == 2 and out.shape[0] == M and out.shape[1] == N
+                 and out.is_contiguous() and out.device == self.dev, f"{op}: out must be contiguous bf16 [M, N]")
+        if torch.cuda.current_device() != self.dev.index:
+            with torch.cuda.device(self.dev):
+                return self(x, out)
+        stream = torch.cuda.current_stream()
+        st = stream.cuda_stream
+        ps = self._per_stream.get(st)
+        if ps is None:
+            xq = torch.empty(16 * self.K, dtype=torch.int8, device=self.dev)
+            sx = torch.empty(16, dtype=torch.float32, device=self.dev)
+            fix = w8a8_fixup(N, self.dev, stream) if N % 128 == 0 else None
+            ps = self._per_stream[st] = (xq.data_ptr(), sx.data_ptr(), _ptr(fix), (xq, sx, fix))
+        _lib.check(self._fn(x.data_ptr(), x.stride(0), *self._args, out.data_ptr(), N, M, N, self.K, ps[0], ps[1],
+                            ps[2], None, self._pdl, st), "w8a8_gemm")
+        return out

@@ -190,3 +190,28 @@ def test_w8linear_equals_w8g_gemm(cuda):
     with pytest.raises(RuntimeError, match="out must be"):
         lin(torch.randn(2, 256, device=cuda).to(torch.bfloat16), torch.empty(3, 200, dtype=torch.bfloat16, device=cuda))
     assert ops.w8g_take_status() == 0
+
+
+def test_w8a8linear_equals_w8a8_gemm_and_oracle(cuda):
+    """ops.W8A8Linear (the weight's checks and arguments made once, per-stream scratch reused) gives the bits of
+    w8a8_gemm and of the oracle: N with and without the fixup buffer (N % 128), several M in a row on one scratch,
+    a caller-given out, and a second stream."""
+    for N, K in ((2048, 2048), (12288, 2048), (384, 640)):
+        q, sw = synthetic.make_w8a8(N, K, seed=N + 1)
+        lin = ops.W8A8Linear(formats.repack_w8(q.to(cuda)), sw.to(cuda))
+        for M in (1, 16, 4, 10):
+            x = synthetic.make_w8a8_tokens(M, K, seed=M + N)
+            y = lin(x.to(cuda))
+            yr, _, _, _ = w8_ref.w8a8_ref(x, q, sw)
+            assert torch.equal(y.cpu(), yr), (N, M)
+            assert torch.equal(y, ops.w8a8_gemm(x.to(cuda), lin.q, lin.sw))
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+        side = torch.cuda.Stream(cuda)
+        side.wait_stream(torch.cuda.current_stream(cuda))
+        with torch.cuda.stream(side):
+            lin(x.to(cuda), out)
+        side.synchronize()
+        assert torch.equal(out.cpu(), yr)
+    with pytest.raises(RuntimeError, match="x must be"):
+        lin(torch.randn(2, 128, device=cuda).to(torch.bfloat16))
+    assert ops.w8a8_take_status() == 0
