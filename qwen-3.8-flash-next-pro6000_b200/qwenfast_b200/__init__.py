@@ -5,8 +5,9 @@ Ops (reference names, serve/qwenfast/qf_bind.cpp): ``router_topk``, ``a16_moe_de
 The kernels live in ``libqwenfast_b200.so`` (C ABI: include/qwenfast_b200.h), built in-tree by ``build.build()``.
 """
 from . import _lib, formats, synthetic  # noqa: F401
-from .ops import (LayerStep, MoELayerWeights, a16_moe_decode, moe_error_word, moe_layer_step,  # noqa: F401
-                  moe_workspace, router_bufs, router_topk, w8a8_gemm, w8g_gemm, w8g_unpack)
+from .ops import (LayerStep, MoELayerWeights, W8A8Linear, W8Linear, a16_moe_decode,  # noqa: F401
+                  moe_error_word, moe_layer_step, moe_workspace, router_bufs, router_topk, w8a8_gemm, w8g_gemm, w8g_unpack)
 
 __all__ = ["router_topk", "a16_moe_decode", "w8g_gemm", "w8g_unpack", "w8a8_gemm", "moe_workspace", "router_bufs",
-           "moe_layer_step", "LayerStep", "MoELayerWeights", "moe_error_word", "formats", "synthetic"]
+           "moe_layer_step", "LayerStep", "MoELayerWeights", "W8Linear", "W8A8Linear", "moe_error_word", "formats",
+           "synthetic"]
